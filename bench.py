@@ -1,0 +1,385 @@
+"""Benchmark of the mHC pre-op training step (forward + backward) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    (N > 1: python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...)
+
+Workload (per GPU, weak scaling): B=4, S=4096, n=4, D=4096 -- the LLM-scale
+configuration the metric is quoted on.  One step = forward with the outflag
+intermediates + backward + (N > 1) one NCCL all-reduce of the flat parameter
+gradient buffer.  Inputs are synthetic, seeded, and larger than L2 (x alone is
+512 MiB per GPU), so no L2 flush is needed between steps.
+
+Prints ONE JSON line on rank 0.  `value` is whole-job tokens/s with inputs
+resident in HBM; `e2e` is the same metric through the public API with the
+step's inputs copied from pinned host memory and the parameter gradients read
+back every step.  `roofline` reports the dominant call (algorithmic bytes /
+CUDA-event time) against the measured HBM copy bandwidth.  `cpu_baseline` is
+the CPU oracle (a numpy restatement of the reference golden) on a bounded token
+sample, spread over all host cores.  `--impl reference` times that CPU
+implementation alone on the same workload (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "fwd+bwd tokens/s and HBM GB/s (% of roofline) at n=4,D=4096, 1/2/4/8 B200"
+WORKLOAD = dict(B=4, S=4096, n=4, D=4096)
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ------------------------------------------------------------------ byte model
+def fwd_bytes_per_token(n, D):
+    N = n * n + 2 * n
+    return 2 * n * D + 2 * D + 4 * n + 4 * n * n + 4 + 4 * N + 4 * n
+
+
+def bwd_bytes_per_token(n, D):
+    N = n * n + 2 * n
+    return 2 * n * D + 2 * D + 4 * n + 4 * n * n + 4 * n + 4 * n + 4 * N + 4 + 2 * n * D
+
+
+def fwd_param_bytes(n, D):
+    N = n * n + 2 * n
+    return 4 * N * n * D
+
+
+def bwd_param_bytes(n, D):
+    N = n * n + 2 * n
+    return 8 * N * n * D + 8 * n * D + 4 * (3 + N)
+
+
+def measured_hbm_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            v = float(json.load(f)["hbm_gbs"])
+        return v, "measured"
+    except Exception:  # noqa: BLE001
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# ------------------------------------------------------------- CPU (oracle) leg
+def _oracle_chunk(args):
+    """fwd+bwd of the oracle on one token chunk (runs in a spawned worker)."""
+    import numpy as np
+    from oracle import mhc_oracle as O
+    xb, phi, alpha, bias, dh_in, dh_post, dh_res, gamma = args
+    f = O.forward(xb, phi, alpha, bias, outflag=True)
+    b = O.backward(xb, phi, alpha, bias, f[3], f[4], f[5], f[1], dh_in, dh_post, dh_res, gamma)
+    return float(np.abs(b[1]).sum())
+
+
+def cpu_oracle_rate(tokens: int, n: int, D: int, steps: int = 1, workers: int | None = None):
+    """Tokens/s of the CPU oracle on `tokens` tokens, spread over a spawn pool."""
+    import multiprocessing as mp
+    import numpy as np
+    import torch
+    from mhc_ops_b200.synthetic import make_inputs
+    workers = workers or (os.cpu_count() or 1)
+    workers = max(1, min(workers, tokens))
+    inp = make_inputs(1, tokens, n, D, seed=99)
+    u16 = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    xb, dh = u16(inp.x), u16(inp.dh_in)
+    bounds = [(tokens * i // workers, tokens * (i + 1) // workers) for i in range(workers)]
+    jobs = [(xb[:, a:b], inp.phi.numpy(), inp.alpha.numpy(), inp.bias.numpy(), dh[:, a:b],
+             inp.dh_post[:, a:b].numpy(), inp.dh_res[:, a:b].numpy(), inp.gamma.numpy()) for a, b in bounds if b > a]
+    env_keep = {k: os.environ.get(k) for k in ("OPENBLAS_NUM_THREADS", "OMP_NUM_THREADS", "MKL_NUM_THREADS")}
+    for k in env_keep:
+        os.environ[k] = "1"
+    try:
+        ctx = mp.get_context("spawn")
+        with ctx.Pool(len(jobs)) as pool:
+            pool.map(_oracle_chunk, [(j[0][:, :1],) + j[1:4] + (j[4][:, :1], j[5][:, :1], j[6][:, :1], j[7])
+                                     for j in jobs])      # warm the workers
+            times = []
+            for _ in range(steps):
+                t0 = time.perf_counter()
+                pool.map(_oracle_chunk, jobs)
+                times.append(time.perf_counter() - t0)
+    finally:
+        for k, v in env_keep.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+    return tokens / statistics.median(times), len(jobs), times
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.out = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(", ") for r in out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    w = WORKLOAD
+    sample = args.ref_tokens
+    _, cores, times = cpu_oracle_rate(sample, w["n"], w["D"], steps=args.warmup + args.steps)
+    value = sample / statistics.median(times[args.warmup:])
+    T = w["B"] * w["S"]
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * T / value,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "mHC pre-op fwd+bwd, B=4,S=4096,n=4,D=4096 per GPU", **w,
+                   "tokens_per_step_sampled": sample},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{sample} tokens of the B=4,S=4096,n=4,D=4096 workload per step, "
+                                   f"numpy restatement of the reference golden fwd(outflag)+bwd, "
+                                   f"{cores} spawn workers x 1 BLAS thread; CPU {cpu_model()}"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+
+    from mhc_ops_b200 import _lib, mhc_backward_manual, mhc_forward_pre
+    from mhc_ops_b200.backward import param_grad_numel
+
+    w = WORKLOAD
+    B, S, n, D = w["B"], w["S"], w["n"], w["D"]
+    N, nD, T = n * n + 2 * n, n * D, w["B"] * w["S"]
+
+    # parameters: identical on every rank; token data: per-rank seeds
+    gp = torch.Generator().manual_seed(0)
+    phi = (torch.randn(N, nD, generator=gp) / math.sqrt(nD)).to(dev)
+    alpha = torch.tensor([1.1, 0.9, 1.05], device=dev)
+    bias = (0.1 * torch.randn(N, generator=gp)).to(dev)
+    gamma = (1.0 + 0.1 * torch.randn(n, D, generator=gp)).to(dev)
+    gd = torch.Generator(device=dev).manual_seed(1000 + rank)
+    x = torch.randn(B, S, n, D, generator=gd, device=dev, dtype=torch.bfloat16)
+    dh_in = torch.randn(B, S, D, generator=gd, device=dev, dtype=torch.bfloat16)
+    dh_post = torch.randn(B, S, n, generator=gd, device=dev)
+    dh_res = torch.randn(B, S, n, n, generator=gd, device=dev)
+    flat = torch.empty(param_grad_numel(n, D), device=dev)
+
+    def step():
+        out = mhc_forward_pre(x, phi, alpha, bias, outflag=True)
+        ev[1].record()
+        mhc_backward_manual(x, phi, alpha, bias, out[3], out[4], out[5], out[1], dh_in, dh_post, dh_res, gamma,
+                            grad_out=flat)
+        ev[2].record()
+        if world > 1:
+            dist.all_reduce(flat)
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    for _ in range(args.warmup):
+        ev[0].record()
+        step()
+    sync_all()
+
+    # timed region (device-resident inputs)
+    clocks = ClockSampler()
+    if rank == 0:
+        clocks.start()
+    launches0 = _lib.launch_count()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sync_all()
+    start.record()
+    for _ in range(args.steps):
+        ev[0].record()
+        step()
+    stop.record()
+    sync_all()
+    total_ms = max_over_ranks(start.elapsed_time(stop))
+    launches = _lib.launch_count() - launches0
+    clk = clocks.stop() if rank == 0 else None
+
+    # per-call durations (separate pass, same work, events between the calls)
+    fwd_ms, bwd_ms = [], []
+    for _ in range(max(3, args.steps)):
+        ev[0].record()
+        step()
+        torch.cuda.synchronize()
+        fwd_ms.append(ev[0].elapsed_time(ev[1]))
+        bwd_ms.append(ev[1].elapsed_time(ev[2]))
+    fwd_ms = max_over_ranks(statistics.median(fwd_ms))
+    bwd_ms = max_over_ranks(statistics.median(bwd_ms))
+
+    # e2e: host buffers, copies inside the timed region
+    e2e = None
+    if not args.no_e2e:
+        hx = x.cpu().pin_memory()
+        hdh = dh_in.cpu().pin_memory()
+        hpost = dh_post.cpu().pin_memory()
+        hres = dh_res.cpu().pin_memory()
+        hflat = torch.empty_like(flat, device="cpu").pin_memory()
+        h2d = sum(t.numel() * t.element_size() for t in (hx, hdh, hpost, hres))
+        d2h = hflat.numel() * hflat.element_size()
+        for it in range(args.warmup + args.steps):
+            if it == args.warmup:
+                sync_all()
+                start.record()
+            x.copy_(hx, non_blocking=True)
+            dh_in.copy_(hdh, non_blocking=True)
+            dh_post.copy_(hpost, non_blocking=True)
+            dh_res.copy_(hres, non_blocking=True)
+            ev[0].record()
+            step()
+            hflat.copy_(flat, non_blocking=True)
+        stop.record()
+        sync_all()
+        e2e_ms = max_over_ranks(start.elapsed_time(stop))
+        e2e = {"value": world * T * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "path": "mhc_forward_pre + mhc_backward_manual (public API, C ABI), pinned host buffers"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, cores, _ = cpu_oracle_rate(args.cpu_tokens, n, D, steps=1)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"{args.cpu_tokens} tokens of the B=4,S=4096,n=4,D=4096 workload, numpy restatement of "
+                         f"the reference golden fwd(outflag)+bwd, {cores} spawn workers; CPU {cpu_model()}"}
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    ms_per_step = total_ms / args.steps
+    value = world * T / (ms_per_step / 1e3)
+    peak, peak_kind = measured_hbm_peak()
+    fwd_alg = fwd_bytes_per_token(n, D) * T + fwd_param_bytes(n, D)
+    bwd_alg = bwd_bytes_per_token(n, D) * T + bwd_param_bytes(n, D)
+    step_alg = fwd_alg + bwd_alg
+    dom = ("mhc_bwd", bwd_alg, bwd_ms) if bwd_ms >= fwd_ms else ("mhc_fwd", fwd_alg, fwd_ms)
+    achieved = dom[1] / (dom[2] / 1e3) / 1e9
+    traffic = load_profile_traffic(dom[0])
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "mHC pre-op fwd(outflag)+bwd, B=4,S=4096,n=4,D=4096 per GPU (LLM-scale config)",
+                   **w, "global_tokens": world * T, "parallelism": f"dp{world} (token shards, NCCL all-reduce of "
+                   "param grads)", "l2": "inputs larger than L2 (x is 512 MiB per GPU); no flush"},
+        "hbm_gbs_step": step_alg / (ms_per_step / 1e3) / 1e9 / 1.0,
+        "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_source": peak_kind, "traffic": traffic,
+                     "algorithmic_bytes": dom[1], "ms": dom[2],
+                     "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+                     "fwd_frac": fwd_alg / (fwd_ms / 1e3) / 1e9 / peak,
+                     "bwd_frac": bwd_alg / (bwd_ms / 1e3) / 1e9 / peak},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def load_profile_traffic(kernel_call: str):
+    """DRAM bytes per launch of the dominant call from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f).get(kernel_call)
+    except Exception:  # noqa: BLE001
+        return None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-tokens", type=int, default=2048)
+    ap.add_argument("--ref-tokens", type=int, default=1024)
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)   # at least 3 untimed warm-up steps, whatever was asked
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,159 @@
+/*
+ * mhc_ops.h -- C ABI of the B200 (sm_100a) mHC pre-op library (libmhc_ops.so).
+ *
+ * The manifold-constrained hyper-connection pre-op of folrent1896/mhc_ops,
+ * forward and backward.  Every entry point takes plain device pointers and
+ * sizes, launches on the given CUDA stream (a cudaStream_t passed as void*;
+ * NULL = legacy default stream) and returns an mhc_status.  No entry point
+ * allocates device memory except where its comment says so: scratch comes
+ * from a caller-owned workspace whose size the *_workspace_size query returns.
+ * Calls hold no global mutable state and may be issued from several host
+ * threads; two calls that share one workspace must be ordered on the device.
+ * A workspace must be zero-filled once before its first use (its first
+ * bytes hold the device status word, see mhc_read_device_status).
+ *
+ * Shapes: T tokens (= B*S of the reference), n streams, D hidden, nD = n*D,
+ * N = n*n + 2n.  Tensors are dense row-major:
+ *   x [T,n,D] bf16, phi [N,nD] f32, alpha [3] f32, bias [N] f32,
+ *   h_in [T,D] bf16, h_post [T,n] f32, h_res [T,n,n] f32,
+ *   inv_rms [T] f32, h_mix [T,N] f32 (pre-RMS projection), h_pre [T,n] f32,
+ *   dh_in [T,D] bf16, dh_post [T,n] f32, dh_res [T,n,n] f32, gamma [n,D] f32,
+ *   dx [T,n,D] bf16, dphi [N,nD] f32, dalpha [3] f32, dbias [N] f32,
+ *   dgamma [nD] f32 (flat, as the reference golden returns it).
+ * bf16 values are passed as uint16_t bit patterns.
+ * Supported: 1 <= n <= 8, D >= 1, T >= 0; pointers 16-byte aligned and
+ * D a multiple of 8 for the tensor-core kernels (other shapes run the
+ * generic CUDA kernels).
+ */
+#ifndef MHC_OPS_H_
+#define MHC_OPS_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MHC_API __attribute__((visibility("default")))
+#else
+#define MHC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum mhc_status {
+  MHC_OK = 0,
+  MHC_ERR_NULL_POINTER = 1,        /* a required pointer is NULL */
+  MHC_ERR_BAD_SHAPE = 2,           /* T < 0, n outside [1,8], D < 1, or overflow */
+  MHC_ERR_MISALIGNED = 3,          /* a pointer is not 16-byte aligned */
+  MHC_ERR_WORKSPACE_TOO_SMALL = 4, /* workspace_bytes below the *_workspace_size answer */
+  MHC_ERR_CUDA = 5,                /* a CUDA runtime/driver call failed (see mhc_last_cuda_error) */
+  MHC_ERR_DEVICE_TIMEOUT = 6,      /* a kernel's bounded wait expired (read by mhc_read_device_status) */
+  MHC_ERR_NO_DEVICE = 7,           /* no sm_100 device is current */
+  MHC_ERR_LIMIT = 8                /* a size beyond a fixed limit of the entry point */
+} mhc_status;
+
+/* Forward arguments.  Replaces the Python signature
+ *   mhc_forward_pre(x, phi, alpha, bias, outflag=False, norm_eps=1e-6, hc_eps=1e-6)
+ * of the reference (src/forward/golden.py:10-11; Triton twin
+ * src/forward/mhc_forward_pre_triton.py:409-417).  inv_rms, h_mix and h_pre
+ * are the outflag outputs (golden.py:65-69): pass NULL to skip writing them. */
+typedef struct mhc_fwd_args {
+  const uint16_t* x;
+  const float* phi;
+  const float* alpha;
+  const float* bias;
+  uint16_t* h_in;
+  float* h_post;
+  float* h_res;
+  float* inv_rms;   /* optional */
+  float* h_mix;     /* optional */
+  float* h_pre;     /* optional */
+  int64_t tokens;
+  int32_t n;
+  int32_t D;
+  float norm_eps;
+  float hc_eps;
+  void* workspace;
+  size_t workspace_bytes;
+} mhc_fwd_args;
+
+/* Backward arguments.  Replaces the Python signature
+ *   mhc_backward_manual(x, phi, alpha, bias, inv_rms, h_mix, h_pre, h_post,
+ *                       dh_in, dh_post, dh_res, gamma, norm_eps=1e-6, hc_eps=1e-6)
+ * of the reference (src/backward/golden.py:10-13, returns at :96; Triton twin
+ * src/backward/mhc_backward_triton.py:467-473).  gamma may be NULL (all ones).
+ * bias and norm_eps are unused by the math, as in the reference. */
+typedef struct mhc_bwd_args {
+  const uint16_t* x;
+  const float* phi;
+  const float* alpha;
+  const float* bias;     /* unused, may be NULL */
+  const float* inv_rms;
+  const float* h_mix;
+  const float* h_pre;
+  const float* h_post;
+  const uint16_t* dh_in;
+  const float* dh_post;
+  const float* dh_res;
+  const float* gamma;    /* optional */
+  uint16_t* dx;
+  float* dphi;
+  float* dalpha;
+  float* dbias;
+  float* dgamma;
+  int64_t tokens;
+  int32_t n;
+  int32_t D;
+  float norm_eps;
+  float hc_eps;
+  void* workspace;
+  size_t workspace_bytes;
+} mhc_bwd_args;
+
+/* Human-readable text for a status code (static storage). */
+MHC_API const char* mhc_status_string(int status);
+
+/* Text of the last CUDA error seen by this thread inside the library. */
+MHC_API const char* mhc_last_cuda_error(void);
+
+/* Workspace bytes mhc_fwd needs for this shape on the current device.
+ * Replaces nothing in the reference (its wrappers allocate with torch.empty,
+ * src/forward/mhc_forward_pre_triton.py:437,466). */
+MHC_API int mhc_fwd_workspace_size(int64_t tokens, int32_t n, int32_t D, size_t* bytes);
+
+/* Forward pass; see mhc_fwd_args.  Replaces mhc_forward_pre
+ * (src/forward/golden.py:10-69) and mhc_forward_pre_triton_optimized
+ * (src/forward/mhc_forward_pre_triton.py:409-514). */
+MHC_API int mhc_fwd(const mhc_fwd_args* args, void* stream);
+
+/* Workspace bytes mhc_bwd needs for this shape on the current device.
+ * Replaces the intermediates the Triton backward allocates
+ * (src/backward/mhc_backward_triton.py:509-510). */
+MHC_API int mhc_bwd_workspace_size(int64_t tokens, int32_t n, int32_t D, size_t* bytes);
+
+/* Backward pass; see mhc_bwd_args.  Replaces mhc_backward_manual
+ * (src/backward/golden.py:10-96) and mhc_backward_triton
+ * (src/backward/mhc_backward_triton.py:467-729).  The parameter gradients
+ * dphi, dgamma, dalpha, dbias are reduced over tokens in a fixed order, so
+ * repeated calls return identical bytes. */
+MHC_API int mhc_bwd(const mhc_bwd_args* args, void* stream);
+
+/* Reads (and clears) the device status word a previous mhc_fwd / mhc_bwd
+ * left in `workspace`; synchronizes `stream`.  *device_status receives
+ * MHC_OK or MHC_ERR_DEVICE_TIMEOUT.  No counterpart in the reference, which
+ * has no bounded device waits. */
+MHC_API int mhc_read_device_status(void* workspace, void* stream, int* device_status);
+
+/* Number of kernels this library has launched in this process (all devices,
+ * all threads).  No counterpart in the reference; used to report launches. */
+MHC_API uint64_t mhc_launch_count(void);
+
+/* Version of this ABI (major*10000 + minor*100 + patch). */
+MHC_API int mhc_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MHC_OPS_H_ */

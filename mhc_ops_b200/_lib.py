@@ -1,0 +1,150 @@
+"""ctypes binding of libmhc_ops.so (the C ABI declared in include/mhc_ops.h).
+
+The library is built in-tree (``python -m mhc_ops_b200.build``) and loaded
+from ``mhc_ops_b200/lib/libmhc_ops.so``.  There is no fallback: if the library
+is missing or no sm_100 GPU is current, the calls raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libmhc_ops.so")
+
+MHC_OK = 0
+MHC_ERR_DEVICE_TIMEOUT = 6
+
+_c_void_p = ctypes.c_void_p
+
+
+class FwdArgs(ctypes.Structure):
+    """Mirror of ``mhc_fwd_args`` (include/mhc_ops.h)."""
+    _fields_ = [
+        ("x", _c_void_p), ("phi", _c_void_p), ("alpha", _c_void_p), ("bias", _c_void_p),
+        ("h_in", _c_void_p), ("h_post", _c_void_p), ("h_res", _c_void_p),
+        ("inv_rms", _c_void_p), ("h_mix", _c_void_p), ("h_pre", _c_void_p),
+        ("tokens", ctypes.c_int64), ("n", ctypes.c_int32), ("D", ctypes.c_int32),
+        ("norm_eps", ctypes.c_float), ("hc_eps", ctypes.c_float),
+        ("workspace", _c_void_p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class BwdArgs(ctypes.Structure):
+    """Mirror of ``mhc_bwd_args`` (include/mhc_ops.h)."""
+    _fields_ = [
+        ("x", _c_void_p), ("phi", _c_void_p), ("alpha", _c_void_p), ("bias", _c_void_p),
+        ("inv_rms", _c_void_p), ("h_mix", _c_void_p), ("h_pre", _c_void_p), ("h_post", _c_void_p),
+        ("dh_in", _c_void_p), ("dh_post", _c_void_p), ("dh_res", _c_void_p), ("gamma", _c_void_p),
+        ("dx", _c_void_p), ("dphi", _c_void_p), ("dalpha", _c_void_p), ("dbias", _c_void_p),
+        ("dgamma", _c_void_p),
+        ("tokens", ctypes.c_int64), ("n", ctypes.c_int32), ("D", ctypes.c_int32),
+        ("norm_eps", ctypes.c_float), ("hc_eps", ctypes.c_float),
+        ("workspace", _c_void_p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+# Every symbol include/mhc_ops.h declares, with its ctypes signature.
+SIGNATURES = {
+    "mhc_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "mhc_last_cuda_error": (ctypes.c_char_p, []),
+    "mhc_fwd_workspace_size": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                              ctypes.POINTER(ctypes.c_size_t)]),
+    "mhc_fwd": (ctypes.c_int, [ctypes.POINTER(FwdArgs), _c_void_p]),
+    "mhc_bwd_workspace_size": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                              ctypes.POINTER(ctypes.c_size_t)]),
+    "mhc_bwd": (ctypes.c_int, [ctypes.POINTER(BwdArgs), _c_void_p]),
+    "mhc_read_device_status": (ctypes.c_int, [_c_void_p, _c_void_p, ctypes.POINTER(ctypes.c_int)]),
+    "mhc_launch_count": (ctypes.c_uint64, []),
+    "mhc_abi_version": (ctypes.c_int, []),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib_path() -> str:
+    return _LIB_PATH
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the library; raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(_LIB_PATH):
+                raise RuntimeError(
+                    f"libmhc_ops.so not found at {_LIB_PATH}; build it with `python -m mhc_ops_b200.build` "
+                    "(there is no CPU fallback)")
+            lib = ctypes.CDLL(_LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+class MhcError(RuntimeError):
+    def __init__(self, status: int, where: str):
+        lib = load()
+        msg = lib.mhc_status_string(status).decode()
+        if status == 5:
+            msg += f" ({lib.mhc_last_cuda_error().decode()})"
+        super().__init__(f"{where}: mhc status {status}: {msg}")
+        self.status = status
+
+
+def check(status: int, where: str) -> None:
+    if status != MHC_OK:
+        raise MhcError(status, where)
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+# ------------------------------------------------------------------ workspaces
+_ws_cache: dict = {}
+
+
+def workspace(nbytes: int, device: torch.device, stream: torch.cuda.Stream) -> torch.Tensor:
+    """A zero-initialised byte workspace of >= nbytes, cached per (device, stream).
+
+    The first bytes hold the device status word, so new workspaces are zero
+    filled once; later calls reuse the buffer, ordered by the stream.
+    """
+    key = (device.index, stream.cuda_stream)
+    buf = _ws_cache.get(key)
+    if buf is None or buf.numel() < nbytes:
+        size = max(nbytes, 1 << 16)
+        buf = torch.zeros(size, dtype=torch.uint8, device=device)
+        _ws_cache[key] = buf
+    return buf
+
+
+def fwd_workspace_size(tokens: int, n: int, D: int) -> int:
+    out = ctypes.c_size_t(0)
+    check(load().mhc_fwd_workspace_size(tokens, n, D, ctypes.byref(out)), "mhc_fwd_workspace_size")
+    return int(out.value)
+
+
+def bwd_workspace_size(tokens: int, n: int, D: int) -> int:
+    out = ctypes.c_size_t(0)
+    check(load().mhc_bwd_workspace_size(tokens, n, D, ctypes.byref(out)), "mhc_bwd_workspace_size")
+    return int(out.value)
+
+
+def launch_count() -> int:
+    return int(load().mhc_launch_count())
+
+
+def read_device_status(ws: torch.Tensor, stream: torch.cuda.Stream) -> int:
+    out = ctypes.c_int(0)
+    check(load().mhc_read_device_status(ws.data_ptr(), stream.cuda_stream, ctypes.byref(out)),
+          "mhc_read_device_status")
+    return int(out.value)

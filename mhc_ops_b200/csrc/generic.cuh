@@ -1,0 +1,247 @@
+// Generic-shape CUDA kernels of the mHC pre-op (any n in [1,8], any D).
+//
+// These run every shape the tensor-core kernels do not take (D not a multiple
+// of 64, tiny token counts, odd n).  One CTA walks one token at a time; the
+// projection re-reads phi from L2 per token, so they are correct but far from
+// the HBM roofline.  The parameter-gradient reduction (bwd_g / finalize) is
+// shared with the tensor-core backward.
+#pragma once
+
+#include "common.cuh"
+
+namespace mhc {
+namespace generic {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+
+template <int n>
+struct Dims {
+  static constexpr int N = n * n + 2 * n;
+};
+
+// Sum NV per-thread values over the CTA; every thread gets the totals in out[].
+// red must hold kWarps * NV floats.  Order is fixed (deterministic).
+template <int NV>
+__device__ __forceinline__ void block_sum(float (&v)[NV], float* red, float* out) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) v[j] = warp_sum(v[j]);
+  if (lane == 0) {
+#pragma unroll
+    for (int j = 0; j < NV; ++j) red[warp * NV + j] = v[j];
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < NV; j += kThreads) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) s += red[w * NV + j];
+    out[j] = s;
+  }
+  __syncthreads();
+}
+
+// Forward, one token per CTA iteration (golden.py:34-69).
+template <int n>
+__global__ void __launch_bounds__(kThreads) fwd_kernel(
+    const uint16_t* __restrict__ x, const float* __restrict__ phi, const float* __restrict__ alpha,
+    const float* __restrict__ bias, uint16_t* __restrict__ h_in, float* __restrict__ h_post,
+    float* __restrict__ h_res, float* __restrict__ inv_rms_out, float* __restrict__ h_mix_out,
+    float* __restrict__ h_pre_out, int64_t T, int D, float norm_eps, float hc_eps) {
+  constexpr int N = Dims<n>::N;
+  const int nD = n * D;
+  __shared__ float red[kWarps * (N + 1)];
+  __shared__ float tot[N + 1];
+  __shared__ float hpre_s[n];
+
+  for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+    const uint16_t* xr = x + t * (int64_t)nD;
+    float acc[N + 1];
+#pragma unroll
+    for (int j = 0; j <= N; ++j) acc[j] = 0.f;
+    for (int k = threadIdx.x; k < nD; k += kThreads) {
+      const float xv = bf16_bits_to_f32(xr[k]);
+      acc[N] = fmaf(xv, xv, acc[N]);
+#pragma unroll
+      for (int j = 0; j < N; ++j) acc[j] = fmaf(xv, __ldg(phi + (int64_t)j * nD + k), acc[j]);
+    }
+    block_sum<N + 1>(acc, red, tot);
+
+    if (threadIdx.x == 0) {
+      const float ir = 1.0f / sqrtf(tot[N] / (float)nD + norm_eps);
+      const float a_pre = alpha[0], a_post = alpha[1], a_res = alpha[2];
+      if (inv_rms_out) inv_rms_out[t] = ir;
+      for (int j = 0; j < N; ++j)
+        if (h_mix_out) h_mix_out[t * N + j] = tot[j];
+      for (int i = 0; i < n; ++i) {
+        const float hp = sigmoid_acc(a_pre * (tot[i] * ir) + bias[i]) + hc_eps;
+        hpre_s[i] = hp;
+        if (h_pre_out) h_pre_out[t * n + i] = hp;
+        h_post[t * n + i] = 2.0f * sigmoid_acc(a_post * (tot[n + i] * ir) + bias[n + i]);
+      }
+      for (int m = 0; m < n * n; ++m) h_res[t * n * n + m] = a_res * (tot[2 * n + m] * ir) + bias[2 * n + m];
+    }
+    __syncthreads();
+    for (int d = threadIdx.x; d < D; d += kThreads) {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < n; ++i) s = fmaf(hpre_s[i], bf16_bits_to_f32(xr[i * D + d]), s);
+      h_in[t * D + d] = f32_to_bf16_bits(s);
+    }
+    __syncthreads();
+  }
+}
+
+// Backward, per-token part (src/backward/golden.py:49-62, 72-94): dx, plus
+// dh_mix [T,N] and the per-token dalpha/dbias terms [T,3+N] for the
+// fixed-order reductions that follow.
+template <int n>
+__global__ void __launch_bounds__(kThreads) bwd_token_kernel(
+    const uint16_t* __restrict__ x, const float* __restrict__ phi, const float* __restrict__ alpha,
+    const float* __restrict__ inv_rms, const float* __restrict__ h_mix, const float* __restrict__ h_pre,
+    const float* __restrict__ h_post, const uint16_t* __restrict__ dh_in,
+    const float* __restrict__ dh_post, const float* __restrict__ dh_res, const float* __restrict__ gamma,
+    uint16_t* __restrict__ dx, float* __restrict__ dh_mix_ws, float* __restrict__ tokpart, int64_t T,
+    int D, float hc_eps) {
+  constexpr int N = Dims<n>::N;
+  constexpr int W = 3 + N;
+  const int nD = n * D;
+  __shared__ float red[kWarps * n];
+  __shared__ float tot[n];
+  __shared__ float dmix_s[N];
+  __shared__ float hpre_s[n];
+  __shared__ float c_s;
+
+  for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+    const uint16_t* xr = x + t * (int64_t)nD;
+    const uint16_t* gr = dh_in + t * (int64_t)D;
+    float p[n];
+#pragma unroll
+    for (int i = 0; i < n; ++i) p[i] = 0.f;
+    for (int d = threadIdx.x; d < D; d += kThreads) {
+      const float g = bf16_bits_to_f32(gr[d]);
+#pragma unroll
+      for (int i = 0; i < n; ++i) p[i] = fmaf(g, bf16_bits_to_f32(xr[i * D + d]), p[i]);
+    }
+    block_sum<n>(p, red, tot);
+
+    if (threadIdx.x == 0) {
+      const float a_pre = alpha[0], a_post = alpha[1], a_res = alpha[2];
+      const float ir = inv_rms[t];
+      float tmp[N];
+      float dal0 = 0.f, dal1 = 0.f, dal2 = 0.f, dinv = 0.f;
+      float* tp = tokpart + t * W;
+      for (int i = 0; i < n; ++i) {
+        const float hp = h_pre[t * n + i];
+        hpre_s[i] = hp;
+        const float s = hp - hc_eps;
+        const float dpre2 = tot[i] * s * (1.0f - s);
+        const float hq = h_post[t * n + i];
+        const float dpost2 = dh_post[t * n + i] * hq * (1.0f - hq / 2.0f);
+        tmp[i] = a_pre * dpre2;
+        tmp[n + i] = a_post * dpost2;
+        dal0 += dpre2 * (h_mix[t * N + i] * ir);
+        dal1 += dpost2 * (h_mix[t * N + n + i] * ir);
+        tp[3 + i] = dpre2;
+        tp[3 + n + i] = dpost2;
+      }
+      for (int m = 0; m < n * n; ++m) {
+        const float dr = dh_res[t * n * n + m];
+        tmp[2 * n + m] = a_res * dr;
+        dal2 += dr * (h_mix[t * N + 2 * n + m] * ir);
+        tp[3 + 2 * n + m] = dr;
+      }
+      for (int j = 0; j < N; ++j) {
+        dinv += tmp[j] * h_mix[t * N + j];
+        const float dm = tmp[j] * ir;
+        dmix_s[j] = dm;
+        dh_mix_ws[t * N + j] = dm;
+      }
+      tp[0] = dal0;
+      tp[1] = dal1;
+      tp[2] = dal2;
+      c_s = dinv * (ir * ir * ir) / (float)nD;
+    }
+    __syncthreads();
+    const float c = c_s;
+    for (int k = threadIdx.x; k < nD; k += kThreads) {
+      const int i = k / D, d = k - i * D;
+      float mm = 0.f;
+#pragma unroll
+      for (int j = 0; j < N; ++j) mm = fmaf(dmix_s[j], __ldg(phi + (int64_t)j * nD + k), mm);
+      const float gmm = gamma ? gamma[k] : 1.0f;
+      const float v = mm * gmm + ((-c) * bf16_bits_to_f32(xr[k]) + hpre_s[i] * bf16_bits_to_f32(gr[d]));
+      dx[t * (int64_t)nD + k] = f32_to_bf16_bits(v);
+    }
+    __syncthreads();
+  }
+}
+
+// G partials: gpart[p][j][k] = sum over tokens of split p of dh_mix[t][j] * x[t][k]
+// (the un-scaled dphi of golden.py:68-69).  grid = (ceil(nD/256), P).
+template <int n>
+__global__ void __launch_bounds__(kThreads) bwd_g_kernel(const uint16_t* __restrict__ x,
+                                                         const float* __restrict__ dh_mix_ws,
+                                                         float* __restrict__ gpart, int64_t T, int nD,
+                                                         int64_t tokens_per_split) {
+  constexpr int N = Dims<n>::N;
+  const int k = blockIdx.x * kThreads + threadIdx.x;
+  const int p = blockIdx.y;
+  const int64_t t0 = (int64_t)p * tokens_per_split;
+  const int64_t t1 = min(T, t0 + tokens_per_split);
+  float acc[N];
+#pragma unroll
+  for (int j = 0; j < N; ++j) acc[j] = 0.f;
+  if (k < nD) {
+    for (int64_t t = t0; t < t1; ++t) {
+      const float xv = bf16_bits_to_f32(x[t * nD + k]);
+#pragma unroll
+      for (int j = 0; j < N; ++j) acc[j] = fmaf(__ldg(dh_mix_ws + t * N + j), xv, acc[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < N; ++j) gpart[((int64_t)p * N + j) * nD + k] = acc[j];
+  }
+}
+
+// dphi[j][k] = gamma[k] * sum_p gpart[p][j][k]; dgamma[k] = sum_j phi[j][k] * G[j][k]
+// (dgamma = sum_t x * dvecX_mm of golden.py:93, regrouped: dvecX_mm = dh_mix @ phi).
+__global__ void __launch_bounds__(kThreads) finalize_param_kernel(const float* __restrict__ gpart, int P, int N,
+                                                                  const float* __restrict__ phi,
+                                                                  const float* __restrict__ gamma,
+                                                                  float* __restrict__ dphi,
+                                                                  float* __restrict__ dgamma, int nD) {
+  const int k = blockIdx.x * kThreads + threadIdx.x;
+  if (k >= nD) return;
+  const float gm = gamma ? gamma[k] : 1.0f;
+  float dg = 0.f;
+  for (int j = 0; j < N; ++j) {
+    float g = 0.f;
+    for (int p = 0; p < P; ++p) g += gpart[((int64_t)p * N + j) * nD + k];
+    dphi[(int64_t)j * nD + k] = gm * g;
+    dg = fmaf(__ldg(phi + (int64_t)j * nD + k), g, dg);
+  }
+  dgamma[k] = dg;
+}
+
+// dalpha / dbias: column c of tokpart [rows][W] summed over rows in a fixed
+// order; one CTA per column.  c < 3 -> dalpha[c], else dbias[c-3].
+__global__ void __launch_bounds__(kThreads) reduce_columns_kernel(const float* __restrict__ part, int64_t rows,
+                                                                  int W, float* __restrict__ dalpha,
+                                                                  float* __restrict__ dbias) {
+  __shared__ float red[kWarps];
+  const int c = blockIdx.x;
+  float s = 0.f;
+  for (int64_t r = threadIdx.x; r < rows; r += kThreads) s += part[r * W + c];
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int w = 0; w < kWarps; ++w) tot += red[w];
+    if (c < 3) dalpha[c] = tot;
+    else dbias[c - 3] = tot;
+  }
+}
+
+}  // namespace generic
+}  // namespace mhc

@@ -1,0 +1,258 @@
+// libmhc_ops: C-ABI entry points of the B200 mHC pre-op (declared in include/mhc_ops.h).
+//
+// Validation, workspace carving and kernel selection live here; the kernels
+// are in generic.cuh (any shape) and fwd_sm100.cuh / bwd_sm100.cuh
+// (tcgen05 + TMA + cluster kernels for the shapes the tensor cores take).
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdio>
+#include <string>
+
+#include "common.cuh"
+#include "generic.cuh"
+
+namespace mhc {
+
+std::atomic<uint64_t> g_launch_count{0};
+static thread_local std::string t_last_cuda_error;
+
+void set_last_cuda_error(cudaError_t e) {
+  t_last_cuda_error = std::string(cudaGetErrorName(e)) + ": " + cudaGetErrorString(e);
+}
+
+namespace {
+
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+template <template <int> class F, typename... Args>
+int dispatch_n(int n, Args&&... args) {
+  switch (n) {
+    case 1: return F<1>::run(args...);
+    case 2: return F<2>::run(args...);
+    case 3: return F<3>::run(args...);
+    case 4: return F<4>::run(args...);
+    case 5: return F<5>::run(args...);
+    case 6: return F<6>::run(args...);
+    case 7: return F<7>::run(args...);
+    case 8: return F<8>::run(args...);
+    default: return MHC_ERR_BAD_SHAPE;
+  }
+}
+
+int check_shape(int64_t T, int32_t n, int32_t D) {
+  if (T < 0 || n < 1 || n > 8 || D < 1) return MHC_ERR_BAD_SHAPE;
+  // Keep every element index inside int64 and every per-token row inside int32.
+  if ((int64_t)n * D > (int64_t)1 << 28) return MHC_ERR_BAD_SHAPE;
+  if (T > ((int64_t)1 << 40) / ((int64_t)n * D)) return MHC_ERR_BAD_SHAPE;
+  return MHC_OK;
+}
+
+int current_sm_count(int* sms) {
+  int dev = 0;
+  MHC_CUDA_TRY(cudaGetDevice(&dev));
+  int major = 0;
+  MHC_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+  if (major != 10) return MHC_ERR_NO_DEVICE;
+  MHC_CUDA_TRY(cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev));
+  return MHC_OK;
+}
+
+// ----------------------------------------------------------------- workspace
+// Backward (generic path) workspace after the header:
+//   dh_mix   [T][N]        f32
+//   tokpart  [T][3+N]      f32   per-token dalpha / dbias terms
+//   gpart    [P][N][nD]    f32   token-split partial sums of dh_mix^T x
+struct BwdGenericLayout {
+  size_t dh_mix, tokpart, gpart, total;
+  int P;
+  int64_t tokens_per_split;
+};
+
+BwdGenericLayout bwd_generic_layout(int64_t T, int n, int D, int sms) {
+  BwdGenericLayout L{};
+  const int N = n * n + 2 * n;
+  const int64_t nD = (int64_t)n * D;
+  const int64_t kblocks = (nD + generic::kThreads - 1) / generic::kThreads;
+  int64_t P = std::max<int64_t>(1, (4 * (int64_t)sms + kblocks - 1) / kblocks);
+  P = std::min<int64_t>(P, std::max<int64_t>(1, (T + 63) / 64));
+  P = std::min<int64_t>(P, 256);
+  L.P = (int)P;
+  L.tokens_per_split = T > 0 ? (T + P - 1) / P : 1;
+  size_t off = kWsHeaderBytes;
+  L.dh_mix = off;
+  off = align_up(off + sizeof(float) * (size_t)T * N, kWsAlign);
+  L.tokpart = off;
+  off = align_up(off + sizeof(float) * (size_t)T * (3 + N), kWsAlign);
+  L.gpart = off;
+  off = align_up(off + sizeof(float) * (size_t)P * N * nD, kWsAlign);
+  L.total = off;
+  return L;
+}
+
+// ----------------------------------------------------------------- generic runners
+template <int n>
+struct FwdGeneric {
+  static int run(const mhc_fwd_args* a, cudaStream_t s, int sms) {
+    const int64_t T = a->tokens;
+    const int grid = (int)std::min<int64_t>(T, (int64_t)sms * 8);
+    generic::fwd_kernel<n><<<grid, generic::kThreads, 0, s>>>(
+        a->x, a->phi, a->alpha, a->bias, a->h_in, a->h_post, a->h_res, a->inv_rms, a->h_mix, a->h_pre, T,
+        a->D, a->norm_eps, a->hc_eps);
+    return after_launch();
+  }
+};
+
+template <int n>
+struct BwdGeneric {
+  static int run(const mhc_bwd_args* a, cudaStream_t s, int sms) {
+    constexpr int N = n * n + 2 * n;
+    const int64_t T = a->tokens;
+    const int nD = n * a->D;
+    BwdGenericLayout L = bwd_generic_layout(T, n, a->D, sms);
+    char* ws = static_cast<char*>(a->workspace);
+    float* dh_mix = reinterpret_cast<float*>(ws + L.dh_mix);
+    float* tokpart = reinterpret_cast<float*>(ws + L.tokpart);
+    float* gpart = reinterpret_cast<float*>(ws + L.gpart);
+    const int grid = (int)std::min<int64_t>(T, (int64_t)sms * 8);
+    generic::bwd_token_kernel<n><<<grid, generic::kThreads, 0, s>>>(
+        a->x, a->phi, a->alpha, a->inv_rms, a->h_mix, a->h_pre, a->h_post, a->dh_in, a->dh_post, a->dh_res,
+        a->gamma, a->dx, dh_mix, tokpart, T, a->D, a->hc_eps);
+    int st = after_launch();
+    if (st) return st;
+    dim3 g2((nD + generic::kThreads - 1) / generic::kThreads, L.P);
+    generic::bwd_g_kernel<n><<<g2, generic::kThreads, 0, s>>>(a->x, dh_mix, gpart, T, nD, L.tokens_per_split);
+    if ((st = after_launch())) return st;
+    generic::finalize_param_kernel<<<(nD + generic::kThreads - 1) / generic::kThreads, generic::kThreads, 0, s>>>(
+        gpart, L.P, N, a->phi, a->gamma, a->dphi, a->dgamma, nD);
+    if ((st = after_launch())) return st;
+    generic::reduce_columns_kernel<<<3 + N, generic::kThreads, 0, s>>>(tokpart, T, 3 + N, a->dalpha, a->dbias);
+    return after_launch();
+  }
+};
+
+int fwd_workspace(int64_t T, int n, int D, size_t* bytes) {
+  (void)T; (void)n; (void)D;
+  *bytes = kWsHeaderBytes;
+  return MHC_OK;
+}
+
+int bwd_workspace(int64_t T, int n, int D, int sms, size_t* bytes) {
+  *bytes = bwd_generic_layout(T, n, D, sms).total;
+  return MHC_OK;
+}
+
+}  // namespace
+}  // namespace mhc
+
+using namespace mhc;
+
+extern "C" {
+
+const char* mhc_status_string(int status) {
+  switch (status) {
+    case MHC_OK: return "ok";
+    case MHC_ERR_NULL_POINTER: return "a required pointer is NULL";
+    case MHC_ERR_BAD_SHAPE: return "unsupported shape (need T >= 0, 1 <= n <= 8, D >= 1)";
+    case MHC_ERR_MISALIGNED: return "a pointer is not aligned to its element size";
+    case MHC_ERR_WORKSPACE_TOO_SMALL: return "workspace smaller than the *_workspace_size answer";
+    case MHC_ERR_CUDA: return "a CUDA call failed";
+    case MHC_ERR_DEVICE_TIMEOUT: return "a kernel's bounded wait expired";
+    case MHC_ERR_NO_DEVICE: return "the current device is not an sm_100 GPU";
+    case MHC_ERR_LIMIT: return "a size is beyond this entry point's fixed limit";
+    default: return "unknown mhc status";
+  }
+}
+
+const char* mhc_last_cuda_error(void) { return t_last_cuda_error.c_str(); }
+
+int mhc_abi_version(void) { return 10000; }
+
+uint64_t mhc_launch_count(void) { return g_launch_count.load(std::memory_order_relaxed); }
+
+int mhc_fwd_workspace_size(int64_t tokens, int32_t n, int32_t D, size_t* bytes) {
+  if (!bytes) return MHC_ERR_NULL_POINTER;
+  int st = check_shape(tokens, n, D);
+  if (st) return st;
+  return fwd_workspace(tokens, n, D, bytes);
+}
+
+int mhc_bwd_workspace_size(int64_t tokens, int32_t n, int32_t D, size_t* bytes) {
+  if (!bytes) return MHC_ERR_NULL_POINTER;
+  int st = check_shape(tokens, n, D);
+  if (st) return st;
+  int sms = 0;
+  if ((st = current_sm_count(&sms))) return st;
+  return bwd_workspace(tokens, n, D, sms, bytes);
+}
+
+int mhc_fwd(const mhc_fwd_args* a, void* stream) {
+  if (!a) return MHC_ERR_NULL_POINTER;
+  int st = check_shape(a->tokens, a->n, a->D);
+  if (st) return st;
+  if (!a->workspace) return MHC_ERR_NULL_POINTER;
+  size_t need = 0;
+  fwd_workspace(a->tokens, a->n, a->D, &need);
+  if (a->workspace_bytes < need) return MHC_ERR_WORKSPACE_TOO_SMALL;
+  if (!aligned(a->workspace, kWsAlign)) return MHC_ERR_MISALIGNED;
+  int sms = 0;
+  if ((st = current_sm_count(&sms))) return st;
+  if (a->tokens == 0) return MHC_OK;
+  if (!a->x || !a->phi || !a->alpha || !a->bias || !a->h_in || !a->h_post || !a->h_res)
+    return MHC_ERR_NULL_POINTER;
+  if (!aligned(a->x, 2) || !aligned(a->h_in, 2) || !aligned(a->phi, 4) || !aligned(a->alpha, 4) ||
+      !aligned(a->bias, 4) || !aligned(a->h_post, 4) || !aligned(a->h_res, 4) || !aligned(a->inv_rms, 4) ||
+      !aligned(a->h_mix, 4) || !aligned(a->h_pre, 4))
+    return MHC_ERR_MISALIGNED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return dispatch_n<FwdGeneric>(a->n, a, s, sms);
+}
+
+int mhc_bwd(const mhc_bwd_args* a, void* stream) {
+  if (!a) return MHC_ERR_NULL_POINTER;
+  int st = check_shape(a->tokens, a->n, a->D);
+  if (st) return st;
+  if (!a->workspace) return MHC_ERR_NULL_POINTER;
+  int sms = 0;
+  if ((st = current_sm_count(&sms))) return st;
+  size_t need = 0;
+  bwd_workspace(a->tokens, a->n, a->D, sms, &need);
+  if (a->workspace_bytes < need) return MHC_ERR_WORKSPACE_TOO_SMALL;
+  if (!aligned(a->workspace, kWsAlign)) return MHC_ERR_MISALIGNED;
+  if (!a->dphi || !a->dalpha || !a->dbias || !a->dgamma || !a->alpha || !a->phi) return MHC_ERR_NULL_POINTER;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int N = a->n * a->n + 2 * a->n;
+  if (a->tokens == 0) {
+    MHC_CUDA_TRY(cudaMemsetAsync(a->dphi, 0, sizeof(float) * (size_t)N * a->n * a->D, s));
+    MHC_CUDA_TRY(cudaMemsetAsync(a->dgamma, 0, sizeof(float) * (size_t)a->n * a->D, s));
+    MHC_CUDA_TRY(cudaMemsetAsync(a->dalpha, 0, sizeof(float) * 3, s));
+    MHC_CUDA_TRY(cudaMemsetAsync(a->dbias, 0, sizeof(float) * (size_t)N, s));
+    return MHC_OK;
+  }
+  if (!a->x || !a->inv_rms || !a->h_mix || !a->h_pre || !a->h_post || !a->dh_in || !a->dh_post ||
+      !a->dh_res || !a->dx)
+    return MHC_ERR_NULL_POINTER;
+  if (!aligned(a->x, 2) || !aligned(a->dh_in, 2) || !aligned(a->dx, 2) || !aligned(a->phi, 4) ||
+      !aligned(a->inv_rms, 4) || !aligned(a->h_mix, 4) || !aligned(a->h_pre, 4) || !aligned(a->h_post, 4) ||
+      !aligned(a->dh_post, 4) || !aligned(a->dh_res, 4) || !aligned(a->gamma, 4) || !aligned(a->dphi, 4) ||
+      !aligned(a->dalpha, 4) || !aligned(a->dbias, 4) || !aligned(a->dgamma, 4))
+    return MHC_ERR_MISALIGNED;
+  return dispatch_n<BwdGeneric>(a->n, a, s, sms);
+}
+
+int mhc_read_device_status(void* workspace, void* stream, int* device_status) {
+  if (!workspace || !device_status) return MHC_ERR_NULL_POINTER;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int host = 0;
+  MHC_CUDA_TRY(cudaMemcpyAsync(&host, workspace, sizeof(int), cudaMemcpyDeviceToHost, s));
+  MHC_CUDA_TRY(cudaStreamSynchronize(s));
+  MHC_CUDA_TRY(cudaMemsetAsync(workspace, 0, sizeof(int), s));
+  MHC_CUDA_TRY(cudaStreamSynchronize(s));
+  *device_status = host;
+  return MHC_OK;
+}
+
+}  // extern "C"

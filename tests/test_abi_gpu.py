@@ -1,0 +1,74 @@
+"""The C ABI called directly with raw device pointers (as a cgo/ctypes user would),
+and its error paths on a GPU."""
+import ctypes
+
+import pytest
+import torch
+
+from mhc_ops_b200 import _lib, mhc_forward_pre
+from mhc_ops_b200.synthetic import make_inputs
+
+pytestmark = pytest.mark.gpu
+
+
+def _fwd_args(d, outs, ws, T, n, D):
+    return _lib.FwdArgs(x=d.x.data_ptr(), phi=d.phi.data_ptr(), alpha=d.alpha.data_ptr(),
+                        bias=d.bias.data_ptr(), h_in=outs[0].data_ptr(), h_post=outs[1].data_ptr(),
+                        h_res=outs[2].data_ptr(), inv_rms=None, h_mix=None, h_pre=None, tokens=T, n=n, D=D,
+                        norm_eps=1e-6, hc_eps=1e-6, workspace=ws.data_ptr(), workspace_bytes=ws.numel())
+
+
+def test_raw_abi_forward_matches_python_api():
+    lib = _lib.load()
+    B, S, n, D = 1, 40, 4, 512
+    d = make_inputs(B, S, n, D, seed=3).to("cuda")
+    T = B * S
+    outs = (torch.empty(T, D, dtype=torch.bfloat16, device="cuda"), torch.empty(T, n, device="cuda"),
+            torch.empty(T, n, n, device="cuda"))
+    size = ctypes.c_size_t(0)
+    assert lib.mhc_fwd_workspace_size(T, n, D, ctypes.byref(size)) == 0
+    ws = torch.zeros(size.value, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.mhc_fwd(ctypes.byref(_fwd_args(d, outs, ws, T, n, D)), stream) == 0
+    ref = mhc_forward_pre(d.x, d.phi, d.alpha, d.bias)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0].view(1, S, D), ref[0])
+    assert torch.equal(outs[1].view(1, S, n), ref[1])
+    status = ctypes.c_int(-1)
+    assert lib.mhc_read_device_status(ws.data_ptr(), stream, ctypes.byref(status)) == 0
+    assert status.value == 0
+
+
+def test_abi_rejects_bad_arguments():
+    lib = _lib.load()
+    B, S, n, D = 1, 8, 4, 64
+    d = make_inputs(B, S, n, D, seed=4).to("cuda")
+    T = B * S
+    outs = (torch.empty(T, D, dtype=torch.bfloat16, device="cuda"), torch.empty(T, n, device="cuda"),
+            torch.empty(T, n, n, device="cuda"))
+    size = ctypes.c_size_t(0)
+    lib.mhc_fwd_workspace_size(T, n, D, ctypes.byref(size))
+    ws = torch.zeros(size.value, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    a = _fwd_args(d, outs, ws, T, n, D)
+    a.workspace_bytes = 16
+    assert lib.mhc_fwd(ctypes.byref(a), stream) == 4            # workspace too small
+    a = _fwd_args(d, outs, ws, T, n, D)
+    a.n = 9
+    assert lib.mhc_fwd(ctypes.byref(a), stream) == 2            # bad shape
+    a = _fwd_args(d, outs, ws, T, n, D)
+    a.phi = d.phi.data_ptr() + 1
+    assert lib.mhc_fwd(ctypes.byref(a), stream) == 3            # misaligned
+    a = _fwd_args(d, outs, ws, T, n, D)
+    a.x = None
+    assert lib.mhc_fwd(ctypes.byref(a), stream) == 1            # NULL input
+    with pytest.raises(ValueError):
+        mhc_forward_pre(d.x, d.phi[:, :-1].contiguous(), d.alpha, d.bias)   # wrong phi shape
+
+
+def test_launch_counter_advances():
+    d = make_inputs(1, 16, 4, 128, seed=5).to("cuda")
+    before = _lib.launch_count()
+    mhc_forward_pre(d.x, d.phi, d.alpha, d.bias)
+    torch.cuda.synchronize()
+    assert _lib.launch_count() > before
