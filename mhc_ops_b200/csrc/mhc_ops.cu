@@ -12,8 +12,14 @@
 #include <cstdio>
 #include <string>
 
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "common.cuh"
 #include "generic.cuh"
+#include "sm100.cuh"
+#include "fwd_sm100.cuh"
 
 namespace mhc {
 
@@ -134,9 +140,184 @@ struct BwdGeneric {
   }
 };
 
+// ----------------------------------------------------------------- TMA maps
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      ptr = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }();
+  return fn;
+}
+
+// Row-major bf16 tensor of `rank` dims (dims[0] innermost) -> tiled TMA map.
+int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                    const uint32_t* box, CUtensorMapSwizzle swz) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return MHC_ERR_CUDA;
+  cuuint64_t d[5];
+  cuuint64_t st[4];
+  cuuint32_t b[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    es[i] = 1;
+    if (i + 1 < rank) st[i] = strides_bytes[i];
+  }
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, st, b, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MHC_OK : MHC_ERR_CUDA;
+}
+
+// ----------------------------------------------------------------- launch plans
+struct ClusterPlan {
+  int C = 0;             // cluster size
+  int max_clusters = 0;  // co-resident clusters on this device
+};
+
+// Largest number of co-resident CTAs over the cluster sizes C (<= 16) that
+// divide D/64; ties go to the larger C (shorter L2 re-read distance).
+template <typename Kernel>
+int plan_clusters(Kernel kernel, int smem, int threads, int D, ClusterPlan* out) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, const void*, int>, ClusterPlan> cache;
+  int dev = 0;
+  MHC_CUDA_TRY(cudaGetDevice(&dev));
+  const auto key = std::make_tuple(dev, reinterpret_cast<const void*>(kernel), D);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *out = it->second;
+      return MHC_OK;
+    }
+  }
+  MHC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  MHC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  ClusterPlan best;
+  for (int C : {16, 8, 4, 2, 1}) {
+    if (D % (64 * C) != 0) continue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(C);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = C;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int ncl = 0;
+    if (cudaOccupancyMaxActiveClusters(&ncl, kernel, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      continue;
+    }
+    if (ncl * C > best.max_clusters * best.C) best = ClusterPlan{C, ncl};
+  }
+  if (best.C == 0) return MHC_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(mu);
+  cache[key] = best;
+  *out = best;
+  return MHC_OK;
+}
+
+// ----------------------------------------------------------------- tensor-core forward
+// Shapes it takes: n in {4, 8}, D a multiple of 64, 16-byte aligned x / h_in,
+// T < 2^31.  Everything else runs the generic kernels.
+bool fwd_tc_eligible(const mhc_fwd_args* a) {
+  if (!(a->n == 4 || a->n == 8)) return false;
+  if (a->D % 64 != 0 || a->tokens >= ((int64_t)1 << 31)) return false;
+  return aligned(a->x, 16) && aligned(a->h_in, 16) && aligned(a->phi, 16);
+}
+
+size_t fwd_tc_phis_bytes(int n, int D) {
+  const int NB = n == 4 ? fwdtc::Cfg<4>::NB : fwdtc::Cfg<8>::NB;
+  return (size_t)NB * n * D * sizeof(uint16_t);
+}
+
+template <int n>
+struct FwdTc {
+  static int run(const mhc_fwd_args* a, cudaStream_t s, int sms) {
+    (void)sms;
+    using Cf = fwdtc::Cfg<n>;
+    const int64_t T = a->tokens;
+    const int D = a->D;
+    const int nD = n * D;
+    char* ws = static_cast<char*>(a->workspace);
+    uint16_t* phis = reinterpret_cast<uint16_t*>(ws + kWsHeaderBytes);
+    int st;
+    ClusterPlan plan;
+    if ((st = plan_clusters(fwdtc::fwd_kernel<n>, Cf::SMEM, fwdtc::kThreads, D, &plan))) return st;
+
+    fwdtc::split_phi_kernel<n><<<std::min<int64_t>(((int64_t)Cf::NB * nD + 255) / 256, 4 * 148), 256, 0, s>>>(
+        a->phi, phis, nD);
+    if ((st = after_launch())) return st;
+
+    CUtensorMap m_x2d, m_phi, m_x3d;
+    {
+      const uint64_t dims[2] = {(uint64_t)nD, (uint64_t)T};
+      const uint64_t strides[1] = {(uint64_t)nD * 2};
+      const uint32_t box[2] = {fwdtc::kBK, fwdtc::kBM};
+      if ((st = encode_bf16_map(&m_x2d, a->x, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    }
+    {
+      const uint64_t dims[2] = {(uint64_t)nD, (uint64_t)Cf::NB};
+      const uint64_t strides[1] = {(uint64_t)nD * 2};
+      const uint32_t box[2] = {fwdtc::kBK, (uint32_t)Cf::NB};
+      if ((st = encode_bf16_map(&m_phi, phis, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    }
+    {
+      const uint64_t dims[3] = {(uint64_t)D, (uint64_t)n, (uint64_t)T};
+      const uint64_t strides[2] = {(uint64_t)D * 2, (uint64_t)nD * 2};
+      const uint32_t box[3] = {fwdtc::kBK, (uint32_t)n, (uint32_t)Cf::RR_TOK};
+      if ((st = encode_bf16_map(&m_x3d, a->x, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE))) return st;
+    }
+    fwdtc::Params p;
+    p.alpha = a->alpha;
+    p.bias = a->bias;
+    p.h_in = a->h_in;
+    p.h_post = a->h_post;
+    p.h_res = a->h_res;
+    p.inv_rms = a->inv_rms;
+    p.h_mix = a->h_mix;
+    p.h_pre = a->h_pre;
+    p.status = reinterpret_cast<int*>(ws);
+    p.T = T;
+    p.D = D;
+    p.C = plan.C;
+    p.Dc = D / plan.C;
+    p.num_tiles = (int)((T + fwdtc::kBM - 1) / fwdtc::kBM);
+    p.norm_eps = a->norm_eps;
+    p.hc_eps = a->hc_eps;
+    const int nclusters = std::max(1, std::min(plan.max_clusters, p.num_tiles));
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(nclusters * plan.C);
+    cfg.blockDim = dim3(fwdtc::kThreads);
+    cfg.dynamicSmemBytes = Cf::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = plan.C;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    MHC_CUDA_TRY(cudaLaunchKernelEx(&cfg, fwdtc::fwd_kernel<n>, m_x2d, m_phi, m_x3d, p));
+    return after_launch();
+  }
+};
+
 int fwd_workspace(int64_t T, int n, int D, size_t* bytes) {
-  (void)T; (void)n; (void)D;
-  *bytes = kWsHeaderBytes;
+  (void)T;
+  size_t b = kWsHeaderBytes;
+  if ((n == 4 || n == 8) && D % 64 == 0) b = align_up(b + fwd_tc_phis_bytes(n, D), kWsAlign);
+  *bytes = b;
   return MHC_OK;
 }
 
@@ -208,6 +389,10 @@ int mhc_fwd(const mhc_fwd_args* a, void* stream) {
       !aligned(a->h_mix, 4) || !aligned(a->h_pre, 4))
     return MHC_ERR_MISALIGNED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (fwd_tc_eligible(a)) {
+    if (a->n == 4) return FwdTc<4>::run(a, s, sms);
+    return FwdTc<8>::run(a, s, sms);
+  }
   return dispatch_n<FwdGeneric>(a->n, a, s, sms);
 }
 

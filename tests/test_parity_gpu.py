@@ -17,7 +17,7 @@ from mhc_ops_b200 import mhc_backward_manual, mhc_forward_pre
 from mhc_ops_b200.synthetic import make_inputs
 from oracle import mhc_oracle as O
 from tests._golden import fixture_names, load_fixture
-from tests._gpu import DEV, assert_bwd_close, assert_fwd_close, bits, from_bits, rel
+from tests._gpu import DEV, FP32_TOL, assert_bwd_close, assert_fwd_close, bits, from_bits, rel
 
 pytestmark = pytest.mark.gpu
 
