@@ -1,0 +1,718 @@
+// Backward of the mHC pre-op on sm_100a: cluster K-split, tcgen05 GEMMs.
+//
+// Math: src/backward/golden.py:38-96.  Per token t (row of x):
+//   dh_pre[i] = sum_d dh_in[d] x[i,d]                                  (:51)
+//   dh_mix    = [a_pre dh_pre2, a_post dh_post2, a_res dh_res] * inv_rms (:53-62)
+//   c         = (sum_j dh_mix_tmp[j] h_mix[j]) inv_rms^3 / nD           (:74, :89)
+//   dx[k]     = gamma[k] (dh_mix @ phi)[k] - c x[k] + h_pre[i] dh_in[d] (:65, :89-94)
+// and over tokens: G = dh_mix^T x, dphi = G * gamma (:68-69), dgamma[k] =
+// sum_j phi[j,k] G[j,k] (= sum_t x dvecX_mm, :93), dalpha (:77-80), dbias (:83-86).
+//
+// A cluster of C CTAs owns one 128-token tile at a time; CTA r owns the
+// d-slice [r*Dc, (r+1)*Dc) of every stream.  Per tile:
+//   * WG_P (4 warps, phase 1) reads x and dh_in of its slice straight from HBM
+//     (warp per token, L2 evict-last), forms the partial dh_pre of each token,
+//     sends it to the token's owner CTA (DSMEM); the owner reduces the C
+//     partials in rank order, computes dh_mix, c, the dalpha/dbias terms and
+//     broadcasts one record per token (dh_mix, c, h_pre) to every CTA.
+//   * W0 re-reads the slice through L2 with TMA (x blocks [128 tok x 64 k],
+//     dh_in blocks, 128-B swizzle, evict-first) and streams pre-laid-out
+//     split-phi images (1-D bulk copies);
+//   * WG_E (4 warps) turns the records into the UMMA operands: DHM [128 tok x
+//     K'] (6 bf16 split products of dh_mix x phi, smallest first, so the
+//     tensor core's fp32 sum is exact to ~2^-23) and DHMT [N x 384] (3 split
+//     terms of dh_mix, tokens contiguous);
+//   * W1 issues tcgen05.mma: dvecX = DHM . PHIT^T per 64-k block (M=128,
+//     N=64, K'=6N) and G += x^T . DHMT^T per 128-k pair (M=128 k, N=N pad,
+//     K=3x128 tokens; x read MN-major straight from the TMA stages);
+//   * WG_E reads dvecX (TMEM lane = token) and writes dx; every FT tiles it
+//     flushes G from TMEM into the per-cluster partial (single writer per
+//     address, fixed order).
+#pragma once
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace mhc {
+namespace bwdtc {
+
+using namespace sm100;
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kThreads = 10 * 32;   // W0, W1, WG_P(4), WG_E(4)
+constexpr int kSmemLimit = 232448;
+
+constexpr int round_up(int v, int a) { return (v + a - 1) / a * a; }
+
+template <int n>
+struct Cfg {
+  static constexpr int N_OUT = n * n + 2 * n;
+  static constexpr int NSEG = 6;                         // split products of dvecX
+  static constexpr int KP = round_up(NSEG * N_OUT, 16);  // dvecX reduction length K'
+  static constexpr int KPC = KP / 8;                     // 16-byte core columns along K'
+  static constexpr int RG_BYTES = KPC * 128;             // one 8-row group of a K'-major image
+  static constexpr int PH_BYTES = 8 * RG_BYTES;          // split-phi image of one 64-k block
+  static constexpr int DHM_BYTES = 16 * RG_BYTES;        // 128 token rows
+  static constexpr int NG = round_up(N_OUT, 16);         // G accumulator columns / DHMT rows
+  static constexpr int GK = 3 * kBM;                     // G reduction length per tile
+  static constexpr int DHMT_SBO = (GK / 8) * 128;
+  static constexpr int DHMT_BYTES = (NG / 8) * DHMT_SBO;
+  static constexpr int X_BYTES = kBM * 128;
+  static constexpr int XS = 4;                           // x ring (2 adjacent pairs)
+  static constexpr int DS = 2;
+  static constexpr int PS = 2;
+  static constexpr int RECW = round_up(N_OUT + 1 + n, 4);
+  static constexpr int RB = 2;                           // dh_pre exchange buffers
+  static constexpr int MAX_TPO = 32;                     // C >= 4
+  static constexpr int MAX_KC = 1792;                    // d-slice * n per CTA
+
+  static constexpr int CW = 3 + N_OUT;                   // dalpha / dbias columns
+  static constexpr int smem_bytes() {
+    return 1024 + XS * X_BYTES + DS * X_BYTES + PS * PH_BYTES + DHM_BYTES + DHMT_BYTES +
+           RB * kBM * n * 4 /*pdh*/ + kBM * RECW * 4 /*bc*/ + MAX_TPO * (n + RECW + CW) * 4 /*owner scratch*/ +
+           512;
+  }
+  static constexpr int SMEM = smem_bytes();
+  static_assert(SMEM <= kSmemLimit, "backward tile does not fit in shared memory");
+  static_assert(n % 2 == 0, "G pairs two streams of a d-chunk");
+};
+
+struct Params {
+  const uint16_t* x;
+  const uint16_t* dh_in;
+  const float* alpha;
+  const float* inv_rms;
+  const float* h_mix;
+  const float* h_pre;
+  const float* h_post;
+  const float* dh_post;
+  const float* dh_res;
+  const float* gamma;     // may be null
+  const uint8_t* phit;    // split-phi images, PH_BYTES per 64-k block
+  uint16_t* dx;
+  float* gpart;           // [num_clusters][N_OUT][nD]
+  float* abpart;          // [num_clusters * C][3 + N_OUT]
+  int* status;
+  int64_t T;
+  int D;
+  int Dc;
+  int C;
+  int num_tiles;
+  int FT;                 // tiles per G flush
+  int dv_bufs;            // 1 or 2 dvecX TMEM buffers
+  float hc_eps;
+};
+
+template <int n>
+struct Bars {
+  using Cf = Cfg<n>;
+  static constexpr int x_full = 0;
+  static constexpr int x_empty = x_full + Cf::XS;
+  static constexpr int dh_full = x_empty + Cf::XS;
+  static constexpr int dh_empty = dh_full + Cf::DS;
+  static constexpr int ph_full = dh_empty + Cf::DS;
+  static constexpr int ph_empty = ph_full + Cf::PS;
+  static constexpr int dv_full = ph_empty + Cf::PS;
+  static constexpr int dv_empty = dv_full + 2;
+  static constexpr int dhm_full = dv_empty + 2;
+  static constexpr int dhm_free = dhm_full + 1;
+  static constexpr int g_full = dhm_free + 1;
+  static constexpr int g_empty = g_full + 1;
+  static constexpr int p_full = g_empty + 1;
+  static constexpr int p_free = p_full + Cf::RB;
+  static constexpr int bc_full = p_free + Cf::RB;
+  static constexpr int bc_free = bc_full + 1;
+  static constexpr int count = bc_free + 1;
+};
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ uint4 ldg_keep(const void* ptr, uint64_t pol) {
+  uint4 v;
+  asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(ptr), "l"(pol));
+  return v;
+}
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                          uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(pol)
+      : "memory");
+}
+
+__device__ __forceinline__ void red_add_f32(float* addr, float v) {
+  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
+}
+
+// K-major operand without swizzle: 8x16-byte core matrices, LBO between
+// K-adjacent cores, SBO between 8-row groups.
+__device__ __forceinline__ uint64_t desc_kmajor_interleave(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  return d;   // layout type 0 = no swizzle
+}
+
+// Byte offset of element (row, kk) in a K-major interleaved image whose
+// 8-row groups are sbo bytes apart.
+__device__ __forceinline__ uint32_t interleave_off(int row, int kk, int sbo) {
+  return (uint32_t)((row >> 3) * sbo + (kk >> 3) * 128 + (row & 7) * 16 + (kk & 7) * 2);
+}
+
+// Split-product order of dvecX (smallest first): A term x B term per segment.
+__device__ __forceinline__ int seg_a_term(int seg) {
+  // segments: m.M, l.H, h.L, m.H, h.M, h.H
+  return seg == 0 ? 1 : seg == 1 ? 2 : seg == 3 ? 1 : 0;
+}
+__host__ __device__ __forceinline__ int seg_b_term(int seg) {
+  return seg == 0 ? 1 : seg == 2 ? 2 : seg == 4 ? 1 : 0;
+}
+
+// t-th bf16 term of v (0 = hi, 1 = mid, 2 = lo): each rounds what is left.
+__device__ __forceinline__ uint16_t split_term(float v, int term) {
+  uint16_t out = 0;
+  for (int tt = 0; tt <= term; ++tt) {
+    out = f32_to_bf16_bits(v);
+    v -= bf16_bits_to_f32(out);
+  }
+  return out;
+}
+
+template <int n>
+__global__ void __launch_bounds__(kThreads, 1)
+    bwd_kernel(const __grid_constant__ CUtensorMap map_x2d, const __grid_constant__ CUtensorMap map_dh,
+               const Params p) {
+  using Cf = Cfg<n>;
+  using B = Bars<n>;
+  constexpr int N_OUT = Cf::N_OUT;
+  constexpr int RECW = Cf::RECW;
+  constexpr int RB = Cf::RB;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* xr = smem;                                  // XS x blocks (pairs adjacent)
+  uint8_t* dhr = xr + Cf::XS * Cf::X_BYTES;            // DS dh_in blocks
+  uint8_t* phr = dhr + Cf::DS * Cf::X_BYTES;           // PS split-phi images
+  uint8_t* dhm = phr + Cf::PS * Cf::PH_BYTES;          // A operand of dvecX
+  uint8_t* dhmt = dhm + Cf::DHM_BYTES;                 // B operand of G
+  float* pdh = reinterpret_cast<float*>(dhmt + Cf::DHMT_BYTES);    // [RB][128][n]
+  float* bc = pdh + RB * kBM * n;                      // [128][RECW]
+  float* dhp_s = bc + kBM * RECW;                      // [TPO][n]
+  float* rec_s = dhp_s + Cf::MAX_TPO * n;              // [TPO][RECW]
+  float* contrib = rec_s + Cf::MAX_TPO * RECW;         // [TPO][CW]: dalpha (3), dbias (N_OUT) terms
+  uint64_t* bars = reinterpret_cast<uint64_t*>(contrib + Cf::MAX_TPO * Cf::CW);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + B::count);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const uint32_t cid = cluster_id_x();
+  const uint32_t ncl = nclusters_x();
+  const int C = p.C;
+  const int TPO = kBM / C;
+  const int D = p.D;
+  const int Dc = p.Dc;
+  const int DCH = Dc / kBK;
+  const int nD = n * D;
+  const int KC = n * Dc;
+  const int NPAIR = KC / 128;                 // G blocks of 128 k per CTA
+  const int DVB = p.dv_bufs;
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+
+  // zero the padding rows of DHMT (j >= N_OUT) once
+  for (int idx = threadIdx.x; idx < Cf::DHMT_BYTES / 16; idx += kThreads) {
+    reinterpret_cast<uint4*>(dhmt)[idx] = make_uint4(0, 0, 0, 0);
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < Cf::XS; ++i) {
+      mbar_init(bar(B::x_full + i), 1);
+      mbar_init(bar(B::x_empty + i), 1 + 4);
+    }
+    for (int i = 0; i < Cf::DS; ++i) {
+      mbar_init(bar(B::dh_full + i), 1);
+      mbar_init(bar(B::dh_empty + i), 4);
+    }
+    for (int i = 0; i < Cf::PS; ++i) {
+      mbar_init(bar(B::ph_full + i), 1);
+      mbar_init(bar(B::ph_empty + i), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(B::dv_full + i), 1);
+      mbar_init(bar(B::dv_empty + i), 4);
+    }
+    mbar_init(bar(B::dhm_full), 128);
+    mbar_init(bar(B::dhm_free), 1);
+    mbar_init(bar(B::g_full), 1);
+    mbar_init(bar(B::g_empty), 4);
+    for (int i = 0; i < RB; ++i) {
+      mbar_init(bar(B::p_full + i), kBM);
+      mbar_init(bar(B::p_free + i), C);
+    }
+    mbar_init(bar(B::bc_full), kBM);
+    mbar_init(bar(B::bc_free), C);
+    *abort_flag = 0;
+    fence_mbarrier_init_cluster();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&map_x2d);
+    prefetch_tensormap(&map_dh);
+  }
+  fence_proxy_async_smem();   // DHMT zeros are read by the tensor core later
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  cluster_sync_all();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tmem_dv = tmem_base;                       // DVB x 64 columns
+  const uint32_t tmem_g = tmem_base + DVB * 64;             // NPAIR x NG columns
+  const WaitCtx wc{abort_flag, p.status};
+  const int my_tiles = (int)cid < p.num_tiles ? (p.num_tiles - 1 - (int)cid) / (int)ncl + 1 : 0;
+  const bool producer = (lane == 0);
+
+  if (warp == 0) {
+    // ------------------------------------------------ W0: TMA producer (phase-2 re-read)
+    if (producer) {
+      const uint64_t pol_drop = l2_policy_evict_first();
+      const uint64_t pol_keep = l2_policy_evict_last();
+      uint32_t q = 0, dq = 0;
+      for (int j = 0; j < my_tiles; ++j) {
+        const int tile = (int)cid + j * (int)ncl;
+        for (int dch = 0; dch < DCH; ++dch, ++dq) {
+          const int ds = dq % Cf::DS;
+          mbar_wait(bar(B::dh_empty + ds), ((dq / Cf::DS) & 1) ^ 1, wc);
+          if (!*abort_flag) {
+            mbar_arrive_expect_tx(bar(B::dh_full + ds), Cf::X_BYTES);
+            tma_load_2d(smem_u32(dhr + ds * Cf::X_BYTES), &map_dh, bar(B::dh_full + ds), (int)rank * Dc + dch * kBK,
+                        tile * kBM, pol_drop);
+          }
+          for (int i = 0; i < n; ++i, ++q) {
+            const int s = q % Cf::XS;
+            const int k0 = i * D + (int)rank * Dc + dch * kBK;
+            mbar_wait(bar(B::x_empty + s), ((q / Cf::XS) & 1) ^ 1, wc);
+            if (!*abort_flag) {
+              mbar_arrive_expect_tx(bar(B::x_full + s), Cf::X_BYTES);
+              tma_load_2d(smem_u32(xr + s * Cf::X_BYTES), &map_x2d, bar(B::x_full + s), k0, tile * kBM, pol_drop);
+            }
+            const int ps = q % Cf::PS;
+            mbar_wait(bar(B::ph_empty + ps), ((q / Cf::PS) & 1) ^ 1, wc);
+            if (!*abort_flag) {
+              mbar_arrive_expect_tx(bar(B::ph_full + ps), Cf::PH_BYTES);
+              bulk_load(smem_u32(phr + ps * Cf::PH_BYTES), p.phit + (size_t)(k0 / kBK) * Cf::PH_BYTES, Cf::PH_BYTES,
+                        bar(B::ph_full + ps), pol_keep);
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ W1: tcgen05.mma issuer
+    if (producer) {
+      constexpr uint32_t idesc_dv = idesc_bf16_f32(kBM, kBK, false, false);
+      constexpr uint32_t idesc_g = idesc_bf16_f32(kBM, Cf::NG, true, false);
+      uint32_t q = 0, flushes = 0;
+      for (int j = 0; j < my_tiles; ++j) {
+        mbar_wait(bar(B::dhm_full), j & 1, wc);
+        tc_fence_after();
+        const bool g_restart = (j % p.FT) == 0;
+        if (g_restart && j > 0) {
+          mbar_wait(bar(B::g_empty), (flushes - 1) & 1, wc);   // previous G group read out
+          tc_fence_after();
+        }
+        for (int dch = 0; dch < DCH; ++dch) {
+          for (int i = 0; i < n; ++i, ++q) {
+            const int s = q % Cf::XS;
+            const int ps = q % Cf::PS;
+            const int dvb = DVB == 2 ? (int)(q & 1) : 0;
+            const uint32_t dvph = DVB == 2 ? (q >> 1) & 1 : q & 1;
+            mbar_wait(bar(B::ph_full + ps), (q / Cf::PS) & 1, wc);
+            mbar_wait(bar(B::dv_empty + dvb), dvph ^ 1, wc);
+            tc_fence_after();
+            if (!*abort_flag) {
+              const uint32_t dhm_a = smem_u32(dhm), ph_a = smem_u32(phr + ps * Cf::PH_BYTES);
+#pragma unroll
+              for (int ks = 0; ks < Cf::KP / 16; ++ks)
+                umma_bf16(tmem_dv + dvb * 64, desc_kmajor_interleave(dhm_a + ks * 256, 128, Cf::RG_BYTES),
+                          desc_kmajor_interleave(ph_a + ks * 256, 128, Cf::RG_BYTES), idesc_dv, ks != 0);
+              umma_commit(bar(B::ph_empty + ps));
+              umma_commit(bar(B::dv_full + dvb));
+            }
+            if (i & 1) {
+              // G over the pair of stages (s-1, s): rows 0..63 stream i-1, 64..127 stream i
+              mbar_wait(bar(B::x_full + s - 1), ((q - 1) / Cf::XS) & 1, wc);
+              mbar_wait(bar(B::x_full + s), (q / Cf::XS) & 1, wc);
+              tc_fence_after();
+              if (!*abort_flag) {
+                const int blk = dch * (n / 2) + i / 2;
+                const uint32_t xa = smem_u32(xr + (s - 1) * Cf::X_BYTES);
+                const uint32_t ga = smem_u32(dhmt);
+#pragma unroll 1
+                for (int e = 0; e < 3; ++e) {
+#pragma unroll
+                  for (int ks = 0; ks < kBM / 16; ++ks) {
+                    const uint64_t ad = desc_mnmajor_sw128(xa + ks * 2048, Cf::X_BYTES, 1024);
+                    const uint64_t bd = desc_kmajor_interleave(ga + (e * kBM + ks * 16) * 16, 128, Cf::DHMT_SBO);
+                    umma_bf16(tmem_g + blk * Cf::NG, ad, bd, idesc_g, !(g_restart && e == 0 && ks == 0));
+                  }
+                }
+                umma_commit(bar(B::x_empty + s - 1));
+                umma_commit(bar(B::x_empty + s));
+              }
+            }
+          }
+        }
+        if (!*abort_flag) umma_commit(bar(B::dhm_free));
+        if ((j + 1) % p.FT == 0 || j == my_tiles - 1) {
+          if (!*abort_flag) umma_commit(bar(B::g_full));
+          ++flushes;
+        }
+      }
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------ WG_P: phase 1 (dh_pre partials) + owner + broadcast
+    const int tid = threadIdx.x - 2 * 32;    // 0..127
+    const int wp = warp - 2;                 // 0..3, 32 token rows each
+    const uint64_t pol_keep = l2_policy_evict_last();
+    const float a_pre = p.alpha[0], a_post = p.alpha[1], a_res = p.alpha[2];
+    const float inv_nd = 1.0f / (float)nD;
+    float ab_acc = 0.f;                      // thread c < 3+N_OUT: running dalpha/dbias column
+    for (int j = 0; j < my_tiles; ++j) {
+      const int tile = (int)cid + j * (int)ncl;
+      // (1) partial dh_pre of this warp's 32 tokens over the CTA's d-slice
+      float mine[n];
+#pragma unroll
+      for (int i = 0; i < n; ++i) mine[i] = 0.f;
+      for (int tt = 0; tt < 32; tt += 4) {
+        float acc[4][n];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int i = 0; i < n; ++i) acc[u][i] = 0.f;
+        for (int e0 = lane * 8; e0 < Dc; e0 += 256) {
+          uint4 g[4], xv[4][n];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int64_t t = (int64_t)tile * kBM + wp * 32 + tt + u;
+            if (t < p.T) {
+              g[u] = ldg_keep(p.dh_in + t * D + (int64_t)rank * Dc + e0, pol_keep);
+#pragma unroll
+              for (int i = 0; i < n; ++i)
+                xv[u][i] = ldg_keep(p.x + t * nD + (int64_t)i * D + (int64_t)rank * Dc + e0, pol_keep);
+            } else {
+              g[u] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+              for (int i = 0; i < n; ++i) xv[u][i] = make_uint4(0, 0, 0, 0);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            float gf[8];
+            bf16x8_to_f32(g[u], gf);
+#pragma unroll
+            for (int i = 0; i < n; ++i) {
+              float xf[8];
+              bf16x8_to_f32(xv[u][i], xf);
+              float s0 = gf[0] * xf[0], s1 = gf[1] * xf[1];
+              s0 = fmaf(gf[2], xf[2], s0);
+              s1 = fmaf(gf[3], xf[3], s1);
+              s0 = fmaf(gf[4], xf[4], s0);
+              s1 = fmaf(gf[5], xf[5], s1);
+              s0 = fmaf(gf[6], xf[6], s0);
+              s1 = fmaf(gf[7], xf[7], s1);
+              acc[u][i] += s0 + s1;
+            }
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int i = 0; i < n; ++i) {
+            const float v = warp_sum(acc[u][i]);
+            if (lane == tt + u) mine[i] = v;
+          }
+      }
+      // (2) send my token's partial to its owner
+      const int pb = j % RB;
+      const uint32_t pph = (j / RB) & 1;
+      const int row = wp * 32 + lane;
+      mbar_wait<true>(bar(B::p_free + pb), pph ^ 1, wc);
+      {
+        const int owner = row / TPO;
+        const uint32_t dst = mapa_shared(smem_u32(pdh + (pb * kBM + (int)rank * TPO + (row % TPO)) * n), owner);
+#pragma unroll
+        for (int i = 0; i < n; ++i) st_cluster_f32(dst + 4 * i, mine[i]);
+        mbar_arrive_remote(bar(B::p_full + pb), owner);
+      }
+      // (3) owner: reduce the C partials of my TPO tokens in rank order
+      mbar_wait<true>(bar(B::p_full + pb), pph, wc);
+      for (int idx = tid; idx < TPO * n; idx += 128) {
+        const int lt = idx / n, i = idx - lt * n;
+        float s = 0.f;
+        for (int src = 0; src < C; ++src) s += pdh[(pb * kBM + src * TPO + lt) * n + i];
+        dhp_s[lt * n + i] = s;
+      }
+      named_sync(1, 128);
+      if (tid == 0)
+        for (int c = 0; c < C; ++c) mbar_arrive_remote(bar(B::p_free + pb), c);
+      // one thread per owned token: dh_mix, c and the dalpha / dbias terms
+      for (int lt = tid; lt < TPO; lt += 128) {
+        const int64_t t = (int64_t)tile * kBM + (int)rank * TPO + lt;
+        const bool valid = t < p.T;
+        const int64_t tv = valid ? t : 0;
+        const float ir = valid ? p.inv_rms[tv] : 0.f;
+        float dinv = 0.f, dal0 = 0.f, dal1 = 0.f, dal2 = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < N_OUT; ++jj) {
+          const float hm = p.h_mix[tv * N_OUT + jj];
+          float g2, tmp;
+          if (jj < n) {
+            const float s = p.h_pre[tv * n + jj] - p.hc_eps;
+            g2 = dhp_s[lt * n + jj] * s * (1.0f - s);
+            tmp = a_pre * g2;
+          } else if (jj < 2 * n) {
+            const float hq = p.h_post[tv * n + (jj - n)];
+            g2 = p.dh_post[tv * n + (jj - n)] * hq * (1.0f - hq / 2.0f);
+            tmp = a_post * g2;
+          } else {
+            g2 = p.dh_res[tv * (n * n) + (jj - 2 * n)];
+            tmp = a_res * g2;
+          }
+          if (!valid) g2 = tmp = 0.f;
+          rec_s[lt * RECW + jj] = tmp * ir;                 // dh_mix (golden.py:62)
+          dinv += tmp * hm;                                 // dinv_rms (golden.py:74)
+          const float dal = g2 * (hm * ir);                 // dalpha terms (golden.py:77-79)
+          if (jj < n) dal0 += dal;
+          else if (jj < 2 * n) dal1 += dal;
+          else dal2 += dal;
+          contrib[lt * Cf::CW + 3 + jj] = g2;               // dbias terms (golden.py:83-85)
+        }
+        contrib[lt * Cf::CW + 0] = dal0;
+        contrib[lt * Cf::CW + 1] = dal1;
+        contrib[lt * Cf::CW + 2] = dal2;
+        rec_s[lt * RECW + N_OUT] = valid ? dinv * (ir * ir * ir) * inv_nd : 0.f;   // c (golden.py:89)
+#pragma unroll
+        for (int i = 0; i < n; ++i) rec_s[lt * RECW + N_OUT + 1 + i] = valid ? p.h_pre[tv * n + i] : 0.f;
+        for (int w = N_OUT + 1 + n; w < RECW; ++w) rec_s[lt * RECW + w] = 0.f;
+      }
+      named_sync(1, 128);
+      // running dalpha / dbias columns of this CTA's owned tokens, fixed order
+      if (tid < Cf::CW)
+        for (int lt = 0; lt < TPO; ++lt) ab_acc += contrib[lt * Cf::CW + tid];
+      named_sync(1, 128);
+      // (4) broadcast the records of my tokens to every CTA of the cluster
+      mbar_wait<true>(bar(B::bc_free), (j & 1) ^ 1, wc);
+      for (int idx = tid; idx < TPO * C; idx += 128) {
+        const int lt = idx % TPO, dstc = idx / TPO;
+        const uint32_t dst = mapa_shared(smem_u32(bc + ((int)rank * TPO + lt) * RECW), dstc);
+#pragma unroll
+        for (int w = 0; w < RECW; w += 4)
+          st_cluster_v4_f32(dst + 4 * w, rec_s[lt * RECW + w], rec_s[lt * RECW + w + 1], rec_s[lt * RECW + w + 2],
+                            rec_s[lt * RECW + w + 3]);
+        mbar_arrive_remote(bar(B::bc_full), dstc);
+      }
+      named_sync(1, 128);
+    }
+    if (tid < Cf::CW) p.abpart[((int64_t)cid * C + rank) * Cf::CW + tid] = ab_acc;
+  } else {
+    // ------------------------------------------------ WG_E: operands, dx epilogue, G flush
+    const int q4 = warp & 3;
+    const int row = 32 * q4 + lane;          // token row = TMEM lane
+    uint32_t q = 0, dq = 0, flushes = 0;
+    for (int j = 0; j < my_tiles; ++j) {
+      const int tile = (int)cid + j * (int)ncl;
+      const int64_t t = (int64_t)tile * kBM + row;
+      // (a) record -> DHM row / DHMT column of this token
+      mbar_wait<true>(bar(B::bc_full), j & 1, wc);
+      mbar_wait(bar(B::dhm_free), (j & 1) ^ 1, wc);
+      float dmix[N_OUT];
+#pragma unroll
+      for (int jj = 0; jj < N_OUT; ++jj) dmix[jj] = bc[row * RECW + jj];
+      const float c_t = bc[row * RECW + N_OUT];
+      float hp[n];
+#pragma unroll
+      for (int i = 0; i < n; ++i) hp[i] = bc[row * RECW + N_OUT + 1 + i];
+      {
+        uint16_t tr[3][N_OUT];
+#pragma unroll
+        for (int jj = 0; jj < N_OUT; ++jj) {
+          float v = dmix[jj];
+#pragma unroll
+          for (int e = 0; e < 3; ++e) {
+            tr[e][jj] = f32_to_bf16_bits(v);
+            v -= bf16_bits_to_f32(tr[e][jj]);
+          }
+        }
+        // DHM row: K' = seg*N_OUT + jj, A-side term of each segment, zero padding
+#pragma unroll
+        for (int kc = 0; kc < Cf::KPC; ++kc) {
+          uint32_t w[4];
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            uint32_t lohi[2];
+#pragma unroll
+            for (int b2 = 0; b2 < 2; ++b2) {
+              const int kp = kc * 8 + h * 2 + b2;
+              const int seg = kp / N_OUT, jj = kp - seg * N_OUT;
+              lohi[b2] = kp < Cf::NSEG * N_OUT ? tr[seg_a_term(seg)][jj] : 0;
+            }
+            w[h] = lohi[0] | (lohi[1] << 16);
+          }
+          *reinterpret_cast<uint4*>(dhm + interleave_off(row, kc * 8, Cf::RG_BYTES)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        // DHMT: row jj, K = e*128 + token; e = 0 lo, 1 mid, 2 hi (smallest first)
+#pragma unroll
+        for (int jj = 0; jj < N_OUT; ++jj)
+#pragma unroll
+          for (int e = 0; e < 3; ++e)
+            *reinterpret_cast<uint16_t*>(dhmt + interleave_off(jj, e * kBM + row, Cf::DHMT_SBO)) = tr[2 - e][jj];
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(bar(B::dhm_full));
+      named_sync(2, 128);
+      if (q4 == 0 && lane == 0)
+        for (int c = 0; c < p.C; ++c) mbar_arrive_remote(bar(B::bc_free), c);
+      // (b) dx of every 64-k block of the slice
+      for (int dch = 0; dch < DCH; ++dch, ++dq) {
+        const int ds = dq % Cf::DS;
+        mbar_wait(bar(B::dh_full + ds), (dq / Cf::DS) & 1, wc);
+        const uint32_t dh_row = smem_u32(dhr + ds * Cf::X_BYTES) + row * 128;
+        for (int i = 0; i < n; ++i, ++q) {
+          const int s = q % Cf::XS;
+          const int dvb = DVB == 2 ? (int)(q & 1) : 0;
+          const uint32_t dvph = DVB == 2 ? (q >> 1) & 1 : q & 1;
+          mbar_wait(bar(B::x_full + s), (q / Cf::XS) & 1, wc);
+          mbar_wait(bar(B::dv_full + dvb), dvph, wc);
+          tc_fence_after();
+          const uint32_t x_row = smem_u32(xr + s * Cf::X_BYTES) + row * 128;
+          const float* gm = p.gamma ? p.gamma + (int64_t)i * D + (int64_t)rank * Dc + dch * kBK : nullptr;
+          uint16_t* dst = p.dx + t * nD + (int64_t)i * D + (int64_t)rank * Dc + dch * kBK;
+#pragma unroll
+          for (int c16 = 0; c16 < 4; ++c16) {
+            float v[16];
+            tmem_ld16(tmem_dv + dvb * 64 + ((uint32_t)(32 * q4) << 16) + c16 * 16, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int hc = 0; hc < 2; ++hc) {
+              const int c = c16 * 2 + hc;             // 16-byte chunk 0..7 of the 128-byte row
+              const uint32_t sw = (uint32_t)((c ^ (row & 7)) << 4);
+              float xf[8], gf[8], gam[8];
+              bf16x8_to_f32(lds128(x_row + sw), xf);
+              bf16x8_to_f32(lds128(dh_row + sw), gf);
+              if (gm) {
+                const float4 g0 = __ldg(reinterpret_cast<const float4*>(gm + c * 8));
+                const float4 g1 = __ldg(reinterpret_cast<const float4*>(gm + c * 8 + 4));
+                gam[0] = g0.x; gam[1] = g0.y; gam[2] = g0.z; gam[3] = g0.w;
+                gam[4] = g1.x; gam[5] = g1.y; gam[6] = g1.z; gam[7] = g1.w;
+              } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) gam[e] = 1.0f;
+              }
+              uint32_t o[4];
+#pragma unroll
+              for (int e = 0; e < 8; e += 2) {
+                const float d0 = v[hc * 8 + e] * gam[e] + ((-c_t) * xf[e] + hp[i] * gf[e]);
+                const float d1 = v[hc * 8 + e + 1] * gam[e + 1] + ((-c_t) * xf[e + 1] + hp[i] * gf[e + 1]);
+                o[e / 2] = (uint32_t)f32_to_bf16_bits(d0) | ((uint32_t)f32_to_bf16_bits(d1) << 16);
+              }
+              if (t < p.T) *reinterpret_cast<uint4*>(dst + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(bar(B::dv_empty + dvb));
+            mbar_arrive(bar(B::x_empty + s));
+            if (i == n - 1) mbar_arrive(bar(B::dh_empty + ds));
+          }
+        }
+      }
+      // (c) flush G of the finished group into the per-cluster partial
+      if ((j + 1) % p.FT == 0 || j == my_tiles - 1) {
+        mbar_wait(bar(B::g_full), flushes & 1, wc);
+        tc_fence_after();
+        for (int blk = 0; blk < NPAIR; ++blk) {
+          const int dch = blk / (n / 2), i0 = (blk % (n / 2)) * 2;
+          const int i = i0 + (row >> 6);
+          const int64_t k = (int64_t)i * D + (int64_t)rank * Dc + dch * kBK + (row & 63);
+          float* gp = p.gpart + (int64_t)cid * N_OUT * nD + k;
+#pragma unroll
+          for (int c16 = 0; c16 < Cf::NG / 16; ++c16) {
+            float v[16];
+            tmem_ld16(tmem_g + blk * Cf::NG + ((uint32_t)(32 * q4) << 16) + c16 * 16, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int jj = c16 * 16 + e;
+              if (jj < N_OUT) {
+                if (flushes == 0) gp[(int64_t)jj * nD] = v[e];
+                else red_add_f32(gp + (int64_t)jj * nD, v[e]);
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B::g_empty));
+        ++flushes;
+      }
+    }
+  }
+
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+  cluster_sync_all();
+}
+
+// phi [N_OUT, nD] f32 -> per 64-k block the K'-major interleaved image that
+// W1 reads as the B operand of dvecX: element (kk, K'=seg*N_OUT+j) holds the
+// B-side split term of segment seg of phi[j][block*64+kk].
+template <int n>
+__global__ void __launch_bounds__(256) phit_kernel(const float* __restrict__ phi, uint16_t* __restrict__ img,
+                                                   int nD) {
+  using Cf = Cfg<n>;
+  const int64_t per_block = (int64_t)kBK * Cf::KP;
+  const int64_t total = (int64_t)(nD / kBK) * per_block;
+  for (int64_t idx = blockIdx.x * 256ll + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * 256) {
+    const int64_t blk = idx / per_block;
+    const int r = (int)(idx - blk * per_block);
+    const int kk = r / Cf::KP, kp = r - kk * Cf::KP;
+    uint16_t v = 0;
+    if (kp < Cf::NSEG * Cf::N_OUT) {
+      const int seg = kp / Cf::N_OUT, jj = kp - seg * Cf::N_OUT;
+      v = split_term(phi[(int64_t)jj * nD + blk * kBK + kk], seg_b_term(seg));
+    }
+    img[blk * (Cf::PH_BYTES / 2) + interleave_off(kk, kp, Cf::RG_BYTES) / 2] = v;
+  }
+}
+
+}  // namespace bwdtc
+}  // namespace mhc

@@ -9,14 +9,18 @@
 // {i*D + d : d in slice} of each 128-token row block.  Per tile and CTA:
 //   * W0 streams x (128 x 64 bf16, 128-B swizzle) and the bf16-split phi
 //     block (NB x 64) of each K-block into an S-stage ring with TMA;
-//   * W1 issues tcgen05.mma (M=128 tokens, N=NB split-phi rows, K=16) into a
-//     double-buffered TMEM accumulator;
-//   * WG_S (4 warps) sums x^2 of each token row from the same smem stages;
-//   * WG_A (4 warps) reads the accumulator (one TMEM lane per token), folds
-//     the phi split terms, and sends its partial (h_mix, sum x^2) of every
-//     token to the token's owner CTA through DSMEM; the owner reduces the C
-//     partials in fixed rank order, writes h_mix / inv_rms / h_pre / h_post /
-//     h_res and broadcasts h_pre to every CTA of the cluster;
+//   * W1 issues tcgen05.mma (M=128 tokens, N=NB split-phi rows, K=16); every
+//     K-block of 64 starts a fresh accumulator in a ring of NBUF TMEM buffers;
+//   * WG_SR (4 warps, one thread per token row = TMEM lane) sums x^2 of its
+//     row from the smem stage (tree sum per stage) and folds each K-block's
+//     accumulator and the phi split terms into its fp32 partial h_mix with
+//     round-to-nearest adds -- the tensor core's own accumulation across many
+//     K steps drifts (about 2^-23 per step, one-signed), per K-block it does
+//     not -- then sends (h_mix, sum x^2) of its token to the token's owner CTA
+//     through DSMEM;
+//   * WG_A (4 warps): the owner reduces the C partials of its tokens in fixed
+//     rank order, writes h_mix / inv_rms / h_pre / h_post / h_res and
+//     broadcasts h_pre to every CTA of the cluster;
 //   * WG_B (4 warps) re-reads its d-slice of the tile from L2 (W2 issues 3-D
 //     TMA loads, evict-first) and writes h_in for the slice.
 // phi is split into NT bf16 terms (hi, mid[, lo]) stacked as UMMA N rows, so
@@ -35,7 +39,7 @@ using namespace sm100;
 
 constexpr int kBM = 128;          // tokens per tile = UMMA M = TMEM lanes
 constexpr int kBK = 64;           // bf16 elements per 128-byte row
-constexpr int kThreads = 15 * 32; // W0, W1, W2, WG_S(4), WG_A(4), WG_B(4)
+constexpr int kThreads = 15 * 32; // W0, W1, W2, WG_SR(4), WG_A(4), WG_B(4)
 constexpr int kSmemLimit = 232448;
 
 constexpr int round_up(int v, int a) { return (v + a - 1) / a * a; }
@@ -57,12 +61,13 @@ struct Cfg {
   static constexpr int RR_BYTES = RR_TOK * n * 128;
   static constexpr int RS = round_up(N_OUT + 1, 4);        // floats per partial row
   static constexpr int ACC_COLS = round_up(NB, 32);
-  static constexpr int TMEM_COLS = pow2_at_least(2 * ACC_COLS);
+  static constexpr int NBUF = (512 / ACC_COLS) < 4 ? (512 / ACC_COLS) : 4;   // accumulator ring
+  static constexpr int TMEM_COLS = pow2_at_least(NBUF * ACC_COLS);
   static constexpr int R = 3;                              // re-read stages
 
   static constexpr int smem_bytes(int S, int RB) {
     return 1024 /*align slack*/ + S * STAGE_BYTES + R * RR_BYTES + RB * kBM * RS * 4 /*red*/ +
-           RB * kBM * n * 4 /*hpre*/ + 2 * kBM * 4 /*ss*/ + kBM * RS * 4 /*tot (owner)*/ + kBM * n * 4 /*hp_s*/ +
+           RB * kBM * n * 4 /*hpre*/ + kBM * RS * 4 /*tot (owner)*/ + kBM * n * 4 /*hp_s*/ +
            512 /*barriers + slots*/;
   }
   static constexpr int RB = smem_bytes(3, 2) <= kSmemLimit ? 2 : 1;
@@ -75,6 +80,7 @@ struct Cfg {
   static constexpr int SMEM = smem_bytes(S, RB);
   static_assert(SMEM <= kSmemLimit, "forward tile does not fit in shared memory");
   static_assert(NB <= 256, "UMMA N above 256");
+  static_assert(NBUF >= 2 && TMEM_COLS <= 512, "TMEM accumulator ring");
 };
 
 struct Params {
@@ -103,10 +109,8 @@ struct Bars {
   static constexpr int full = 0;
   static constexpr int empty = full + Cf::S;
   static constexpr int acc_full = empty + Cf::S;
-  static constexpr int acc_empty = acc_full + 2;
-  static constexpr int ss_full = acc_empty + 2;
-  static constexpr int ss_empty = ss_full + 2;
-  static constexpr int red_full = ss_empty + 2;
+  static constexpr int acc_empty = acc_full + Cf::NBUF;
+  static constexpr int red_full = acc_empty + Cf::NBUF;
   static constexpr int red_free = red_full + Cf::RB;
   static constexpr int hpre_full = red_free + Cf::RB;
   static constexpr int hpre_free = hpre_full + Cf::RB;
@@ -148,8 +152,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* rr = ring + S * Cf::STAGE_BYTES;                          // R re-read stages
   float* red = reinterpret_cast<float*>(rr + R * Cf::RR_BYTES);      // [RB][C][TPO][RS] == [RB][128][RS]
   float* hpre = red + RB * kBM * RS;                                 // [RB][128][n]
-  float* ss = hpre + RB * kBM * n;                                   // [2][128]
-  float* tot = ss + 2 * kBM;                                         // [TPO][RS]  (owner sums)
+  float* tot = hpre + RB * kBM * n;                                  // [TPO][RS]  (owner sums)
   float* hp_s = tot + kBM * RS;                                      // [TPO][n]
   uint64_t* bars = reinterpret_cast<uint64_t*>(hp_s + kBM * n);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + B::count);
@@ -174,11 +177,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(B::full + i), 1);
       mbar_init(bar(B::empty + i), 1 + 4);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < Cf::NBUF; ++i) {
       mbar_init(bar(B::acc_full + i), 1);
       mbar_init(bar(B::acc_empty + i), 4);
-      mbar_init(bar(B::ss_full + i), 128);
-      mbar_init(bar(B::ss_empty + i), 128);
     }
     for (int i = 0; i < RB; ++i) {
       mbar_init(bar(B::red_full + i), kBM);
@@ -240,13 +241,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------ W1: tcgen05.mma issuer
     if (producer) {
       constexpr uint32_t idesc = idesc_bf16_f32(kBM, Cf::NB, false, false);
-      uint32_t it = 0;
+      uint32_t it = 0, g = 0;
       for (int j = 0; j < my_tiles; ++j) {
-        const int ab = j & 1;
-        mbar_wait(bar(B::acc_empty + ab), ((j >> 1) & 1) ^ 1, wc);
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + ab * Cf::ACC_COLS;
-        for (int kb = 0; kb < KB; ++kb, ++it) {
+        for (int kb = 0; kb < KB; ++kb, ++it, ++g) {
+          // one fresh accumulator per K-block
+          const int ab = g % Cf::NBUF;
+          mbar_wait(bar(B::acc_empty + ab), ((g / Cf::NBUF) & 1) ^ 1, wc);
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + ab * Cf::ACC_COLS;
           const int s = it % S;
           mbar_wait(bar(B::full + s), (it / S) & 1, wc);
           tc_fence_after();
@@ -255,11 +257,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t a0 = desc_kmajor_sw128(smem_u32(st));
           const uint64_t b0 = desc_kmajor_sw128(smem_u32(st + Cf::A_BYTES));
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            umma_bf16(d_tmem, a0 + 2 * kk, b0 + 2 * kk, idesc, (kb | kk) != 0);
+          for (int kk = 0; kk < kBK / 16; ++kk) umma_bf16(d_tmem, a0 + 2 * kk, b0 + 2 * kk, idesc, kk != 0);
           umma_commit(bar(B::empty + s));
+          umma_commit(bar(B::acc_full + ab));
         }
-        if (!*abort_flag) umma_commit(bar(B::acc_full + ab));
       }
     }
   } else if (warp == 2) {
@@ -282,83 +283,90 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp < 7) {
-    // ------------------------------------------------ WG_S: sum of squares per token row
-    const int row = threadIdx.x - 3 * 32;     // 0..127
-    uint32_t it = 0;
-    for (int j = 0; j < my_tiles; ++j) {
-      float acc = 0.f;
-      for (int kb = 0; kb < KB; ++kb, ++it) {
-        const int s = it % S;
-        mbar_wait(bar(B::full + s), (it / S) & 1, wc);
-        const uint32_t base = smem_u32(ring + s * Cf::STAGE_BYTES) + row * 128;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          float f[8];
-          bf16x8_to_f32(lds128(base + (((c + row) & 7) << 4)), f);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc = fmaf(f[e], f[e], acc);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B::empty + s));
-      }
-      const int sb = j & 1;
-      mbar_wait(bar(B::ss_empty + sb), ((j >> 1) & 1) ^ 1, wc);
-      ss[sb * kBM + row] = acc;
-      mbar_arrive(bar(B::ss_full + sb));
-    }
-  } else if (warp < 11) {
-    // ------------------------------------------------ WG_A: accumulator -> owner reduction -> gates
-    const int tid = threadIdx.x - 7 * 32;     // 0..127
+    // ------------------------------------------------ WG_SR: sum x^2 + fold accumulators, send to owner
     const int q = warp & 3;                   // TMEM lane quadrant of this warp
-    const int row = 32 * q + lane;            // token row of the tile = TMEM lane
-    const float a_pre = p.alpha[0], a_post = p.alpha[1], a_res = p.alpha[2];
+    const int row = 32 * q + lane;            // token row of the tile = TMEM lane = smem row
+    uint32_t it = 0, g = 0;
     for (int j = 0; j < my_tiles; ++j) {
-      const int tile = (int)cid + j * (int)ncl;
-      const int ab = j & 1;
-      // (1) partial projection of this CTA's K-subset, split terms folded
-      mbar_wait(bar(B::acc_full + ab), (j >> 1) & 1, wc);
-      tc_fence_after();
       float part[N_OUT];
 #pragma unroll
       for (int jj = 0; jj < N_OUT; ++jj) part[jj] = 0.f;
-      const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + ab * Cf::ACC_COLS;
+      float sq = 0.f;
+      for (int kb = 0; kb < KB; ++kb, ++it, ++g) {
+        const int s = it % S;
+        mbar_wait(bar(B::full + s), (it / S) & 1, wc);
+        {
+          const uint32_t base = smem_u32(ring + s * Cf::STAGE_BYTES) + row * 128;
+          float c8[8];
 #pragma unroll
-      for (int c16 = 0; c16 < Cf::NB / 16; ++c16) {
-        float v[16];
-        tmem_ld16(taddr + c16 * 16, v);
-        tmem_wait_ld();
+          for (int c = 0; c < 8; ++c) {
+            float f[8];
+            bf16x8_to_f32(lds128(base + (((c + row) & 7) << 4)), f);
+            const float a = fmaf(f[0], f[0], f[1] * f[1]) + fmaf(f[2], f[2], f[3] * f[3]);
+            const float b = fmaf(f[4], f[4], f[5] * f[5]) + fmaf(f[6], f[6], f[7] * f[7]);
+            c8[c] = a + b;
+          }
+          sq += ((c8[0] + c8[1]) + (c8[2] + c8[3])) + ((c8[4] + c8[5]) + (c8[6] + c8[7]));
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B::empty + s));
+        // fold this K-block's accumulator (NT split terms of each output) into part
+        const int ab = g % Cf::NBUF;
+        mbar_wait(bar(B::acc_full + ab), (g / Cf::NBUF) & 1, wc);
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + ab * Cf::ACC_COLS;
+        // Narrow outputs: sum this block's split terms (smallest first) before
+        // adding to the running partial; wide outputs fold in place (registers).
+        constexpr bool kBlockSum = N_OUT <= 32;
+        float blk[kBlockSum ? N_OUT : 1];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int col = c16 * 16 + e;
-          if (col < Cf::NT * N_OUT) part[col % N_OUT] += v[e];
+        for (int jj = 0; jj < (kBlockSum ? N_OUT : 1); ++jj) blk[jj] = 0.f;
+#pragma unroll
+        for (int c16 = Cf::NB / 16 - 1; c16 >= 0; --c16) {
+          float v[16];
+          tmem_ld16(taddr + c16 * 16, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 15; e >= 0; --e) {
+            const int col = c16 * 16 + e;
+            if (col < Cf::NT * N_OUT) {
+              if constexpr (kBlockSum) blk[col % N_OUT] += v[e];
+              else part[col % N_OUT] += v[e];
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B::acc_empty + ab));
+        if constexpr (kBlockSum) {
+#pragma unroll
+          for (int jj = 0; jj < N_OUT; ++jj) part[jj] += blk[jj];
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B::acc_empty + ab));
-      // (2) partial sum of squares from WG_S
-      const int sb = j & 1;
-      mbar_wait(bar(B::ss_full + sb), (j >> 1) & 1, wc);
-      const float sq = ss[sb * kBM + row];
-      mbar_arrive(bar(B::ss_empty + sb));
-      // (3) send (part, sq) of token `row` to its owner CTA
+      // send (part, sq) of token `row` to its owner CTA
       const int rb = j % RB;
       const uint32_t rph = (j / RB) & 1;
       mbar_wait<true>(bar(B::red_free + rb), rph ^ 1, wc);
       const int owner = row / TPO;
-      {
-        const uint32_t local = smem_u32(red + (rb * kBM + (int)rank * TPO + (row % TPO)) * RS);
-        const uint32_t dst = mapa_shared(local, owner);
+      const uint32_t local = smem_u32(red + (rb * kBM + (int)rank * TPO + (row % TPO)) * RS);
+      const uint32_t dst = mapa_shared(local, owner);
 #pragma unroll
-        for (int jj = 0; jj + 4 <= N_OUT + 1; jj += 4) {
-          const float v3 = (jj + 3 < N_OUT) ? part[jj + 3] : sq;
-          st_cluster_v4_f32(dst + 4 * jj, part[jj], part[jj + 1], part[jj + 2], v3);
-        }
-#pragma unroll
-        for (int jj = (N_OUT + 1) / 4 * 4; jj < N_OUT + 1; ++jj)
-          st_cluster_f32(dst + 4 * jj, jj < N_OUT ? part[jj] : sq);
-        mbar_arrive_remote(bar(B::red_full + rb), owner);
+      for (int jj = 0; jj + 4 <= N_OUT + 1; jj += 4) {
+        const float v3 = (jj + 3 < N_OUT) ? part[jj + 3] : sq;
+        st_cluster_v4_f32(dst + 4 * jj, part[jj], part[jj + 1], part[jj + 2], v3);
       }
+#pragma unroll
+      for (int jj = (N_OUT + 1) / 4 * 4; jj < N_OUT + 1; ++jj) st_cluster_f32(dst + 4 * jj, jj < N_OUT ? part[jj] : sq);
+      mbar_arrive_remote(bar(B::red_full + rb), owner);
+    }
+  } else if (warp < 11) {
+    // ------------------------------------------------ WG_A: owner reduction -> gates -> h_pre broadcast
+    const int tid = threadIdx.x - 7 * 32;     // 0..127
+    const float a_pre = p.alpha[0], a_post = p.alpha[1], a_res = p.alpha[2];
+    for (int j = 0; j < my_tiles; ++j) {
+      const int tile = (int)cid + j * (int)ncl;
+      const int rb = j % RB;
+      const uint32_t rph = (j / RB) & 1;
       // (4) owner: fixed-order sum over the C partials of my TPO tokens
       mbar_wait<true>(bar(B::red_full + rb), rph, wc);
       for (int idx = tid; idx < TPO * (N_OUT + 1); idx += 128) {

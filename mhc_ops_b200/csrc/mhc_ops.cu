@@ -20,6 +20,7 @@
 #include "generic.cuh"
 #include "sm100.cuh"
 #include "fwd_sm100.cuh"
+#include "bwd_sm100.cuh"
 
 namespace mhc {
 
@@ -181,8 +182,10 @@ struct ClusterPlan {
 
 // Largest number of co-resident CTAs over the cluster sizes C (<= 16) that
 // divide D/64; ties go to the larger C (shorter L2 re-read distance).
-template <typename Kernel>
-int plan_clusters(Kernel kernel, int smem, int threads, int D, ClusterPlan* out) {
+inline bool any_cluster(int) { return true; }
+
+template <typename Kernel, typename Allowed = bool (*)(int)>
+int plan_clusters(Kernel kernel, int smem, int threads, int D, ClusterPlan* out, Allowed allowed = any_cluster) {
   static std::mutex mu;
   static std::map<std::tuple<int, const void*, int>, ClusterPlan> cache;
   int dev = 0;
@@ -200,7 +203,7 @@ int plan_clusters(Kernel kernel, int smem, int threads, int D, ClusterPlan* out)
   MHC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   ClusterPlan best;
   for (int C : {16, 8, 4, 2, 1}) {
-    if (D % (64 * C) != 0) continue;
+    if (D % (64 * C) != 0 || !allowed(C)) continue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(C);
     cfg.blockDim = dim3(threads);
@@ -321,8 +324,144 @@ int fwd_workspace(int64_t T, int n, int D, size_t* bytes) {
   return MHC_OK;
 }
 
+// ----------------------------------------------------------------- tensor-core backward
+// Shapes it takes: n == 4, D a multiple of 256 with a cluster size C in
+// {4, 8, 16} whose slice n*D/C fits the TMEM / smem budget (<= 1792),
+// 16-byte aligned x / dh_in / dx / phi, T < 2^31.
+constexpr int kBwdN = 4;
+
+struct BwdTcLayout {
+  size_t phit, gpart, abpart, total;
+  ClusterPlan plan;
+  int dv_bufs;
+};
+
+bool bwd_c_allowed(int D, int C) {
+  using Cf = bwdtc::Cfg<kBwdN>;
+  if (C < 4) return false;
+  const int kc = kBwdN * D / C;
+  if (kc > Cf::MAX_KC) return false;
+  return 64 + (kc / 128) * Cf::NG <= 512;
+}
+
+int bwd_tc_layout(int64_t T, int D, BwdTcLayout* L) {
+  using Cf = bwdtc::Cfg<kBwdN>;
+  (void)T;
+  int st = plan_clusters(bwdtc::bwd_kernel<kBwdN>, Cf::SMEM, bwdtc::kThreads, D, &L->plan,
+                         [D](int C) { return bwd_c_allowed(D, C); });
+  if (st) return st;
+  const int kc = kBwdN * D / L->plan.C;
+  L->dv_bufs = (128 + (kc / 128) * Cf::NG <= 512) ? 2 : 1;
+  const int64_t nD = (int64_t)kBwdN * D;
+  size_t off = kWsHeaderBytes;
+  L->phit = off;
+  off = align_up(off + (size_t)(nD / 64) * Cf::PH_BYTES, kWsAlign);
+  L->gpart = off;
+  off = align_up(off + sizeof(float) * (size_t)L->plan.max_clusters * Cf::N_OUT * nD, kWsAlign);
+  L->abpart = off;
+  off = align_up(off + sizeof(float) * (size_t)L->plan.max_clusters * L->plan.C * (3 + Cf::N_OUT), kWsAlign);
+  L->total = off;
+  return MHC_OK;
+}
+
+bool bwd_tc_shape(int64_t T, int n, int D) {
+  if (n != kBwdN || D % 256 != 0 || T >= ((int64_t)1 << 31)) return false;
+  for (int C : {16, 8, 4})
+    if (D % (64 * C) == 0 && bwd_c_allowed(D, C)) return true;
+  return false;
+}
+
+bool bwd_tc_eligible(const mhc_bwd_args* a) {
+  return bwd_tc_shape(a->tokens, a->n, a->D) && aligned(a->x, 16) && aligned(a->dh_in, 16) &&
+         aligned(a->dx, 16) && aligned(a->phi, 16);
+}
+
+int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s) {
+  using Cf = bwdtc::Cfg<kBwdN>;
+  constexpr int n = kBwdN;
+  const int64_t T = a->tokens;
+  const int D = a->D;
+  const int nD = n * D;
+  BwdTcLayout L;
+  int st = bwd_tc_layout(T, D, &L);
+  if (st) return st;
+  char* ws = static_cast<char*>(a->workspace);
+  const int num_tiles = (int)((T + bwdtc::kBM - 1) / bwdtc::kBM);
+  const int nclusters = std::max(1, std::min(L.plan.max_clusters, num_tiles));
+
+  bwdtc::phit_kernel<n><<<4 * 148, 256, 0, s>>>(a->phi, reinterpret_cast<uint16_t*>(ws + L.phit), nD);
+  if ((st = after_launch())) return st;
+
+  CUtensorMap m_x2d, m_dh;
+  {
+    const uint64_t dims[2] = {(uint64_t)nD, (uint64_t)T};
+    const uint64_t strides[1] = {(uint64_t)nD * 2};
+    const uint32_t box[2] = {bwdtc::kBK, bwdtc::kBM};
+    if ((st = encode_bf16_map(&m_x2d, a->x, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)D, (uint64_t)T};
+    const uint64_t strides[1] = {(uint64_t)D * 2};
+    const uint32_t box[2] = {bwdtc::kBK, bwdtc::kBM};
+    if ((st = encode_bf16_map(&m_dh, a->dh_in, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  bwdtc::Params p;
+  p.x = a->x;
+  p.dh_in = a->dh_in;
+  p.alpha = a->alpha;
+  p.inv_rms = a->inv_rms;
+  p.h_mix = a->h_mix;
+  p.h_pre = a->h_pre;
+  p.h_post = a->h_post;
+  p.dh_post = a->dh_post;
+  p.dh_res = a->dh_res;
+  p.gamma = a->gamma;
+  p.phit = reinterpret_cast<const uint8_t*>(ws + L.phit);
+  p.dx = a->dx;
+  p.gpart = reinterpret_cast<float*>(ws + L.gpart);
+  p.abpart = reinterpret_cast<float*>(ws + L.abpart);
+  p.status = reinterpret_cast<int*>(ws);
+  p.T = T;
+  p.D = D;
+  p.C = L.plan.C;
+  p.Dc = D / L.plan.C;
+  p.num_tiles = num_tiles;
+  p.FT = 4;
+  p.dv_bufs = L.dv_bufs;
+  p.hc_eps = a->hc_eps;
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nclusters * L.plan.C);
+  cfg.blockDim = dim3(bwdtc::kThreads);
+  cfg.dynamicSmemBytes = Cf::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = L.plan.C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  MHC_CUDA_TRY(cudaLaunchKernelEx(&cfg, bwdtc::bwd_kernel<n>, m_x2d, m_dh, p));
+  if ((st = after_launch())) return st;
+
+  generic::finalize_param_kernel<<<(nD + generic::kThreads - 1) / generic::kThreads, generic::kThreads, 0, s>>>(
+      p.gpart, nclusters, Cf::N_OUT, a->phi, a->gamma, a->dphi, a->dgamma, nD);
+  if ((st = after_launch())) return st;
+  generic::reduce_columns_kernel<<<3 + Cf::N_OUT, generic::kThreads, 0, s>>>(
+      p.abpart, (int64_t)nclusters * L.plan.C, 3 + Cf::N_OUT, a->dalpha, a->dbias);
+  return after_launch();
+}
+
 int bwd_workspace(int64_t T, int n, int D, int sms, size_t* bytes) {
-  *bytes = bwd_generic_layout(T, n, D, sms).total;
+  size_t b = bwd_generic_layout(T, n, D, sms).total;
+  if (bwd_tc_shape(T, n, D)) {
+    BwdTcLayout L;
+    int st = bwd_tc_layout(T, D, &L);
+    if (st) return st;
+    b = std::max(b, L.total);
+  }
+  *bytes = b;
   return MHC_OK;
 }
 
@@ -404,7 +543,7 @@ int mhc_bwd(const mhc_bwd_args* a, void* stream) {
   int sms = 0;
   if ((st = current_sm_count(&sms))) return st;
   size_t need = 0;
-  bwd_workspace(a->tokens, a->n, a->D, sms, &need);
+  if ((st = bwd_workspace(a->tokens, a->n, a->D, sms, &need))) return st;
   if (a->workspace_bytes < need) return MHC_ERR_WORKSPACE_TOO_SMALL;
   if (!aligned(a->workspace, kWsAlign)) return MHC_ERR_MISALIGNED;
   if (!a->dphi || !a->dalpha || !a->dbias || !a->dgamma || !a->alpha || !a->phi) return MHC_ERR_NULL_POINTER;
@@ -425,6 +564,7 @@ int mhc_bwd(const mhc_bwd_args* a, void* stream) {
       !aligned(a->dh_post, 4) || !aligned(a->dh_res, 4) || !aligned(a->gamma, 4) || !aligned(a->dphi, 4) ||
       !aligned(a->dalpha, 4) || !aligned(a->dbias, 4) || !aligned(a->dgamma, 4))
     return MHC_ERR_MISALIGNED;
+  if (bwd_tc_eligible(a)) return bwd_tc_run(a, s);
   return dispatch_n<BwdGeneric>(a->n, a, s, sms);
 }
 
