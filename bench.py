@@ -336,6 +336,7 @@ def run_ours(args):
     if rank != 0:
         return 0
 
+    plans = {"fwd": _lib.query_plan(0, T, n, D), "bwd": _lib.query_plan(1, T, n, D)}
     ms_per_step = total_ms / args.steps
     value = world * T / (ms_per_step / 1e3)
     peak, peak_kind = measured_hbm_peak()

@@ -145,6 +145,14 @@ MHC_API int mhc_bwd(const mhc_bwd_args* args, void* stream);
  * has no bounded device waits. */
 MHC_API int mhc_read_device_status(void* workspace, void* stream, int* device_status);
 
+/* Launch plan the library uses for this shape on the current device:
+ * *path = 0 generic kernels, 1 tensor-core cluster kernels; for path 1,
+ * *cluster_size CTAs per cluster and *clusters co-resident clusters (the
+ * persistent grid).  which = 0 forward, 1 backward.  No counterpart in the
+ * reference (its Triton grids are fixed per call). */
+MHC_API int mhc_query_plan(int which, int64_t tokens, int32_t n, int32_t D, int* path, int* cluster_size,
+                           int* clusters);
+
 /* Number of kernels this library has launched in this process (all devices,
  * all threads).  No counterpart in the reference; used to report launches. */
 MHC_API uint64_t mhc_launch_count(void);

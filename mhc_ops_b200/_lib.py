@@ -57,6 +57,9 @@ SIGNATURES = {
                                               ctypes.POINTER(ctypes.c_size_t)]),
     "mhc_bwd": (ctypes.c_int, [ctypes.POINTER(BwdArgs), _c_void_p]),
     "mhc_read_device_status": (ctypes.c_int, [_c_void_p, _c_void_p, ctypes.POINTER(ctypes.c_int)]),
+    "mhc_query_plan": (ctypes.c_int, [ctypes.c_int, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                      ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
+                                      ctypes.POINTER(ctypes.c_int)]),
     "mhc_launch_count": (ctypes.c_uint64, []),
     "mhc_abi_version": (ctypes.c_int, []),
 }
@@ -137,6 +140,15 @@ def bwd_workspace_size(tokens: int, n: int, D: int) -> int:
     out = ctypes.c_size_t(0)
     check(load().mhc_bwd_workspace_size(tokens, n, D, ctypes.byref(out)), "mhc_bwd_workspace_size")
     return int(out.value)
+
+
+def query_plan(which: int, tokens: int, n: int, D: int) -> dict:
+    """Launch plan for forward (which=0) or backward (1) of this shape on the current device."""
+    path, cs, ncl = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+    check(load().mhc_query_plan(which, tokens, n, D, ctypes.byref(path), ctypes.byref(cs), ctypes.byref(ncl)),
+          "mhc_query_plan")
+    return {"path": "tensor-core cluster" if path.value else "generic", "cluster_size": cs.value,
+            "clusters": ncl.value}
 
 
 def launch_count() -> int:

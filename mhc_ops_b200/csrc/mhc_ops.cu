@@ -568,6 +568,37 @@ int mhc_bwd(const mhc_bwd_args* a, void* stream) {
   return dispatch_n<BwdGeneric>(a->n, a, s, sms);
 }
 
+int mhc_query_plan(int which, int64_t tokens, int32_t n, int32_t D, int* path, int* cluster_size, int* clusters) {
+  if (!path || !cluster_size || !clusters) return MHC_ERR_NULL_POINTER;
+  int st = check_shape(tokens, n, D);
+  if (st) return st;
+  int sms = 0;
+  if ((st = current_sm_count(&sms))) return st;
+  *path = 0;
+  *cluster_size = 0;
+  *clusters = 0;
+  ClusterPlan plan;
+  const int64_t tiles = (tokens + 127) / 128;
+  if (which == 0 && (n == 4 || n == 8) && D % 64 == 0 && tokens < ((int64_t)1 << 31)) {
+    st = n == 4 ? plan_clusters(fwdtc::fwd_kernel<4>, fwdtc::Cfg<4>::SMEM, fwdtc::kThreads, D, &plan)
+                : plan_clusters(fwdtc::fwd_kernel<8>, fwdtc::Cfg<8>::SMEM, fwdtc::kThreads, D, &plan);
+    if (st) return st;
+    *path = 1;
+  } else if (which == 1 && bwd_tc_shape(tokens, n, D)) {
+    BwdTcLayout L;
+    if ((st = bwd_tc_layout(tokens, D, &L))) return st;
+    plan = L.plan;
+    *path = 1;
+  } else if (which != 0 && which != 1) {
+    return MHC_ERR_BAD_SHAPE;
+  }
+  if (*path == 1) {
+    *cluster_size = plan.C;
+    *clusters = (int)std::max<int64_t>(1, std::min<int64_t>(plan.max_clusters, tiles));
+  }
+  return MHC_OK;
+}
+
 int mhc_read_device_status(void* workspace, void* stream, int* device_status) {
   if (!workspace || !device_status) return MHC_ERR_NULL_POINTER;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
