@@ -222,7 +222,7 @@ def run_ours(args):
     from mhc_ops_b200 import _lib, mhc_backward_manual, mhc_forward_pre
     from mhc_ops_b200.backward import param_grad_numel
 
-    w = WORKLOAD
+    w = dict(WORKLOAD, B=args.batch)
     B, S, n, D = w["B"], w["S"], w["n"], w["D"]
     N, nD, T = n * n + 2 * n, n * D, w["B"] * w["S"]
 
@@ -350,9 +350,10 @@ def run_ours(args):
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "mHC pre-op fwd(outflag)+bwd, B=4,S=4096,n=4,D=4096 per GPU (LLM-scale config)",
+        "config": {"workload": f"mHC pre-op fwd(outflag)+bwd, B={B},S=4096,n=4,D=4096 per GPU (LLM-scale config)",
                    **w, "global_tokens": world * T, "parallelism": f"dp{world} (token shards, NCCL all-reduce of "
-                   "param grads)", "l2": "inputs larger than L2 (x is 512 MiB per GPU); no flush"},
+                   "param grads)", "l2": "inputs larger than L2 (x is 512 MiB per GPU); no flush",
+                   "launch_plan": plans},
         "hbm_gbs_step": step_alg / (ms_per_step / 1e3) / 1e9 / 1.0,
         "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": peak_kind, "traffic": traffic,
@@ -389,6 +390,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--ref-tokens", type=int, default=1024)
+    ap.add_argument("--batch", type=int, default=WORKLOAD["B"],
+                    help="B per GPU (default 4, the metric's configuration; smaller only for profiling)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)   # at least 3 untimed warm-up steps, whatever was asked
     if args.impl == "reference":

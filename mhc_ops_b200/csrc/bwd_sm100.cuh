@@ -16,15 +16,16 @@
 //     partials in rank order, computes dh_mix, c, the dalpha/dbias terms and
 //     broadcasts one record per token (dh_mix, c, h_pre) to every CTA.
 //   * W0 re-reads the slice through L2 with TMA (x blocks [128 tok x 64 k],
-//     dh_in blocks, 128-B swizzle, evict-first) and streams pre-laid-out
-//     split-phi images (1-D bulk copies);
-//   * WG_E (4 warps) turns the records into the UMMA operands: DHM [128 tok x
-//     K'] (6 bf16 split products of dh_mix x phi, smallest first, so the
-//     tensor core's fp32 sum is exact to ~2^-23) and DHMT [N x 384] (3 split
-//     terms of dh_mix, tokens contiguous);
-//   * W1 issues tcgen05.mma: dvecX = DHM . PHIT^T per 64-k block (M=128,
-//     N=64, K'=6N) and G += x^T . DHMT^T per 128-k pair (M=128 k, N=N pad,
-//     K=3x128 tokens; x read MN-major straight from the TMA stages);
+//     dh_in blocks, 128-B swizzle, evict-first); W2 streams pre-laid-out
+//     split-phi images (1-D bulk copies, 3 bf16 terms of phi per k);
+//   * WG_E (4 warps) turns the records into the UMMA operand DHM [128 tok x
+//     3 segments]: the 3 bf16 terms (hi, mid, lo) of dh_mix, each segment
+//     padded to a multiple of 16;
+//   * W1 issues tcgen05.mma: dvecX = sum over 6 (dh term, phi term) products
+//     (smallest first: m.M, l.H, h.L, m.H, h.M, h.H; exact to ~2^-23 in the
+//     fp32 sum) per 64-k block (M=128 tok, N=64, K=segment) and
+//     G += x^T . DHM (M=128 k, N=segment, K=3x128 tokens; x read MN-major
+//     straight from two adjacent TMA stages, DHM read MN-major);
 //   * WG_E reads dvecX (TMEM lane = token) and writes dx; every FT tiles it
 //     flushes G from TMEM into the per-cluster partial (single writer per
 //     address, fixed order).
@@ -33,6 +34,11 @@
 #include "common.cuh"
 #include "sm100.cuh"
 
+// Optional per-tile timestamp hook (a profiling build defines it); no-op here.
+#ifndef MHC_BWD_TRACE
+#define MHC_BWD_TRACE(slot) ((void)0)
+#endif
+
 namespace mhc {
 namespace bwdtc {
 
@@ -40,7 +46,7 @@ using namespace sm100;
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 10 * 32;   // W0, W1, WG_P(4), WG_E(4)
+constexpr int kThreads = 11 * 32;   // W0, W1, W2, WG_P(4), WG_E(4)
 constexpr int kSmemLimit = 232448;
 
 constexpr int round_up(int v, int a) { return (v + a - 1) / a * a; }
@@ -48,30 +54,29 @@ constexpr int round_up(int v, int a) { return (v + a - 1) / a * a; }
 template <int n>
 struct Cfg {
   static constexpr int N_OUT = n * n + 2 * n;
-  static constexpr int NSEG = 6;                         // split products of dvecX
-  static constexpr int KP = round_up(NSEG * N_OUT, 16);  // dvecX reduction length K'
-  static constexpr int KPC = KP / 8;                     // 16-byte core columns along K'
-  static constexpr int RG_BYTES = KPC * 128;             // one 8-row group of a K'-major image
+  static constexpr int SEGW = round_up(N_OUT, 16);       // one split-term segment (N of G)
+  static constexpr int KA = 3 * SEGW;                    // DHM / phi-image row: 3 term segments
+  static constexpr int RG_BYTES = (KA / 8) * 128;        // one 8-row group of a K-major interleaved image
   static constexpr int PH_BYTES = 8 * RG_BYTES;          // split-phi image of one 64-k block
   static constexpr int DHM_BYTES = 16 * RG_BYTES;        // 128 token rows
-  static constexpr int NG = round_up(N_OUT, 16);         // G accumulator columns / DHMT rows
-  static constexpr int GK = 3 * kBM;                     // G reduction length per tile
-  static constexpr int DHMT_SBO = (GK / 8) * 128;
-  static constexpr int DHMT_BYTES = (NG / 8) * DHMT_SBO;
+  static constexpr int NG = SEGW;                        // G accumulator columns
   static constexpr int X_BYTES = kBM * 128;
   static constexpr int XS = 4;                           // x ring (2 adjacent pairs)
   static constexpr int DS = 2;
-  static constexpr int PS = 2;
+  static constexpr int PS = 3;
   static constexpr int RECW = round_up(N_OUT + 1 + n, 4);
   static constexpr int RB = 2;                           // dh_pre exchange buffers
   static constexpr int MAX_TPO = 32;                     // C >= 4
   static constexpr int MAX_KC = 1792;                    // d-slice * n per CTA
-
   static constexpr int CW = 3 + N_OUT;                   // dalpha / dbias columns
+  // owner inputs per token: h_mix[N_OUT], h_pre[n], h_post[n], dh_post[n], dh_res[n*n], inv_rms
+  static constexpr int OWN_IN = N_OUT + 3 * n + n * n + 1;
+  static constexpr int OWNW = round_up(OWN_IN, 4);
+
   static constexpr int smem_bytes() {
-    return 1024 + XS * X_BYTES + DS * X_BYTES + PS * PH_BYTES + DHM_BYTES + DHMT_BYTES +
-           RB * kBM * n * 4 /*pdh*/ + kBM * RECW * 4 /*bc*/ + MAX_TPO * (n + RECW + CW) * 4 /*owner scratch*/ +
-           512;
+    return 1024 + XS * X_BYTES + DS * X_BYTES + PS * PH_BYTES + DHM_BYTES + X_BYTES /*dx staging*/ +
+           MAX_KC * 4 /*gamma slice*/ + RB * kBM * n * 4 /*pdh*/ + kBM * RECW * 4 /*bc*/ +
+           MAX_TPO * (n + RECW + CW + OWNW) * 4 /*owner scratch*/ + 512;
   }
   static constexpr int SMEM = smem_bytes();
   static_assert(SMEM <= kSmemLimit, "backward tile does not fit in shared memory");
@@ -158,6 +163,22 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       : "memory");
 }
 
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// smem -> global tiled TMA store (out-of-range rows of the box are not written).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void red_add_f32(float* addr, float v) {
   asm volatile("red.global.add.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
 }
@@ -179,14 +200,10 @@ __device__ __forceinline__ uint32_t interleave_off(int row, int kk, int sbo) {
   return (uint32_t)((row >> 3) * sbo + (kk >> 3) * 128 + (row & 7) * 16 + (kk & 7) * 2);
 }
 
-// Split-product order of dvecX (smallest first): A term x B term per segment.
-__device__ __forceinline__ int seg_a_term(int seg) {
-  // segments: m.M, l.H, h.L, m.H, h.M, h.H
-  return seg == 0 ? 1 : seg == 1 ? 2 : seg == 3 ? 1 : 0;
-}
-__host__ __device__ __forceinline__ int seg_b_term(int seg) {
-  return seg == 0 ? 1 : seg == 2 ? 2 : seg == 4 ? 1 : 0;
-}
+// The six (dh_mix term, phi term) products of dvecX, smallest first:
+// m.M, l.H, h.L, m.H, h.M, h.H (term 0 = hi, 1 = mid, 2 = lo).
+__device__ __forceinline__ int prod_a_term(int pr) { return pr == 0 ? 1 : pr == 1 ? 2 : pr == 3 ? 1 : 0; }
+__device__ __forceinline__ int prod_b_term(int pr) { return pr == 0 ? 1 : pr == 2 ? 2 : pr == 4 ? 1 : 0; }
 
 // t-th bf16 term of v (0 = hi, 1 = mid, 2 = lo): each rounds what is left.
 __device__ __forceinline__ uint16_t split_term(float v, int term) {
@@ -201,7 +218,7 @@ __device__ __forceinline__ uint16_t split_term(float v, int term) {
 template <int n>
 __global__ void __launch_bounds__(kThreads, 1)
     bwd_kernel(const __grid_constant__ CUtensorMap map_x2d, const __grid_constant__ CUtensorMap map_dh,
-               const Params p) {
+               const __grid_constant__ CUtensorMap map_dx, const Params p) {
   using Cf = Cfg<n>;
   using B = Bars<n>;
   constexpr int N_OUT = Cf::N_OUT;
@@ -213,14 +230,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* xr = smem;                                  // XS x blocks (pairs adjacent)
   uint8_t* dhr = xr + Cf::XS * Cf::X_BYTES;            // DS dh_in blocks
   uint8_t* phr = dhr + Cf::DS * Cf::X_BYTES;           // PS split-phi images
-  uint8_t* dhm = phr + Cf::PS * Cf::PH_BYTES;          // A operand of dvecX
-  uint8_t* dhmt = dhm + Cf::DHM_BYTES;                 // B operand of G
-  float* pdh = reinterpret_cast<float*>(dhmt + Cf::DHMT_BYTES);    // [RB][128][n]
+  uint8_t* dhm = phr + Cf::PS * Cf::PH_BYTES;          // dh_mix terms: A of dvecX, B of G
+  uint8_t* dxs = dhm + Cf::DHM_BYTES;                  // dx staging [128 tok x 64] (128-B swizzle)
+  float* gam_s = reinterpret_cast<float*>(dxs + Cf::X_BYTES);       // [n][Dc] gamma slice
+  float* pdh = gam_s + Cf::MAX_KC;                     // [RB][128][n]
   float* bc = pdh + RB * kBM * n;                      // [128][RECW]
   float* dhp_s = bc + kBM * RECW;                      // [TPO][n]
   float* rec_s = dhp_s + Cf::MAX_TPO * n;              // [TPO][RECW]
   float* contrib = rec_s + Cf::MAX_TPO * RECW;         // [TPO][CW]: dalpha (3), dbias (N_OUT) terms
-  uint64_t* bars = reinterpret_cast<uint64_t*>(contrib + Cf::MAX_TPO * Cf::CW);
+  float* own_in = contrib + Cf::MAX_TPO * Cf::CW;      // [TPO][OWNW] owner inputs of this tile
+  uint64_t* bars = reinterpret_cast<uint64_t*>(own_in + Cf::MAX_TPO * Cf::OWNW);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + B::count);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -240,9 +259,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int DVB = p.dv_bufs;
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
 
-  // zero the padding rows of DHMT (j >= N_OUT) once
-  for (int idx = threadIdx.x; idx < Cf::DHMT_BYTES / 16; idx += kThreads) {
-    reinterpret_cast<uint4*>(dhmt)[idx] = make_uint4(0, 0, 0, 0);
+  // gamma slice of this CTA: gam_s[i*Dc + dd] = gamma[i*D + rank*Dc + dd]
+  for (int idx = threadIdx.x; idx < KC; idx += kThreads) {
+    const int i = idx / Dc, dd = idx - i * Dc;
+    gam_s[idx] = p.gamma ? p.gamma[(int64_t)i * D + (int64_t)rank * Dc + dd] : 1.0f;
   }
   if (threadIdx.x == 0) {
     for (int i = 0; i < Cf::XS; ++i) {
@@ -281,8 +301,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tensormap(&map_x2d);
     prefetch_tensormap(&map_dh);
+    prefetch_tensormap(&map_dx);
   }
-  fence_proxy_async_smem();   // DHMT zeros are read by the tensor core later
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -298,7 +318,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------ W0: TMA producer (phase-2 re-read)
     if (producer) {
       const uint64_t pol_drop = l2_policy_evict_first();
-      const uint64_t pol_keep = l2_policy_evict_last();
       uint32_t q = 0, dq = 0;
       for (int j = 0; j < my_tiles; ++j) {
         const int tile = (int)cid + j * (int)ncl;
@@ -314,16 +333,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int s = q % Cf::XS;
             const int k0 = i * D + (int)rank * Dc + dch * kBK;
             mbar_wait(bar(B::x_empty + s), ((q / Cf::XS) & 1) ^ 1, wc);
+            if (dch == 0 && i == 0) MHC_BWD_TRACE(11);
+            if (dch == DCH - 1 && i == n - 1) MHC_BWD_TRACE(12);
             if (!*abort_flag) {
               mbar_arrive_expect_tx(bar(B::x_full + s), Cf::X_BYTES);
               tma_load_2d(smem_u32(xr + s * Cf::X_BYTES), &map_x2d, bar(B::x_full + s), k0, tile * kBM, pol_drop);
-            }
-            const int ps = q % Cf::PS;
-            mbar_wait(bar(B::ph_empty + ps), ((q / Cf::PS) & 1) ^ 1, wc);
-            if (!*abort_flag) {
-              mbar_arrive_expect_tx(bar(B::ph_full + ps), Cf::PH_BYTES);
-              bulk_load(smem_u32(phr + ps * Cf::PH_BYTES), p.phit + (size_t)(k0 / kBK) * Cf::PH_BYTES, Cf::PH_BYTES,
-                        bar(B::ph_full + ps), pol_keep);
             }
           }
         }
@@ -333,10 +347,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------ W1: tcgen05.mma issuer
     if (producer) {
       constexpr uint32_t idesc_dv = idesc_bf16_f32(kBM, kBK, false, false);
-      constexpr uint32_t idesc_g = idesc_bf16_f32(kBM, Cf::NG, true, false);
+      constexpr uint32_t idesc_g = idesc_bf16_f32(kBM, Cf::NG, true, true);
       uint32_t q = 0, flushes = 0;
       for (int j = 0; j < my_tiles; ++j) {
         mbar_wait(bar(B::dhm_full), j & 1, wc);
+        MHC_BWD_TRACE(9);
         tc_fence_after();
         const bool g_restart = (j % p.FT) == 0;
         if (g_restart && j > 0) {
@@ -355,9 +370,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!*abort_flag) {
               const uint32_t dhm_a = smem_u32(dhm), ph_a = smem_u32(phr + ps * Cf::PH_BYTES);
 #pragma unroll
-              for (int ks = 0; ks < Cf::KP / 16; ++ks)
-                umma_bf16(tmem_dv + dvb * 64, desc_kmajor_interleave(dhm_a + ks * 256, 128, Cf::RG_BYTES),
-                          desc_kmajor_interleave(ph_a + ks * 256, 128, Cf::RG_BYTES), idesc_dv, ks != 0);
+              for (int pr = 0; pr < 6; ++pr) {
+#pragma unroll
+                for (int ks = 0; ks < Cf::SEGW / 16; ++ks) {
+                  const uint32_t ca = (prod_a_term(pr) * Cf::SEGW + ks * 16) * 16;
+                  const uint32_t cb = (prod_b_term(pr) * Cf::SEGW + ks * 16) * 16;
+                  umma_bf16(tmem_dv + dvb * 64, desc_kmajor_interleave(dhm_a + ca, 128, Cf::RG_BYTES),
+                            desc_kmajor_interleave(ph_a + cb, 128, Cf::RG_BYTES), idesc_dv, pr != 0 || ks != 0);
+                }
+              }
               umma_commit(bar(B::ph_empty + ps));
               umma_commit(bar(B::dv_full + dvb));
             }
@@ -369,14 +390,16 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (!*abort_flag) {
                 const int blk = dch * (n / 2) + i / 2;
                 const uint32_t xa = smem_u32(xr + (s - 1) * Cf::X_BYTES);
-                const uint32_t ga = smem_u32(dhmt);
+                const uint32_t ga = smem_u32(dhm);
 #pragma unroll 1
-                for (int e = 0; e < 3; ++e) {
+                for (int e = 2; e >= 0; --e) {            // lo, mid, hi terms of dh_mix
 #pragma unroll
                   for (int ks = 0; ks < kBM / 16; ++ks) {
                     const uint64_t ad = desc_mnmajor_sw128(xa + ks * 2048, Cf::X_BYTES, 1024);
-                    const uint64_t bd = desc_kmajor_interleave(ga + (e * kBM + ks * 16) * 16, 128, Cf::DHMT_SBO);
-                    umma_bf16(tmem_g + blk * Cf::NG, ad, bd, idesc_g, !(g_restart && e == 0 && ks == 0));
+                    // DHM read MN-major: N = the SEGW columns of term e, K = tokens
+                    const uint64_t bd =
+                        desc_kmajor_interleave(ga + e * Cf::SEGW * 16 + ks * 2 * Cf::RG_BYTES, Cf::RG_BYTES, 128);
+                    umma_bf16(tmem_g + blk * Cf::NG, ad, bd, idesc_g, !(g_restart && e == 2 && ks == 0));
                   }
                 }
                 umma_commit(bar(B::x_empty + s - 1));
@@ -385,6 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+        MHC_BWD_TRACE(10);
         if (!*abort_flag) umma_commit(bar(B::dhm_free));
         if ((j + 1) % p.FT == 0 || j == my_tiles - 1) {
           if (!*abort_flag) umma_commit(bar(B::g_full));
@@ -392,16 +416,53 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp < 6) {
+  } else if (warp == 2) {
+    // ------------------------------------------------ W2: split-phi image producer
+    if (producer) {
+      const uint64_t pol_keep = l2_policy_evict_last();
+      uint32_t q = 0;
+      for (int j = 0; j < my_tiles; ++j) {
+        for (int dch = 0; dch < DCH; ++dch) {
+          for (int i = 0; i < n; ++i, ++q) {
+            const int ps = q % Cf::PS;
+            const int k0 = i * D + (int)rank * Dc + dch * kBK;
+            mbar_wait(bar(B::ph_empty + ps), ((q / Cf::PS) & 1) ^ 1, wc);
+            if (*abort_flag) continue;
+            mbar_arrive_expect_tx(bar(B::ph_full + ps), Cf::PH_BYTES);
+            bulk_load(smem_u32(phr + ps * Cf::PH_BYTES), p.phit + (size_t)(k0 / kBK) * Cf::PH_BYTES, Cf::PH_BYTES,
+                      bar(B::ph_full + ps), pol_keep);
+          }
+        }
+      }
+    }
+  } else if (warp < 7) {
     // ------------------------------------------------ WG_P: phase 1 (dh_pre partials) + owner + broadcast
-    const int tid = threadIdx.x - 2 * 32;    // 0..127
-    const int wp = warp - 2;                 // 0..3, 32 token rows each
+    const int tid = threadIdx.x - 3 * 32;    // 0..127
+    const int wp = warp - 3;                 // 0..3, 32 token rows each
     const uint64_t pol_keep = l2_policy_evict_last();
     const float a_pre = p.alpha[0], a_post = p.alpha[1], a_res = p.alpha[2];
     const float inv_nd = 1.0f / (float)nD;
     float ab_acc = 0.f;                      // thread c < 3+N_OUT: running dalpha/dbias column
     for (int j = 0; j < my_tiles; ++j) {
       const int tile = (int)cid + j * (int)ncl;
+      if (tid == 0) MHC_BWD_TRACE(0);
+      // (0) small per-token inputs of the tokens this CTA owns, loaded in
+      // parallel now so the owner step reads them from smem.  own_in is free:
+      // the previous tile's owner step finished before its last named barrier.
+      for (int idx = tid; idx < TPO * Cf::OWN_IN; idx += 128) {
+        const int lt = idx / Cf::OWN_IN, f = idx - lt * Cf::OWN_IN;
+        const int64_t t = (int64_t)tile * kBM + (int)rank * TPO + lt;
+        float v = 0.f;
+        if (t < p.T) {
+          if (f < N_OUT) v = __ldg(p.h_mix + t * N_OUT + f);
+          else if (f < N_OUT + n) v = __ldg(p.h_pre + t * n + (f - N_OUT));
+          else if (f < N_OUT + 2 * n) v = __ldg(p.h_post + t * n + (f - N_OUT - n));
+          else if (f < N_OUT + 3 * n) v = __ldg(p.dh_post + t * n + (f - N_OUT - 2 * n));
+          else if (f < N_OUT + 3 * n + n * n) v = __ldg(p.dh_res + t * (n * n) + (f - N_OUT - 3 * n));
+          else v = __ldg(p.inv_rms + t);
+        }
+        own_in[lt * Cf::OWNW + f] = v;
+      }
       // (1) partial dh_pre of this warp's 32 tokens over the CTA's d-slice
       float mine[n];
 #pragma unroll
@@ -456,6 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
       }
       // (2) send my token's partial to its owner
+      if (tid == 0) MHC_BWD_TRACE(1);
       const int pb = j % RB;
       const uint32_t pph = (j / RB) & 1;
       const int row = wp * 32 + lane;
@@ -469,6 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // (3) owner: reduce the C partials of my TPO tokens in rank order
       mbar_wait<true>(bar(B::p_full + pb), pph, wc);
+      if (tid == 0) MHC_BWD_TRACE(2);
       for (int idx = tid; idx < TPO * n; idx += 128) {
         const int lt = idx / n, i = idx - lt * n;
         float s = 0.f;
@@ -482,23 +545,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int lt = tid; lt < TPO; lt += 128) {
         const int64_t t = (int64_t)tile * kBM + (int)rank * TPO + lt;
         const bool valid = t < p.T;
-        const int64_t tv = valid ? t : 0;
-        const float ir = valid ? p.inv_rms[tv] : 0.f;
+        const float* oi = own_in + lt * Cf::OWNW;
+        const float ir = oi[Cf::OWN_IN - 1];
         float dinv = 0.f, dal0 = 0.f, dal1 = 0.f, dal2 = 0.f;
 #pragma unroll
         for (int jj = 0; jj < N_OUT; ++jj) {
-          const float hm = p.h_mix[tv * N_OUT + jj];
+          const float hm = oi[jj];
           float g2, tmp;
           if (jj < n) {
-            const float s = p.h_pre[tv * n + jj] - p.hc_eps;
+            const float s = oi[N_OUT + jj] - p.hc_eps;
             g2 = dhp_s[lt * n + jj] * s * (1.0f - s);
             tmp = a_pre * g2;
           } else if (jj < 2 * n) {
-            const float hq = p.h_post[tv * n + (jj - n)];
-            g2 = p.dh_post[tv * n + (jj - n)] * hq * (1.0f - hq / 2.0f);
+            const float hq = oi[N_OUT + n + (jj - n)];
+            g2 = oi[N_OUT + 2 * n + (jj - n)] * hq * (1.0f - hq / 2.0f);
             tmp = a_post * g2;
           } else {
-            g2 = p.dh_res[tv * (n * n) + (jj - 2 * n)];
+            g2 = oi[N_OUT + 3 * n + (jj - 2 * n)];
             tmp = a_res * g2;
           }
           if (!valid) g2 = tmp = 0.f;
@@ -515,7 +578,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         contrib[lt * Cf::CW + 2] = dal2;
         rec_s[lt * RECW + N_OUT] = valid ? dinv * (ir * ir * ir) * inv_nd : 0.f;   // c (golden.py:89)
 #pragma unroll
-        for (int i = 0; i < n; ++i) rec_s[lt * RECW + N_OUT + 1 + i] = valid ? p.h_pre[tv * n + i] : 0.f;
+        for (int i = 0; i < n; ++i) rec_s[lt * RECW + N_OUT + 1 + i] = valid ? oi[N_OUT + i] : 0.f;
         for (int w = N_OUT + 1 + n; w < RECW; ++w) rec_s[lt * RECW + w] = 0.f;
       }
       named_sync(1, 128);
@@ -535,6 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_remote(bar(B::bc_full), dstc);
       }
       named_sync(1, 128);
+      if (tid == 0) MHC_BWD_TRACE(3);
     }
     if (tid < Cf::CW) p.abpart[((int64_t)cid * C + rank) * Cf::CW + tid] = ab_acc;
   } else {
@@ -544,9 +608,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t q = 0, dq = 0, flushes = 0;
     for (int j = 0; j < my_tiles; ++j) {
       const int tile = (int)cid + j * (int)ncl;
-      const int64_t t = (int64_t)tile * kBM + row;
-      // (a) record -> DHM row / DHMT column of this token
+      // (a) record -> DHM row of this token (the three bf16 terms of dh_mix)
       mbar_wait<true>(bar(B::bc_full), j & 1, wc);
+      if (row == 0) MHC_BWD_TRACE(4);
       mbar_wait(bar(B::dhm_free), (j & 1) ^ 1, wc);
       float dmix[N_OUT];
 #pragma unroll
@@ -566,33 +630,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             v -= bf16_bits_to_f32(tr[e][jj]);
           }
         }
-        // DHM row: K' = seg*N_OUT + jj, A-side term of each segment, zero padding
+        // DHM row: segment e holds term e of dh_mix[0..N_OUT), zero padded to SEGW
 #pragma unroll
-        for (int kc = 0; kc < Cf::KPC; ++kc) {
+        for (int kc = 0; kc < Cf::KA / 8; ++kc) {
           uint32_t w[4];
 #pragma unroll
           for (int h = 0; h < 4; ++h) {
             uint32_t lohi[2];
 #pragma unroll
             for (int b2 = 0; b2 < 2; ++b2) {
-              const int kp = kc * 8 + h * 2 + b2;
-              const int seg = kp / N_OUT, jj = kp - seg * N_OUT;
-              lohi[b2] = kp < Cf::NSEG * N_OUT ? tr[seg_a_term(seg)][jj] : 0;
+              const int ca = kc * 8 + h * 2 + b2;
+              const int e = ca / Cf::SEGW, jj = ca - e * Cf::SEGW;
+              lohi[b2] = jj < N_OUT ? tr[e][jj] : 0;
             }
             w[h] = lohi[0] | (lohi[1] << 16);
           }
           *reinterpret_cast<uint4*>(dhm + interleave_off(row, kc * 8, Cf::RG_BYTES)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
-        // DHMT: row jj, K = e*128 + token; e = 0 lo, 1 mid, 2 hi (smallest first)
-#pragma unroll
-        for (int jj = 0; jj < N_OUT; ++jj)
-#pragma unroll
-          for (int e = 0; e < 3; ++e)
-            *reinterpret_cast<uint16_t*>(dhmt + interleave_off(jj, e * kBM + row, Cf::DHMT_SBO)) = tr[2 - e][jj];
       }
       fence_proxy_async_smem();
       mbar_arrive(bar(B::dhm_full));
       named_sync(2, 128);
+      if (row == 0) MHC_BWD_TRACE(5);
       if (q4 == 0 && lane == 0)
         for (int c = 0; c < p.C; ++c) mbar_arrive_remote(bar(B::bc_free), c);
       // (b) dx of every 64-k block of the slice
@@ -608,29 +667,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_wait(bar(B::dv_full + dvb), dvph, wc);
           tc_fence_after();
           const uint32_t x_row = smem_u32(xr + s * Cf::X_BYTES) + row * 128;
-          const float* gm = p.gamma ? p.gamma + (int64_t)i * D + (int64_t)rank * Dc + dch * kBK : nullptr;
-          uint16_t* dst = p.dx + t * nD + (int64_t)i * D + (int64_t)rank * Dc + dch * kBK;
+          const uint32_t gm = smem_u32(gam_s + i * Dc + dch * kBK);
+          // the staging buffer is free once the previous TMA store has read it
+          if (row == 0) bulk_wait_read0();
+          named_sync(2, 128);
+          const uint32_t st_row = smem_u32(dxs) + row * 128;
 #pragma unroll
-          for (int c16 = 0; c16 < 4; ++c16) {
-            float v[16];
-            tmem_ld16(tmem_dv + dvb * 64 + ((uint32_t)(32 * q4) << 16) + c16 * 16, v);
-            tmem_wait_ld();
+          for (int half = 0; half < 2; ++half) {
+            float v[32];
+            {
+              float v0[16], v1[16];
+              const uint32_t ta = tmem_dv + dvb * 64 + ((uint32_t)(32 * q4) << 16) + half * 32;
+              tmem_ld16(ta, v0);
+              tmem_ld16(ta + 16, v1);
+              tmem_wait_ld();
 #pragma unroll
-            for (int hc = 0; hc < 2; ++hc) {
-              const int c = c16 * 2 + hc;             // 16-byte chunk 0..7 of the 128-byte row
+              for (int e = 0; e < 16; ++e) {
+                v[e] = v0[e];
+                v[16 + e] = v1[e];
+              }
+            }
+#pragma unroll
+            for (int hc = 0; hc < 4; ++hc) {
+              const int c = half * 4 + hc;            // 16-byte chunk 0..7 of the 128-byte row
               const uint32_t sw = (uint32_t)((c ^ (row & 7)) << 4);
-              float xf[8], gf[8], gam[8];
+              float xf[8], gf[8];
               bf16x8_to_f32(lds128(x_row + sw), xf);
               bf16x8_to_f32(lds128(dh_row + sw), gf);
-              if (gm) {
-                const float4 g0 = __ldg(reinterpret_cast<const float4*>(gm + c * 8));
-                const float4 g1 = __ldg(reinterpret_cast<const float4*>(gm + c * 8 + 4));
-                gam[0] = g0.x; gam[1] = g0.y; gam[2] = g0.z; gam[3] = g0.w;
-                gam[4] = g1.x; gam[5] = g1.y; gam[6] = g1.z; gam[7] = g1.w;
-              } else {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) gam[e] = 1.0f;
-              }
+              const uint4 ga = lds128(gm + c * 32), gb = lds128(gm + c * 32 + 16);
+              const float gam[8] = {__uint_as_float(ga.x), __uint_as_float(ga.y), __uint_as_float(ga.z),
+                                    __uint_as_float(ga.w), __uint_as_float(gb.x), __uint_as_float(gb.y),
+                                    __uint_as_float(gb.z), __uint_as_float(gb.w)};
               uint32_t o[4];
 #pragma unroll
               for (int e = 0; e < 8; e += 2) {
@@ -638,9 +705,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float d1 = v[hc * 8 + e + 1] * gam[e + 1] + ((-c_t) * xf[e + 1] + hp[i] * gf[e + 1]);
                 o[e / 2] = (uint32_t)f32_to_bf16_bits(d0) | ((uint32_t)f32_to_bf16_bits(d1) << 16);
               }
-              if (t < p.T) *reinterpret_cast<uint4*>(dst + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+              sts128(st_row + sw, make_uint4(o[0], o[1], o[2], o[3]));
             }
           }
+          fence_proxy_async_smem();
+          named_sync(2, 128);
+          if (row == 0 && !*abort_flag) {
+            tma_store_2d(&map_dx, smem_u32(dxs), i * D + (int)rank * Dc + dch * kBK, tile * kBM);
+            bulk_commit();
+          }
+          if (row == 0 && dch == 0 && i == 0) MHC_BWD_TRACE(6);
+          if (row == 0 && dch == DCH - 1 && i == n - 1) MHC_BWD_TRACE(7);
           tc_fence_before();
           __syncwarp();
           if (lane == 0) {
@@ -677,12 +752,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B::g_empty));
+        if (row == 0) MHC_BWD_TRACE(8);
         ++flushes;
       }
     }
   }
 
   // ---------------------------------------------------------------- teardown
+  if (warp >= 7 && lane == 0 && (warp & 3) == 0) bulk_wait_all0();   // dx stores of WG_E issued by row 0
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -692,25 +769,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync_all();
 }
 
-// phi [N_OUT, nD] f32 -> per 64-k block the K'-major interleaved image that
-// W1 reads as the B operand of dvecX: element (kk, K'=seg*N_OUT+j) holds the
-// B-side split term of segment seg of phi[j][block*64+kk].
+// phi [N_OUT, nD] f32 -> per 64-k block the K-major interleaved image W1
+// reads as the B operand of dvecX: row kk, column e*SEGW + j holds bf16 term
+// e (hi, mid, lo) of phi[j][block*64 + kk]; padding columns are zero.
 template <int n>
 __global__ void __launch_bounds__(256) phit_kernel(const float* __restrict__ phi, uint16_t* __restrict__ img,
                                                    int nD) {
   using Cf = Cfg<n>;
-  const int64_t per_block = (int64_t)kBK * Cf::KP;
+  const int64_t per_block = (int64_t)kBK * Cf::KA;
   const int64_t total = (int64_t)(nD / kBK) * per_block;
   for (int64_t idx = blockIdx.x * 256ll + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * 256) {
     const int64_t blk = idx / per_block;
     const int r = (int)(idx - blk * per_block);
-    const int kk = r / Cf::KP, kp = r - kk * Cf::KP;
-    uint16_t v = 0;
-    if (kp < Cf::NSEG * Cf::N_OUT) {
-      const int seg = kp / Cf::N_OUT, jj = kp - seg * Cf::N_OUT;
-      v = split_term(phi[(int64_t)jj * nD + blk * kBK + kk], seg_b_term(seg));
-    }
-    img[blk * (Cf::PH_BYTES / 2) + interleave_off(kk, kp, Cf::RG_BYTES) / 2] = v;
+    const int kk = r / Cf::KA, ca = r - kk * Cf::KA;
+    const int e = ca / Cf::SEGW, jj = ca - e * Cf::SEGW;
+    const uint16_t v = jj < Cf::N_OUT ? split_term(phi[(int64_t)jj * nD + blk * kBK + kk], e) : 0;
+    img[blk * (Cf::PH_BYTES / 2) + interleave_off(kk, ca, Cf::RG_BYTES) / 2] = v;
   }
 }
 

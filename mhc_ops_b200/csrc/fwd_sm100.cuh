@@ -287,11 +287,48 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;                   // TMEM lane quadrant of this warp
     const int row = 32 * q + lane;            // token row of the tile = TMEM lane = smem row
     uint32_t it = 0, g = 0;
+    constexpr int LAG = 2;                    // fold K-block kb-LAG while reading stage kb
+    static_assert(LAG < Cf::NBUF, "accumulator ring shorter than the fold lag");
+    // Fold accumulator ring slot of K-block counter gg (NT split terms of each
+    // output) into part; narrow outputs sum the block's terms (smallest first)
+    // before adding, wide outputs fold in place to stay in registers.
+    auto fold = [&](uint32_t gg, float (&part)[N_OUT]) {
+      const int ab = gg % Cf::NBUF;
+      mbar_wait(bar(B::acc_full + ab), (gg / Cf::NBUF) & 1, wc);
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + ab * Cf::ACC_COLS;
+      constexpr bool kBlockSum = N_OUT <= 32;
+      float blk[kBlockSum ? N_OUT : 1];
+#pragma unroll
+      for (int jj = 0; jj < (kBlockSum ? N_OUT : 1); ++jj) blk[jj] = 0.f;
+#pragma unroll
+      for (int c16 = Cf::NB / 16 - 1; c16 >= 0; --c16) {
+        float v[16];
+        tmem_ld16(taddr + c16 * 16, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 15; e >= 0; --e) {
+          const int col = c16 * 16 + e;
+          if (col < Cf::NT * N_OUT) {
+            if constexpr (kBlockSum) blk[col % N_OUT] += v[e];
+            else part[col % N_OUT] += v[e];
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B::acc_empty + ab));
+      if constexpr (kBlockSum) {
+#pragma unroll
+        for (int jj = 0; jj < N_OUT; ++jj) part[jj] += blk[jj];
+      }
+    };
     for (int j = 0; j < my_tiles; ++j) {
       float part[N_OUT];
 #pragma unroll
       for (int jj = 0; jj < N_OUT; ++jj) part[jj] = 0.f;
       float sq = 0.f;
+      const uint32_t g0 = g;
       for (int kb = 0; kb < KB; ++kb, ++it, ++g) {
         const int s = it % S;
         mbar_wait(bar(B::full + s), (it / S) & 1, wc);
@@ -310,39 +347,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B::empty + s));
-        // fold this K-block's accumulator (NT split terms of each output) into part
-        const int ab = g % Cf::NBUF;
-        mbar_wait(bar(B::acc_full + ab), (g / Cf::NBUF) & 1, wc);
-        tc_fence_after();
-        const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + ab * Cf::ACC_COLS;
-        // Narrow outputs: sum this block's split terms (smallest first) before
-        // adding to the running partial; wide outputs fold in place (registers).
-        constexpr bool kBlockSum = N_OUT <= 32;
-        float blk[kBlockSum ? N_OUT : 1];
-#pragma unroll
-        for (int jj = 0; jj < (kBlockSum ? N_OUT : 1); ++jj) blk[jj] = 0.f;
-#pragma unroll
-        for (int c16 = Cf::NB / 16 - 1; c16 >= 0; --c16) {
-          float v[16];
-          tmem_ld16(taddr + c16 * 16, v);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 15; e >= 0; --e) {
-            const int col = c16 * 16 + e;
-            if (col < Cf::NT * N_OUT) {
-              if constexpr (kBlockSum) blk[col % N_OUT] += v[e];
-              else part[col % N_OUT] += v[e];
-            }
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B::acc_empty + ab));
-        if constexpr (kBlockSum) {
-#pragma unroll
-          for (int jj = 0; jj < N_OUT; ++jj) part[jj] += blk[jj];
-        }
+        if (kb >= LAG) fold(g - LAG, part);
       }
+      for (uint32_t gg = (g - g0 >= LAG ? g - LAG : g0); gg < g; ++gg) fold(gg, part);
       // send (part, sq) of token `row` to its owner CTA
       const int rb = j % RB;
       const uint32_t rph = (j / RB) & 1;
@@ -376,8 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tot[lt * RS + jj] = sum;
       }
       named_sync(1, 128);
-      if (tid == 0)
-        for (int c = 0; c < C; ++c) mbar_arrive_remote(bar(B::red_free + rb), c);
+      if (tid < C) mbar_arrive_remote(bar(B::red_free + rb), tid);   // one release per destination CTA
       // (5) outputs of my tokens
       const float inv_nd = 1.0f / (float)nD;
       for (int idx = tid; idx < TPO * N_OUT; idx += 128) {
@@ -455,8 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       named_sync(2, 128);
-      if (tid == 0)
-        for (int c = 0; c < C; ++c) mbar_arrive_remote(bar(B::hpre_free + rb), c);
+      if (tid < C) mbar_arrive_remote(bar(B::hpre_free + rb), tid);
     }
   }
 

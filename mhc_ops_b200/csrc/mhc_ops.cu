@@ -180,51 +180,73 @@ struct ClusterPlan {
   int max_clusters = 0;  // co-resident clusters on this device
 };
 
-// Largest number of co-resident CTAs over the cluster sizes C (<= 16) that
-// divide D/64; ties go to the larger C (shorter L2 re-read distance).
+// Cluster size for a persistent cluster kernel: among the C (<= 16, dividing
+// D/64, allowed by the kernel) pick the one with the least work per CTA,
+// ceil(tiles / clusters) / C tile-units, where clusters = min(co-resident
+// clusters, tiles); ties go to the larger C (shorter L2 re-read distance).
+#ifndef MHC_MAX_CLUSTER
+#define MHC_MAX_CLUSTER 16   // largest cluster size the planner considers (build-time)
+#endif
 inline bool any_cluster(int) { return true; }
 
 template <typename Kernel, typename Allowed = bool (*)(int)>
-int plan_clusters(Kernel kernel, int smem, int threads, int D, ClusterPlan* out, Allowed allowed = any_cluster) {
+int plan_clusters(Kernel kernel, int smem, int threads, int D, int64_t tiles, ClusterPlan* out,
+                  Allowed allowed = any_cluster) {
   static std::mutex mu;
-  static std::map<std::tuple<int, const void*, int>, ClusterPlan> cache;
+  static std::map<std::tuple<int, const void*, int>, std::map<int, int>> cache;   // -> {C: max clusters}
   int dev = 0;
   MHC_CUDA_TRY(cudaGetDevice(&dev));
   const auto key = std::make_tuple(dev, reinterpret_cast<const void*>(kernel), D);
+  std::map<int, int> occ;
+  bool have = false;
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
     if (it != cache.end()) {
-      *out = it->second;
-      return MHC_OK;
+      occ = it->second;
+      have = true;
     }
   }
-  MHC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  MHC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-  ClusterPlan best;
-  for (int C : {16, 8, 4, 2, 1}) {
-    if (D % (64 * C) != 0 || !allowed(C)) continue;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(C);
-    cfg.blockDim = dim3(threads);
-    cfg.dynamicSmemBytes = smem;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = C;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    int ncl = 0;
-    if (cudaOccupancyMaxActiveClusters(&ncl, kernel, &cfg) != cudaSuccess) {
-      cudaGetLastError();
-      continue;
+  if (!have) {
+    MHC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    MHC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    for (int C : {16, 8, 4, 2, 1}) {
+      if (D % (64 * C) != 0) continue;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(C);
+      cfg.blockDim = dim3(threads);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = C;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int ncl = 0;
+      if (cudaOccupancyMaxActiveClusters(&ncl, kernel, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        ncl = 0;
+      }
+      occ[C] = ncl;
     }
-    if (ncl * C > best.max_clusters * best.C) best = ClusterPlan{C, ncl};
+    std::lock_guard<std::mutex> lk(mu);
+    cache[key] = occ;
+  }
+  ClusterPlan best;
+  double best_cost = 0.0;
+  tiles = std::max<int64_t>(tiles, 1);
+  for (int C : {16, 8, 4, 2, 1}) {
+    auto it = occ.find(C);
+    if (C > MHC_MAX_CLUSTER || it == occ.end() || it->second <= 0 || !allowed(C)) continue;
+    const int64_t ncl = std::min<int64_t>(it->second, tiles);
+    const double cost = (double)((tiles + ncl - 1) / ncl) / C;
+    if (best.C == 0 || cost < best_cost - 1e-9) {
+      best = ClusterPlan{C, it->second};
+      best_cost = cost;
+    }
   }
   if (best.C == 0) return MHC_ERR_CUDA;
-  std::lock_guard<std::mutex> lk(mu);
-  cache[key] = best;
   *out = best;
   return MHC_OK;
 }
@@ -255,7 +277,8 @@ struct FwdTc {
     uint16_t* phis = reinterpret_cast<uint16_t*>(ws + kWsHeaderBytes);
     int st;
     ClusterPlan plan;
-    if ((st = plan_clusters(fwdtc::fwd_kernel<n>, Cf::SMEM, fwdtc::kThreads, D, &plan))) return st;
+    const int64_t tiles = (T + fwdtc::kBM - 1) / fwdtc::kBM;
+    if ((st = plan_clusters(fwdtc::fwd_kernel<n>, Cf::SMEM, fwdtc::kThreads, D, tiles, &plan))) return st;
 
     fwdtc::split_phi_kernel<n><<<std::min<int64_t>(((int64_t)Cf::NB * nD + 255) / 256, 4 * 148), 256, 0, s>>>(
         a->phi, phis, nD);
@@ -346,9 +369,8 @@ bool bwd_c_allowed(int D, int C) {
 
 int bwd_tc_layout(int64_t T, int D, BwdTcLayout* L) {
   using Cf = bwdtc::Cfg<kBwdN>;
-  (void)T;
-  int st = plan_clusters(bwdtc::bwd_kernel<kBwdN>, Cf::SMEM, bwdtc::kThreads, D, &L->plan,
-                         [D](int C) { return bwd_c_allowed(D, C); });
+  int st = plan_clusters(bwdtc::bwd_kernel<kBwdN>, Cf::SMEM, bwdtc::kThreads, D, (T + bwdtc::kBM - 1) / bwdtc::kBM,
+                         &L->plan, [D](int C) { return bwd_c_allowed(D, C); });
   if (st) return st;
   const int kc = kBwdN * D / L->plan.C;
   L->dv_bufs = (128 + (kc / 128) * Cf::NG <= 512) ? 2 : 1;
@@ -392,12 +414,13 @@ int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s) {
   bwdtc::phit_kernel<n><<<4 * 148, 256, 0, s>>>(a->phi, reinterpret_cast<uint16_t*>(ws + L.phit), nD);
   if ((st = after_launch())) return st;
 
-  CUtensorMap m_x2d, m_dh;
+  CUtensorMap m_x2d, m_dh, m_dx;
   {
     const uint64_t dims[2] = {(uint64_t)nD, (uint64_t)T};
     const uint64_t strides[1] = {(uint64_t)nD * 2};
     const uint32_t box[2] = {bwdtc::kBK, bwdtc::kBM};
     if ((st = encode_bf16_map(&m_x2d, a->x, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    if ((st = encode_bf16_map(&m_dx, a->dx, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
   {
     const uint64_t dims[2] = {(uint64_t)D, (uint64_t)T};
@@ -442,7 +465,7 @@ int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  MHC_CUDA_TRY(cudaLaunchKernelEx(&cfg, bwdtc::bwd_kernel<n>, m_x2d, m_dh, p));
+  MHC_CUDA_TRY(cudaLaunchKernelEx(&cfg, bwdtc::bwd_kernel<n>, m_x2d, m_dh, m_dx, p));
   if ((st = after_launch())) return st;
 
   generic::finalize_param_kernel<<<(nD + generic::kThreads - 1) / generic::kThreads, generic::kThreads, 0, s>>>(
@@ -580,8 +603,8 @@ int mhc_query_plan(int which, int64_t tokens, int32_t n, int32_t D, int* path, i
   ClusterPlan plan;
   const int64_t tiles = (tokens + 127) / 128;
   if (which == 0 && (n == 4 || n == 8) && D % 64 == 0 && tokens < ((int64_t)1 << 31)) {
-    st = n == 4 ? plan_clusters(fwdtc::fwd_kernel<4>, fwdtc::Cfg<4>::SMEM, fwdtc::kThreads, D, &plan)
-                : plan_clusters(fwdtc::fwd_kernel<8>, fwdtc::Cfg<8>::SMEM, fwdtc::kThreads, D, &plan);
+    st = n == 4 ? plan_clusters(fwdtc::fwd_kernel<4>, fwdtc::Cfg<4>::SMEM, fwdtc::kThreads, D, tiles, &plan)
+                : plan_clusters(fwdtc::fwd_kernel<8>, fwdtc::Cfg<8>::SMEM, fwdtc::kThreads, D, tiles, &plan);
     if (st) return st;
     *path = 1;
   } else if (which == 1 && bwd_tc_shape(tokens, n, D)) {
