@@ -539,8 +539,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         dhp_s[lt * n + i] = s;
       }
       named_sync(1, 128);
-      if (tid == 0)
-        for (int c = 0; c < C; ++c) mbar_arrive_remote(bar(B::p_free + pb), c);
+      if (tid < C) mbar_arrive_remote(bar(B::p_free + pb), tid);   // one release per destination CTA
       // one thread per owned token: dh_mix, c and the dalpha / dbias terms
       for (int lt = tid; lt < TPO; lt += 128) {
         const int64_t t = (int64_t)tile * kBM + (int)rank * TPO + lt;
@@ -652,8 +651,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(bar(B::dhm_full));
       named_sync(2, 128);
       if (row == 0) MHC_BWD_TRACE(5);
-      if (q4 == 0 && lane == 0)
-        for (int c = 0; c < p.C; ++c) mbar_arrive_remote(bar(B::bc_free), c);
+      if (q4 == 0 && lane < C) mbar_arrive_remote(bar(B::bc_free), lane);
       // (b) dx of every 64-k block of the slice
       for (int dch = 0; dch < DCH; ++dch, ++dq) {
         const int ds = dq % Cf::DS;
