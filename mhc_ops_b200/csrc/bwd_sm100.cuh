@@ -38,6 +38,17 @@
 #ifndef MHC_BWD_TRACE
 #define MHC_BWD_TRACE(slot) ((void)0)
 #endif
+#ifndef MHC_BWD_TRACE_Q
+#define MHC_BWD_TRACE_Q(slot) ((void)0)
+#endif
+// Tiles of look-ahead for the L2 prefetch of the next tiles' slices (tuning).
+#ifndef MHC_BWD_PREFETCH
+#define MHC_BWD_PREFETCH 1
+#endif
+// Phase-2 stages of look-ahead for the producer's L2 prefetch (tuning; 0 = off).
+#ifndef MHC_BWD_PF_STAGES
+#define MHC_BWD_PF_STAGES 0
+#endif
 
 namespace mhc {
 namespace bwdtc {
@@ -46,7 +57,9 @@ using namespace sm100;
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 11 * 32;   // W0, W1, W2, WG_P(4), WG_E(4)
+constexpr int kWarpE0 = 7;          // first epilogue warp
+constexpr int kThreadsE = 8 * 32;   // WG_E: 8 warps
+constexpr int kThreads = kWarpE0 * 32 + kThreadsE;   // W0, W1, W2, WG_P(4), WG_E(8)
 constexpr int kSmemLimit = 232448;
 
 constexpr int round_up(int v, int a) { return (v + a - 1) / a * a; }
@@ -267,11 +280,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < Cf::XS; ++i) {
       mbar_init(bar(B::x_full + i), 1);
-      mbar_init(bar(B::x_empty + i), 1 + 4);
+      mbar_init(bar(B::x_empty + i), 1 + kThreadsE / 32);
     }
     for (int i = 0; i < Cf::DS; ++i) {
       mbar_init(bar(B::dh_full + i), 1);
-      mbar_init(bar(B::dh_empty + i), 4);
+      mbar_init(bar(B::dh_empty + i), kThreadsE / 32);
     }
     for (int i = 0; i < Cf::PS; ++i) {
       mbar_init(bar(B::ph_full + i), 1);
@@ -279,12 +292,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(B::dv_full + i), 1);
-      mbar_init(bar(B::dv_empty + i), 4);
+      mbar_init(bar(B::dv_empty + i), kThreadsE / 32);
     }
-    mbar_init(bar(B::dhm_full), 128);
+    mbar_init(bar(B::dhm_full), kThreadsE);
     mbar_init(bar(B::dhm_free), 1);
     mbar_init(bar(B::g_full), 1);
-    mbar_init(bar(B::g_empty), 4);
+    mbar_init(bar(B::g_empty), kThreadsE / 32);
     for (int i = 0; i < RB; ++i) {
       mbar_init(bar(B::p_full + i), kBM);
       mbar_init(bar(B::p_free + i), C);
@@ -324,6 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int dch = 0; dch < DCH; ++dch, ++dq) {
           const int ds = dq % Cf::DS;
           mbar_wait(bar(B::dh_empty + ds), ((dq / Cf::DS) & 1) ^ 1, wc);
+          MHC_BWD_TRACE_Q(1);
           if (!*abort_flag) {
             mbar_arrive_expect_tx(bar(B::dh_full + ds), Cf::X_BYTES);
             tma_load_2d(smem_u32(dhr + ds * Cf::X_BYTES), &map_dh, bar(B::dh_full + ds), (int)rank * Dc + dch * kBK,
@@ -332,7 +346,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < n; ++i, ++q) {
             const int s = q % Cf::XS;
             const int k0 = i * D + (int)rank * Dc + dch * kBK;
+            if (MHC_BWD_PF_STAGES > 0) {
+              // stage q + PF of this CTA's (tile, dch, i) sequence
+              const int qa = (dch * n + i) + MHC_BWD_PF_STAGES;
+              const int jt = j + qa / (DCH * n), r2 = qa % (DCH * n);
+              if (jt < my_tiles) {
+                const int pd = r2 / n, pi = r2 % n;
+                const int pt = (int)cid + jt * (int)ncl;
+                tma_prefetch_2d(&map_x2d, pi * D + (int)rank * Dc + pd * kBK, pt * kBM);
+                if (pi == 0) tma_prefetch_2d(&map_dh, (int)rank * Dc + pd * kBK, pt * kBM);
+              }
+            }
             mbar_wait(bar(B::x_empty + s), ((q / Cf::XS) & 1) ^ 1, wc);
+            MHC_BWD_TRACE_Q(0);
             if (dch == 0 && i == 0) MHC_BWD_TRACE(11);
             if (dch == DCH - 1 && i == n - 1) MHC_BWD_TRACE(12);
             if (!*abort_flag) {
@@ -366,6 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t dvph = DVB == 2 ? (q >> 1) & 1 : q & 1;
             mbar_wait(bar(B::ph_full + ps), (q / Cf::PS) & 1, wc);
             mbar_wait(bar(B::dv_empty + dvb), dvph ^ 1, wc);
+            MHC_BWD_TRACE_Q(3);
             tc_fence_after();
             if (!*abort_flag) {
               const uint32_t dhm_a = smem_u32(dhm), ph_a = smem_u32(phr + ps * Cf::PH_BYTES);
@@ -386,6 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               // G over the pair of stages (s-1, s): rows 0..63 stream i-1, 64..127 stream i
               mbar_wait(bar(B::x_full + s - 1), ((q - 1) / Cf::XS) & 1, wc);
               mbar_wait(bar(B::x_full + s), (q / Cf::XS) & 1, wc);
+              MHC_BWD_TRACE_Q(4);
               tc_fence_after();
               if (!*abort_flag) {
                 const int blk = dch * (n / 2) + i / 2;
@@ -427,6 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int ps = q % Cf::PS;
             const int k0 = i * D + (int)rank * Dc + dch * kBK;
             mbar_wait(bar(B::ph_empty + ps), ((q / Cf::PS) & 1) ^ 1, wc);
+            MHC_BWD_TRACE_Q(2);
             if (*abort_flag) continue;
             mbar_arrive_expect_tx(bar(B::ph_full + ps), Cf::PH_BYTES);
             bulk_load(smem_u32(phr + ps * Cf::PH_BYTES), p.phit + (size_t)(k0 / kBK) * Cf::PH_BYTES, Cf::PH_BYTES,
@@ -446,6 +475,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < my_tiles; ++j) {
       const int tile = (int)cid + j * (int)ncl;
       if (tid == 0) MHC_BWD_TRACE(0);
+      // Pull the slice of the tile after this one into L2 now (tile 0 too, at
+      // the start), so phase-1 loads see L2 latency and phase 2 re-reads hit.
+      if (tid == 0 && MHC_BWD_PREFETCH > 0) {
+        for (int jt = (j == 0 ? 0 : j + MHC_BWD_PREFETCH); jt <= j + MHC_BWD_PREFETCH && jt < my_tiles; ++jt) {
+          const int pt = (int)cid + jt * (int)ncl;
+          for (int dch = 0; dch < DCH; ++dch) {
+            tma_prefetch_2d(&map_dh, (int)rank * Dc + dch * kBK, pt * kBM);
+            for (int i = 0; i < n; ++i) tma_prefetch_2d(&map_x2d, i * D + (int)rank * Dc + dch * kBK, pt * kBM);
+          }
+        }
+      }
       // (0) small per-token inputs of the tokens this CTA owns, loaded in
       // parallel now so the owner step reads them from smem.  own_in is free:
       // the previous tile's owner step finished before its last named barrier.
@@ -602,56 +642,47 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid < Cf::CW) p.abpart[((int64_t)cid * C + rank) * Cf::CW + tid] = ab_acc;
   } else {
     // ------------------------------------------------ WG_E: operands, dx epilogue, G flush
+    // 8 warps: two per TMEM lane quadrant; eh selects the half of the columns.
     const int q4 = warp & 3;
+    const int eh = (warp - kWarpE0) >> 2;
     const int row = 32 * q4 + lane;          // token row = TMEM lane
+    const bool issuer = (q4 == 0 && lane == 0 && eh == 0);
     uint32_t q = 0, dq = 0, flushes = 0;
     for (int j = 0; j < my_tiles; ++j) {
       const int tile = (int)cid + j * (int)ncl;
       // (a) record -> DHM row of this token (the three bf16 terms of dh_mix)
       mbar_wait<true>(bar(B::bc_full), j & 1, wc);
-      if (row == 0) MHC_BWD_TRACE(4);
+      if (issuer) MHC_BWD_TRACE(4);
       mbar_wait(bar(B::dhm_free), (j & 1) ^ 1, wc);
-      float dmix[N_OUT];
-#pragma unroll
-      for (int jj = 0; jj < N_OUT; ++jj) dmix[jj] = bc[row * RECW + jj];
-      const float c_t = bc[row * RECW + N_OUT];
+      const float* rec = bc + row * RECW;
+      const float c_t = rec[N_OUT];
       float hp[n];
 #pragma unroll
-      for (int i = 0; i < n; ++i) hp[i] = bc[row * RECW + N_OUT + 1 + i];
-      {
-        uint16_t tr[3][N_OUT];
+      for (int i = 0; i < n; ++i) hp[i] = rec[N_OUT + 1 + i];
+      // DHM row: segment e holds term e of dh_mix[0..N_OUT), zero padded to SEGW;
+      // this half writes every other 16-byte chunk of the row.
 #pragma unroll
-        for (int jj = 0; jj < N_OUT; ++jj) {
-          float v = dmix[jj];
+      for (int kc0 = 0; kc0 < Cf::KA / 8; kc0 += 2) {
+        const int kc = kc0 + eh;
+        const int e = (kc * 8) / Cf::SEGW, j0 = kc * 8 - e * Cf::SEGW;
+        uint32_t w[4];
 #pragma unroll
-          for (int e = 0; e < 3; ++e) {
-            tr[e][jj] = f32_to_bf16_bits(v);
-            v -= bf16_bits_to_f32(tr[e][jj]);
+        for (int h = 0; h < 4; ++h) {
+          uint32_t lohi[2];
+#pragma unroll
+          for (int b2 = 0; b2 < 2; ++b2) {
+            const int jj = j0 + h * 2 + b2;
+            lohi[b2] = jj < N_OUT ? split_term(rec[jj], e) : 0;
           }
+          w[h] = lohi[0] | (lohi[1] << 16);
         }
-        // DHM row: segment e holds term e of dh_mix[0..N_OUT), zero padded to SEGW
-#pragma unroll
-        for (int kc = 0; kc < Cf::KA / 8; ++kc) {
-          uint32_t w[4];
-#pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            uint32_t lohi[2];
-#pragma unroll
-            for (int b2 = 0; b2 < 2; ++b2) {
-              const int ca = kc * 8 + h * 2 + b2;
-              const int e = ca / Cf::SEGW, jj = ca - e * Cf::SEGW;
-              lohi[b2] = jj < N_OUT ? tr[e][jj] : 0;
-            }
-            w[h] = lohi[0] | (lohi[1] << 16);
-          }
-          *reinterpret_cast<uint4*>(dhm + interleave_off(row, kc * 8, Cf::RG_BYTES)) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
+        *reinterpret_cast<uint4*>(dhm + interleave_off(row, kc * 8, Cf::RG_BYTES)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
       fence_proxy_async_smem();
       mbar_arrive(bar(B::dhm_full));
-      named_sync(2, 128);
-      if (row == 0) MHC_BWD_TRACE(5);
-      if (q4 == 0 && lane < C) mbar_arrive_remote(bar(B::bc_free), lane);
+      named_sync(2, kThreadsE);
+      if (issuer) MHC_BWD_TRACE(5);
+      if (q4 == 0 && eh == 0 && lane < C) mbar_arrive_remote(bar(B::bc_free), lane);
       // (b) dx of every 64-k block of the slice
       for (int dch = 0; dch < DCH; ++dch, ++dq) {
         const int ds = dq % Cf::DS;
@@ -662,62 +693,63 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int dvb = DVB == 2 ? (int)(q & 1) : 0;
           const uint32_t dvph = DVB == 2 ? (q >> 1) & 1 : q & 1;
           mbar_wait(bar(B::x_full + s), (q / Cf::XS) & 1, wc);
+          if (issuer) MHC_BWD_TRACE_Q(5);
           mbar_wait(bar(B::dv_full + dvb), dvph, wc);
+          if (issuer) MHC_BWD_TRACE_Q(6);
           tc_fence_after();
           const uint32_t x_row = smem_u32(xr + s * Cf::X_BYTES) + row * 128;
           const uint32_t gm = smem_u32(gam_s + i * Dc + dch * kBK);
-          // the staging buffer is free once the previous TMA store has read it
-          if (row == 0) bulk_wait_read0();
-          named_sync(2, 128);
-          const uint32_t st_row = smem_u32(dxs) + row * 128;
+          float v[32];
+          {
+            float v0[16], v1[16];
+            const uint32_t ta = tmem_dv + dvb * 64 + ((uint32_t)(32 * q4) << 16) + eh * 32;
+            tmem_ld16(ta, v0);
+            tmem_ld16(ta + 16, v1);
+            tmem_wait_ld();
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            float v[32];
-            {
-              float v0[16], v1[16];
-              const uint32_t ta = tmem_dv + dvb * 64 + ((uint32_t)(32 * q4) << 16) + half * 32;
-              tmem_ld16(ta, v0);
-              tmem_ld16(ta + 16, v1);
-              tmem_wait_ld();
-#pragma unroll
-              for (int e = 0; e < 16; ++e) {
-                v[e] = v0[e];
-                v[16 + e] = v1[e];
-              }
-            }
-#pragma unroll
-            for (int hc = 0; hc < 4; ++hc) {
-              const int c = half * 4 + hc;            // 16-byte chunk 0..7 of the 128-byte row
-              const uint32_t sw = (uint32_t)((c ^ (row & 7)) << 4);
-              float xf[8], gf[8];
-              bf16x8_to_f32(lds128(x_row + sw), xf);
-              bf16x8_to_f32(lds128(dh_row + sw), gf);
-              const uint4 ga = lds128(gm + c * 32), gb = lds128(gm + c * 32 + 16);
-              const float gam[8] = {__uint_as_float(ga.x), __uint_as_float(ga.y), __uint_as_float(ga.z),
-                                    __uint_as_float(ga.w), __uint_as_float(gb.x), __uint_as_float(gb.y),
-                                    __uint_as_float(gb.z), __uint_as_float(gb.w)};
-              uint32_t o[4];
-#pragma unroll
-              for (int e = 0; e < 8; e += 2) {
-                const float d0 = v[hc * 8 + e] * gam[e] + ((-c_t) * xf[e] + hp[i] * gf[e]);
-                const float d1 = v[hc * 8 + e + 1] * gam[e + 1] + ((-c_t) * xf[e + 1] + hp[i] * gf[e + 1]);
-                o[e / 2] = (uint32_t)f32_to_bf16_bits(d0) | ((uint32_t)f32_to_bf16_bits(d1) << 16);
-              }
-              sts128(st_row + sw, make_uint4(o[0], o[1], o[2], o[3]));
+            for (int e = 0; e < 16; ++e) {
+              v[e] = v0[e];
+              v[16 + e] = v1[e];
             }
           }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(B::dv_empty + dvb));
+          // the staging buffer is free once the previous TMA store has read it
+          if (issuer) bulk_wait_read0();
+          named_sync(2, kThreadsE);
+          const uint32_t st_row = smem_u32(dxs) + row * 128;
+#pragma unroll
+          for (int hc = 0; hc < 4; ++hc) {
+            const int c = eh * 4 + hc;                // 16-byte chunk 0..7 of the 128-byte row
+            const uint32_t sw = (uint32_t)((c ^ (row & 7)) << 4);
+            float xf[8], gf[8];
+            bf16x8_to_f32(lds128(x_row + sw), xf);
+            bf16x8_to_f32(lds128(dh_row + sw), gf);
+            const uint4 ga = lds128(gm + c * 32), gb = lds128(gm + c * 32 + 16);
+            const float gam[8] = {__uint_as_float(ga.x), __uint_as_float(ga.y), __uint_as_float(ga.z),
+                                  __uint_as_float(ga.w), __uint_as_float(gb.x), __uint_as_float(gb.y),
+                                  __uint_as_float(gb.z), __uint_as_float(gb.w)};
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+              const float d0 = v[hc * 8 + e] * gam[e] + ((-c_t) * xf[e] + hp[i] * gf[e]);
+              const float d1 = v[hc * 8 + e + 1] * gam[e + 1] + ((-c_t) * xf[e + 1] + hp[i] * gf[e + 1]);
+              o[e / 2] = (uint32_t)f32_to_bf16_bits(d0) | ((uint32_t)f32_to_bf16_bits(d1) << 16);
+            }
+            sts128(st_row + sw, make_uint4(o[0], o[1], o[2], o[3]));
+          }
           fence_proxy_async_smem();
-          named_sync(2, 128);
-          if (row == 0 && !*abort_flag) {
+          named_sync(2, kThreadsE);
+          if (issuer && !*abort_flag) {
             tma_store_2d(&map_dx, smem_u32(dxs), i * D + (int)rank * Dc + dch * kBK, tile * kBM);
             bulk_commit();
           }
-          if (row == 0 && dch == 0 && i == 0) MHC_BWD_TRACE(6);
-          if (row == 0 && dch == DCH - 1 && i == n - 1) MHC_BWD_TRACE(7);
-          tc_fence_before();
+          if (issuer) MHC_BWD_TRACE_Q(7);
+          if (issuer && dch == 0 && i == 0) MHC_BWD_TRACE(6);
+          if (issuer && dch == DCH - 1 && i == n - 1) MHC_BWD_TRACE(7);
           __syncwarp();
           if (lane == 0) {
-            mbar_arrive(bar(B::dv_empty + dvb));
             mbar_arrive(bar(B::x_empty + s));
             if (i == n - 1) mbar_arrive(bar(B::dh_empty + ds));
           }
@@ -732,8 +764,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int i = i0 + (row >> 6);
           const int64_t k = (int64_t)i * D + (int64_t)rank * Dc + dch * kBK + (row & 63);
           float* gp = p.gpart + (int64_t)cid * N_OUT * nD + k;
-#pragma unroll
-          for (int c16 = 0; c16 < Cf::NG / 16; ++c16) {
+          for (int c16 = eh; c16 < Cf::NG / 16; c16 += 2) {
             float v[16];
             tmem_ld16(tmem_g + blk * Cf::NG + ((uint32_t)(32 * q4) << 16) + c16 * 16, v);
             tmem_wait_ld();
@@ -750,14 +781,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B::g_empty));
-        if (row == 0) MHC_BWD_TRACE(8);
+        if (issuer) MHC_BWD_TRACE(8);
         ++flushes;
       }
     }
   }
 
   // ---------------------------------------------------------------- teardown
-  if (warp >= 7 && lane == 0 && (warp & 3) == 0) bulk_wait_all0();   // dx stores of WG_E issued by row 0
+  if (warp >= kWarpE0 && lane == 0 && (warp & 3) == 0 && ((warp - kWarpE0) >> 2) == 0)
+    bulk_wait_all0();   // the dx stores this thread issued have completed
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

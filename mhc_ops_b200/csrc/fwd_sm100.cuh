@@ -224,6 +224,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0;
       for (int j = 0; j < my_tiles; ++j) {
         const int tile = (int)cid + j * (int)ncl;
+        // Pull the slice of the next tile (and, at the start, this one) into
+        // L2 so the ring's TMA loads see L2 latency rather than HBM latency.
+        for (int jt = (j == 0 ? 0 : j + 1); jt <= j + 1 && jt < my_tiles; ++jt) {
+          const int pt = (int)cid + jt * (int)ncl;
+          for (int kb = 0; kb < KB; ++kb) {
+            const int i = kb / DCH, dch = kb - i * DCH;
+            tma_prefetch_2d(&map_x2d, i * D + (int)rank * Dc + dch * kBK, pt * kBM);
+          }
+        }
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % S;
           mbar_wait(bar(B::empty + s), ((it / S) & 1) ^ 1, wc);

@@ -189,8 +189,14 @@ struct ClusterPlan {
 #endif
 inline bool any_cluster(int) { return true; }
 
+// The kernels re-read each tile's slice from L2 one tile after its first
+// read, so the bytes of all concurrently processed tiles (tile_bytes each)
+// must stay L2-resident; plans whose footprint exceeds kL2BudgetBytes count
+// double (their re-reads would come from HBM).
+constexpr double kL2BudgetBytes = 48.0 * 1024 * 1024;
+
 template <typename Kernel, typename Allowed = bool (*)(int)>
-int plan_clusters(Kernel kernel, int smem, int threads, int D, int64_t tiles, ClusterPlan* out,
+int plan_clusters(Kernel kernel, int smem, int threads, int D, int64_t tiles, double tile_bytes, ClusterPlan* out,
                   Allowed allowed = any_cluster) {
   static std::mutex mu;
   static std::map<std::tuple<int, const void*, int>, std::map<int, int>> cache;   // -> {C: max clusters}
@@ -240,7 +246,8 @@ int plan_clusters(Kernel kernel, int smem, int threads, int D, int64_t tiles, Cl
     auto it = occ.find(C);
     if (C > MHC_MAX_CLUSTER || it == occ.end() || it->second <= 0 || !allowed(C)) continue;
     const int64_t ncl = std::min<int64_t>(it->second, tiles);
-    const double cost = (double)((tiles + ncl - 1) / ncl) / C;
+    double cost = (double)((tiles + ncl - 1) / ncl) / C;
+    if ((double)ncl * tile_bytes > kL2BudgetBytes) cost *= 2.0;
     if (best.C == 0 || cost < best_cost - 1e-9) {
       best = ClusterPlan{C, it->second};
       best_cost = cost;
@@ -278,7 +285,9 @@ struct FwdTc {
     int st;
     ClusterPlan plan;
     const int64_t tiles = (T + fwdtc::kBM - 1) / fwdtc::kBM;
-    if ((st = plan_clusters(fwdtc::fwd_kernel<n>, Cf::SMEM, fwdtc::kThreads, D, tiles, &plan))) return st;
+    if ((st = plan_clusters(fwdtc::fwd_kernel<n>, Cf::SMEM, fwdtc::kThreads, D, tiles, 2.0 * fwdtc::kBM * nD,
+                            &plan)))
+      return st;
 
     fwdtc::split_phi_kernel<n><<<std::min<int64_t>(((int64_t)Cf::NB * nD + 255) / 256, 4 * 148), 256, 0, s>>>(
         a->phi, phis, nD);
@@ -370,7 +379,7 @@ bool bwd_c_allowed(int D, int C) {
 int bwd_tc_layout(int64_t T, int D, BwdTcLayout* L) {
   using Cf = bwdtc::Cfg<kBwdN>;
   int st = plan_clusters(bwdtc::bwd_kernel<kBwdN>, Cf::SMEM, bwdtc::kThreads, D, (T + bwdtc::kBM - 1) / bwdtc::kBM,
-                         &L->plan, [D](int C) { return bwd_c_allowed(D, C); });
+                         2.0 * bwdtc::kBM * (kBwdN + 1) * D, &L->plan, [D](int C) { return bwd_c_allowed(D, C); });
   if (st) return st;
   const int kc = kBwdN * D / L->plan.C;
   L->dv_bufs = (128 + (kc / 128) * Cf::NG <= 512) ? 2 : 1;
@@ -603,8 +612,9 @@ int mhc_query_plan(int which, int64_t tokens, int32_t n, int32_t D, int* path, i
   ClusterPlan plan;
   const int64_t tiles = (tokens + 127) / 128;
   if (which == 0 && (n == 4 || n == 8) && D % 64 == 0 && tokens < ((int64_t)1 << 31)) {
-    st = n == 4 ? plan_clusters(fwdtc::fwd_kernel<4>, fwdtc::Cfg<4>::SMEM, fwdtc::kThreads, D, tiles, &plan)
-                : plan_clusters(fwdtc::fwd_kernel<8>, fwdtc::Cfg<8>::SMEM, fwdtc::kThreads, D, tiles, &plan);
+    const double tb = 2.0 * 128 * n * D;
+    st = n == 4 ? plan_clusters(fwdtc::fwd_kernel<4>, fwdtc::Cfg<4>::SMEM, fwdtc::kThreads, D, tiles, tb, &plan)
+                : plan_clusters(fwdtc::fwd_kernel<8>, fwdtc::Cfg<8>::SMEM, fwdtc::kThreads, D, tiles, tb, &plan);
     if (st) return st;
     *path = 1;
   } else if (which == 1 && bwd_tc_shape(tokens, n, D)) {
