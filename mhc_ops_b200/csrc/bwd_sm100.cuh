@@ -41,9 +41,11 @@
 #ifndef MHC_BWD_TRACE_Q
 #define MHC_BWD_TRACE_Q(slot) ((void)0)
 #endif
-// Tiles of look-ahead for the L2 prefetch of the next tiles' slices (tuning).
+// Tiles of look-ahead for an L2 prefetch of the next tiles' slices (tuning;
+// off: on B200 data survives in L2 only for ~55 MB of intervening traffic, and
+// a whole-tile prefetch pushes the phase-2 re-reads past that distance).
 #ifndef MHC_BWD_PREFETCH
-#define MHC_BWD_PREFETCH 1
+#define MHC_BWD_PREFETCH 0
 #endif
 // Phase-2 stages of look-ahead for the producer's L2 prefetch (tuning; 0 = off).
 #ifndef MHC_BWD_PF_STAGES
@@ -181,16 +183,25 @@ __device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
                : "memory");
 }
 
-// smem -> global tiled TMA store (out-of-range rows of the box are not written).
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t c0, int32_t c1) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+// smem -> global tiled TMA store (out-of-range rows of the box are not written)
+// with an L2 eviction-priority hint.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t c0, int32_t c1,
+                                             uint64_t policy) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
-               "r"(src), "r"(c0), "r"(c1)
+               "r"(src), "r"(c0), "r"(c1), "l"(policy)
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
 
 __device__ __forceinline__ void red_add_f32(float* addr, float v) {
   asm volatile("red.global.add.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
@@ -287,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(B::dh_empty + i), kThreadsE / 32);
     }
     for (int i = 0; i < Cf::PS; ++i) {
-      mbar_init(bar(B::ph_full + i), 1);
+      mbar_init(bar(B::ph_full + i), 32);   // one cp.async arrival per lane of W2
       mbar_init(bar(B::ph_empty + i), 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -446,21 +457,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 2) {
     // ------------------------------------------------ W2: split-phi image producer
-    if (producer) {
-      const uint64_t pol_keep = l2_policy_evict_last();
-      uint32_t q = 0;
-      for (int j = 0; j < my_tiles; ++j) {
-        for (int dch = 0; dch < DCH; ++dch) {
-          for (int i = 0; i < n; ++i, ++q) {
-            const int ps = q % Cf::PS;
-            const int k0 = i * D + (int)rank * Dc + dch * kBK;
-            mbar_wait(bar(B::ph_empty + ps), ((q / Cf::PS) & 1) ^ 1, wc);
-            MHC_BWD_TRACE_Q(2);
-            if (*abort_flag) continue;
-            mbar_arrive_expect_tx(bar(B::ph_full + ps), Cf::PH_BYTES);
-            bulk_load(smem_u32(phr + ps * Cf::PH_BYTES), p.phit + (size_t)(k0 / kBK) * Cf::PH_BYTES, Cf::PH_BYTES,
-                      bar(B::ph_full + ps), pol_keep);
+    // The whole warp copies each image with 16-byte cp.async (LSU path), so the
+    // TMA engine only carries x, dh_in and the dx stores.
+    uint32_t q = 0;
+    for (int j = 0; j < my_tiles; ++j) {
+      for (int dch = 0; dch < DCH; ++dch) {
+        for (int i = 0; i < n; ++i, ++q) {
+          const int ps = q % Cf::PS;
+          const int k0 = i * D + (int)rank * Dc + dch * kBK;
+          mbar_wait(bar(B::ph_empty + ps), ((q / Cf::PS) & 1) ^ 1, wc);
+          if (lane == 0) MHC_BWD_TRACE_Q(2);
+          if (!*abort_flag) {
+            const uint8_t* src = p.phit + (size_t)(k0 / kBK) * Cf::PH_BYTES;
+            const uint32_t dst = smem_u32(phr + ps * Cf::PH_BYTES);
+#pragma unroll 4
+            for (int off = lane * 16; off < Cf::PH_BYTES; off += 32 * 16) cp_async16(dst + off, src + off);
           }
+          cp_async_arrive_noinc(bar(B::ph_full + ps));   // fires when this lane's copies have landed
         }
       }
     }
@@ -647,6 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int eh = (warp - kWarpE0) >> 2;
     const int row = 32 * q4 + lane;          // token row = TMEM lane
     const bool issuer = (q4 == 0 && lane == 0 && eh == 0);
+    const uint64_t pol_out = l2_policy_evict_first();   // dx must not push out data awaiting re-read
     uint32_t q = 0, dq = 0, flushes = 0;
     for (int j = 0; j < my_tiles; ++j) {
       const int tile = (int)cid + j * (int)ncl;
@@ -742,7 +756,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async_smem();
           named_sync(2, kThreadsE);
           if (issuer && !*abort_flag) {
-            tma_store_2d(&map_dx, smem_u32(dxs), i * D + (int)rank * Dc + dch * kBK, tile * kBM);
+            tma_store_2d(&map_dx, smem_u32(dxs), i * D + (int)rank * Dc + dch * kBK, tile * kBM, pol_out);
             bulk_commit();
           }
           if (issuer) MHC_BWD_TRACE_Q(7);

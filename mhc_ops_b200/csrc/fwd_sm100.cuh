@@ -32,6 +32,10 @@
 #include "common.cuh"
 #include "sm100.cuh"
 
+#ifndef MHC_FWD_PREFETCH
+#define MHC_FWD_PREFETCH 0
+#endif
+
 namespace mhc {
 namespace fwdtc {
 
@@ -126,6 +130,12 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
     f[2 * i] = __uint_as_float(w[i] << 16);
     f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
   }
+}
+
+__device__ __forceinline__ void st_global_evict_first(void* ptr, uint4 v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.v4.u32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(ptr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w), "l"(pol)
+               : "memory");
 }
 
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
@@ -224,9 +234,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0;
       for (int j = 0; j < my_tiles; ++j) {
         const int tile = (int)cid + j * (int)ncl;
-        // Pull the slice of the next tile (and, at the start, this one) into
-        // L2 so the ring's TMA loads see L2 latency rather than HBM latency.
-        for (int jt = (j == 0 ? 0 : j + 1); jt <= j + 1 && jt < my_tiles; ++jt) {
+        // Optional L2 prefetch of the next tile's slice (tuning; off by default:
+        // it doubles the L2 footprint between a tile's first read and the h_in
+        // re-read, and B200 keeps only ~55 MB of such reuse distance).
+        for (int jt = (j == 0 ? 0 : j + 1); MHC_FWD_PREFETCH && jt <= j + 1 && jt < my_tiles; ++jt) {
           const int pt = (int)cid + jt * (int)ncl;
           for (int kb = 0; kb < KB; ++kb) {
             const int i = kb / DCH, dch = kb - i * DCH;
@@ -431,6 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------ WG_B: h_in of this CTA's d-slice
     const int tid = threadIdx.x - 11 * 32;    // 0..127
+    const uint64_t pol_out = l2_policy_evict_first();   // h_in must not push out data awaiting re-read
     uint32_t it = 0;
     for (int j = 0; j < my_tiles; ++j) {
       const int tile = (int)cid + j * (int)ncl;
@@ -462,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               o.y = (uint32_t)f32_to_bf16_bits(acc[2]) | ((uint32_t)f32_to_bf16_bits(acc[3]) << 16);
               o.z = (uint32_t)f32_to_bf16_bits(acc[4]) | ((uint32_t)f32_to_bf16_bits(acc[5]) << 16);
               o.w = (uint32_t)f32_to_bf16_bits(acc[6]) | ((uint32_t)f32_to_bf16_bits(acc[7]) << 16);
-              *reinterpret_cast<uint4*>(p.h_in + tok * D + (int)rank * Dc + dch * kBK + c * 8) = o;
+              st_global_evict_first(p.h_in + tok * D + (int)rank * Dc + dch * kBK + c * 8, o, pol_out);
             }
           }
           __syncwarp();
