@@ -127,6 +127,31 @@ MHC_API int mhc_fwd_workspace_size(int64_t tokens, int32_t n, int32_t D, size_t*
  * (src/forward/mhc_forward_pre_triton.py:409-514). */
 MHC_API int mhc_fwd(const mhc_fwd_args* args, void* stream);
 
+/* Forward pass that allocates nothing and takes no workspace: for callers that
+ * may not call cudaMalloc, such as a host whose allocator owns all device
+ * memory or a runtime that plans memory ahead and forbids allocation in its
+ * serving loop.  No counterpart in the reference.
+ *
+ * Same arguments, validation, kernels and results as mhc_fwd, except that
+ * args->workspace and args->workspace_bytes are ignored.  The scratch the
+ * forward needs (the bf16 split-phi images, 160 bytes per element of phi's
+ * n*D row for n = 4 and 320 for n = 8) comes from one 16 MiB device array
+ * inside the library.  Every GPU that loads the library holds those 16 MiB
+ * until the process exits.
+ *   Limit: a shape needing more than 16 MiB returns MHC_ERR_LIMIT.  That
+ *   means D > 26176 for n = 4 and D > 6528 for n = 8 (D a multiple of 64);
+ *   other shapes need only the 256-byte status header.
+ *   The first call on each device looks up the array's device address, with
+ *   that device current.  Make that first call before any stream capture.
+ *   Every call on a device uses the same array.  Calls that overlap on the
+ *   GPU (two streams, or two host threads) race on it and may return wrong
+ *   results.  Order them on one stream, or use mhc_fwd with a workspace per
+ *   stream.  The array keeps the previous call's contents.  Nothing in it
+ *   must start at zero, because each call rewrites all the scratch it reads.
+ *   A bounded-wait timeout sets the array's status word, which no entry
+ *   point returns.  Use mhc_fwd and mhc_read_device_status when you need it. */
+MHC_API int mhc_fwd_static(const mhc_fwd_args* args, void* stream);
+
 /* Workspace bytes mhc_bwd needs for this shape on the current device.
  * Replaces the intermediates the Triton backward allocates
  * (src/backward/mhc_backward_triton.py:509-510). */

@@ -53,6 +53,7 @@ SIGNATURES = {
     "mhc_fwd_workspace_size": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
                                               ctypes.POINTER(ctypes.c_size_t)]),
     "mhc_fwd": (ctypes.c_int, [ctypes.POINTER(FwdArgs), _c_void_p]),
+    "mhc_fwd_static": (ctypes.c_int, [ctypes.POINTER(FwdArgs), _c_void_p]),
     "mhc_bwd_workspace_size": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
                                               ctypes.POINTER(ctypes.c_size_t)]),
     "mhc_bwd": (ctypes.c_int, [ctypes.POINTER(BwdArgs), _c_void_p]),

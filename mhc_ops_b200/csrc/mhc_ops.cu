@@ -497,6 +497,36 @@ int bwd_workspace(int64_t T, int n, int D, int sms, size_t* bytes) {
   return MHC_OK;
 }
 
+// ----------------------------------------------------------------- forward without a caller workspace
+// Scratch of mhc_fwd_static: the forward's workspace (the status word in the
+// first kWsHeaderBytes, then the bf16 split-phi images) carved from one
+// file-scope device array instead of caller memory.  Every device that loads
+// the library holds the array until the process exits.
+constexpr size_t kStaticScratchBytes = (size_t)16 << 20;
+constexpr int kStaticMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+// Device address of g_static_scratch on the current device.  In host code the
+// symbol names a host-side shadow, so the address comes from
+// cudaGetSymbolAddress, asked once per device with that device current.
+int static_scratch_address(void** out) {
+  static std::mutex mu;
+  static void* addr[kStaticMaxDevices] = {};
+  int dev = 0;
+  MHC_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kStaticMaxDevices) return MHC_ERR_LIMIT;
+  std::lock_guard<std::mutex> g(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    MHC_CUDA_TRY(cudaGetSymbolAddress(&p, g_static_scratch));
+    if (!p) return MHC_ERR_CUDA;
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return MHC_OK;
+}
+
 }  // namespace
 }  // namespace mhc
 
@@ -598,6 +628,27 @@ int mhc_bwd(const mhc_bwd_args* a, void* stream) {
     return MHC_ERR_MISALIGNED;
   if (bwd_tc_eligible(a)) return bwd_tc_run(a, s);
   return dispatch_n<BwdGeneric>(a->n, a, s, sms);
+}
+
+int mhc_fwd_static(const mhc_fwd_args* a, void* stream) {
+  if (!a) return MHC_ERR_NULL_POINTER;
+  int st = check_shape(a->tokens, a->n, a->D);
+  if (st) return st;
+  size_t need = 0;
+  fwd_workspace(a->tokens, a->n, a->D, &need);
+  if (need > kStaticScratchBytes) return MHC_ERR_LIMIT;
+  int sms = 0;
+  if ((st = current_sm_count(&sms))) return st;
+  void* scratch = nullptr;
+  if ((st = static_scratch_address(&scratch))) return st;
+  // Same validation and kernels as mhc_fwd; only the workspace differs.  The
+  // split-phi images are rewritten in full (padding rows included) by every
+  // call and the status word is only ever written, so nothing in the array
+  // has to start at zero.
+  mhc_fwd_args b = *a;
+  b.workspace = scratch;
+  b.workspace_bytes = kStaticScratchBytes;
+  return mhc_fwd(&b, stream);
 }
 
 int mhc_query_plan(int which, int64_t tokens, int32_t n, int32_t D, int* path, int* cluster_size, int* clusters) {
