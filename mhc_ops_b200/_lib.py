@@ -148,8 +148,11 @@ def query_plan(which: int, tokens: int, n: int, D: int) -> dict:
     path, cs, ncl = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
     check(load().mhc_query_plan(which, tokens, n, D, ctypes.byref(path), ctypes.byref(cs), ctypes.byref(ncl)),
           "mhc_query_plan")
-    return {"path": "tensor-core cluster" if path.value else "generic", "cluster_size": cs.value,
-            "clusters": ncl.value}
+    if not path.value:
+        return {"path": "generic"}
+    if which == 0:
+        return {"path": "tensor-core cluster", "cluster_size": cs.value, "clusters": ncl.value}
+    return {"path": "tensor-core", "d_slices": cs.value, "token_groups": ncl.value}
 
 
 def launch_count() -> int:

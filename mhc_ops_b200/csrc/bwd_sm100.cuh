@@ -1,4 +1,5 @@
-// Backward of the mHC pre-op on sm_100a: cluster K-split, tcgen05 GEMMs.
+// Backward of the mHC pre-op on sm_100a, second half: tcgen05 GEMMs over
+// per-token records.
 //
 // Math: src/backward/golden.py:38-96.  Per token t (row of x):
 //   dh_pre[i] = sum_d dh_in[d] x[i,d]                                  (:51)
@@ -8,48 +9,38 @@
 // and over tokens: G = dh_mix^T x, dphi = G * gamma (:68-69), dgamma[k] =
 // sum_j phi[j,k] G[j,k] (= sum_t x dvecX_mm, :93), dalpha (:77-80), dbias (:83-86).
 //
-// A cluster of C CTAs owns one 128-token tile at a time; CTA r owns the
-// d-slice [r*Dc, (r+1)*Dc) of every stream.  Per tile:
-//   * WG_P (4 warps, phase 1) reads x and dh_in of its slice straight from HBM
-//     (warp per token, L2 evict-last), forms the partial dh_pre of each token,
-//     sends it to the token's owner CTA (DSMEM); the owner reduces the C
-//     partials in rank order, computes dh_mix, c, the dalpha/dbias terms and
-//     broadcasts one record per token (dh_mix, c, h_pre) to every CTA.
-//   * W0 re-reads the slice through L2 with TMA (x blocks [128 tok x 64 k],
-//     dh_in blocks, 128-B swizzle, evict-first); W2 streams pre-laid-out
-//     split-phi images (1-D bulk copies, 3 bf16 terms of phi per k);
-//   * WG_E (4 warps) turns the records into the UMMA operand DHM [128 tok x
-//     3 segments]: the 3 bf16 terms (hi, mid, lo) of dh_mix, each segment
-//     padded to a multiple of 16;
+// The whole-row reductions (dh_pre, c, dalpha, dbias) run first in a
+// streaming kernel (rowdot.cuh, bwd_rows_kernel) that leaves one record per
+// token {dh_mix, c, h_pre}.  This kernel does the rest.  CTA (s, g) owns the
+// d-slice [s*Dc, (s+1)*Dc) of every stream and the 128-token tiles g, g+S_T,
+// ... of the batch; CTAs never talk to each other.  Per tile:
+//   * W3 loads the tile's records (TMA, 16 KB); W0 streams the slice's x
+//     blocks [128 tok x 64 k] and dh_in blocks (TMA, 128-B swizzle); W2 streams
+//     the pre-laid-out split-phi images (3 bf16 terms of phi per k);
+//   * WG_E turns the records into the dh_mix operands: DHM, the 3 bf16 terms
+//     (hi, mid, lo) of dh_mix per token, each segment padded to a multiple of
+//     16, written to tensor memory (A of dvecX, so the per-stage MMAs read no
+//     A bytes from shared memory), and DHS, the hi and mid terms, in shared
+//     memory (B of G).  Both are double buffered: tile j+1's are built during
+//     tile j;
 //   * W1 issues tcgen05.mma: dvecX = sum over 6 (dh term, phi term) products
 //     (smallest first: m.M, l.H, h.L, m.H, h.M, h.H; exact to ~2^-23 in the
 //     fp32 sum) per 64-k block (M=128 tok, N=64, K=segment) and
-//     G += x^T . DHM (M=128 k, N=segment, K=3x128 tokens; x read MN-major
-//     straight from two adjacent TMA stages, DHM read MN-major);
-//   * WG_E reads dvecX (TMEM lane = token) and writes dx; every FT tiles it
-//     flushes G from TMEM into the per-cluster partial (single writer per
-//     address, fixed order).
+//     G += x^T . DHS (M=128 k, N=segment, K=2x128 tokens; x read MN-major
+//     straight from two adjacent TMA stages, DHS read MN-major);
+//   * WG_E reads dvecX (TMEM lane = token) and writes dx through a TMA store;
+//     every FT tiles it flushes G from TMEM into the group's partial (single
+//     writer per address, fixed order).
 #pragma once
 
 #include "common.cuh"
 #include "sm100.cuh"
 
-// Optional per-tile timestamp hook (a profiling build defines it); no-op here.
-#ifndef MHC_BWD_TRACE
-#define MHC_BWD_TRACE(slot) ((void)0)
-#endif
-#ifndef MHC_BWD_TRACE_Q
-#define MHC_BWD_TRACE_Q(slot) ((void)0)
-#endif
-// Tiles of look-ahead for an L2 prefetch of the next tiles' slices (tuning;
-// off: on B200 data survives in L2 only for ~55 MB of intervening traffic, and
-// a whole-tile prefetch pushes the phase-2 re-reads past that distance).
-#ifndef MHC_BWD_PREFETCH
-#define MHC_BWD_PREFETCH 0
-#endif
-// Phase-2 stages of look-ahead for the producer's L2 prefetch (tuning; 0 = off).
+// Stages of look-ahead of the producer's L2 prefetch: HBM latency under full
+// load is a few microseconds, longer than the smem ring covers, so the x and
+// dh_in boxes are pulled into L2 this many stages before their TMA load.
 #ifndef MHC_BWD_PF_STAGES
-#define MHC_BWD_PF_STAGES 0
+#define MHC_BWD_PF_STAGES 8
 #endif
 
 namespace mhc {
@@ -59,9 +50,9 @@ using namespace sm100;
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kWarpE0 = 7;          // first epilogue warp
-constexpr int kThreadsE = 8 * 32;   // WG_E: 8 warps
-constexpr int kThreads = kWarpE0 * 32 + kThreadsE;   // W0, W1, W2, WG_P(4), WG_E(8)
+constexpr int kWarpE0 = 4;          // first epilogue warp
+constexpr int kThreadsE = 8 * 32;   // WG_E: 8 warps, two per TMEM lane quadrant
+constexpr int kThreads = kWarpE0 * 32 + kThreadsE;   // W0, W1, W2, W3, WG_E(8)
 constexpr int kSmemLimit = 232448;
 
 constexpr int round_up(int v, int a) { return (v + a - 1) / a * a; }
@@ -73,55 +64,46 @@ struct Cfg {
   static constexpr int KA = 3 * SEGW;                    // DHM / phi-image row: 3 term segments
   static constexpr int RG_BYTES = (KA / 8) * 128;        // one 8-row group of a K-major interleaved image
   static constexpr int PH_BYTES = 8 * RG_BYTES;          // split-phi image of one 64-k block
-  static constexpr int DHM_BYTES = 16 * RG_BYTES;        // 128 token rows
+  static constexpr int DHM_TCOLS = KA / 2;               // TMEM columns of one DHM buffer (bf16 pairs)
+  static constexpr int KA_G = 2 * SEGW;                  // DHS row: hi and mid segments
+  static constexpr int RG_G = (KA_G / 8) * 128;          // one 8-row group of DHS
+  static constexpr int DHS_BYTES = 16 * RG_G;            // 128 token rows
+  static constexpr int G_COLS_MAX = 256;                 // TMEM: G [0,256), dvecX [256,384), DHM [384,480)
   static constexpr int NG = SEGW;                        // G accumulator columns
   static constexpr int X_BYTES = kBM * 128;
   static constexpr int XS = 4;                           // x ring (2 adjacent pairs)
   static constexpr int DS = 2;
   static constexpr int PS = 3;
-  static constexpr int RECW = round_up(N_OUT + 1 + n, 4);
-  static constexpr int RB = 2;                           // dh_pre exchange buffers
-  static constexpr int MAX_TPO = 32;                     // C >= 4
-  static constexpr int MAX_KC = 1792;                    // d-slice * n per CTA
+  static constexpr int RECW = round_up(N_OUT + 1 + n, 4);   // record: dh_mix, c, h_pre, pad
+  static constexpr int REC_BYTES = kBM * RECW * 4;
+  static constexpr int MAX_KC = 1024;                    // d-slice * n per CTA
   static constexpr int CW = 3 + N_OUT;                   // dalpha / dbias columns
-  // owner inputs per token: h_mix[N_OUT], h_pre[n], h_post[n], dh_post[n], dh_res[n*n], inv_rms
-  static constexpr int OWN_IN = N_OUT + 3 * n + n * n + 1;
-  static constexpr int OWNW = round_up(OWN_IN, 4);
 
   static constexpr int smem_bytes() {
-    return 1024 + XS * X_BYTES + DS * X_BYTES + PS * PH_BYTES + DHM_BYTES + X_BYTES /*dx staging*/ +
-           MAX_KC * 4 /*gamma slice*/ + RB * kBM * n * 4 /*pdh*/ + kBM * RECW * 4 /*bc*/ +
-           MAX_TPO * (n + RECW + CW + OWNW) * 4 /*owner scratch*/ + 512;
+    return 1024 + XS * X_BYTES + DS * X_BYTES + PS * PH_BYTES + 2 * DHS_BYTES + 2 * X_BYTES /*dx staging*/ +
+           MAX_KC * 4 /*gamma slice*/ + REC_BYTES + 512;
   }
   static constexpr int SMEM = smem_bytes();
   static_assert(SMEM <= kSmemLimit, "backward tile does not fit in shared memory");
   static_assert(n % 2 == 0, "G pairs two streams of a d-chunk");
+  static_assert(RECW == 32, "records are loaded as one 128-byte swizzled row per token");
+  static_assert(SEGW == 32, "a DHM half covers 16 of the 32 columns of each segment");
+  static_assert((MAX_KC / 128) * NG <= G_COLS_MAX && G_COLS_MAX + 2 * 64 + 2 * DHM_TCOLS <= 512, "TMEM budget");
 };
 
 struct Params {
-  const uint16_t* x;
-  const uint16_t* dh_in;
-  const float* alpha;
-  const float* inv_rms;
-  const float* h_mix;
-  const float* h_pre;
-  const float* h_post;
-  const float* dh_post;
-  const float* dh_res;
   const float* gamma;     // may be null
   const uint8_t* phit;    // split-phi images, PH_BYTES per 64-k block
-  uint16_t* dx;
-  float* gpart;           // [num_clusters][N_OUT][nD]
-  float* abpart;          // [num_clusters * C][3 + N_OUT]
+  float* gpart;           // [S_T][N_OUT][nD]
   int* status;
   int64_t T;
   int D;
-  int Dc;
-  int C;
+  int Dc;                 // d-slice width (multiple of 64)
+  int S_K;                // d-slices: D / Dc
+  int S_T;                // token groups
   int num_tiles;
   int FT;                 // tiles per G flush
-  int dv_bufs;            // 1 or 2 dvecX TMEM buffers
-  float hc_eps;
+  int dv_shift;           // log2 of the dvecX TMEM buffers (1, 2 or 4 buffers of 64 columns)
 };
 
 template <int n>
@@ -134,16 +116,14 @@ struct Bars {
   static constexpr int ph_full = dh_empty + Cf::DS;
   static constexpr int ph_empty = ph_full + Cf::PS;
   static constexpr int dv_full = ph_empty + Cf::PS;
-  static constexpr int dv_empty = dv_full + 2;
-  static constexpr int dhm_full = dv_empty + 2;
-  static constexpr int dhm_free = dhm_full + 1;
-  static constexpr int g_full = dhm_free + 1;
+  static constexpr int dv_empty = dv_full + 4;
+  static constexpr int dhm_full = dv_empty + 4;
+  static constexpr int dhm_free = dhm_full + 2;
+  static constexpr int g_full = dhm_free + 2;
   static constexpr int g_empty = g_full + 1;
-  static constexpr int p_full = g_empty + 1;
-  static constexpr int p_free = p_full + Cf::RB;
-  static constexpr int bc_full = p_free + Cf::RB;
-  static constexpr int bc_free = bc_full + 1;
-  static constexpr int count = bc_free + 1;
+  static constexpr int rec_full = g_empty + 1;
+  static constexpr int rec_free = rec_full + 1;
+  static constexpr int count = rec_free + 1;
 };
 
 __device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
@@ -161,23 +141,6 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   return v;
 }
 
-__device__ __forceinline__ uint4 ldg_keep(const void* ptr, uint64_t pol) {
-  uint4 v;
-  asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(ptr), "l"(pol));
-  return v;
-}
-
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
-                                          uint64_t pol) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
-          dst),
-      "l"(src), "r"(bytes), "r"(bar), "l"(pol)
-      : "memory");
-}
-
 __device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");
@@ -193,7 +156,7 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t sr
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
@@ -239,54 +202,78 @@ __device__ __forceinline__ uint16_t split_term(float v, int term) {
   return out;
 }
 
+// One token's dh_mix operands from its record.  DHM (tensor memory, A of
+// dvecX): lane `row`, columns [16e, 16e+16) of the buffer hold bf16 term e of
+// dh_mix[0..SEGW), two per column.  DHS (shared memory, B of G): K-major
+// interleaved row `row`, segments e = 0, 1.  Half EH covers j in
+// [16 EH, 16 EH + 16); the partner warp writes the other half.
+template <int n, int EH>
+__device__ __forceinline__ void dhm_row_half(const float (&rec)[Cfg<n>::RECW], uint8_t* dhs, int row,
+                                             uint32_t t_row) {
+  using Cf = Cfg<n>;
+  constexpr int J0 = 16 * EH;
+#pragma unroll
+  for (int e = 0; e < 3; ++e) {
+    uint32_t w[8];
+#pragma unroll
+    for (int h = 0; h < 8; ++h) {
+      const int ja = J0 + 2 * h, jb = ja + 1;
+      const uint32_t lo = ja < Cf::N_OUT ? split_term(rec[ja < Cf::N_OUT ? ja : 0], e) : 0;
+      const uint32_t hi = jb < Cf::N_OUT ? split_term(rec[jb < Cf::N_OUT ? jb : 0], e) : 0;
+      w[h] = lo | (hi << 16);
+    }
+    tmem_st8(t_row + e * (Cf::SEGW / 2) + EH * 8, w);
+    if (e < 2) {
+      *reinterpret_cast<uint4*>(dhs + interleave_off(row, e * Cf::SEGW + J0, Cf::RG_G)) =
+          make_uint4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<uint4*>(dhs + interleave_off(row, e * Cf::SEGW + J0 + 8, Cf::RG_G)) =
+          make_uint4(w[4], w[5], w[6], w[7]);
+    }
+  }
+}
+
 template <int n>
 __global__ void __launch_bounds__(kThreads, 1)
     bwd_kernel(const __grid_constant__ CUtensorMap map_x2d, const __grid_constant__ CUtensorMap map_dh,
-               const __grid_constant__ CUtensorMap map_dx, const Params p) {
+               const __grid_constant__ CUtensorMap map_dx, const __grid_constant__ CUtensorMap map_rec,
+               const Params p) {
   using Cf = Cfg<n>;
   using B = Bars<n>;
   constexpr int N_OUT = Cf::N_OUT;
   constexpr int RECW = Cf::RECW;
-  constexpr int RB = Cf::RB;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* xr = smem;                                  // XS x blocks (pairs adjacent)
   uint8_t* dhr = xr + Cf::XS * Cf::X_BYTES;            // DS dh_in blocks
   uint8_t* phr = dhr + Cf::DS * Cf::X_BYTES;           // PS split-phi images
-  uint8_t* dhm = phr + Cf::PS * Cf::PH_BYTES;          // dh_mix terms: A of dvecX, B of G
-  uint8_t* dxs = dhm + Cf::DHM_BYTES;                  // dx staging [128 tok x 64] (128-B swizzle)
-  float* gam_s = reinterpret_cast<float*>(dxs + Cf::X_BYTES);       // [n][Dc] gamma slice
-  float* pdh = gam_s + Cf::MAX_KC;                     // [RB][128][n]
-  float* bc = pdh + RB * kBM * n;                      // [128][RECW]
-  float* dhp_s = bc + kBM * RECW;                      // [TPO][n]
-  float* rec_s = dhp_s + Cf::MAX_TPO * n;              // [TPO][RECW]
-  float* contrib = rec_s + Cf::MAX_TPO * RECW;         // [TPO][CW]: dalpha (3), dbias (N_OUT) terms
-  float* own_in = contrib + Cf::MAX_TPO * Cf::CW;      // [TPO][OWNW] owner inputs of this tile
-  uint64_t* bars = reinterpret_cast<uint64_t*>(own_in + Cf::MAX_TPO * Cf::OWNW);
+  uint8_t* dhs = phr + Cf::PS * Cf::PH_BYTES;          // 2 x DHS (hi, mid terms of dh_mix): B of G
+  uint8_t* dxs = dhs + 2 * Cf::DHS_BYTES;              // 2 x dx staging [128 tok x 64] (128-B swizzle)
+  float* recs = reinterpret_cast<float*>(dxs + 2 * Cf::X_BYTES);    // [128][RECW] records, 128-B swizzle
+  float* gam_s = recs + kBM * RECW;                    // [n][Dc] gamma slice
+  uint64_t* bars = reinterpret_cast<uint64_t*>(gam_s + Cf::MAX_KC);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + B::count);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_ctarank();
-  const uint32_t cid = cluster_id_x();
-  const uint32_t ncl = nclusters_x();
-  const int C = p.C;
-  const int TPO = kBM / C;
+  const int slice = (int)blockIdx.x % p.S_K;
+  const int group = (int)blockIdx.x / p.S_K;
   const int D = p.D;
   const int Dc = p.Dc;
   const int DCH = Dc / kBK;
   const int nD = n * D;
   const int KC = n * Dc;
   const int NPAIR = KC / 128;                 // G blocks of 128 k per CTA
-  const int DVB = p.dv_bufs;
+  const int DVB = 1 << p.dv_shift;
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  // Tiles run last-first, so the first ones re-read what the row kernel read last.
+  auto tile_of = [&](int j) { return p.num_tiles - 1 - (group + j * p.S_T); };
 
-  // gamma slice of this CTA: gam_s[i*Dc + dd] = gamma[i*D + rank*Dc + dd]
+  // gamma slice of this CTA: gam_s[i*Dc + dd] = gamma[i*D + slice*Dc + dd]
   for (int idx = threadIdx.x; idx < KC; idx += kThreads) {
     const int i = idx / Dc, dd = idx - i * Dc;
-    gam_s[idx] = p.gamma ? p.gamma[(int64_t)i * D + (int64_t)rank * Dc + dd] : 1.0f;
+    gam_s[idx] = p.gamma ? p.gamma[(int64_t)i * D + (int64_t)slice * Dc + dd] : 1.0f;
   }
   if (threadIdx.x == 0) {
     for (int i = 0; i < Cf::XS; ++i) {
@@ -301,20 +288,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(B::ph_full + i), 32);   // one cp.async arrival per lane of W2
       mbar_init(bar(B::ph_empty + i), 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 4; ++i) {
       mbar_init(bar(B::dv_full + i), 1);
       mbar_init(bar(B::dv_empty + i), kThreadsE / 32);
     }
-    mbar_init(bar(B::dhm_full), kThreadsE);
-    mbar_init(bar(B::dhm_free), 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(B::dhm_full + i), kThreadsE);
+      mbar_init(bar(B::dhm_free + i), 1);
+    }
     mbar_init(bar(B::g_full), 1);
     mbar_init(bar(B::g_empty), kThreadsE / 32);
-    for (int i = 0; i < RB; ++i) {
-      mbar_init(bar(B::p_full + i), kBM);
-      mbar_init(bar(B::p_free + i), C);
-    }
-    mbar_init(bar(B::bc_full), kBM);
-    mbar_init(bar(B::bc_free), C);
+    mbar_init(bar(B::rec_full), 1);
+    mbar_init(bar(B::rec_free), kThreadsE);
     *abort_flag = 0;
     fence_mbarrier_init_cluster();
   }
@@ -326,52 +311,50 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&map_x2d);
     prefetch_tensormap(&map_dh);
     prefetch_tensormap(&map_dx);
+    prefetch_tensormap(&map_rec);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  cluster_sync_all();
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t tmem_dv = tmem_base;                       // DVB x 64 columns
-  const uint32_t tmem_g = tmem_base + DVB * 64;             // NPAIR x NG columns
+  const uint32_t tmem_g = tmem_base;                                  // NPAIR x NG columns
+  const uint32_t tmem_dv = tmem_base + Cf::G_COLS_MAX;                // DVB x 64 columns
+  const uint32_t tmem_dhm = tmem_base + Cf::G_COLS_MAX + 2 * 64;      // 2 x DHM_TCOLS columns
   const WaitCtx wc{abort_flag, p.status};
-  const int my_tiles = (int)cid < p.num_tiles ? (p.num_tiles - 1 - (int)cid) / (int)ncl + 1 : 0;
+  const int my_tiles = group < p.num_tiles ? (p.num_tiles - 1 - group) / p.S_T + 1 : 0;
   const bool producer = (lane == 0);
 
   if (warp == 0) {
-    // ------------------------------------------------ W0: TMA producer (phase-2 re-read)
+    // ------------------------------------------------ W0: TMA producer (x, dh_in)
     if (producer) {
       const uint64_t pol_drop = l2_policy_evict_first();
       uint32_t q = 0, dq = 0;
       for (int j = 0; j < my_tiles; ++j) {
-        const int tile = (int)cid + j * (int)ncl;
+        const int tile = tile_of(j);
         for (int dch = 0; dch < DCH; ++dch, ++dq) {
           const int ds = dq % Cf::DS;
           mbar_wait(bar(B::dh_empty + ds), ((dq / Cf::DS) & 1) ^ 1, wc);
-          MHC_BWD_TRACE_Q(1);
           if (!*abort_flag) {
             mbar_arrive_expect_tx(bar(B::dh_full + ds), Cf::X_BYTES);
-            tma_load_2d(smem_u32(dhr + ds * Cf::X_BYTES), &map_dh, bar(B::dh_full + ds), (int)rank * Dc + dch * kBK,
+            tma_load_2d(smem_u32(dhr + ds * Cf::X_BYTES), &map_dh, bar(B::dh_full + ds), slice * Dc + dch * kBK,
                         tile * kBM, pol_drop);
           }
           for (int i = 0; i < n; ++i, ++q) {
             const int s = q % Cf::XS;
-            const int k0 = i * D + (int)rank * Dc + dch * kBK;
+            const int k0 = i * D + slice * Dc + dch * kBK;
             if (MHC_BWD_PF_STAGES > 0) {
-              // stage q + PF of this CTA's (tile, dch, i) sequence
-              const int qa = (dch * n + i) + MHC_BWD_PF_STAGES;
-              const int jt = j + qa / (DCH * n), r2 = qa % (DCH * n);
-              if (jt < my_tiles) {
-                const int pd = r2 / n, pi = r2 % n;
-                const int pt = (int)cid + jt * (int)ncl;
-                tma_prefetch_2d(&map_x2d, pi * D + (int)rank * Dc + pd * kBK, pt * kBM);
-                if (pi == 0) tma_prefetch_2d(&map_dh, (int)rank * Dc + pd * kBK, pt * kBM);
+              // L2 prefetch of the stage MHC_BWD_PF_STAGES ahead of this one
+              // (and, at the start, of the first MHC_BWD_PF_STAGES stages)
+              for (uint32_t qg = (q == 0 ? 0u : q + MHC_BWD_PF_STAGES); qg <= q + MHC_BWD_PF_STAGES; ++qg) {
+                const int jt = (int)(qg / (uint32_t)(DCH * n)), r2 = (int)(qg % (uint32_t)(DCH * n));
+                if (jt < my_tiles) {
+                  const int pd = r2 / n, pi = r2 % n, pt = tile_of(jt);
+                  tma_prefetch_2d(&map_x2d, pi * D + slice * Dc + pd * kBK, pt * kBM);
+                  if (pi == 0) tma_prefetch_2d(&map_dh, slice * Dc + pd * kBK, pt * kBM);
+                }
               }
             }
             mbar_wait(bar(B::x_empty + s), ((q / Cf::XS) & 1) ^ 1, wc);
-            MHC_BWD_TRACE_Q(0);
-            if (dch == 0 && i == 0) MHC_BWD_TRACE(11);
-            if (dch == DCH - 1 && i == n - 1) MHC_BWD_TRACE(12);
             if (!*abort_flag) {
               mbar_arrive_expect_tx(bar(B::x_full + s), Cf::X_BYTES);
               tma_load_2d(smem_u32(xr + s * Cf::X_BYTES), &map_x2d, bar(B::x_full + s), k0, tile * kBM, pol_drop);
@@ -387,34 +370,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc_g = idesc_bf16_f32(kBM, Cf::NG, true, true);
       uint32_t q = 0, flushes = 0;
       for (int j = 0; j < my_tiles; ++j) {
-        mbar_wait(bar(B::dhm_full), j & 1, wc);
-        MHC_BWD_TRACE(9);
+        const int hb = j & 1;
+        mbar_wait(bar(B::dhm_full + hb), (j >> 1) & 1, wc);
         tc_fence_after();
         const bool g_restart = (j % p.FT) == 0;
         if (g_restart && j > 0) {
           mbar_wait(bar(B::g_empty), (flushes - 1) & 1, wc);   // previous G group read out
           tc_fence_after();
         }
+        const uint32_t dhm_t = tmem_dhm + hb * Cf::DHM_TCOLS;
+        const uint32_t dhs_a = smem_u32(dhs + hb * Cf::DHS_BYTES);
         for (int dch = 0; dch < DCH; ++dch) {
           for (int i = 0; i < n; ++i, ++q) {
             const int s = q % Cf::XS;
             const int ps = q % Cf::PS;
-            const int dvb = DVB == 2 ? (int)(q & 1) : 0;
-            const uint32_t dvph = DVB == 2 ? (q >> 1) & 1 : q & 1;
+            const int dvb = (int)(q & (uint32_t)(DVB - 1));
+            const uint32_t dvph = (q >> p.dv_shift) & 1;
             mbar_wait(bar(B::ph_full + ps), (q / Cf::PS) & 1, wc);
             mbar_wait(bar(B::dv_empty + dvb), dvph ^ 1, wc);
-            MHC_BWD_TRACE_Q(3);
             tc_fence_after();
             if (!*abort_flag) {
-              const uint32_t dhm_a = smem_u32(dhm), ph_a = smem_u32(phr + ps * Cf::PH_BYTES);
+              const uint32_t ph_a = smem_u32(phr + ps * Cf::PH_BYTES);
 #pragma unroll
               for (int pr = 0; pr < 6; ++pr) {
 #pragma unroll
                 for (int ks = 0; ks < Cf::SEGW / 16; ++ks) {
-                  const uint32_t ca = (prod_a_term(pr) * Cf::SEGW + ks * 16) * 16;
+                  const uint32_t ca = (prod_a_term(pr) * Cf::SEGW + ks * 16) / 2;   // TMEM column
                   const uint32_t cb = (prod_b_term(pr) * Cf::SEGW + ks * 16) * 16;
-                  umma_bf16(tmem_dv + dvb * 64, desc_kmajor_interleave(dhm_a + ca, 128, Cf::RG_BYTES),
-                            desc_kmajor_interleave(ph_a + cb, 128, Cf::RG_BYTES), idesc_dv, pr != 0 || ks != 0);
+                  umma_bf16_ta(tmem_dv + dvb * 64, dhm_t + ca, desc_kmajor_interleave(ph_a + cb, 128, Cf::RG_BYTES),
+                               idesc_dv, pr != 0 || ks != 0);
                 }
               }
               umma_commit(bar(B::ph_empty + ps));
@@ -424,21 +408,19 @@ __global__ void __launch_bounds__(kThreads, 1)
               // G over the pair of stages (s-1, s): rows 0..63 stream i-1, 64..127 stream i
               mbar_wait(bar(B::x_full + s - 1), ((q - 1) / Cf::XS) & 1, wc);
               mbar_wait(bar(B::x_full + s), (q / Cf::XS) & 1, wc);
-              MHC_BWD_TRACE_Q(4);
               tc_fence_after();
               if (!*abort_flag) {
                 const int blk = dch * (n / 2) + i / 2;
                 const uint32_t xa = smem_u32(xr + (s - 1) * Cf::X_BYTES);
-                const uint32_t ga = smem_u32(dhm);
 #pragma unroll 1
-                for (int e = 2; e >= 0; --e) {            // lo, mid, hi terms of dh_mix
+                for (int e = 1; e >= 0; --e) {            // mid, hi terms of dh_mix (G needs ~2^-17)
 #pragma unroll
                   for (int ks = 0; ks < kBM / 16; ++ks) {
                     const uint64_t ad = desc_mnmajor_sw128(xa + ks * 2048, Cf::X_BYTES, 1024);
-                    // DHM read MN-major: N = the SEGW columns of term e, K = tokens
+                    // DHS read MN-major: N = the SEGW columns of term e, K = tokens
                     const uint64_t bd =
-                        desc_kmajor_interleave(ga + e * Cf::SEGW * 16 + ks * 2 * Cf::RG_BYTES, Cf::RG_BYTES, 128);
-                    umma_bf16(tmem_g + blk * Cf::NG, ad, bd, idesc_g, !(g_restart && e == 2 && ks == 0));
+                        desc_kmajor_interleave(dhs_a + e * Cf::SEGW * 16 + ks * 2 * Cf::RG_G, Cf::RG_G, 128);
+                    umma_bf16(tmem_g + blk * Cf::NG, ad, bd, idesc_g, !(g_restart && e == 1 && ks == 0));
                   }
                 }
                 umma_commit(bar(B::x_empty + s - 1));
@@ -447,8 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        MHC_BWD_TRACE(10);
-        if (!*abort_flag) umma_commit(bar(B::dhm_free));
+        if (!*abort_flag) umma_commit(bar(B::dhm_free + hb));
         if ((j + 1) % p.FT == 0 || j == my_tiles - 1) {
           if (!*abort_flag) umma_commit(bar(B::g_full));
           ++flushes;
@@ -458,15 +439,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 2) {
     // ------------------------------------------------ W2: split-phi image producer
     // The whole warp copies each image with 16-byte cp.async (LSU path), so the
-    // TMA engine only carries x, dh_in and the dx stores.
+    // TMA engine only carries x, dh_in, the records and the dx stores.
     uint32_t q = 0;
     for (int j = 0; j < my_tiles; ++j) {
       for (int dch = 0; dch < DCH; ++dch) {
         for (int i = 0; i < n; ++i, ++q) {
           const int ps = q % Cf::PS;
-          const int k0 = i * D + (int)rank * Dc + dch * kBK;
+          const int k0 = i * D + slice * Dc + dch * kBK;
           mbar_wait(bar(B::ph_empty + ps), ((q / Cf::PS) & 1) ^ 1, wc);
-          if (lane == 0) MHC_BWD_TRACE_Q(2);
           if (!*abort_flag) {
             const uint8_t* src = p.phit + (size_t)(k0 / kBK) * Cf::PH_BYTES;
             const uint32_t dst = smem_u32(phr + ps * Cf::PH_BYTES);
@@ -477,182 +457,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp < 7) {
-    // ------------------------------------------------ WG_P: phase 1 (dh_pre partials) + owner + broadcast
-    const int tid = threadIdx.x - 3 * 32;    // 0..127
-    const int wp = warp - 3;                 // 0..3, 32 token rows each
-    const uint64_t pol_keep = l2_policy_evict_last();
-    const float a_pre = p.alpha[0], a_post = p.alpha[1], a_res = p.alpha[2];
-    const float inv_nd = 1.0f / (float)nD;
-    float ab_acc = 0.f;                      // thread c < 3+N_OUT: running dalpha/dbias column
-    for (int j = 0; j < my_tiles; ++j) {
-      const int tile = (int)cid + j * (int)ncl;
-      if (tid == 0) MHC_BWD_TRACE(0);
-      // Pull the slice of the tile after this one into L2 now (tile 0 too, at
-      // the start), so phase-1 loads see L2 latency and phase 2 re-reads hit.
-      if (tid == 0 && MHC_BWD_PREFETCH > 0) {
-        for (int jt = (j == 0 ? 0 : j + MHC_BWD_PREFETCH); jt <= j + MHC_BWD_PREFETCH && jt < my_tiles; ++jt) {
-          const int pt = (int)cid + jt * (int)ncl;
-          for (int dch = 0; dch < DCH; ++dch) {
-            tma_prefetch_2d(&map_dh, (int)rank * Dc + dch * kBK, pt * kBM);
-            for (int i = 0; i < n; ++i) tma_prefetch_2d(&map_x2d, i * D + (int)rank * Dc + dch * kBK, pt * kBM);
-          }
+  } else if (warp == 3) {
+    // ------------------------------------------------ W3: record producer (one TMA box per tile)
+    if (producer) {
+      const uint64_t pol_keep = l2_policy_evict_last();   // every d-slice of the tile reads it
+      for (int j = 0; j < my_tiles; ++j) {
+        mbar_wait(bar(B::rec_free), (j & 1) ^ 1, wc);
+        if (!*abort_flag) {
+          mbar_arrive_expect_tx(bar(B::rec_full), Cf::REC_BYTES);
+          tma_load_2d(smem_u32(recs), &map_rec, bar(B::rec_full), 0, tile_of(j) * kBM, pol_keep);
         }
       }
-      // (0) small per-token inputs of the tokens this CTA owns, loaded in
-      // parallel now so the owner step reads them from smem.  own_in is free:
-      // the previous tile's owner step finished before its last named barrier.
-      for (int idx = tid; idx < TPO * Cf::OWN_IN; idx += 128) {
-        const int lt = idx / Cf::OWN_IN, f = idx - lt * Cf::OWN_IN;
-        const int64_t t = (int64_t)tile * kBM + (int)rank * TPO + lt;
-        float v = 0.f;
-        if (t < p.T) {
-          if (f < N_OUT) v = __ldg(p.h_mix + t * N_OUT + f);
-          else if (f < N_OUT + n) v = __ldg(p.h_pre + t * n + (f - N_OUT));
-          else if (f < N_OUT + 2 * n) v = __ldg(p.h_post + t * n + (f - N_OUT - n));
-          else if (f < N_OUT + 3 * n) v = __ldg(p.dh_post + t * n + (f - N_OUT - 2 * n));
-          else if (f < N_OUT + 3 * n + n * n) v = __ldg(p.dh_res + t * (n * n) + (f - N_OUT - 3 * n));
-          else v = __ldg(p.inv_rms + t);
-        }
-        own_in[lt * Cf::OWNW + f] = v;
-      }
-      // (1) partial dh_pre of this warp's 32 tokens over the CTA's d-slice
-      float mine[n];
-#pragma unroll
-      for (int i = 0; i < n; ++i) mine[i] = 0.f;
-      for (int tt = 0; tt < 32; tt += 4) {
-        float acc[4][n];
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-#pragma unroll
-          for (int i = 0; i < n; ++i) acc[u][i] = 0.f;
-        for (int e0 = lane * 8; e0 < Dc; e0 += 256) {
-          uint4 g[4], xv[4][n];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int64_t t = (int64_t)tile * kBM + wp * 32 + tt + u;
-            if (t < p.T) {
-              g[u] = ldg_keep(p.dh_in + t * D + (int64_t)rank * Dc + e0, pol_keep);
-#pragma unroll
-              for (int i = 0; i < n; ++i)
-                xv[u][i] = ldg_keep(p.x + t * nD + (int64_t)i * D + (int64_t)rank * Dc + e0, pol_keep);
-            } else {
-              g[u] = make_uint4(0, 0, 0, 0);
-#pragma unroll
-              for (int i = 0; i < n; ++i) xv[u][i] = make_uint4(0, 0, 0, 0);
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            float gf[8];
-            bf16x8_to_f32(g[u], gf);
-#pragma unroll
-            for (int i = 0; i < n; ++i) {
-              float xf[8];
-              bf16x8_to_f32(xv[u][i], xf);
-              float s0 = gf[0] * xf[0], s1 = gf[1] * xf[1];
-              s0 = fmaf(gf[2], xf[2], s0);
-              s1 = fmaf(gf[3], xf[3], s1);
-              s0 = fmaf(gf[4], xf[4], s0);
-              s1 = fmaf(gf[5], xf[5], s1);
-              s0 = fmaf(gf[6], xf[6], s0);
-              s1 = fmaf(gf[7], xf[7], s1);
-              acc[u][i] += s0 + s1;
-            }
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-#pragma unroll
-          for (int i = 0; i < n; ++i) {
-            const float v = warp_sum(acc[u][i]);
-            if (lane == tt + u) mine[i] = v;
-          }
-      }
-      // (2) send my token's partial to its owner
-      if (tid == 0) MHC_BWD_TRACE(1);
-      const int pb = j % RB;
-      const uint32_t pph = (j / RB) & 1;
-      const int row = wp * 32 + lane;
-      mbar_wait<true>(bar(B::p_free + pb), pph ^ 1, wc);
-      {
-        const int owner = row / TPO;
-        const uint32_t dst = mapa_shared(smem_u32(pdh + (pb * kBM + (int)rank * TPO + (row % TPO)) * n), owner);
-#pragma unroll
-        for (int i = 0; i < n; ++i) st_cluster_f32(dst + 4 * i, mine[i]);
-        mbar_arrive_remote(bar(B::p_full + pb), owner);
-      }
-      // (3) owner: reduce the C partials of my TPO tokens in rank order
-      mbar_wait<true>(bar(B::p_full + pb), pph, wc);
-      if (tid == 0) MHC_BWD_TRACE(2);
-      for (int idx = tid; idx < TPO * n; idx += 128) {
-        const int lt = idx / n, i = idx - lt * n;
-        float s = 0.f;
-        for (int src = 0; src < C; ++src) s += pdh[(pb * kBM + src * TPO + lt) * n + i];
-        dhp_s[lt * n + i] = s;
-      }
-      named_sync(1, 128);
-      if (tid < C) mbar_arrive_remote(bar(B::p_free + pb), tid);   // one release per destination CTA
-      // one thread per owned token: dh_mix, c and the dalpha / dbias terms
-      for (int lt = tid; lt < TPO; lt += 128) {
-        const int64_t t = (int64_t)tile * kBM + (int)rank * TPO + lt;
-        const bool valid = t < p.T;
-        const float* oi = own_in + lt * Cf::OWNW;
-        const float ir = oi[Cf::OWN_IN - 1];
-        float dinv = 0.f, dal0 = 0.f, dal1 = 0.f, dal2 = 0.f;
-#pragma unroll
-        for (int jj = 0; jj < N_OUT; ++jj) {
-          const float hm = oi[jj];
-          float g2, tmp;
-          if (jj < n) {
-            const float s = oi[N_OUT + jj] - p.hc_eps;
-            g2 = dhp_s[lt * n + jj] * s * (1.0f - s);
-            tmp = a_pre * g2;
-          } else if (jj < 2 * n) {
-            const float hq = oi[N_OUT + n + (jj - n)];
-            g2 = oi[N_OUT + 2 * n + (jj - n)] * hq * (1.0f - hq / 2.0f);
-            tmp = a_post * g2;
-          } else {
-            g2 = oi[N_OUT + 3 * n + (jj - 2 * n)];
-            tmp = a_res * g2;
-          }
-          if (!valid) g2 = tmp = 0.f;
-          rec_s[lt * RECW + jj] = tmp * ir;                 // dh_mix (golden.py:62)
-          dinv += tmp * hm;                                 // dinv_rms (golden.py:74)
-          const float dal = g2 * (hm * ir);                 // dalpha terms (golden.py:77-79)
-          if (jj < n) dal0 += dal;
-          else if (jj < 2 * n) dal1 += dal;
-          else dal2 += dal;
-          contrib[lt * Cf::CW + 3 + jj] = g2;               // dbias terms (golden.py:83-85)
-        }
-        contrib[lt * Cf::CW + 0] = dal0;
-        contrib[lt * Cf::CW + 1] = dal1;
-        contrib[lt * Cf::CW + 2] = dal2;
-        rec_s[lt * RECW + N_OUT] = valid ? dinv * (ir * ir * ir) * inv_nd : 0.f;   // c (golden.py:89)
-#pragma unroll
-        for (int i = 0; i < n; ++i) rec_s[lt * RECW + N_OUT + 1 + i] = valid ? oi[N_OUT + i] : 0.f;
-        for (int w = N_OUT + 1 + n; w < RECW; ++w) rec_s[lt * RECW + w] = 0.f;
-      }
-      named_sync(1, 128);
-      // running dalpha / dbias columns of this CTA's owned tokens, fixed order
-      if (tid < Cf::CW)
-        for (int lt = 0; lt < TPO; ++lt) ab_acc += contrib[lt * Cf::CW + tid];
-      named_sync(1, 128);
-      // (4) broadcast the records of my tokens to every CTA of the cluster
-      mbar_wait<true>(bar(B::bc_free), (j & 1) ^ 1, wc);
-      for (int idx = tid; idx < TPO * C; idx += 128) {
-        const int lt = idx % TPO, dstc = idx / TPO;
-        const uint32_t dst = mapa_shared(smem_u32(bc + ((int)rank * TPO + lt) * RECW), dstc);
-#pragma unroll
-        for (int w = 0; w < RECW; w += 4)
-          st_cluster_v4_f32(dst + 4 * w, rec_s[lt * RECW + w], rec_s[lt * RECW + w + 1], rec_s[lt * RECW + w + 2],
-                            rec_s[lt * RECW + w + 3]);
-        mbar_arrive_remote(bar(B::bc_full), dstc);
-      }
-      named_sync(1, 128);
-      if (tid == 0) MHC_BWD_TRACE(3);
     }
-    if (tid < Cf::CW) p.abpart[((int64_t)cid * C + rank) * Cf::CW + tid] = ab_acc;
   } else {
     // ------------------------------------------------ WG_E: operands, dx epilogue, G flush
     // 8 warps: two per TMEM lane quadrant; eh selects the half of the columns.
@@ -660,56 +476,66 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int eh = (warp - kWarpE0) >> 2;
     const int row = 32 * q4 + lane;          // token row = TMEM lane
     const bool issuer = (q4 == 0 && lane == 0 && eh == 0);
-    const uint64_t pol_out = l2_policy_evict_first();   // dx must not push out data awaiting re-read
-    uint32_t q = 0, dq = 0, flushes = 0;
-    for (int j = 0; j < my_tiles; ++j) {
-      const int tile = (int)cid + j * (int)ncl;
-      // (a) record -> DHM row of this token (the three bf16 terms of dh_mix)
-      mbar_wait<true>(bar(B::bc_full), j & 1, wc);
-      if (issuer) MHC_BWD_TRACE(4);
-      mbar_wait(bar(B::dhm_free), (j & 1) ^ 1, wc);
-      const float* rec = bc + row * RECW;
-      const float c_t = rec[N_OUT];
-      float hp[n];
+    const uint64_t pol_out = l2_policy_evict_first();
+    // Record of tile jj -> DHM / DHS buffers jj&1 (the bf16 terms of dh_mix);
+    // returns this row's c and h_pre.  Rows past the batch arrive zero-filled.
+    auto build_dhm = [&](int jj, float& c_t, float (&hp)[n]) {
+      mbar_wait(bar(B::rec_full), jj & 1, wc);
+      mbar_wait(bar(B::dhm_free + (jj & 1)), ((jj >> 1) & 1) ^ 1, wc);
+      // row `row` of the swizzled record box: 16-byte chunk c sits at c ^ (row & 7)
+      float rec[RECW];
+      {
+        const uint32_t rb = smem_u32(recs) + row * 128;
+#pragma unroll
+        for (int c = 0; c < RECW / 4; ++c) {
+          const uint4 v = lds128(rb + ((c ^ (row & 7)) << 4));
+          rec[4 * c] = __uint_as_float(v.x);
+          rec[4 * c + 1] = __uint_as_float(v.y);
+          rec[4 * c + 2] = __uint_as_float(v.z);
+          rec[4 * c + 3] = __uint_as_float(v.w);
+        }
+      }
+      uint8_t* dst = dhs + (jj & 1) * Cf::DHS_BYTES;
+      const uint32_t t_row = tmem_dhm + (jj & 1) * Cf::DHM_TCOLS + ((uint32_t)(32 * q4) << 16);
+      c_t = rec[N_OUT];
 #pragma unroll
       for (int i = 0; i < n; ++i) hp[i] = rec[N_OUT + 1 + i];
-      // DHM row: segment e holds term e of dh_mix[0..N_OUT), zero padded to SEGW;
-      // this half writes every other 16-byte chunk of the row.
-#pragma unroll
-      for (int kc0 = 0; kc0 < Cf::KA / 8; kc0 += 2) {
-        const int kc = kc0 + eh;
-        const int e = (kc * 8) / Cf::SEGW, j0 = kc * 8 - e * Cf::SEGW;
-        uint32_t w[4];
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          uint32_t lohi[2];
-#pragma unroll
-          for (int b2 = 0; b2 < 2; ++b2) {
-            const int jj = j0 + h * 2 + b2;
-            lohi[b2] = jj < N_OUT ? split_term(rec[jj], e) : 0;
-          }
-          w[h] = lohi[0] | (lohi[1] << 16);
-        }
-        *reinterpret_cast<uint4*>(dhm + interleave_off(row, kc * 8, Cf::RG_BYTES)) = make_uint4(w[0], w[1], w[2], w[3]);
-      }
+      if (eh == 0) dhm_row_half<n, 0>(rec, dst, row, t_row);
+      else dhm_row_half<n, 1>(rec, dst, row, t_row);
+      tmem_wait_st();
+      tc_fence_before();
       fence_proxy_async_smem();
-      mbar_arrive(bar(B::dhm_full));
-      named_sync(2, kThreadsE);
-      if (issuer) MHC_BWD_TRACE(5);
-      if (q4 == 0 && eh == 0 && lane < C) mbar_arrive_remote(bar(B::bc_free), lane);
-      // (b) dx of every 64-k block of the slice
+      mbar_arrive(bar(B::rec_free));
+      mbar_arrive(bar(B::dhm_full + (jj & 1)));
+    };
+    float c_cur = 0.f, hp_cur[n];
+    if (my_tiles > 0) build_dhm(0, c_cur, hp_cur);
+    uint32_t q = 0, dq = 0, flushes = 0;
+    for (int j = 0; j < my_tiles; ++j) {
+      const int tile = tile_of(j);
+      float c_nxt = 0.f, hp_nxt[n];
+#pragma unroll
+      for (int i = 0; i < n; ++i) hp_nxt[i] = 0.f;
+      if (j + 1 < my_tiles) build_dhm(j + 1, c_nxt, hp_nxt);
+      // dx of every 64-k block of the slice
       for (int dch = 0; dch < DCH; ++dch, ++dq) {
         const int ds = dq % Cf::DS;
         mbar_wait(bar(B::dh_full + ds), (dq / Cf::DS) & 1, wc);
-        const uint32_t dh_row = smem_u32(dhr + ds * Cf::X_BYTES) + row * 128;
+        // this row's dh_in chunks serve all n streams: read once, release the stage
+        uint4 dhv[4];
+        {
+          const uint32_t dh_row = smem_u32(dhr + ds * Cf::X_BYTES) + row * 128;
+#pragma unroll
+          for (int hc = 0; hc < 4; ++hc) dhv[hc] = lds128(dh_row + (((eh * 4 + hc) ^ (row & 7)) << 4));
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B::dh_empty + ds));
         for (int i = 0; i < n; ++i, ++q) {
           const int s = q % Cf::XS;
-          const int dvb = DVB == 2 ? (int)(q & 1) : 0;
-          const uint32_t dvph = DVB == 2 ? (q >> 1) & 1 : q & 1;
+          const int dvb = (int)(q & (uint32_t)(DVB - 1));
+          const uint32_t dvph = (q >> p.dv_shift) & 1;
           mbar_wait(bar(B::x_full + s), (q / Cf::XS) & 1, wc);
-          if (issuer) MHC_BWD_TRACE_Q(5);
           mbar_wait(bar(B::dv_full + dvb), dvph, wc);
-          if (issuer) MHC_BWD_TRACE_Q(6);
           tc_fence_after();
           const uint32_t x_row = smem_u32(xr + s * Cf::X_BYTES) + row * 128;
           const uint32_t gm = smem_u32(gam_s + i * Dc + dch * kBK);
@@ -729,17 +555,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(B::dv_empty + dvb));
-          // the staging buffer is free once the previous TMA store has read it
-          if (issuer) bulk_wait_read0();
+          // staging buffer q&1 is free once the store issued from it two stages
+          // ago has read it (at most one newer store may still be reading)
+          if (issuer) bulk_wait_read1();
           named_sync(2, kThreadsE);
-          const uint32_t st_row = smem_u32(dxs) + row * 128;
+          const uint32_t st_buf = smem_u32(dxs) + (q & 1) * Cf::X_BYTES;
+          const uint32_t st_row = st_buf + row * 128;
 #pragma unroll
           for (int hc = 0; hc < 4; ++hc) {
             const int c = eh * 4 + hc;                // 16-byte chunk 0..7 of the 128-byte row
             const uint32_t sw = (uint32_t)((c ^ (row & 7)) << 4);
             float xf[8], gf[8];
             bf16x8_to_f32(lds128(x_row + sw), xf);
-            bf16x8_to_f32(lds128(dh_row + sw), gf);
+            bf16x8_to_f32(dhv[hc], gf);
             const uint4 ga = lds128(gm + c * 32), gb = lds128(gm + c * 32 + 16);
             const float gam[8] = {__uint_as_float(ga.x), __uint_as_float(ga.y), __uint_as_float(ga.z),
                                   __uint_as_float(ga.w), __uint_as_float(gb.x), __uint_as_float(gb.y),
@@ -747,8 +575,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t o[4];
 #pragma unroll
             for (int e = 0; e < 8; e += 2) {
-              const float d0 = v[hc * 8 + e] * gam[e] + ((-c_t) * xf[e] + hp[i] * gf[e]);
-              const float d1 = v[hc * 8 + e + 1] * gam[e + 1] + ((-c_t) * xf[e + 1] + hp[i] * gf[e + 1]);
+              const float d0 = v[hc * 8 + e] * gam[e] + ((-c_cur) * xf[e] + hp_cur[i] * gf[e]);
+              const float d1 = v[hc * 8 + e + 1] * gam[e + 1] + ((-c_cur) * xf[e + 1] + hp_cur[i] * gf[e + 1]);
               o[e / 2] = (uint32_t)f32_to_bf16_bits(d0) | ((uint32_t)f32_to_bf16_bits(d1) << 16);
             }
             sts128(st_row + sw, make_uint4(o[0], o[1], o[2], o[3]));
@@ -756,28 +584,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async_smem();
           named_sync(2, kThreadsE);
           if (issuer && !*abort_flag) {
-            tma_store_2d(&map_dx, smem_u32(dxs), i * D + (int)rank * Dc + dch * kBK, tile * kBM, pol_out);
+            tma_store_2d(&map_dx, st_buf, i * D + slice * Dc + dch * kBK, tile * kBM, pol_out);
             bulk_commit();
           }
-          if (issuer) MHC_BWD_TRACE_Q(7);
-          if (issuer && dch == 0 && i == 0) MHC_BWD_TRACE(6);
-          if (issuer && dch == DCH - 1 && i == n - 1) MHC_BWD_TRACE(7);
           __syncwarp();
           if (lane == 0) {
             mbar_arrive(bar(B::x_empty + s));
-            if (i == n - 1) mbar_arrive(bar(B::dh_empty + ds));
           }
         }
       }
-      // (c) flush G of the finished group into the per-cluster partial
+      // flush G of the finished group into this token group's partial
       if ((j + 1) % p.FT == 0 || j == my_tiles - 1) {
         mbar_wait(bar(B::g_full), flushes & 1, wc);
         tc_fence_after();
         for (int blk = 0; blk < NPAIR; ++blk) {
           const int dch = blk / (n / 2), i0 = (blk % (n / 2)) * 2;
           const int i = i0 + (row >> 6);
-          const int64_t k = (int64_t)i * D + (int64_t)rank * Dc + dch * kBK + (row & 63);
-          float* gp = p.gpart + (int64_t)cid * N_OUT * nD + k;
+          const int64_t k = (int64_t)i * D + (int64_t)slice * Dc + dch * kBK + (row & 63);
+          float* gp = p.gpart + (int64_t)group * N_OUT * nD + k;
           for (int c16 = eh; c16 < Cf::NG / 16; c16 += 2) {
             float v[16];
             tmem_ld16(tmem_g + blk * Cf::NG + ((uint32_t)(32 * q4) << 16) + c16 * 16, v);
@@ -795,9 +619,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B::g_empty));
-        if (issuer) MHC_BWD_TRACE(8);
         ++flushes;
       }
+      c_cur = c_nxt;
+#pragma unroll
+      for (int i = 0; i < n; ++i) hp_cur[i] = hp_nxt[i];
     }
   }
 
@@ -810,25 +636,40 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
   }
-  cluster_sync_all();
 }
 
 // phi [N_OUT, nD] f32 -> per 64-k block the K-major interleaved image W1
 // reads as the B operand of dvecX: row kk, column e*SEGW + j holds bf16 term
 // e (hi, mid, lo) of phi[j][block*64 + kk]; padding columns are zero.
+// One CTA per 64-k block: the block's phi columns are staged in smem, then
+// each thread writes whole 16-byte chunks, consecutive threads consecutive chunks.
 template <int n>
 __global__ void __launch_bounds__(256) phit_kernel(const float* __restrict__ phi, uint16_t* __restrict__ img,
                                                    int nD) {
   using Cf = Cfg<n>;
-  const int64_t per_block = (int64_t)kBK * Cf::KA;
-  const int64_t total = (int64_t)(nD / kBK) * per_block;
-  for (int64_t idx = blockIdx.x * 256ll + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * 256) {
-    const int64_t blk = idx / per_block;
-    const int r = (int)(idx - blk * per_block);
-    const int kk = r / Cf::KA, ca = r - kk * Cf::KA;
-    const int e = ca / Cf::SEGW, jj = ca - e * Cf::SEGW;
-    const uint16_t v = jj < Cf::N_OUT ? split_term(phi[(int64_t)jj * nD + blk * kBK + kk], e) : 0;
-    img[blk * (Cf::PH_BYTES / 2) + interleave_off(kk, ca, Cf::RG_BYTES) / 2] = v;
+  constexpr int CPR = Cf::KA / 8;                  // 16-byte chunks per image row
+  __shared__ float cols[Cf::N_OUT][kBK + 1];
+  const int blk = blockIdx.x;
+  for (int idx = threadIdx.x; idx < Cf::N_OUT * kBK; idx += 256) {
+    const int j = idx / kBK, kk = idx - j * kBK;
+    cols[j][kk] = __ldg(phi + (int64_t)j * nD + (int64_t)blk * kBK + kk);
+  }
+  __syncthreads();
+  uint8_t* out = reinterpret_cast<uint8_t*>(img) + (size_t)blk * Cf::PH_BYTES;
+  for (int t = threadIdx.x; t < Cf::PH_BYTES / 16; t += 256) {
+    // byte offset 16*t = (kk/8)*RG_BYTES + cc*128 + (kk%8)*16
+    const int grp = t / (8 * CPR), rem = t - grp * 8 * CPR;
+    const int cc = rem >> 3, kk = grp * 8 + (rem & 7);
+    const int e = (cc * 8) / Cf::SEGW, j0 = cc * 8 - e * Cf::SEGW;
+    uint32_t w[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const int ja = j0 + 2 * h, jb = ja + 1;
+      const uint32_t lo = ja < Cf::N_OUT ? split_term(cols[ja][kk], e) : 0;
+      const uint32_t hi = jb < Cf::N_OUT ? split_term(cols[jb][kk], e) : 0;
+      w[h] = lo | (hi << 16);
+    }
+    *reinterpret_cast<uint4*>(out + (size_t)t * 16) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 

@@ -502,21 +502,38 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int n>
 __global__ void __launch_bounds__(256) split_phi_kernel(const float* __restrict__ phi, uint16_t* __restrict__ phis,
                                                         int nD) {
+  // phis [NB][nD]: row term*N_OUT + j holds bf16 term `term` of phi[j]; rows
+  // past NT*N_OUT are zero.  Each thread writes 8 consecutive k (one 16-byte
+  // store); needs nD % 8 == 0.
   using Cf = Cfg<n>;
-  const int64_t total = (int64_t)Cf::NB * nD;
+  const int64_t per_row = nD / 8;
+  const int64_t total = (int64_t)Cf::NB * per_row;
   for (int64_t idx = blockIdx.x * 256ll + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * 256) {
-    const int r = (int)(idx / nD);
-    const int64_t k = idx - (int64_t)r * nD;
-    uint16_t out = 0;
+    const int r = (int)(idx / per_row);
+    const int64_t k = (idx - (int64_t)r * per_row) * 8;
+    uint32_t w[4] = {0, 0, 0, 0};
     if (r < Cf::NT * Cf::N_OUT) {
       const int term = r / Cf::N_OUT, j = r - term * Cf::N_OUT;
-      float rem = phi[(int64_t)j * nD + k];
-      for (int tt = 0; tt <= term; ++tt) {
-        out = f32_to_bf16_bits(rem);
-        rem -= bf16_bits_to_f32(out);
+      const float4 a = __ldg(reinterpret_cast<const float4*>(phi + (int64_t)j * nD + k));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(phi + (int64_t)j * nD + k + 4));
+      const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        uint32_t t2[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          float rem = v[2 * h + q];
+          uint16_t o = 0;
+          for (int tt = 0; tt <= term; ++tt) {
+            o = f32_to_bf16_bits(rem);
+            rem -= bf16_bits_to_f32(o);
+          }
+          t2[q] = o;
+        }
+        w[h] = t2[0] | (t2[1] << 16);
       }
     }
-    phis[idx] = out;
+    *reinterpret_cast<uint4*>(phis + (int64_t)r * nD + k) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 

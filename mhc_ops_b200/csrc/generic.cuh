@@ -203,24 +203,38 @@ __global__ void __launch_bounds__(kThreads) bwd_g_kernel(const uint16_t* __restr
   }
 }
 
-// dphi[j][k] = gamma[k] * sum_p gpart[p][j][k]; dgamma[k] = sum_j phi[j][k] * G[j][k]
-// (dgamma = sum_t x * dvecX_mm of golden.py:93, regrouped: dvecX_mm = dh_mix @ phi).
+// dphi[j][k] = gamma[k] * sum_p gpart[p][j][k]; dgamma[k] = sum_j phi[j][k] * G[j][k].
+// CTA = 32 columns k x 8 row groups (j = jg, jg+8, ...); the 8 dgamma partials
+// are added in a fixed order.  Launch with ceil(nD / kFinCols) CTAs of kThreads.
+constexpr int kFinCols = 32;
 __global__ void __launch_bounds__(kThreads) finalize_param_kernel(const float* __restrict__ gpart, int P, int N,
                                                                   const float* __restrict__ phi,
                                                                   const float* __restrict__ gamma,
                                                                   float* __restrict__ dphi,
                                                                   float* __restrict__ dgamma, int nD) {
-  const int k = blockIdx.x * kThreads + threadIdx.x;
-  if (k >= nD) return;
-  const float gm = gamma ? gamma[k] : 1.0f;
+  constexpr int JG = kThreads / kFinCols;
+  __shared__ float part[JG][kFinCols];
+  const int kk = threadIdx.x % kFinCols, jg = threadIdx.x / kFinCols;
+  const int k = blockIdx.x * kFinCols + kk;
   float dg = 0.f;
-  for (int j = 0; j < N; ++j) {
-    float g = 0.f;
-    for (int p = 0; p < P; ++p) g += gpart[((int64_t)p * N + j) * nD + k];
-    dphi[(int64_t)j * nD + k] = gm * g;
-    dg = fmaf(__ldg(phi + (int64_t)j * nD + k), g, dg);
+  if (k < nD) {
+    const float gm = gamma ? __ldg(gamma + k) : 1.0f;
+    for (int j = jg; j < N; j += JG) {
+      float g = 0.f;
+#pragma unroll 8
+      for (int p = 0; p < P; ++p) g += __ldg(gpart + ((int64_t)p * N + j) * nD + k);
+      dphi[(int64_t)j * nD + k] = gm * g;
+      dg = fmaf(__ldg(phi + (int64_t)j * nD + k), g, dg);
+    }
   }
-  dgamma[k] = dg;
+  part[jg][kk] = dg;
+  __syncthreads();
+  if (jg == 0 && k < nD) {
+    float s = part[0][kk];
+#pragma unroll
+    for (int g2 = 1; g2 < JG; ++g2) s += part[g2][kk];
+    dgamma[k] = s;
+  }
 }
 
 // dalpha / dbias: column c of tokpart [rows][W] summed over rows in a fixed

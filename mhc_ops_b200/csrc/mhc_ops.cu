@@ -1,8 +1,9 @@
 // libmhc_ops: C-ABI entry points of the B200 mHC pre-op (declared in include/mhc_ops.h).
 //
 // Validation, workspace carving and kernel selection live here; the kernels
-// are in generic.cuh (any shape) and fwd_sm100.cuh / bwd_sm100.cuh
-// (tcgen05 + TMA + cluster kernels for the shapes the tensor cores take).
+// are in generic.cuh (any shape), fwd_sm100.cuh / bwd_sm100.cuh (tcgen05 +
+// TMA kernels for the shapes the tensor cores take) and rowdot.cuh (the
+// streaming whole-row kernels beside them).
 
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -21,6 +22,7 @@
 #include "sm100.cuh"
 #include "fwd_sm100.cuh"
 #include "bwd_sm100.cuh"
+#include "rowdot.cuh"
 
 namespace mhc {
 
@@ -133,7 +135,7 @@ struct BwdGeneric {
     dim3 g2((nD + generic::kThreads - 1) / generic::kThreads, L.P);
     generic::bwd_g_kernel<n><<<g2, generic::kThreads, 0, s>>>(a->x, dh_mix, gpart, T, nD, L.tokens_per_split);
     if ((st = after_launch())) return st;
-    generic::finalize_param_kernel<<<(nD + generic::kThreads - 1) / generic::kThreads, generic::kThreads, 0, s>>>(
+    generic::finalize_param_kernel<<<(nD + generic::kFinCols - 1) / generic::kFinCols, generic::kThreads, 0, s>>>(
         gpart, L.P, N, a->phi, a->gamma, a->dphi, a->dgamma, nD);
     if ((st = after_launch())) return st;
     generic::reduce_columns_kernel<<<3 + N, generic::kThreads, 0, s>>>(tokpart, T, 3 + N, a->dalpha, a->dbias);
@@ -154,9 +156,9 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// Row-major bf16 tensor of `rank` dims (dims[0] innermost) -> tiled TMA map.
-int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
-                    const uint32_t* box, CUtensorMapSwizzle swz) {
+// Row-major tensor of `rank` dims (dims[0] innermost) -> tiled TMA map.
+int encode_map(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, int rank, const uint64_t* dims,
+               const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz) {
   auto enc = tensor_map_encoder();
   if (!enc) return MHC_ERR_CUDA;
   cuuint64_t d[5];
@@ -168,10 +170,15 @@ int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t
     es[i] = 1;
     if (i + 1 < rank) st[i] = strides_bytes[i];
   }
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, st, b, es,
+  CUresult r = enc(map, dtype, rank, const_cast<void*>(base), d, st, b, es,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? MHC_OK : MHC_ERR_CUDA;
+}
+
+int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                    const uint32_t* box, CUtensorMapSwizzle swz) {
+  return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, rank, dims, strides_bytes, box, swz);
 }
 
 // ----------------------------------------------------------------- launch plans
@@ -289,7 +296,7 @@ struct FwdTc {
                             &plan)))
       return st;
 
-    fwdtc::split_phi_kernel<n><<<std::min<int64_t>(((int64_t)Cf::NB * nD + 255) / 256, 4 * 148), 256, 0, s>>>(
+    fwdtc::split_phi_kernel<n><<<std::min<int64_t>(((int64_t)Cf::NB * nD / 8 + 255) / 256, 4 * 148), 256, 0, s>>>(
         a->phi, phis, nD);
     if ((st = after_launch())) return st;
 
@@ -357,49 +364,74 @@ int fwd_workspace(int64_t T, int n, int D, size_t* bytes) {
 }
 
 // ----------------------------------------------------------------- tensor-core backward
-// Shapes it takes: n == 4, D a multiple of 256 with a cluster size C in
-// {4, 8, 16} whose slice n*D/C fits the TMEM / smem budget (<= 1792),
+// Two kernels: rowdot::bwd_rows_kernel (whole-row reductions -> one record
+// per token) and bwdtc::bwd_kernel (tcgen05 GEMMs over the records, CTA =
+// d-slice x token group).  Shapes they take: n == 4, D a multiple of 64,
 // 16-byte aligned x / dh_in / dx / phi, T < 2^31.
 constexpr int kBwdN = 4;
+constexpr int kRowsWarps = rowdot::kWarps;
 
-struct BwdTcLayout {
-  size_t phit, gpart, abpart, total;
-  ClusterPlan plan;
-  int dv_bufs;
+struct BwdTcPlan {
+  int Dc = 0;     // d-slice width
+  int S_K = 0;    // d-slices
+  int S_T = 0;    // token groups
+  int dv_shift = 0;   // log2 of the dvecX TMEM buffers
 };
 
-bool bwd_c_allowed(int D, int C) {
+struct BwdTcLayout {
+  size_t phit, rec, gpart, abpart, total;
+  BwdTcPlan plan;
+  int rows_grid;  // CTAs of the row kernel
+};
+
+// Slice width Dc (multiple of 64 dividing D, n*Dc <= MAX_KC) with the least
+// per-CTA work: waves * ceil(tiles / S_T) * Dc, with S_T = sms / S_K token
+// groups; ties go to the wider slice (fewer, longer CTAs).
+BwdTcPlan bwd_tc_plan(int64_t T, int D, int sms) {
   using Cf = bwdtc::Cfg<kBwdN>;
-  if (C < 4) return false;
-  const int kc = kBwdN * D / C;
-  if (kc > Cf::MAX_KC) return false;
-  return 64 + (kc / 128) * Cf::NG <= 512;
+  const int64_t tiles = std::max<int64_t>(1, (T + bwdtc::kBM - 1) / bwdtc::kBM);
+  BwdTcPlan best;
+  double best_cost = 0.0;
+  for (int Dc = 64; Dc * kBwdN <= Cf::MAX_KC; Dc += 64) {
+    if (D % Dc != 0) continue;
+    const int S_K = D / Dc;
+    const int64_t S_T = std::min<int64_t>(std::max(1, sms / S_K), tiles);
+    const int64_t waves = ((int64_t)S_K * S_T + sms - 1) / sms;
+    const double cost = (double)waves * (double)((tiles + S_T - 1) / S_T) * Dc;
+    if (best.Dc == 0 || cost <= best_cost + 1e-9) {
+      best = BwdTcPlan{Dc, S_K, (int)S_T, 0};
+      best_cost = cost;
+    }
+  }
+  best.dv_shift = 1;   // two dvecX buffers (the fixed TMEM layout of bwd_kernel)
+  return best;
 }
 
-int bwd_tc_layout(int64_t T, int D, BwdTcLayout* L) {
+int bwd_rows_grid(int64_t T, int sms) {
+  return (int)std::max<int64_t>(1, std::min<int64_t>(sms, (T + kRowsWarps - 1) / kRowsWarps));
+}
+
+BwdTcLayout bwd_tc_layout(int64_t T, int D, int sms) {
   using Cf = bwdtc::Cfg<kBwdN>;
-  int st = plan_clusters(bwdtc::bwd_kernel<kBwdN>, Cf::SMEM, bwdtc::kThreads, D, (T + bwdtc::kBM - 1) / bwdtc::kBM,
-                         2.0 * bwdtc::kBM * (kBwdN + 1) * D, &L->plan, [D](int C) { return bwd_c_allowed(D, C); });
-  if (st) return st;
-  const int kc = kBwdN * D / L->plan.C;
-  L->dv_bufs = (128 + (kc / 128) * Cf::NG <= 512) ? 2 : 1;
+  BwdTcLayout L{};
+  L.plan = bwd_tc_plan(T, D, sms);
+  L.rows_grid = bwd_rows_grid(T, sms);
   const int64_t nD = (int64_t)kBwdN * D;
   size_t off = kWsHeaderBytes;
-  L->phit = off;
+  L.phit = off;
   off = align_up(off + (size_t)(nD / 64) * Cf::PH_BYTES, kWsAlign);
-  L->gpart = off;
-  off = align_up(off + sizeof(float) * (size_t)L->plan.max_clusters * Cf::N_OUT * nD, kWsAlign);
-  L->abpart = off;
-  off = align_up(off + sizeof(float) * (size_t)L->plan.max_clusters * L->plan.C * (3 + Cf::N_OUT), kWsAlign);
-  L->total = off;
-  return MHC_OK;
+  L.rec = off;
+  off = align_up(off + sizeof(float) * (size_t)T * Cf::RECW, kWsAlign);
+  L.gpart = off;
+  off = align_up(off + sizeof(float) * (size_t)L.plan.S_T * Cf::N_OUT * nD, kWsAlign);
+  L.abpart = off;
+  off = align_up(off + sizeof(float) * (size_t)L.rows_grid * kRowsWarps * Cf::CW, kWsAlign);
+  L.total = off;
+  return L;
 }
 
 bool bwd_tc_shape(int64_t T, int n, int D) {
-  if (n != kBwdN || D % 256 != 0 || T >= ((int64_t)1 << 31)) return false;
-  for (int C : {16, 8, 4})
-    if (D % (64 * C) == 0 && bwd_c_allowed(D, C)) return true;
-  return false;
+  return n == kBwdN && D % 64 == 0 && T < ((int64_t)1 << 31);
 }
 
 bool bwd_tc_eligible(const mhc_bwd_args* a) {
@@ -407,23 +439,29 @@ bool bwd_tc_eligible(const mhc_bwd_args* a) {
          aligned(a->dx, 16) && aligned(a->phi, 16);
 }
 
-int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s) {
+int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s, int sms) {
   using Cf = bwdtc::Cfg<kBwdN>;
   constexpr int n = kBwdN;
+  static_assert(rowdot::Rec<n>::W == Cf::RECW && rowdot::Rec<n>::CW == Cf::CW, "record layouts differ");
   const int64_t T = a->tokens;
   const int D = a->D;
   const int nD = n * D;
-  BwdTcLayout L;
-  int st = bwd_tc_layout(T, D, &L);
-  if (st) return st;
+  const BwdTcLayout L = bwd_tc_layout(T, D, sms);
   char* ws = static_cast<char*>(a->workspace);
+  float* rec = reinterpret_cast<float*>(ws + L.rec);
+  float* gpart = reinterpret_cast<float*>(ws + L.gpart);
+  float* abpart = reinterpret_cast<float*>(ws + L.abpart);
   const int num_tiles = (int)((T + bwdtc::kBM - 1) / bwdtc::kBM);
-  const int nclusters = std::max(1, std::min(L.plan.max_clusters, num_tiles));
+  int st;
 
-  bwdtc::phit_kernel<n><<<4 * 148, 256, 0, s>>>(a->phi, reinterpret_cast<uint16_t*>(ws + L.phit), nD);
+  bwdtc::phit_kernel<n><<<nD / bwdtc::kBK, 256, 0, s>>>(a->phi, reinterpret_cast<uint16_t*>(ws + L.phit), nD);
+  if ((st = after_launch())) return st;
+  rowdot::bwd_rows_kernel<n><<<L.rows_grid, rowdot::kThreads, 0, s>>>(
+      a->x, a->dh_in, a->alpha, a->inv_rms, a->h_mix, a->h_pre, a->h_post, a->dh_post, a->dh_res, rec, abpart, T, D,
+      a->hc_eps);
   if ((st = after_launch())) return st;
 
-  CUtensorMap m_x2d, m_dh, m_dx;
+  CUtensorMap m_x2d, m_dh, m_dx, m_rec;
   {
     const uint64_t dims[2] = {(uint64_t)nD, (uint64_t)T};
     const uint64_t strides[1] = {(uint64_t)nD * 2};
@@ -437,62 +475,43 @@ int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s) {
     const uint32_t box[2] = {bwdtc::kBK, bwdtc::kBM};
     if ((st = encode_bf16_map(&m_dh, a->dh_in, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
+  {
+    const uint64_t dims[2] = {(uint64_t)Cf::RECW, (uint64_t)T};
+    const uint64_t strides[1] = {(uint64_t)Cf::RECW * 4};
+    const uint32_t box[2] = {(uint32_t)Cf::RECW, bwdtc::kBM};
+    if ((st = encode_map(&m_rec, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rec, 2, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
+  }
   bwdtc::Params p;
-  p.x = a->x;
-  p.dh_in = a->dh_in;
-  p.alpha = a->alpha;
-  p.inv_rms = a->inv_rms;
-  p.h_mix = a->h_mix;
-  p.h_pre = a->h_pre;
-  p.h_post = a->h_post;
-  p.dh_post = a->dh_post;
-  p.dh_res = a->dh_res;
   p.gamma = a->gamma;
   p.phit = reinterpret_cast<const uint8_t*>(ws + L.phit);
-  p.dx = a->dx;
-  p.gpart = reinterpret_cast<float*>(ws + L.gpart);
-  p.abpart = reinterpret_cast<float*>(ws + L.abpart);
+  p.gpart = gpart;
   p.status = reinterpret_cast<int*>(ws);
   p.T = T;
   p.D = D;
-  p.C = L.plan.C;
-  p.Dc = D / L.plan.C;
+  p.Dc = L.plan.Dc;
+  p.S_K = L.plan.S_K;
+  p.S_T = L.plan.S_T;
   p.num_tiles = num_tiles;
   p.FT = 4;
-  p.dv_bufs = L.dv_bufs;
-  p.hc_eps = a->hc_eps;
+  p.dv_shift = L.plan.dv_shift;
 
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(nclusters * L.plan.C);
-  cfg.blockDim = dim3(bwdtc::kThreads);
-  cfg.dynamicSmemBytes = Cf::SMEM;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = L.plan.C;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  MHC_CUDA_TRY(cudaLaunchKernelEx(&cfg, bwdtc::bwd_kernel<n>, m_x2d, m_dh, m_dx, p));
+  MHC_CUDA_TRY(cudaFuncSetAttribute(bwdtc::bwd_kernel<n>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM));
+  bwdtc::bwd_kernel<n><<<L.plan.S_K * L.plan.S_T, bwdtc::kThreads, Cf::SMEM, s>>>(m_x2d, m_dh, m_dx, m_rec, p);
   if ((st = after_launch())) return st;
 
-  generic::finalize_param_kernel<<<(nD + generic::kThreads - 1) / generic::kThreads, generic::kThreads, 0, s>>>(
-      p.gpart, nclusters, Cf::N_OUT, a->phi, a->gamma, a->dphi, a->dgamma, nD);
+  generic::finalize_param_kernel<<<(nD + generic::kFinCols - 1) / generic::kFinCols, generic::kThreads, 0, s>>>(
+      gpart, L.plan.S_T, Cf::N_OUT, a->phi, a->gamma, a->dphi, a->dgamma, nD);
   if ((st = after_launch())) return st;
   generic::reduce_columns_kernel<<<3 + Cf::N_OUT, generic::kThreads, 0, s>>>(
-      p.abpart, (int64_t)nclusters * L.plan.C, 3 + Cf::N_OUT, a->dalpha, a->dbias);
+      abpart, (int64_t)L.rows_grid * kRowsWarps, 3 + Cf::N_OUT, a->dalpha, a->dbias);
   return after_launch();
 }
 
 int bwd_workspace(int64_t T, int n, int D, int sms, size_t* bytes) {
   size_t b = bwd_generic_layout(T, n, D, sms).total;
-  if (bwd_tc_shape(T, n, D)) {
-    BwdTcLayout L;
-    int st = bwd_tc_layout(T, D, &L);
-    if (st) return st;
-    b = std::max(b, L.total);
-  }
+  if (bwd_tc_shape(T, n, D)) b = std::max(b, bwd_tc_layout(T, D, sms).total);
   *bytes = b;
   return MHC_OK;
 }
@@ -626,7 +645,7 @@ int mhc_bwd(const mhc_bwd_args* a, void* stream) {
       !aligned(a->dh_post, 4) || !aligned(a->dh_res, 4) || !aligned(a->gamma, 4) || !aligned(a->dphi, 4) ||
       !aligned(a->dalpha, 4) || !aligned(a->dbias, 4) || !aligned(a->dgamma, 4))
     return MHC_ERR_MISALIGNED;
-  if (bwd_tc_eligible(a)) return bwd_tc_run(a, s);
+  if (bwd_tc_eligible(a)) return bwd_tc_run(a, s, sms);
   return dispatch_n<BwdGeneric>(a->n, a, s, sms);
 }
 
@@ -669,10 +688,12 @@ int mhc_query_plan(int which, int64_t tokens, int32_t n, int32_t D, int* path, i
     if (st) return st;
     *path = 1;
   } else if (which == 1 && bwd_tc_shape(tokens, n, D)) {
-    BwdTcLayout L;
-    if ((st = bwd_tc_layout(tokens, D, &L))) return st;
-    plan = L.plan;
+    // no clusters: report the grid as S_T token groups of S_K d-slice CTAs
+    const BwdTcPlan bp = bwd_tc_plan(tokens, D, sms);
     *path = 1;
+    *cluster_size = bp.S_K;
+    *clusters = bp.S_T;
+    return MHC_OK;
   } else if (which != 0 && which != 1) {
     return MHC_ERR_BAD_SHAPE;
   }

@@ -1,0 +1,242 @@
+// Streaming per-token kernels of the mHC pre-op that need whole token rows
+// and no tensor cores: the first half of the backward (B1) and the h_in pass
+// of the forward (F2).  Pure HBM streams: warps own whole tokens, every load
+// is 512 contiguous bytes per warp, many loads in flight per lane.
+#pragma once
+
+#include "common.cuh"
+
+namespace mhc {
+namespace rowdot {
+
+constexpr int kWarps = 16;
+constexpr int kThreads = kWarps * 32;
+
+template <int n>
+struct Rec {
+  static constexpr int N_OUT = n * n + 2 * n;
+  static constexpr int W = ((N_OUT + 1 + n) + 3) / 4 * 4;   // record width in floats
+  static constexpr int CW = 3 + N_OUT;                       // dalpha / dbias columns
+};
+
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 v;
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void bf16x8(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+// B1: per token t (src/backward/golden.py:51-62, 74, 77-86, 89):
+//   dh_pre[i] = sum_d dh_in[d] x[i,d]; dh_pre2, dh_post2; dh_mix = tmp * inv_rms;
+//   c = (sum_j tmp_j h_mix_j) inv_rms^3 / nD
+// writes rec[t] = {dh_mix[0..N), c, h_pre[0..n), 0...} and, per warp, the
+// running dalpha (3) and dbias (N) sums of its tokens to abpart[warp][CW].
+// Token t is owned by global warp t % W, so every sum has a fixed order.
+// Needs D % 8 == 0 and 16-byte aligned x / dh_in.
+template <int n>
+__global__ void __launch_bounds__(kThreads, 1) bwd_rows_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ dh_in, const float* __restrict__ alpha,
+    const float* __restrict__ inv_rms, const float* __restrict__ h_mix, const float* __restrict__ h_pre,
+    const float* __restrict__ h_post, const float* __restrict__ dh_post, const float* __restrict__ dh_res,
+    float* __restrict__ rec, float* __restrict__ abpart, int64_t T, int D, float hc_eps) {
+  using R = Rec<n>;
+  constexpr int N_OUT = R::N_OUT;
+  constexpr int M = (N_OUT + 31) / 32;   // output columns per lane
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int64_t W = (int64_t)gridDim.x * kWarps;
+  const int nD = n * D;
+  const float inv_nd = 1.0f / (float)nD;
+  const float a_pre = alpha[0], a_post = alpha[1], a_res = alpha[2];
+  float acc_al0 = 0.f, acc_al1 = 0.f, acc_al2 = 0.f;   // lane 0
+  float acc_b[M];                                      // lane l: dbias[l + 32 m]
+#pragma unroll
+  for (int m = 0; m < M; ++m) acc_b[m] = 0.f;
+
+  for (int64_t t = gw; t < T; t += W) {
+    // small per-token inputs first, so they are in flight during the row stream
+    float hm[M], gin[M], dpo[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const int jj = lane + 32 * m;
+      hm[m] = gin[m] = dpo[m] = 0.f;
+      if (jj < N_OUT) {
+        hm[m] = __ldg(h_mix + t * N_OUT + jj);
+        if (jj < n) {
+          gin[m] = __ldg(h_pre + t * n + jj);
+        } else if (jj < 2 * n) {
+          gin[m] = __ldg(h_post + t * n + (jj - n));
+          dpo[m] = __ldg(dh_post + t * n + (jj - n));
+        } else {
+          gin[m] = __ldg(dh_res + t * (n * n) + (jj - 2 * n));
+        }
+      }
+    }
+    const float ir = __ldg(inv_rms + t);
+
+    const uint16_t* xr = x + t * nD;
+    const uint16_t* gr = dh_in + t * D;
+    float p[n];
+#pragma unroll
+    for (int i = 0; i < n; ++i) p[i] = 0.f;
+    constexpr int U = 4;   // 256-element chunks in flight per lane
+    for (int c0 = 0; c0 < D; c0 += 256 * U) {
+      uint4 g[U], xv[U][n];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int d = c0 + u * 256 + lane * 8;
+        if (d < D) {
+          g[u] = ldg_stream(gr + d);
+#pragma unroll
+          for (int i = 0; i < n; ++i) xv[u][i] = ldg_stream(xr + i * D + d);
+        } else {
+          g[u] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+          for (int i = 0; i < n; ++i) xv[u][i] = make_uint4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        float gf[8];
+        bf16x8(g[u], gf);
+#pragma unroll
+        for (int i = 0; i < n; ++i) {
+          float xf[8];
+          bf16x8(xv[u][i], xf);
+          float s0 = gf[0] * xf[0], s1 = gf[1] * xf[1];
+          s0 = fmaf(gf[2], xf[2], s0);
+          s1 = fmaf(gf[3], xf[3], s1);
+          s0 = fmaf(gf[4], xf[4], s0);
+          s1 = fmaf(gf[5], xf[5], s1);
+          s0 = fmaf(gf[6], xf[6], s0);
+          s1 = fmaf(gf[7], xf[7], s1);
+          p[i] += s0 + s1;
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < n; ++i) p[i] = warp_sum(p[i]);
+
+    float* rt = rec + t * R::W;
+    float dinv = 0.f, dal0 = 0.f, dal1 = 0.f, dal2 = 0.f;
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const int jj = lane + 32 * m;
+      if (jj < N_OUT) {
+        float g2, tmp;
+        if (jj < n) {
+          float dp = p[0];
+#pragma unroll
+          for (int i = 1; i < n; ++i)
+            if (jj == i) dp = p[i];
+          const float s = gin[m] - hc_eps;
+          g2 = dp * s * (1.0f - s);                 // golden.py:54
+          tmp = a_pre * g2;
+        } else if (jj < 2 * n) {
+          const float hq = gin[m];
+          g2 = dpo[m] * hq * (1.0f - hq / 2.0f);    // golden.py:55
+          tmp = a_post * g2;
+        } else {
+          g2 = gin[m];
+          tmp = a_res * g2;
+        }
+        rt[jj] = tmp * ir;                          // dh_mix (golden.py:62)
+        acc_b[m] += g2;                             // dbias terms (golden.py:83-85)
+        const float dal = g2 * (hm[m] * ir);        // dalpha terms (golden.py:77-79)
+        if (jj < n) dal0 += dal;
+        else if (jj < 2 * n) dal1 += dal;
+        else dal2 += dal;
+        dinv += tmp * hm[m];
+      }
+    }
+    dinv = warp_sum(dinv);                          // golden.py:74
+    dal0 = warp_sum(dal0);
+    dal1 = warp_sum(dal1);
+    dal2 = warp_sum(dal2);
+    if (lane == 0) {
+      rt[N_OUT] = dinv * (ir * ir * ir) * inv_nd;   // c (golden.py:89)
+      acc_al0 += dal0;
+      acc_al1 += dal1;
+      acc_al2 += dal2;
+    }
+    for (int w = N_OUT + 1 + lane; w < R::W; w += 32)
+      rt[w] = (w - N_OUT - 1 < n) ? __ldg(h_pre + t * n + (w - N_OUT - 1)) : 0.f;
+  }
+  float* ap = abpart + gw * R::CW;
+  if (lane == 0) {
+    ap[0] = acc_al0;
+    ap[1] = acc_al1;
+    ap[2] = acc_al2;
+  }
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    const int jj = lane + 32 * m;
+    if (jj < N_OUT) ap[3 + jj] = acc_b[m];
+  }
+}
+
+// F2: h_in[t, d] = bf16(sum_i h_pre[t,i] x[t,i,d])  (src/forward/golden.py:62-63).
+// Task = (token, 8 consecutive d); consecutive threads take consecutive d.
+template <int n>
+__global__ void __launch_bounds__(kThreads) h_in_kernel(const uint16_t* __restrict__ x,
+                                                        const float* __restrict__ h_pre,
+                                                        uint16_t* __restrict__ h_in, int64_t T, int D) {
+  const int64_t per_tok = D / 8;
+  const int64_t tasks = T * per_tok;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  constexpr int U = 4;
+  for (int64_t base = (int64_t)blockIdx.x * kThreads + threadIdx.x; base < tasks; base += stride * U) {
+    uint4 xv[U][n];
+    float hp[U][n];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t task = base + u * stride;
+      if (task < tasks) {
+        const int64_t t = task / per_tok;
+        const int d = (int)(task - t * per_tok) * 8;
+#pragma unroll
+        for (int i = 0; i < n; ++i) {
+          xv[u][i] = ldg_stream(x + (t * n + i) * D + d);
+          hp[u][i] = __ldg(h_pre + t * n + i);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t task = base + u * stride;
+      if (task < tasks) {
+        const int64_t t = task / per_tok;
+        const int d = (int)(task - t * per_tok) * 8;
+        float acc[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+#pragma unroll
+        for (int i = 0; i < n; ++i) {
+          float f[8];
+          bf16x8(xv[u][i], f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] = fmaf(hp[u][i], f[e], acc[e]);
+        }
+        uint4 o;
+        o.x = (uint32_t)f32_to_bf16_bits(acc[0]) | ((uint32_t)f32_to_bf16_bits(acc[1]) << 16);
+        o.y = (uint32_t)f32_to_bf16_bits(acc[2]) | ((uint32_t)f32_to_bf16_bits(acc[3]) << 16);
+        o.z = (uint32_t)f32_to_bf16_bits(acc[4]) | ((uint32_t)f32_to_bf16_bits(acc[5]) << 16);
+        o.w = (uint32_t)f32_to_bf16_bits(acc[6]) | ((uint32_t)f32_to_bf16_bits(acc[7]) << 16);
+        *reinterpret_cast<uint4*>(h_in + t * D + d) = o;
+      }
+    }
+  }
+}
+
+}  // namespace rowdot
+}  // namespace mhc
