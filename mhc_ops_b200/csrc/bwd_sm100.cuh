@@ -17,20 +17,24 @@
 //   * W3 loads the tile's records (TMA, 16 KB); W0 streams the slice's x
 //     blocks [128 tok x 64 k] and dh_in blocks (TMA, 128-B swizzle); W2 streams
 //     the pre-laid-out split-phi images (3 bf16 terms of phi per k);
-//   * WG_E turns the records into the dh_mix operands: DHM, the 3 bf16 terms
-//     (hi, mid, lo) of dh_mix per token, each segment padded to a multiple of
-//     16, written to tensor memory (A of dvecX, so the per-stage MMAs read no
-//     A bytes from shared memory), and DHS, the hi and mid terms, in shared
-//     memory (B of G).  Both are double buffered: tile j+1's are built during
-//     tile j;
-//   * W1 issues tcgen05.mma: dvecX = sum over 6 (dh term, phi term) products
-//     (smallest first: m.M, l.H, h.L, m.H, h.M, h.H; exact to ~2^-23 in the
-//     fp32 sum) per 64-k block (M=128 tok, N=64, K=segment) and
-//     G += x^T . DHS (M=128 k, N=segment, K=2x128 tokens; x read MN-major
-//     straight from two adjacent TMA stages, DHS read MN-major);
-//   * WG_E reads dvecX (TMEM lane = token) and writes dx through a TMA store;
-//     every FT tiles it flushes G from TMEM into the group's partial (single
-//     writer per address, fixed order).
+//   * WG_E turns the records into the UMMA operand DHM [128 tok x 3 segments]:
+//     the 3 bf16 terms (hi, mid, lo) of dh_mix, each segment padded to a
+//     multiple of 16 (double buffered: tile j+1's DHM is built during tile j);
+//   * W1 issues tcgen05.mma per pair of stages (streams 2ip, 2ip+1 of a
+//     64-k chunk): dvecX = dh_mix @ (phi * gamma) (gamma folded into the
+//     split-phi images, so the epilogue has no gamma term) as one N=128
+//     accumulation over the two stacked images, the sum over 6 (dh term, phi
+//     term) products (smallest first: m.M, l.H, h.L, m.H, h.M, h.H; exact to
+//     ~2^-23 in the fp32 sum), M=128 tok, K=segment; and G += x^T . DHM over
+//     the hi and mid terms (M=128 k, N=segment, K=2x128 tokens; x read
+//     MN-major straight from the two TMA stages, DHM read MN-major).  Wide
+//     MMAs matter here: a tcgen05.mma costs ~45-65 cycles to issue whatever
+//     its N, so an N=128 MMA does twice the work of an N=64 one for the same
+//     time;
+//   * WG_E reads dvecX (TMEM lane = token) and writes dx through a TMA store
+//     (two warp groups take alternate stages); every FT tiles it flushes G
+//     from TMEM into the group's partial (single writer per address, fixed
+//     order).
 #pragma once
 
 #include "common.cuh"
@@ -51,7 +55,7 @@ using namespace sm100;
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kWarpE0 = 4;          // first epilogue warp
-constexpr int kThreadsE = 8 * 32;   // WG_E: 8 warps, two per TMEM lane quadrant
+constexpr int kThreadsE = 8 * 32;   // WG_E: 8 warps, two groups of one warp per TMEM lane quadrant
 constexpr int kThreads = kWarpE0 * 32 + kThreadsE;   // W0, W1, W2, W3, WG_E(8)
 constexpr int kSmemLimit = 232448;
 
@@ -64,36 +68,33 @@ struct Cfg {
   static constexpr int KA = 3 * SEGW;                    // DHM / phi-image row: 3 term segments
   static constexpr int RG_BYTES = (KA / 8) * 128;        // one 8-row group of a K-major interleaved image
   static constexpr int PH_BYTES = 8 * RG_BYTES;          // split-phi image of one 64-k block
-  static constexpr int DHM_TCOLS = KA / 2;               // TMEM columns of one DHM buffer (bf16 pairs)
-  static constexpr int KA_G = 2 * SEGW;                  // DHS row: hi and mid segments
-  static constexpr int RG_G = (KA_G / 8) * 128;          // one 8-row group of DHS
-  static constexpr int DHS_BYTES = 16 * RG_G;            // 128 token rows
-  static constexpr int G_COLS_MAX = 256;                 // TMEM: G [0,256), dvecX [256,384), DHM [384,480)
-  static constexpr int NG = SEGW;                        // G accumulator columns
+  static constexpr int DHM_BYTES = 16 * RG_BYTES;        // 128 token rows
+  static constexpr int NG = SEGW;                        // G accumulator columns per 128-k block
   static constexpr int X_BYTES = kBM * 128;
-  static constexpr int XS = 4;                           // x ring (2 adjacent pairs)
-  static constexpr int DS = 2;
-  static constexpr int PS = 3;
+  static constexpr int XS = 4;                           // x ring: two stage pairs
+  static constexpr int DS = 1;                           // dh_in (held in registers for its n stages)
+  static constexpr int PS = 4;                           // phi-image ring: two stage pairs
   static constexpr int RECW = round_up(N_OUT + 1 + n, 4);   // record: dh_mix, c, h_pre, pad
   static constexpr int REC_BYTES = kBM * RECW * 4;
   static constexpr int MAX_KC = 1024;                    // d-slice * n per CTA
   static constexpr int CW = 3 + N_OUT;                   // dalpha / dbias columns
+  // tensor memory: G [0, 256), dvecX of a stage pair in two buffers [256, 512)
+  static constexpr int G_COLS = 256;
+  static constexpr int DV_COLS = 2 * kBK;
 
   static constexpr int smem_bytes() {
-    return 1024 + XS * X_BYTES + DS * X_BYTES + PS * PH_BYTES + 2 * DHS_BYTES + 2 * X_BYTES /*dx staging*/ +
-           MAX_KC * 4 /*gamma slice*/ + REC_BYTES + 512;
+    return 1024 + XS * X_BYTES + DS * X_BYTES + PS * PH_BYTES + 2 * DHM_BYTES + 2 * X_BYTES /*dx staging*/ +
+           REC_BYTES + 512;
   }
   static constexpr int SMEM = smem_bytes();
   static_assert(SMEM <= kSmemLimit, "backward tile does not fit in shared memory");
-  static_assert(n % 2 == 0, "G pairs two streams of a d-chunk");
+  static_assert(n % 2 == 0, "stages pair two streams of a d-chunk");
   static_assert(RECW == 32, "records are loaded as one 128-byte swizzled row per token");
-  static_assert(SEGW == 32, "a DHM half covers 16 of the 32 columns of each segment");
-  static_assert((MAX_KC / 128) * NG <= G_COLS_MAX && G_COLS_MAX + 2 * 64 + 2 * DHM_TCOLS <= 512, "TMEM budget");
+  static_assert((MAX_KC / 128) * NG <= G_COLS && G_COLS + 2 * DV_COLS <= 512, "TMEM budget");
 };
 
 struct Params {
-  const float* gamma;     // may be null
-  const uint8_t* phit;    // split-phi images, PH_BYTES per 64-k block
+  const uint8_t* phit;    // split images of phi * gamma, PH_BYTES per 64-k block
   float* gpart;           // [S_T][N_OUT][nD]
   int* status;
   int64_t T;
@@ -103,7 +104,6 @@ struct Params {
   int S_T;                // token groups
   int num_tiles;
   int FT;                 // tiles per G flush
-  int dv_shift;           // log2 of the dvecX TMEM buffers (1, 2 or 4 buffers of 64 columns)
 };
 
 template <int n>
@@ -113,11 +113,11 @@ struct Bars {
   static constexpr int x_empty = x_full + Cf::XS;
   static constexpr int dh_full = x_empty + Cf::XS;
   static constexpr int dh_empty = dh_full + Cf::DS;
-  static constexpr int ph_full = dh_empty + Cf::DS;
-  static constexpr int ph_empty = ph_full + Cf::PS;
-  static constexpr int dv_full = ph_empty + Cf::PS;
-  static constexpr int dv_empty = dv_full + 4;
-  static constexpr int dhm_full = dv_empty + 4;
+  static constexpr int ph_full = dh_empty + Cf::DS;      // per image pair
+  static constexpr int ph_empty = ph_full + 2;
+  static constexpr int dv_full = ph_empty + 2;           // per dvecX buffer (stage pair)
+  static constexpr int dv_empty = dv_full + 2;
+  static constexpr int dhm_full = dv_empty + 2;
   static constexpr int dhm_free = dhm_full + 2;
   static constexpr int g_full = dhm_free + 2;
   static constexpr int g_empty = g_full + 1;
@@ -156,7 +156,7 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t sr
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
@@ -202,33 +202,25 @@ __device__ __forceinline__ uint16_t split_term(float v, int term) {
   return out;
 }
 
-// One token's dh_mix operands from its record.  DHM (tensor memory, A of
-// dvecX): lane `row`, columns [16e, 16e+16) of the buffer hold bf16 term e of
-// dh_mix[0..SEGW), two per column.  DHS (shared memory, B of G): K-major
-// interleaved row `row`, segments e = 0, 1.  Half EH covers j in
-// [16 EH, 16 EH + 16); the partner warp writes the other half.
+// One token's DHM row from its record: segment e holds bf16 term e of
+// dh_mix[0..N_OUT), zero padded to SEGW (K-major interleaved image).  Half EH
+// writes the 16-byte chunks kc = EH, EH+2, ... of the row; the partner warp
+// of the other epilogue group writes the rest.
 template <int n, int EH>
-__device__ __forceinline__ void dhm_row_half(const float (&rec)[Cfg<n>::RECW], uint8_t* dhs, int row,
-                                             uint32_t t_row) {
+__device__ __forceinline__ void dhm_row_half(const float (&rec)[Cfg<n>::RECW], uint8_t* dst, int row) {
   using Cf = Cfg<n>;
-  constexpr int J0 = 16 * EH;
 #pragma unroll
-  for (int e = 0; e < 3; ++e) {
-    uint32_t w[8];
+  for (int kc = EH; kc < Cf::KA / 8; kc += 2) {
+    const int e = (kc * 8) / Cf::SEGW, j0 = kc * 8 - e * Cf::SEGW;
+    uint32_t w[4];
 #pragma unroll
-    for (int h = 0; h < 8; ++h) {
-      const int ja = J0 + 2 * h, jb = ja + 1;
+    for (int h = 0; h < 4; ++h) {
+      const int ja = j0 + 2 * h, jb = ja + 1;
       const uint32_t lo = ja < Cf::N_OUT ? split_term(rec[ja < Cf::N_OUT ? ja : 0], e) : 0;
       const uint32_t hi = jb < Cf::N_OUT ? split_term(rec[jb < Cf::N_OUT ? jb : 0], e) : 0;
       w[h] = lo | (hi << 16);
     }
-    tmem_st8(t_row + e * (Cf::SEGW / 2) + EH * 8, w);
-    if (e < 2) {
-      *reinterpret_cast<uint4*>(dhs + interleave_off(row, e * Cf::SEGW + J0, Cf::RG_G)) =
-          make_uint4(w[0], w[1], w[2], w[3]);
-      *reinterpret_cast<uint4*>(dhs + interleave_off(row, e * Cf::SEGW + J0 + 8, Cf::RG_G)) =
-          make_uint4(w[4], w[5], w[6], w[7]);
-    }
+    *reinterpret_cast<uint4*>(dst + interleave_off(row, kc * 8, Cf::RG_BYTES)) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
@@ -241,17 +233,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   using B = Bars<n>;
   constexpr int N_OUT = Cf::N_OUT;
   constexpr int RECW = Cf::RECW;
+  constexpr int NP = n / 2;                              // stage pairs per d-chunk
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* xr = smem;                                  // XS x blocks (pairs adjacent)
   uint8_t* dhr = xr + Cf::XS * Cf::X_BYTES;            // DS dh_in blocks
-  uint8_t* phr = dhr + Cf::DS * Cf::X_BYTES;           // PS split-phi images
-  uint8_t* dhs = phr + Cf::PS * Cf::PH_BYTES;          // 2 x DHS (hi, mid terms of dh_mix): B of G
-  uint8_t* dxs = dhs + 2 * Cf::DHS_BYTES;              // 2 x dx staging [128 tok x 64] (128-B swizzle)
+  uint8_t* phr = dhr + Cf::DS * Cf::X_BYTES;           // PS split-phi images (pairs adjacent)
+  uint8_t* dhm = phr + Cf::PS * Cf::PH_BYTES;          // 2 x DHM: A of dvecX, B of G
+  uint8_t* dxs = dhm + 2 * Cf::DHM_BYTES;              // 2 x dx staging [128 tok x 64] (128-B swizzle)
   float* recs = reinterpret_cast<float*>(dxs + 2 * Cf::X_BYTES);    // [128][RECW] records, 128-B swizzle
-  float* gam_s = recs + kBM * RECW;                    // [n][Dc] gamma slice
-  uint64_t* bars = reinterpret_cast<uint64_t*>(gam_s + Cf::MAX_KC);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(recs + kBM * RECW);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + B::count);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -265,34 +257,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nD = n * D;
   const int KC = n * Dc;
   const int NPAIR = KC / 128;                 // G blocks of 128 k per CTA
-  const int DVB = 1 << p.dv_shift;
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   // Tiles run last-first, so the first ones re-read what the row kernel read last.
   auto tile_of = [&](int j) { return p.num_tiles - 1 - (group + j * p.S_T); };
 
-  // gamma slice of this CTA: gam_s[i*Dc + dd] = gamma[i*D + slice*Dc + dd]
-  for (int idx = threadIdx.x; idx < KC; idx += kThreads) {
-    const int i = idx / Dc, dd = idx - i * Dc;
-    gam_s[idx] = p.gamma ? p.gamma[(int64_t)i * D + (int64_t)slice * Dc + dd] : 1.0f;
-  }
   if (threadIdx.x == 0) {
     for (int i = 0; i < Cf::XS; ++i) {
       mbar_init(bar(B::x_full + i), 1);
-      mbar_init(bar(B::x_empty + i), 1 + kThreadsE / 32);
+      mbar_init(bar(B::x_empty + i), 1 + kThreadsE / 64);   // G commit + the stage's epilogue group
     }
     for (int i = 0; i < Cf::DS; ++i) {
       mbar_init(bar(B::dh_full + i), 1);
       mbar_init(bar(B::dh_empty + i), kThreadsE / 32);
     }
-    for (int i = 0; i < Cf::PS; ++i) {
+    for (int i = 0; i < 2; ++i) {
       mbar_init(bar(B::ph_full + i), 32);   // one cp.async arrival per lane of W2
       mbar_init(bar(B::ph_empty + i), 1);
-    }
-    for (int i = 0; i < 4; ++i) {
       mbar_init(bar(B::dv_full + i), 1);
-      mbar_init(bar(B::dv_empty + i), kThreadsE / 32);
-    }
-    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(B::dv_empty + i), kThreadsE / 32);    // both groups read their stage of the pair
       mbar_init(bar(B::dhm_full + i), kThreadsE);
       mbar_init(bar(B::dhm_free + i), 1);
     }
@@ -317,9 +299,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t tmem_g = tmem_base;                                  // NPAIR x NG columns
-  const uint32_t tmem_dv = tmem_base + Cf::G_COLS_MAX;                // DVB x 64 columns
-  const uint32_t tmem_dhm = tmem_base + Cf::G_COLS_MAX + 2 * 64;      // 2 x DHM_TCOLS columns
+  const uint32_t tmem_g = tmem_base;                        // NPAIR x NG columns
+  const uint32_t tmem_dv = tmem_base + Cf::G_COLS;          // 2 x DV_COLS: dvecX of a stage pair
   const WaitCtx wc{abort_flag, p.status};
   const int my_tiles = group < p.num_tiles ? (p.num_tiles - 1 - group) / p.S_T + 1 : 0;
   const bool producer = (lane == 0);
@@ -365,10 +346,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------ W1: tcgen05.mma issuer
+    // Per stage pair (streams 2ip, 2ip+1 of a d-chunk): dvecX as one N=128
+    // accumulation over the two stacked phi images, then G over the x pair.
+    // Descriptors are built once and advanced by adding (bytes >> 4) to their
+    // start-address field.
     if (producer) {
-      constexpr uint32_t idesc_dv = idesc_bf16_f32(kBM, kBK, false, false);
+      constexpr uint32_t idesc_dv = idesc_bf16_f32(kBM, 2 * kBK, false, false);
       constexpr uint32_t idesc_g = idesc_bf16_f32(kBM, Cf::NG, true, true);
-      uint32_t q = 0, flushes = 0;
+      uint32_t pq = 0, flushes = 0;
       for (int j = 0; j < my_tiles; ++j) {
         const int hb = j & 1;
         mbar_wait(bar(B::dhm_full + hb), (j >> 1) & 1, wc);
@@ -378,54 +363,48 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_wait(bar(B::g_empty), (flushes - 1) & 1, wc);   // previous G group read out
           tc_fence_after();
         }
-        const uint32_t dhm_t = tmem_dhm + hb * Cf::DHM_TCOLS;
-        const uint32_t dhs_a = smem_u32(dhs + hb * Cf::DHS_BYTES);
+        const uint32_t dhm_a = smem_u32(dhm + hb * Cf::DHM_BYTES);
+        const uint64_t a_dv = desc_kmajor_interleave(dhm_a, 128, Cf::RG_BYTES);      // DHM, K-major
+        const uint64_t b_g = desc_kmajor_interleave(dhm_a, Cf::RG_BYTES, 128);       // DHM read MN-major
         for (int dch = 0; dch < DCH; ++dch) {
-          for (int i = 0; i < n; ++i, ++q) {
-            const int s = q % Cf::XS;
-            const int ps = q % Cf::PS;
-            const int dvb = (int)(q & (uint32_t)(DVB - 1));
-            const uint32_t dvph = (q >> p.dv_shift) & 1;
-            mbar_wait(bar(B::ph_full + ps), (q / Cf::PS) & 1, wc);
-            mbar_wait(bar(B::dv_empty + dvb), dvph ^ 1, wc);
+          for (int ip = 0; ip < NP; ++ip, ++pq) {
+            const int pb = (int)(pq & 1);
+            mbar_wait(bar(B::ph_full + pb), (pq >> 1) & 1, wc);
+            mbar_wait(bar(B::dv_empty + pb), ((pq >> 1) & 1) ^ 1, wc);
             tc_fence_after();
             if (!*abort_flag) {
-              const uint32_t ph_a = smem_u32(phr + ps * Cf::PH_BYTES);
+              const uint64_t b_dv = desc_kmajor_interleave(smem_u32(phr + pb * 2 * Cf::PH_BYTES), 128, Cf::RG_BYTES);
+              const uint32_t d = tmem_dv + pb * Cf::DV_COLS;
 #pragma unroll
               for (int pr = 0; pr < 6; ++pr) {
 #pragma unroll
                 for (int ks = 0; ks < Cf::SEGW / 16; ++ks) {
-                  const uint32_t ca = (prod_a_term(pr) * Cf::SEGW + ks * 16) / 2;   // TMEM column
+                  const uint32_t ca = (prod_a_term(pr) * Cf::SEGW + ks * 16) * 16;
                   const uint32_t cb = (prod_b_term(pr) * Cf::SEGW + ks * 16) * 16;
-                  umma_bf16_ta(tmem_dv + dvb * 64, dhm_t + ca, desc_kmajor_interleave(ph_a + cb, 128, Cf::RG_BYTES),
-                               idesc_dv, pr != 0 || ks != 0);
+                  umma_bf16(d, a_dv + (ca >> 4), b_dv + (cb >> 4), idesc_dv, pr != 0 || ks != 0);
                 }
               }
-              umma_commit(bar(B::ph_empty + ps));
-              umma_commit(bar(B::dv_full + dvb));
+              umma_commit(bar(B::ph_empty + pb));
+              umma_commit(bar(B::dv_full + pb));
             }
-            if (i & 1) {
-              // G over the pair of stages (s-1, s): rows 0..63 stream i-1, 64..127 stream i
-              mbar_wait(bar(B::x_full + s - 1), ((q - 1) / Cf::XS) & 1, wc);
-              mbar_wait(bar(B::x_full + s), (q / Cf::XS) & 1, wc);
-              tc_fence_after();
-              if (!*abort_flag) {
-                const int blk = dch * (n / 2) + i / 2;
-                const uint32_t xa = smem_u32(xr + (s - 1) * Cf::X_BYTES);
-#pragma unroll 1
-                for (int e = 1; e >= 0; --e) {            // mid, hi terms of dh_mix (G needs ~2^-17)
+            // G over the x pair: rows 0..63 stream 2ip, 64..127 stream 2ip+1
+            const uint32_t q0 = 2 * pq;
+            const int s0 = (int)(q0 % Cf::XS);
+            mbar_wait(bar(B::x_full + s0), (q0 / Cf::XS) & 1, wc);
+            mbar_wait(bar(B::x_full + s0 + 1), ((q0 + 1) / Cf::XS) & 1, wc);
+            tc_fence_after();
+            if (!*abort_flag) {
+              const uint32_t d = tmem_g + (dch * NP + ip) * Cf::NG;
+              const uint64_t a_g = desc_mnmajor_sw128(smem_u32(xr + s0 * Cf::X_BYTES), Cf::X_BYTES, 1024);
 #pragma unroll
-                  for (int ks = 0; ks < kBM / 16; ++ks) {
-                    const uint64_t ad = desc_mnmajor_sw128(xa + ks * 2048, Cf::X_BYTES, 1024);
-                    // DHS read MN-major: N = the SEGW columns of term e, K = tokens
-                    const uint64_t bd =
-                        desc_kmajor_interleave(dhs_a + e * Cf::SEGW * 16 + ks * 2 * Cf::RG_G, Cf::RG_G, 128);
-                    umma_bf16(tmem_g + blk * Cf::NG, ad, bd, idesc_g, !(g_restart && e == 1 && ks == 0));
-                  }
-                }
-                umma_commit(bar(B::x_empty + s - 1));
-                umma_commit(bar(B::x_empty + s));
+              for (int e = 1; e >= 0; --e) {            // mid, hi terms of dh_mix (G needs ~2^-17)
+#pragma unroll
+                for (int ks = 0; ks < kBM / 16; ++ks)
+                  umma_bf16(d, a_g + ((ks * 2048) >> 4), b_g + ((e * Cf::SEGW * 16 + ks * 2 * Cf::RG_BYTES) >> 4),
+                            idesc_g, !(g_restart && e == 1 && ks == 0));
               }
+              umma_commit(bar(B::x_empty + s0));
+              umma_commit(bar(B::x_empty + s0 + 1));
             }
           }
         }
@@ -437,23 +416,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 2) {
-    // ------------------------------------------------ W2: split-phi image producer
-    // The whole warp copies each image with 16-byte cp.async (LSU path), so the
-    // TMA engine only carries x, dh_in, the records and the dx stores.
-    uint32_t q = 0;
+    // ------------------------------------------------ W2: split-phi image producer (one pair at a time)
+    // The whole warp copies the two images with 16-byte cp.async (LSU path), so
+    // the TMA engine only carries x, dh_in, the records and the dx stores.
+    uint32_t pq = 0;
     for (int j = 0; j < my_tiles; ++j) {
       for (int dch = 0; dch < DCH; ++dch) {
-        for (int i = 0; i < n; ++i, ++q) {
-          const int ps = q % Cf::PS;
-          const int k0 = i * D + slice * Dc + dch * kBK;
-          mbar_wait(bar(B::ph_empty + ps), ((q / Cf::PS) & 1) ^ 1, wc);
+        for (int ip = 0; ip < NP; ++ip, ++pq) {
+          const int pb = (int)(pq & 1);
+          mbar_wait(bar(B::ph_empty + pb), ((pq >> 1) & 1) ^ 1, wc);
           if (!*abort_flag) {
-            const uint8_t* src = p.phit + (size_t)(k0 / kBK) * Cf::PH_BYTES;
-            const uint32_t dst = smem_u32(phr + ps * Cf::PH_BYTES);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int k0 = (2 * ip + h) * D + slice * Dc + dch * kBK;
+              const uint8_t* src = p.phit + (size_t)(k0 / kBK) * Cf::PH_BYTES;
+              const uint32_t dst = smem_u32(phr + (pb * 2 + h) * Cf::PH_BYTES);
 #pragma unroll 4
-            for (int off = lane * 16; off < Cf::PH_BYTES; off += 32 * 16) cp_async16(dst + off, src + off);
+              for (int off = lane * 16; off < Cf::PH_BYTES; off += 32 * 16) cp_async16(dst + off, src + off);
+            }
           }
-          cp_async_arrive_noinc(bar(B::ph_full + ps));   // fires when this lane's copies have landed
+          cp_async_arrive_noinc(bar(B::ph_full + pb));   // fires when this lane's copies have landed
         }
       }
     }
@@ -471,13 +453,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------ WG_E: operands, dx epilogue, G flush
-    // 8 warps: two per TMEM lane quadrant; eh selects the half of the columns.
+    // 8 warps: two groups of four, one warp per TMEM lane quadrant each.  The
+    // dx epilogue ping-pongs: group eh takes the stages q with q & 1 == eh
+    // (columns eh*64.. of the pair's dvecX buffer, its own staging buffer),
+    // so one group's TMEM -> smem -> TMA-store chain overlaps the other's.
+    // For the DHM rows and the G flush eh selects the half of the columns.
     const int q4 = warp & 3;
     const int eh = (warp - kWarpE0) >> 2;
     const int row = 32 * q4 + lane;          // token row = TMEM lane
-    const bool issuer = (q4 == 0 && lane == 0 && eh == 0);
+    const bool issuer = (q4 == 0 && lane == 0);   // one per group
     const uint64_t pol_out = l2_policy_evict_first();
-    // Record of tile jj -> DHM / DHS buffers jj&1 (the bf16 terms of dh_mix);
+    // Record of tile jj -> DHM buffer jj&1 (the three bf16 terms of dh_mix);
     // returns this row's c and h_pre.  Rows past the batch arrive zero-filled.
     auto build_dhm = [&](int jj, float& c_t, float (&hp)[n]) {
       mbar_wait(bar(B::rec_full), jj & 1, wc);
@@ -495,15 +481,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           rec[4 * c + 3] = __uint_as_float(v.w);
         }
       }
-      uint8_t* dst = dhs + (jj & 1) * Cf::DHS_BYTES;
-      const uint32_t t_row = tmem_dhm + (jj & 1) * Cf::DHM_TCOLS + ((uint32_t)(32 * q4) << 16);
+      uint8_t* dst = dhm + (jj & 1) * Cf::DHM_BYTES;
       c_t = rec[N_OUT];
 #pragma unroll
       for (int i = 0; i < n; ++i) hp[i] = rec[N_OUT + 1 + i];
-      if (eh == 0) dhm_row_half<n, 0>(rec, dst, row, t_row);
-      else dhm_row_half<n, 1>(rec, dst, row, t_row);
-      tmem_wait_st();
-      tc_fence_before();
+      if (eh == 0) dhm_row_half<n, 0>(rec, dst, row);
+      else dhm_row_half<n, 1>(rec, dst, row);
       fence_proxy_async_smem();
       mbar_arrive(bar(B::rec_free));
       mbar_arrive(bar(B::dhm_full + (jj & 1)));
@@ -521,76 +504,78 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int dch = 0; dch < DCH; ++dch, ++dq) {
         const int ds = dq % Cf::DS;
         mbar_wait(bar(B::dh_full + ds), (dq / Cf::DS) & 1, wc);
-        // this row's dh_in chunks serve all n streams: read once, release the stage
-        uint4 dhv[4];
+        // this row's dh_in chunks serve the group's streams: read once, release
+        uint4 dhv[8];
         {
           const uint32_t dh_row = smem_u32(dhr + ds * Cf::X_BYTES) + row * 128;
 #pragma unroll
-          for (int hc = 0; hc < 4; ++hc) dhv[hc] = lds128(dh_row + (((eh * 4 + hc) ^ (row & 7)) << 4));
+          for (int c = 0; c < 8; ++c) dhv[c] = lds128(dh_row + ((c ^ (row & 7)) << 4));
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B::dh_empty + ds));
         for (int i = 0; i < n; ++i, ++q) {
+          if ((int)(q & 1) != eh) continue;          // the other group's stage
           const int s = q % Cf::XS;
-          const int dvb = (int)(q & (uint32_t)(DVB - 1));
-          const uint32_t dvph = (q >> p.dv_shift) & 1;
+          const uint32_t pq = q >> 1;
+          const int pb = (int)(pq & 1);
           mbar_wait(bar(B::x_full + s), (q / Cf::XS) & 1, wc);
-          mbar_wait(bar(B::dv_full + dvb), dvph, wc);
+          mbar_wait(bar(B::dv_full + pb), (pq >> 1) & 1, wc);
           tc_fence_after();
           const uint32_t x_row = smem_u32(xr + s * Cf::X_BYTES) + row * 128;
-          const uint32_t gm = smem_u32(gam_s + i * Dc + dch * kBK);
-          float v[32];
-          {
-            float v0[16], v1[16];
-            const uint32_t ta = tmem_dv + dvb * 64 + ((uint32_t)(32 * q4) << 16) + eh * 32;
-            tmem_ld16(ta, v0);
-            tmem_ld16(ta + 16, v1);
-            tmem_wait_ld();
+          const uint32_t st_buf = smem_u32(dxs) + eh * Cf::X_BYTES;
+          const uint32_t st_row = st_buf + row * 128;
+          float hpi = hp_cur[0];   // h_pre of stream i (selects keep hp_cur in registers)
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              v[e] = v0[e];
-              v[16 + e] = v1[e];
+          for (int k = 1; k < n; ++k)
+            if (i == k) hpi = hp_cur[k];
+          // this group's staging buffer is free once its previous store has read it
+          if (issuer) bulk_wait_read0();
+          named_sync(2 + eh, kThreadsE / 2);
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {           // 32 columns at a time
+            float v[32];
+            {
+              float v0[16], v1[16];
+              const uint32_t ta = tmem_dv + pb * Cf::DV_COLS + ((uint32_t)(32 * q4) << 16) + eh * kBK + hf * 32;
+              tmem_ld16(ta, v0);
+              tmem_ld16(ta + 16, v1);
+              uint4 xv[4];
+#pragma unroll
+              for (int hc = 0; hc < 4; ++hc) xv[hc] = lds128(x_row + (((hf * 4 + hc) ^ (row & 7)) << 4));
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                v[e] = v0[e];
+                v[16 + e] = v1[e];
+              }
+#pragma unroll
+              for (int hc = 0; hc < 4; ++hc) {
+                const int c = hf * 4 + hc;             // 16-byte chunk 0..7 of the 128-byte row
+                float xf[8], gf[8];
+                bf16x8_to_f32(xv[hc], xf);
+                bf16x8_to_f32(dhv[c], gf);
+                uint32_t o[4];
+#pragma unroll
+                for (int e = 0; e < 8; e += 2) {
+                  const float d0 = v[hc * 8 + e] + ((-c_cur) * xf[e] + hpi * gf[e]);
+                  const float d1 = v[hc * 8 + e + 1] + ((-c_cur) * xf[e + 1] + hpi * gf[e + 1]);
+                  o[e / 2] = pack_bf16x2(d0, d1);
+                }
+                sts128(st_row + (uint32_t)((c ^ (row & 7)) << 4), make_uint4(o[0], o[1], o[2], o[3]));
+              }
             }
           }
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar(B::dv_empty + dvb));
-          // staging buffer q&1 is free once the store issued from it two stages
-          // ago has read it (at most one newer store may still be reading)
-          if (issuer) bulk_wait_read1();
-          named_sync(2, kThreadsE);
-          const uint32_t st_buf = smem_u32(dxs) + (q & 1) * Cf::X_BYTES;
-          const uint32_t st_row = st_buf + row * 128;
-#pragma unroll
-          for (int hc = 0; hc < 4; ++hc) {
-            const int c = eh * 4 + hc;                // 16-byte chunk 0..7 of the 128-byte row
-            const uint32_t sw = (uint32_t)((c ^ (row & 7)) << 4);
-            float xf[8], gf[8];
-            bf16x8_to_f32(lds128(x_row + sw), xf);
-            bf16x8_to_f32(dhv[hc], gf);
-            const uint4 ga = lds128(gm + c * 32), gb = lds128(gm + c * 32 + 16);
-            const float gam[8] = {__uint_as_float(ga.x), __uint_as_float(ga.y), __uint_as_float(ga.z),
-                                  __uint_as_float(ga.w), __uint_as_float(gb.x), __uint_as_float(gb.y),
-                                  __uint_as_float(gb.z), __uint_as_float(gb.w)};
-            uint32_t o[4];
-#pragma unroll
-            for (int e = 0; e < 8; e += 2) {
-              const float d0 = v[hc * 8 + e] * gam[e] + ((-c_cur) * xf[e] + hp_cur[i] * gf[e]);
-              const float d1 = v[hc * 8 + e + 1] * gam[e + 1] + ((-c_cur) * xf[e + 1] + hp_cur[i] * gf[e + 1]);
-              o[e / 2] = (uint32_t)f32_to_bf16_bits(d0) | ((uint32_t)f32_to_bf16_bits(d1) << 16);
-            }
-            sts128(st_row + sw, make_uint4(o[0], o[1], o[2], o[3]));
-          }
+          if (lane == 0) mbar_arrive(bar(B::dv_empty + pb));
           fence_proxy_async_smem();
-          named_sync(2, kThreadsE);
+          named_sync(2 + eh, kThreadsE / 2);
           if (issuer && !*abort_flag) {
             tma_store_2d(&map_dx, st_buf, i * D + slice * Dc + dch * kBK, tile * kBM, pol_out);
             bulk_commit();
           }
           __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(bar(B::x_empty + s));
-          }
+          if (lane == 0) mbar_arrive(bar(B::x_empty + s));
         }
       }
       // flush G of the finished group into this token group's partial
@@ -598,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(bar(B::g_full), flushes & 1, wc);
         tc_fence_after();
         for (int blk = 0; blk < NPAIR; ++blk) {
-          const int dch = blk / (n / 2), i0 = (blk % (n / 2)) * 2;
+          const int dch = blk / NP, i0 = (blk % NP) * 2;
           const int i = i0 + (row >> 6);
           const int64_t k = (int64_t)i * D + (int64_t)slice * Dc + dch * kBK + (row & 63);
           float* gp = p.gpart + (int64_t)group * N_OUT * nD + k;
@@ -628,8 +613,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // ---------------------------------------------------------------- teardown
-  if (warp >= kWarpE0 && lane == 0 && (warp & 3) == 0 && ((warp - kWarpE0) >> 2) == 0)
-    bulk_wait_all0();   // the dx stores this thread issued have completed
+  if (warp >= kWarpE0 && lane == 0 && (warp & 3) == 0)
+    bulk_wait_all0();   // the dx stores this thread (one issuer per epilogue group) issued have completed
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -638,21 +623,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// phi [N_OUT, nD] f32 -> per 64-k block the K-major interleaved image W1
-// reads as the B operand of dvecX: row kk, column e*SEGW + j holds bf16 term
-// e (hi, mid, lo) of phi[j][block*64 + kk]; padding columns are zero.
+// phi [N_OUT, nD] f32, gamma [nD] (NULL = ones) -> per 64-k block the K-major
+// interleaved image W1 reads as the B operand of dvecX: row kk, column
+// e*SEGW + j holds bf16 term e (hi, mid, lo) of phi[j][k] * gamma[k],
+// k = block*64 + kk; padding columns are zero.
 // One CTA per 64-k block: the block's phi columns are staged in smem, then
 // each thread writes whole 16-byte chunks, consecutive threads consecutive chunks.
 template <int n>
-__global__ void __launch_bounds__(256) phit_kernel(const float* __restrict__ phi, uint16_t* __restrict__ img,
-                                                   int nD) {
+__global__ void __launch_bounds__(256) phit_kernel(const float* __restrict__ phi, const float* __restrict__ gamma,
+                                                   uint16_t* __restrict__ img, int nD) {
   using Cf = Cfg<n>;
   constexpr int CPR = Cf::KA / 8;                  // 16-byte chunks per image row
   __shared__ float cols[Cf::N_OUT][kBK + 1];
   const int blk = blockIdx.x;
   for (int idx = threadIdx.x; idx < Cf::N_OUT * kBK; idx += 256) {
     const int j = idx / kBK, kk = idx - j * kBK;
-    cols[j][kk] = __ldg(phi + (int64_t)j * nD + (int64_t)blk * kBK + kk);
+    const int64_t k = (int64_t)blk * kBK + kk;
+    cols[j][kk] = __ldg(phi + (int64_t)j * nD + k) * (gamma ? __ldg(gamma + k) : 1.0f);
   }
   __syncthreads();
   uint8_t* out = reinterpret_cast<uint8_t*>(img) + (size_t)blk * Cf::PH_BYTES;

@@ -52,6 +52,13 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(f));
 }
 
+// Two floats -> packed bf16x2 bits (lo in the low half), round-to-nearest-even,
+// one conversion instruction for both.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 __device__ __forceinline__ float sigmoidf_(float v) { return 1.0f / (1.0f + __expf(-v)); }
 
 // Exact-ish sigmoid using the accurate expf (the gates feed fp32 outputs that

@@ -132,12 +132,6 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
   }
 }
 
-__device__ __forceinline__ void st_global_evict_first(void* ptr, uint4 v, uint64_t pol) {
-  asm volatile("st.global.L2::cache_hint.v4.u32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(ptr), "r"(v.x), "r"(v.y), "r"(v.z),
-               "r"(v.w), "l"(pol)
-               : "memory");
-}
-
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
@@ -470,11 +464,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int64_t tok = (int64_t)tile * kBM + trow;
             if (tok < p.T) {
               uint4 o;
-              o.x = (uint32_t)f32_to_bf16_bits(acc[0]) | ((uint32_t)f32_to_bf16_bits(acc[1]) << 16);
-              o.y = (uint32_t)f32_to_bf16_bits(acc[2]) | ((uint32_t)f32_to_bf16_bits(acc[3]) << 16);
-              o.z = (uint32_t)f32_to_bf16_bits(acc[4]) | ((uint32_t)f32_to_bf16_bits(acc[5]) << 16);
-              o.w = (uint32_t)f32_to_bf16_bits(acc[6]) | ((uint32_t)f32_to_bf16_bits(acc[7]) << 16);
-              st_global_evict_first(p.h_in + tok * D + (int)rank * Dc + dch * kBK + c * 8, o, pol_out);
+              o.x = pack_bf16x2(acc[0], acc[1]);
+              o.y = pack_bf16x2(acc[2], acc[3]);
+              o.z = pack_bf16x2(acc[4], acc[5]);
+              o.w = pack_bf16x2(acc[6], acc[7]);
+              st_global_hint(p.h_in + tok * D + (int)rank * Dc + dch * kBK + c * 8, o, pol_out);
             }
           }
           __syncwarp();

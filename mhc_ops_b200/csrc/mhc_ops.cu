@@ -375,7 +375,6 @@ struct BwdTcPlan {
   int Dc = 0;     // d-slice width
   int S_K = 0;    // d-slices
   int S_T = 0;    // token groups
-  int dv_shift = 0;   // log2 of the dvecX TMEM buffers
 };
 
 struct BwdTcLayout {
@@ -399,11 +398,10 @@ BwdTcPlan bwd_tc_plan(int64_t T, int D, int sms) {
     const int64_t waves = ((int64_t)S_K * S_T + sms - 1) / sms;
     const double cost = (double)waves * (double)((tiles + S_T - 1) / S_T) * Dc;
     if (best.Dc == 0 || cost <= best_cost + 1e-9) {
-      best = BwdTcPlan{Dc, S_K, (int)S_T, 0};
+      best = BwdTcPlan{Dc, S_K, (int)S_T};
       best_cost = cost;
     }
   }
-  best.dv_shift = 1;   // two dvecX buffers (the fixed TMEM layout of bwd_kernel)
   return best;
 }
 
@@ -454,7 +452,8 @@ int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s, int sms) {
   const int num_tiles = (int)((T + bwdtc::kBM - 1) / bwdtc::kBM);
   int st;
 
-  bwdtc::phit_kernel<n><<<nD / bwdtc::kBK, 256, 0, s>>>(a->phi, reinterpret_cast<uint16_t*>(ws + L.phit), nD);
+  bwdtc::phit_kernel<n><<<nD / bwdtc::kBK, 256, 0, s>>>(a->phi, a->gamma, reinterpret_cast<uint16_t*>(ws + L.phit),
+                                                        nD);
   if ((st = after_launch())) return st;
   rowdot::bwd_rows_kernel<n><<<L.rows_grid, rowdot::kThreads, 0, s>>>(
       a->x, a->dh_in, a->alpha, a->inv_rms, a->h_mix, a->h_pre, a->h_post, a->dh_post, a->dh_res, rec, abpart, T, D,
@@ -484,7 +483,6 @@ int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s, int sms) {
       return st;
   }
   bwdtc::Params p;
-  p.gamma = a->gamma;
   p.phit = reinterpret_cast<const uint8_t*>(ws + L.phit);
   p.gpart = gpart;
   p.status = reinterpret_cast<int*>(ws);
@@ -495,7 +493,6 @@ int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s, int sms) {
   p.S_T = L.plan.S_T;
   p.num_tiles = num_tiles;
   p.FT = 4;
-  p.dv_shift = L.plan.dv_shift;
 
   MHC_CUDA_TRY(cudaFuncSetAttribute(bwdtc::bwd_kernel<n>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM));
   bwdtc::bwd_kernel<n><<<L.plan.S_K * L.plan.S_T, bwdtc::kThreads, Cf::SMEM, s>>>(m_x2d, m_dh, m_dx, m_rec, p);

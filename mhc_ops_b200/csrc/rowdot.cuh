@@ -228,10 +228,10 @@ __global__ void __launch_bounds__(kThreads) h_in_kernel(const uint16_t* __restri
           for (int e = 0; e < 8; ++e) acc[e] = fmaf(hp[u][i], f[e], acc[e]);
         }
         uint4 o;
-        o.x = (uint32_t)f32_to_bf16_bits(acc[0]) | ((uint32_t)f32_to_bf16_bits(acc[1]) << 16);
-        o.y = (uint32_t)f32_to_bf16_bits(acc[2]) | ((uint32_t)f32_to_bf16_bits(acc[3]) << 16);
-        o.z = (uint32_t)f32_to_bf16_bits(acc[4]) | ((uint32_t)f32_to_bf16_bits(acc[5]) << 16);
-        o.w = (uint32_t)f32_to_bf16_bits(acc[6]) | ((uint32_t)f32_to_bf16_bits(acc[7]) << 16);
+        o.x = pack_bf16x2(acc[0], acc[1]);
+        o.y = pack_bf16x2(acc[2], acc[3]);
+        o.z = pack_bf16x2(acc[4], acc[5]);
+        o.w = pack_bf16x2(acc[6], acc[7]);
         *reinterpret_cast<uint4*>(h_in + t * D + d) = o;
       }
     }

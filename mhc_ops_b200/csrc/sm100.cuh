@@ -88,13 +88,15 @@ struct WaitCtx {
   int* status;           // global device status word (workspace header)
 };
 
+// The clock is read once every 256 polls (the common case, a wait that ends
+// within a few polls, reads it never).
 template <bool kClusterScope = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtx& w) {
   if (*w.abort) return false;
   uint64_t t0 = 0;
   for (uint32_t spin = 0;; ++spin) {
 #pragma unroll 1
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < 256; ++i) {
       const bool ok = kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
       if (ok) return true;
     }
@@ -146,6 +148,13 @@ __device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int32_t 
   asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
                "r"(c0), "r"(c1)
+               : "memory");
+}
+
+// 16-byte global store with an L2 eviction-priority hint.
+__device__ __forceinline__ void st_global_hint(void* ptr, uint4 v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.v4.u32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(ptr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w), "l"(pol)
                : "memory");
 }
 
