@@ -284,14 +284,20 @@ def run_ours(args):
     launches = _lib.launch_count() - launches0
     clk = clocks.stop() if rank == 0 else None
 
-    # per-call durations (separate pass, same work, events between the calls)
+    # per-call durations (separate pass, same work, events between the calls).  No
+    # synchronize inside the loop: the host stays ahead of the GPU, so each pair of
+    # events brackets device time only, not the host's enqueue of the next call.
     fwd_ms, bwd_ms = [], []
-    for _ in range(max(3, args.steps)):
+    step_evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(max(3, args.steps))]
+    sync_all()
+    for evs in step_evs:
+        ev = evs
         ev[0].record()
         step()
-        torch.cuda.synchronize()
-        fwd_ms.append(ev[0].elapsed_time(ev[1]))
-        bwd_ms.append(ev[1].elapsed_time(ev[2]))
+    torch.cuda.synchronize()
+    for evs in step_evs:
+        fwd_ms.append(evs[0].elapsed_time(evs[1]))
+        bwd_ms.append(evs[1].elapsed_time(evs[2]))
     fwd_ms = max_over_ranks(statistics.median(fwd_ms))
     bwd_ms = max_over_ranks(statistics.median(bwd_ms))
 
