@@ -172,11 +172,12 @@ MHC_API int mhc_read_device_status(void* workspace, void* stream, int* device_st
 
 /* Launch plan the library uses for this shape on the current device:
  * *path = 0 generic kernels, 1 tensor-core kernels.  which = 0 forward: for
- * path 1, *cluster_size CTAs per thread-block cluster and *clusters
- * co-resident clusters (the persistent grid).  which = 1 backward: for path
- * 1, the tensor-core kernel's grid is *clusters token groups of
- * *cluster_size d-slice CTAs each (plain CTAs, no thread-block clusters).
- * No counterpart in the reference (its Triton grids are fixed per call). */
+ * path 1, *cluster_size is the number of K-slices the projection is split
+ * into and *clusters the CTAs of its persistent grid.  which = 1 backward:
+ * for path 1, the tensor-core kernel's grid is *clusters token groups of
+ * *cluster_size d-slice CTAs each.  (No kernel uses thread-block clusters;
+ * the parameter names are kept for ABI stability.)  No counterpart in the
+ * reference (its Triton grids are fixed per call). */
 MHC_API int mhc_query_plan(int which, int64_t tokens, int32_t n, int32_t D, int* path, int* cluster_size,
                            int* clusters);
 

@@ -13,9 +13,9 @@
 #include <cstdio>
 #include <string>
 
-#include <map>
 #include <mutex>
-#include <tuple>
+#include <set>
+#include <utility>
 
 #include "common.cuh"
 #include "generic.cuh"
@@ -181,97 +181,38 @@ int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t
   return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, rank, dims, strides_bytes, box, swz);
 }
 
-// ----------------------------------------------------------------- launch plans
-struct ClusterPlan {
-  int C = 0;             // cluster size
-  int max_clusters = 0;  // co-resident clusters on this device
-};
-
-// Cluster size for a persistent cluster kernel: among the C (<= 16, dividing
-// D/64, allowed by the kernel) pick the one with the least work per CTA,
-// ceil(tiles / clusters) / C tile-units, where clusters = min(co-resident
-// clusters, tiles); ties go to the larger C (shorter L2 re-read distance).
-#ifndef MHC_MAX_CLUSTER
-#define MHC_MAX_CLUSTER 16   // largest cluster size the planner considers (build-time)
-#endif
-inline bool any_cluster(int) { return true; }
-
-// The kernels re-read each tile's slice from L2 one tile after its first
-// read, so the bytes of all concurrently processed tiles (tile_bytes each)
-// must stay L2-resident; plans whose footprint exceeds kL2BudgetBytes count
-// double (their re-reads would come from HBM).
-constexpr double kL2BudgetBytes = 48.0 * 1024 * 1024;
-
-template <typename Kernel, typename Allowed = bool (*)(int)>
-int plan_clusters(Kernel kernel, int smem, int threads, int D, int64_t tiles, double tile_bytes, ClusterPlan* out,
-                  Allowed allowed = any_cluster) {
+// ----------------------------------------------------------------- launch helpers
+// Raise a kernel's dynamic shared memory limit once per (device, kernel).
+template <typename Kernel>
+int set_smem_limit_once(Kernel kernel, int bytes) {
   static std::mutex mu;
-  static std::map<std::tuple<int, const void*, int>, std::map<int, int>> cache;   // -> {C: max clusters}
+  static std::set<std::pair<int, const void*>> done;
   int dev = 0;
   MHC_CUDA_TRY(cudaGetDevice(&dev));
-  const auto key = std::make_tuple(dev, reinterpret_cast<const void*>(kernel), D);
-  std::map<int, int> occ;
-  bool have = false;
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    auto it = cache.find(key);
-    if (it != cache.end()) {
-      occ = it->second;
-      have = true;
-    }
-  }
-  if (!have) {
-    MHC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    MHC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-    for (int C : {16, 8, 4, 2, 1}) {
-      if (D % (64 * C) != 0) continue;
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(C);
-      cfg.blockDim = dim3(threads);
-      cfg.dynamicSmemBytes = smem;
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = C;
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      int ncl = 0;
-      if (cudaOccupancyMaxActiveClusters(&ncl, kernel, &cfg) != cudaSuccess) {
-        cudaGetLastError();
-        ncl = 0;
-      }
-      occ[C] = ncl;
-    }
-    std::lock_guard<std::mutex> lk(mu);
-    cache[key] = occ;
-  }
-  ClusterPlan best;
-  double best_cost = 0.0;
-  tiles = std::max<int64_t>(tiles, 1);
-  for (int C : {16, 8, 4, 2, 1}) {
-    auto it = occ.find(C);
-    if (C > MHC_MAX_CLUSTER || it == occ.end() || it->second <= 0 || !allowed(C)) continue;
-    const int64_t ncl = std::min<int64_t>(it->second, tiles);
-    double cost = (double)((tiles + ncl - 1) / ncl) / C;
-    if ((double)ncl * tile_bytes > kL2BudgetBytes) cost *= 2.0;
-    if (best.C == 0 || cost < best_cost - 1e-9) {
-      best = ClusterPlan{C, it->second};
-      best_cost = cost;
-    }
-  }
-  if (best.C == 0) return MHC_ERR_CUDA;
-  *out = best;
+  const auto key = std::make_pair(dev, reinterpret_cast<const void*>(kernel));
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.count(key)) return MHC_OK;
+  MHC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.insert(key);
   return MHC_OK;
 }
 
 // ----------------------------------------------------------------- tensor-core forward
-// Shapes it takes: n in {4, 8}, D a multiple of 64, 16-byte aligned x / h_in,
-// T < 2^31.  Everything else runs the generic kernels.
+// Two kernels: fwdtc::proj_kernel (tcgen05 projection -> per (token, K-slice)
+// partial rows, parked in the token's h_in row) and rowdot::fwd_rows_kernel
+// (gates, outputs, h_in).  Shapes they take: n in {4, 8}, D a multiple of 64
+// whose h_in row holds at least one partial row (n = 8: D >= 192), 16-byte
+// aligned x / h_in / phi, T < 2^31.  Everything else runs the generic kernels.
+int fwd_part_row_bytes(int n) { return 4 * (n == 4 ? fwdtc::Cfg<4>::RW : fwdtc::Cfg<8>::RW); }
+
+bool fwd_tc_shape(int64_t T, int n, int D) {
+  if (!(n == 4 || n == 8)) return false;
+  if (D % 64 != 0 || T >= ((int64_t)1 << 31)) return false;
+  return 2 * D >= fwd_part_row_bytes(n);
+}
+
 bool fwd_tc_eligible(const mhc_fwd_args* a) {
-  if (!(a->n == 4 || a->n == 8)) return false;
-  if (a->D % 64 != 0 || a->tokens >= ((int64_t)1 << 31)) return false;
-  return aligned(a->x, 16) && aligned(a->h_in, 16) && aligned(a->phi, 16);
+  return fwd_tc_shape(a->tokens, a->n, a->D) && aligned(a->x, 16) && aligned(a->h_in, 16) && aligned(a->phi, 16);
 }
 
 size_t fwd_tc_phis_bytes(int n, int D) {
@@ -279,28 +220,52 @@ size_t fwd_tc_phis_bytes(int n, int D) {
   return (size_t)NB * n * D * sizeof(uint16_t);
 }
 
+struct FwdTcPlan {
+  int S_K = 1;      // K-slices
+  int KB_PER = 1;   // 64-wide K-blocks per slice
+  int units = 1;    // tiles * S_K
+  int grid = 1;     // persistent CTAs of proj_kernel
+};
+
+// The fewest K-slices (a divisor of the n*D/64 K-blocks, at most 16, and no
+// more than an h_in row holds) that give every SM at least ~4 units.
+FwdTcPlan fwd_tc_plan(int64_t T, int n, int D, int sms) {
+  FwdTcPlan P;
+  const int KB = n * D / fwdtc::kBK;
+  const int64_t tiles = std::max<int64_t>(1, (T + fwdtc::kBM - 1) / fwdtc::kBM);
+  const int max_sk = std::min(16, 2 * D / fwd_part_row_bytes(n));
+  for (int sk = 1; sk <= max_sk; ++sk) {
+    if (KB % sk != 0) continue;
+    P.S_K = sk;
+    if (tiles * sk >= 4 * (int64_t)sms) break;
+  }
+  P.KB_PER = KB / P.S_K;
+  P.units = (int)(tiles * P.S_K);
+  P.grid = std::min(P.units, sms);
+  return P;
+}
+
+int fwd_rows_grid(int64_t T, int sms) {
+  return (int)std::max<int64_t>(1, std::min<int64_t>(sms, (T + rowdot::kWarps - 1) / rowdot::kWarps));
+}
+
 template <int n>
 struct FwdTc {
   static int run(const mhc_fwd_args* a, cudaStream_t s, int sms) {
-    (void)sms;
     using Cf = fwdtc::Cfg<n>;
     const int64_t T = a->tokens;
     const int D = a->D;
     const int nD = n * D;
     char* ws = static_cast<char*>(a->workspace);
     uint16_t* phis = reinterpret_cast<uint16_t*>(ws + kWsHeaderBytes);
+    const FwdTcPlan P = fwd_tc_plan(T, n, D, sms);
     int st;
-    ClusterPlan plan;
-    const int64_t tiles = (T + fwdtc::kBM - 1) / fwdtc::kBM;
-    if ((st = plan_clusters(fwdtc::fwd_kernel<n>, Cf::SMEM, fwdtc::kThreads, D, tiles, 2.0 * fwdtc::kBM * nD,
-                            &plan)))
-      return st;
 
     fwdtc::split_phi_kernel<n><<<std::min<int64_t>(((int64_t)Cf::NB * nD / 8 + 255) / 256, 4 * 148), 256, 0, s>>>(
         a->phi, phis, nD);
     if ((st = after_launch())) return st;
 
-    CUtensorMap m_x2d, m_phi, m_x3d;
+    CUtensorMap m_x2d, m_phi;
     {
       const uint64_t dims[2] = {(uint64_t)nD, (uint64_t)T};
       const uint64_t strides[1] = {(uint64_t)nD * 2};
@@ -313,44 +278,20 @@ struct FwdTc {
       const uint32_t box[2] = {fwdtc::kBK, (uint32_t)Cf::NB};
       if ((st = encode_bf16_map(&m_phi, phis, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
     }
-    {
-      const uint64_t dims[3] = {(uint64_t)D, (uint64_t)n, (uint64_t)T};
-      const uint64_t strides[2] = {(uint64_t)D * 2, (uint64_t)nD * 2};
-      const uint32_t box[3] = {fwdtc::kBK, (uint32_t)n, (uint32_t)Cf::RR_TOK};
-      if ((st = encode_bf16_map(&m_x3d, a->x, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE))) return st;
-    }
     fwdtc::Params p;
-    p.alpha = a->alpha;
-    p.bias = a->bias;
-    p.h_in = a->h_in;
-    p.h_post = a->h_post;
-    p.h_res = a->h_res;
-    p.inv_rms = a->inv_rms;
-    p.h_mix = a->h_mix;
-    p.h_pre = a->h_pre;
+    p.part = reinterpret_cast<float*>(a->h_in);
+    p.part_stride = D / 2;
     p.status = reinterpret_cast<int*>(ws);
     p.T = T;
-    p.D = D;
-    p.C = plan.C;
-    p.Dc = D / plan.C;
-    p.num_tiles = (int)((T + fwdtc::kBM - 1) / fwdtc::kBM);
-    p.norm_eps = a->norm_eps;
-    p.hc_eps = a->hc_eps;
-    const int nclusters = std::max(1, std::min(plan.max_clusters, p.num_tiles));
-
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(nclusters * plan.C);
-    cfg.blockDim = dim3(fwdtc::kThreads);
-    cfg.dynamicSmemBytes = Cf::SMEM;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = plan.C;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    MHC_CUDA_TRY(cudaLaunchKernelEx(&cfg, fwdtc::fwd_kernel<n>, m_x2d, m_phi, m_x3d, p));
+    p.S_K = P.S_K;
+    p.KB_PER = P.KB_PER;
+    p.num_units = P.units;
+    if ((st = set_smem_limit_once(fwdtc::proj_kernel<n>, Cf::SMEM))) return st;
+    fwdtc::proj_kernel<n><<<P.grid, fwdtc::kThreads, Cf::SMEM, s>>>(m_x2d, m_phi, p);
+    if ((st = after_launch())) return st;
+    rowdot::fwd_rows_kernel<n><<<fwd_rows_grid(T, sms), rowdot::kThreads, 0, s>>>(
+        a->x, a->alpha, a->bias, a->h_in, a->h_post, a->h_res, a->inv_rms, a->h_mix, a->h_pre, T, D, P.S_K, Cf::RW,
+        a->norm_eps, a->hc_eps);
     return after_launch();
   }
 };
@@ -358,7 +299,7 @@ struct FwdTc {
 int fwd_workspace(int64_t T, int n, int D, size_t* bytes) {
   (void)T;
   size_t b = kWsHeaderBytes;
-  if ((n == 4 || n == 8) && D % 64 == 0) b = align_up(b + fwd_tc_phis_bytes(n, D), kWsAlign);
+  if (fwd_tc_shape(T, n, D)) b = align_up(b + fwd_tc_phis_bytes(n, D), kWsAlign);
   *bytes = b;
   return MHC_OK;
 }
@@ -494,7 +435,7 @@ int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s, int sms) {
   p.num_tiles = num_tiles;
   p.FT = 4;
 
-  MHC_CUDA_TRY(cudaFuncSetAttribute(bwdtc::bwd_kernel<n>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM));
+  if ((st = set_smem_limit_once(bwdtc::bwd_kernel<n>, Cf::SMEM))) return st;
   bwdtc::bwd_kernel<n><<<L.plan.S_K * L.plan.S_T, bwdtc::kThreads, Cf::SMEM, s>>>(m_x2d, m_dh, m_dx, m_rec, p);
   if ((st = after_launch())) return st;
 
@@ -676,27 +617,18 @@ int mhc_query_plan(int which, int64_t tokens, int32_t n, int32_t D, int* path, i
   *path = 0;
   *cluster_size = 0;
   *clusters = 0;
-  ClusterPlan plan;
-  const int64_t tiles = (tokens + 127) / 128;
-  if (which == 0 && (n == 4 || n == 8) && D % 64 == 0 && tokens < ((int64_t)1 << 31)) {
-    const double tb = 2.0 * 128 * n * D;
-    st = n == 4 ? plan_clusters(fwdtc::fwd_kernel<4>, fwdtc::Cfg<4>::SMEM, fwdtc::kThreads, D, tiles, tb, &plan)
-                : plan_clusters(fwdtc::fwd_kernel<8>, fwdtc::Cfg<8>::SMEM, fwdtc::kThreads, D, tiles, tb, &plan);
-    if (st) return st;
+  if (which == 0 && fwd_tc_shape(tokens, n, D)) {
+    const FwdTcPlan fp = fwd_tc_plan(tokens, n, D, sms);
     *path = 1;
+    *cluster_size = fp.S_K;
+    *clusters = fp.grid;
   } else if (which == 1 && bwd_tc_shape(tokens, n, D)) {
-    // no clusters: report the grid as S_T token groups of S_K d-slice CTAs
     const BwdTcPlan bp = bwd_tc_plan(tokens, D, sms);
     *path = 1;
     *cluster_size = bp.S_K;
     *clusters = bp.S_T;
-    return MHC_OK;
   } else if (which != 0 && which != 1) {
     return MHC_ERR_BAD_SHAPE;
-  }
-  if (*path == 1) {
-    *cluster_size = plan.C;
-    *clusters = (int)std::max<int64_t>(1, std::min<int64_t>(plan.max_clusters, tiles));
   }
   return MHC_OK;
 }

@@ -1,6 +1,6 @@
 // Streaming per-token kernels of the mHC pre-op that need whole token rows
-// and no tensor cores: the first half of the backward (B1) and the h_in pass
-// of the forward (F2).  Pure HBM streams: warps own whole tokens, every load
+// and no tensor cores: the first kernel of the backward (bwd_rows_kernel) and
+// the second kernel of the forward (fwd_rows_kernel).  Pure HBM streams: warps own whole tokens, every load
 // is 512 contiguous bytes per warp, many loads in flight per lane.
 #pragma once
 
@@ -185,54 +185,108 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_rows_kernel(
   }
 }
 
-// F2: h_in[t, d] = bf16(sum_i h_pre[t,i] x[t,i,d])  (src/forward/golden.py:62-63).
-// Task = (token, 8 consecutive d); consecutive threads take consecutive d.
+// Forward, second kernel (src/forward/golden.py:34-69).  Per token t (warp t
+// % W): sum the S_K partial rows [h_mix (N_OUT), sum x^2] the projection
+// kernel parked in h_in's row t, in slice order; inv_rms = 1/sqrt(sum x^2 / nD
+// + norm_eps); gates from h_mix * inv_rms; then h_in[t, d] = bf16(sum_i
+// h_pre[t,i] x[t,i,d]) streamed over the row (all partial loads of the warp
+// complete, through the shuffles, before its first h_in store).
+// Needs D % 8 == 0 and 16-byte aligned x / h_in.
 template <int n>
-__global__ void __launch_bounds__(kThreads) h_in_kernel(const uint16_t* __restrict__ x,
-                                                        const float* __restrict__ h_pre,
-                                                        uint16_t* __restrict__ h_in, int64_t T, int D) {
-  const int64_t per_tok = D / 8;
-  const int64_t tasks = T * per_tok;
-  const int64_t stride = (int64_t)gridDim.x * kThreads;
-  constexpr int U = 4;
-  for (int64_t base = (int64_t)blockIdx.x * kThreads + threadIdx.x; base < tasks; base += stride * U) {
-    uint4 xv[U][n];
-    float hp[U][n];
+__global__ void __launch_bounds__(kThreads, 1) fwd_rows_kernel(
+    const uint16_t* __restrict__ x, const float* __restrict__ alpha, const float* __restrict__ bias,
+    uint16_t* h_in, float* __restrict__ h_post, float* __restrict__ h_res, float* __restrict__ inv_rms,
+    float* __restrict__ h_mix, float* __restrict__ h_pre, int64_t T, int D, int S_K, int RW, float norm_eps,
+    float hc_eps) {
+  constexpr int N_OUT = n * n + 2 * n;
+  constexpr int M = (N_OUT + 1 + 31) / 32;   // partial columns per lane (N_OUT outputs + sum x^2)
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int64_t W = (int64_t)gridDim.x * kWarps;
+  const int nD = n * D;
+  const float inv_nd = 1.0f / (float)nD;
+  const float a_pre = alpha[0], a_post = alpha[1], a_res = alpha[2];
+  float bj[M];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int64_t task = base + u * stride;
-      if (task < tasks) {
-        const int64_t t = task / per_tok;
-        const int d = (int)(task - t * per_tok) * 8;
+  for (int m = 0; m < M; ++m) bj[m] = (lane + 32 * m) < N_OUT ? __ldg(bias + lane + 32 * m) : 0.f;
+
+  for (int64_t t = gw; t < T; t += W) {
+    // (1) partial rows of token t, summed in slice order
+    const float* pr = reinterpret_cast<const float*>(h_in + t * D);
+    float hm[M];
 #pragma unroll
-        for (int i = 0; i < n; ++i) {
-          xv[u][i] = ldg_stream(x + (t * n + i) * D + d);
-          hp[u][i] = __ldg(h_pre + t * n + i);
+    for (int m = 0; m < M; ++m) {
+      const int c = lane + 32 * m;
+      float acc = 0.f;
+      if (c <= N_OUT)
+        for (int ks = 0; ks < S_K; ++ks) acc += pr[ks * RW + c];
+      hm[m] = acc;
+    }
+    const float sq = __shfl_sync(0xffffffffu, hm[N_OUT / 32], N_OUT % 32);
+    const float ir = 1.0f / sqrtf(sq * inv_nd + norm_eps);
+    // (2) gates and the fp32 outputs
+    float hp_lane = 0.f;
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const int jj = lane + 32 * m;
+      if (jj < N_OUT) {
+        const float v = hm[m] * ir;
+        if (jj < n) {
+          hp_lane = sigmoid_acc(a_pre * v + bj[m]) + hc_eps;
+          if (h_pre) h_pre[t * n + jj] = hp_lane;
+        } else if (jj < 2 * n) {
+          h_post[t * n + (jj - n)] = 2.0f * sigmoid_acc(a_post * v + bj[m]);
+        } else {
+          h_res[t * (n * n) + (jj - 2 * n)] = a_res * v + bj[m];
         }
+        if (h_mix) h_mix[t * N_OUT + jj] = hm[m];
       }
     }
+    if (lane == 0 && inv_rms) inv_rms[t] = ir;
+    // Every lane has used its partials (the stores above consume them): only
+    // now may row t of h_in, which holds them, be overwritten.
+    __syncwarp();
+    asm volatile("" ::: "memory");
+    float hp[n];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int64_t task = base + u * stride;
-      if (task < tasks) {
-        const int64_t t = task / per_tok;
-        const int d = (int)(task - t * per_tok) * 8;
-        float acc[8];
+    for (int i = 0; i < n; ++i) hp[i] = __shfl_sync(0xffffffffu, hp_lane, i);
+    // (3) h_in = sum_i h_pre[i] x[i, :], streamed (U 256-element chunks in flight per lane)
+    const uint16_t* xr = x + t * nD;
+    uint16_t* hr = h_in + t * D;
+    constexpr int U = n <= 4 ? 4 : 2;
+    for (int c0 = 0; c0 < D; c0 += 256 * U) {
+      uint4 xv[U][n];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+      for (int u = 0; u < U; ++u) {
+        const int d = c0 + u * 256 + lane * 8;
 #pragma unroll
-        for (int i = 0; i < n; ++i) {
-          float f[8];
-          bf16x8(xv[u][i], f);
+        for (int i = 0; i < n; ++i) xv[u][i] = d < D ? ldg_stream(xr + (int64_t)i * D + d) : make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc[e] = fmaf(hp[u][i], f[e], acc[e]);
+      for (int u = 0; u < U; ++u) {
+        const int d = c0 + u * 256 + lane * 8;
+        if (d < D) {
+          float acc[8];
+          {
+            float f[8];
+            bf16x8(xv[u][0], f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] = hp[0] * f[e];
+          }
+#pragma unroll
+          for (int i = 1; i < n; ++i) {
+            float f[8];
+            bf16x8(xv[u][i], f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] = fmaf(hp[i], f[e], acc[e]);
+          }
+          uint4 o;
+          o.x = pack_bf16x2(acc[0], acc[1]);
+          o.y = pack_bf16x2(acc[2], acc[3]);
+          o.z = pack_bf16x2(acc[4], acc[5]);
+          o.w = pack_bf16x2(acc[6], acc[7]);
+          *reinterpret_cast<uint4*>(hr + d) = o;
         }
-        uint4 o;
-        o.x = pack_bf16x2(acc[0], acc[1]);
-        o.y = pack_bf16x2(acc[2], acc[3]);
-        o.z = pack_bf16x2(acc[4], acc[5]);
-        o.w = pack_bf16x2(acc[6], acc[7]);
-        *reinterpret_cast<uint4*>(h_in + t * D + d) = o;
       }
     }
   }
