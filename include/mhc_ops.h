@@ -170,6 +170,14 @@ MHC_API int mhc_bwd(const mhc_bwd_args* args, void* stream);
  * has no bounded device waits. */
 MHC_API int mhc_read_device_status(void* workspace, void* stream, int* device_status);
 
+/* Self test of the device-side failure detection: launches one CTA that
+ * waits, through the same bounded wait every tensor-core kernel uses, on a
+ * barrier nothing completes.  After about a second the wait gives up, the
+ * kernel writes MHC_ERR_DEVICE_TIMEOUT into the workspace's status word
+ * (read it with mhc_read_device_status) and returns; the context stays
+ * usable.  No counterpart in the reference (it has no device waits). */
+MHC_API int mhc_selftest_wait_expiry(void* workspace, void* stream);
+
 /* Launch plan the library uses for this shape on the current device:
  * *path = 0 generic kernels, 1 tensor-core kernels.  which = 0 forward: for
  * path 1, *cluster_size is the number of K-slices the projection is split

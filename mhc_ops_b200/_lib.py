@@ -58,6 +58,7 @@ SIGNATURES = {
                                               ctypes.POINTER(ctypes.c_size_t)]),
     "mhc_bwd": (ctypes.c_int, [ctypes.POINTER(BwdArgs), _c_void_p]),
     "mhc_read_device_status": (ctypes.c_int, [_c_void_p, _c_void_p, ctypes.POINTER(ctypes.c_int)]),
+    "mhc_selftest_wait_expiry": (ctypes.c_int, [_c_void_p, _c_void_p]),
     "mhc_query_plan": (ctypes.c_int, [ctypes.c_int, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
                                       ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
                                       ctypes.POINTER(ctypes.c_int)]),

@@ -25,16 +25,16 @@
 //     split-phi images, so the epilogue has no gamma term) as one N=128
 //     accumulation over the two stacked images, the sum over 6 (dh term, phi
 //     term) products (smallest first: m.M, l.H, h.L, m.H, h.M, h.H; exact to
-//     ~2^-23 in the fp32 sum), M=128 tok, K=segment; and G += x^T . DHM over
-//     the hi and mid terms (M=128 k, N=segment, K=2x128 tokens; x read
-//     MN-major straight from the two TMA stages, DHM read MN-major).  Wide
-//     MMAs matter here: a tcgen05.mma costs ~45-65 cycles to issue whatever
-//     its N, so an N=128 MMA does twice the work of an N=64 one for the same
-//     time;
+//     ~2^-23 in the fp32 sum), M=128 tok, K=segment; and the pair's G block,
+//     x^T . DHM over the hi and mid terms as one N=64 accumulation (M=128 k,
+//     K=128 tokens; x read MN-major straight from the two TMA stages, DHM
+//     read MN-major).  Wide MMAs matter here: a tcgen05.mma costs ~45-65
+//     cycles to issue whatever its N, so an N=128 MMA does twice the work of
+//     an N=64 one for the same time;
 //   * WG_E reads dvecX (TMEM lane = token) and writes dx through a TMA store
-//     (two warp groups take alternate stages); every FT tiles it flushes G
-//     from TMEM into the group's partial (single writer per address, fixed
-//     order).
+//     (two warp groups take alternate stages) and flushes each pair's G block
+//     from TMEM into the token group's partial (first tile stores, later
+//     tiles add; one thread per address, so the order is fixed).
 #pragma once
 
 #include "common.cuh"
@@ -78,8 +78,10 @@ struct Cfg {
   static constexpr int REC_BYTES = kBM * RECW * 4;
   static constexpr int MAX_KC = 1024;                    // d-slice * n per CTA
   static constexpr int CW = 3 + N_OUT;                   // dalpha / dbias columns
-  // tensor memory: G [0, 256), dvecX of a stage pair in two buffers [256, 512)
-  static constexpr int G_COLS = 256;
+  // tensor memory: G of a stage pair (hi and mid terms, 2 x SEGW columns) in
+  // two buffers [0, 128), dvecX of a stage pair in two buffers [128, 384)
+  static constexpr int G_BUF = 2 * SEGW;
+  static constexpr int G_COLS = 2 * G_BUF;
   static constexpr int DV_COLS = 2 * kBK;
 
   static constexpr int smem_bytes() {
@@ -90,7 +92,8 @@ struct Cfg {
   static_assert(SMEM <= kSmemLimit, "backward tile does not fit in shared memory");
   static_assert(n % 2 == 0, "stages pair two streams of a d-chunk");
   static_assert(RECW == 32, "records are loaded as one 128-byte swizzled row per token");
-  static_assert((MAX_KC / 128) * NG <= G_COLS && G_COLS + 2 * DV_COLS <= 512, "TMEM budget");
+  static_assert(G_COLS + 2 * DV_COLS <= 512, "TMEM budget");
+  static_assert(G_BUF <= 256, "UMMA N of the G products");
 };
 
 struct Params {
@@ -103,7 +106,6 @@ struct Params {
   int S_K;                // d-slices: D / Dc
   int S_T;                // token groups
   int num_tiles;
-  int FT;                 // tiles per G flush
 };
 
 template <int n>
@@ -119,9 +121,9 @@ struct Bars {
   static constexpr int dv_empty = dv_full + 2;
   static constexpr int dhm_full = dv_empty + 2;
   static constexpr int dhm_free = dhm_full + 2;
-  static constexpr int g_full = dhm_free + 2;
-  static constexpr int g_empty = g_full + 1;
-  static constexpr int rec_full = g_empty + 1;
+  static constexpr int g_full = dhm_free + 2;            // per G buffer
+  static constexpr int g_empty = g_full + 2;
+  static constexpr int rec_full = g_empty + 2;
   static constexpr int rec_free = rec_full + 1;
   static constexpr int count = rec_free + 1;
 };
@@ -256,7 +258,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int DCH = Dc / kBK;
   const int nD = n * D;
   const int KC = n * Dc;
-  const int NPAIR = KC / 128;                 // G blocks of 128 k per CTA
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   // Tiles run last-first, so the first ones re-read what the row kernel read last.
   auto tile_of = [&](int j) { return p.num_tiles - 1 - (group + j * p.S_T); };
@@ -278,8 +279,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(B::dhm_full + i), kThreadsE);
       mbar_init(bar(B::dhm_free + i), 1);
     }
-    mbar_init(bar(B::g_full), 1);
-    mbar_init(bar(B::g_empty), kThreadsE / 32);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(B::g_full + i), 1);
+      mbar_init(bar(B::g_empty + i), kThreadsE / 64);   // the flushing epilogue group
+    }
     mbar_init(bar(B::rec_full), 1);
     mbar_init(bar(B::rec_free), kThreadsE);
     *abort_flag = 0;
@@ -299,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t tmem_g = tmem_base;                        // NPAIR x NG columns
+  const uint32_t tmem_g = tmem_base;                        // 2 x G_BUF: G of a stage pair
   const uint32_t tmem_dv = tmem_base + Cf::G_COLS;          // 2 x DV_COLS: dvecX of a stage pair
   const WaitCtx wc{abort_flag, p.status};
   const int my_tiles = group < p.num_tiles ? (p.num_tiles - 1 - group) / p.S_T + 1 : 0;
@@ -352,17 +355,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // start-address field.
     if (producer) {
       constexpr uint32_t idesc_dv = idesc_bf16_f32(kBM, 2 * kBK, false, false);
-      constexpr uint32_t idesc_g = idesc_bf16_f32(kBM, Cf::NG, true, true);
-      uint32_t pq = 0, flushes = 0;
+      constexpr uint32_t idesc_g = idesc_bf16_f32(kBM, Cf::G_BUF, true, true);
+      uint32_t pq = 0;
       for (int j = 0; j < my_tiles; ++j) {
         const int hb = j & 1;
         mbar_wait(bar(B::dhm_full + hb), (j >> 1) & 1, wc);
         tc_fence_after();
-        const bool g_restart = (j % p.FT) == 0;
-        if (g_restart && j > 0) {
-          mbar_wait(bar(B::g_empty), (flushes - 1) & 1, wc);   // previous G group read out
-          tc_fence_after();
-        }
         const uint32_t dhm_a = smem_u32(dhm + hb * Cf::DHM_BYTES);
         const uint64_t a_dv = desc_kmajor_interleave(dhm_a, 128, Cf::RG_BYTES);      // DHM, K-major
         const uint64_t b_g = desc_kmajor_interleave(dhm_a, Cf::RG_BYTES, 128);       // DHM read MN-major
@@ -392,27 +390,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int s0 = (int)(q0 % Cf::XS);
             mbar_wait(bar(B::x_full + s0), (q0 / Cf::XS) & 1, wc);
             mbar_wait(bar(B::x_full + s0 + 1), ((q0 + 1) / Cf::XS) & 1, wc);
+            mbar_wait(bar(B::g_empty + pb), ((pq >> 1) & 1) ^ 1, wc);
             tc_fence_after();
             if (!*abort_flag) {
-              const uint32_t d = tmem_g + (dch * NP + ip) * Cf::NG;
+              // N = the hi and mid segments of DHM (G needs ~2^-17), one N=64
+              // accumulation over the tile's 128 tokens; flushed per pair
+              const uint32_t d = tmem_g + pb * Cf::G_BUF;
               const uint64_t a_g = desc_mnmajor_sw128(smem_u32(xr + s0 * Cf::X_BYTES), Cf::X_BYTES, 1024);
 #pragma unroll
-              for (int e = 1; e >= 0; --e) {            // mid, hi terms of dh_mix (G needs ~2^-17)
-#pragma unroll
-                for (int ks = 0; ks < kBM / 16; ++ks)
-                  umma_bf16(d, a_g + ((ks * 2048) >> 4), b_g + ((e * Cf::SEGW * 16 + ks * 2 * Cf::RG_BYTES) >> 4),
-                            idesc_g, !(g_restart && e == 1 && ks == 0));
-              }
+              for (int ks = 0; ks < kBM / 16; ++ks)
+                umma_bf16(d, a_g + ((ks * 2048) >> 4), b_g + ((ks * 2 * Cf::RG_BYTES) >> 4), idesc_g, ks != 0);
               umma_commit(bar(B::x_empty + s0));
               umma_commit(bar(B::x_empty + s0 + 1));
+              umma_commit(bar(B::g_full + pb));
             }
           }
         }
         if (!*abort_flag) umma_commit(bar(B::dhm_free + hb));
-        if ((j + 1) % p.FT == 0 || j == my_tiles - 1) {
-          if (!*abort_flag) umma_commit(bar(B::g_full));
-          ++flushes;
-        }
       }
     }
   } else if (warp == 2) {
@@ -493,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     float c_cur = 0.f, hp_cur[n];
     if (my_tiles > 0) build_dhm(0, c_cur, hp_cur);
-    uint32_t q = 0, dq = 0, flushes = 0;
+    uint32_t q = 0, dq = 0;
     for (int j = 0; j < my_tiles; ++j) {
       const int tile = tile_of(j);
       float c_nxt = 0.f, hp_nxt[n];
@@ -576,35 +570,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(B::x_empty + s));
-        }
-      }
-      // flush G of the finished group into this token group's partial
-      if ((j + 1) % p.FT == 0 || j == my_tiles - 1) {
-        mbar_wait(bar(B::g_full), flushes & 1, wc);
-        tc_fence_after();
-        for (int blk = 0; blk < NPAIR; ++blk) {
-          const int dch = blk / NP, i0 = (blk % NP) * 2;
-          const int i = i0 + (row >> 6);
-          const int64_t k = (int64_t)i * D + (int64_t)slice * Dc + dch * kBK + (row & 63);
-          float* gp = p.gpart + (int64_t)group * N_OUT * nD + k;
-          for (int c16 = eh; c16 < Cf::NG / 16; c16 += 2) {
-            float v[16];
-            tmem_ld16(tmem_g + blk * Cf::NG + ((uint32_t)(32 * q4) << 16) + c16 * 16, v);
-            tmem_wait_ld();
+          if (pb == eh) {
+            // G of this stage pair -> the token group's partial (rows 0..63
+            // stream i & ~1, 64..127 the next); the same thread owns each
+            // address in every tile: first tile stores, later tiles add
+            mbar_wait(bar(B::g_full + pb), (pq >> 1) & 1, wc);
+            tc_fence_after();
+            const int ig = (i & ~1) + (row >> 6);
+            float* gp = p.gpart + (int64_t)group * N_OUT * nD + (int64_t)ig * D + (int64_t)slice * Dc + dch * kBK +
+                        (row & 63);
+            const uint32_t tg = tmem_g + pb * Cf::G_BUF + ((uint32_t)(32 * q4) << 16);
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const int jj = c16 * 16 + e;
-              if (jj < N_OUT) {
-                if (flushes == 0) gp[(int64_t)jj * nD] = v[e];
-                else red_add_f32(gp + (int64_t)jj * nD, v[e]);
+            for (int c16 = 0; c16 < Cf::SEGW / 16; ++c16) {
+              float hi[16], mid[16];
+              tmem_ld16(tg + c16 * 16, hi);
+              tmem_ld16(tg + Cf::SEGW + c16 * 16, mid);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                const int jj = c16 * 16 + e;
+                if (jj < N_OUT) {
+                  const float v = mid[e] + hi[e];
+                  if (j == 0) gp[(int64_t)jj * nD] = v;
+                  else red_add_f32(gp + (int64_t)jj * nD, v);
+                }
               }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B::g_empty + pb));
           }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B::g_empty));
-        ++flushes;
       }
       c_cur = c_nxt;
 #pragma unroll

@@ -433,7 +433,6 @@ int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s, int sms) {
   p.S_K = L.plan.S_K;
   p.S_T = L.plan.S_T;
   p.num_tiles = num_tiles;
-  p.FT = 4;
 
   if ((st = set_smem_limit_once(bwdtc::bwd_kernel<n>, Cf::SMEM))) return st;
   bwdtc::bwd_kernel<n><<<L.plan.S_K * L.plan.S_T, bwdtc::kThreads, Cf::SMEM, s>>>(m_x2d, m_dh, m_dx, m_rec, p);
@@ -452,6 +451,26 @@ int bwd_workspace(int64_t T, int n, int D, int sms, size_t* bytes) {
   if (bwd_tc_shape(T, n, D)) b = std::max(b, bwd_tc_layout(T, D, sms).total);
   *bytes = b;
   return MHC_OK;
+}
+
+// ----------------------------------------------------------------- bounded-wait self test
+// One thread waits, through the same bounded mbar_wait every tensor-core
+// kernel uses, on an mbarrier that nothing ever completes.  The wait gives
+// up after its limit (about a second), sets the status word to
+// MHC_ERR_DEVICE_TIMEOUT and the kernel returns.  No fault is involved.
+__global__ void wait_expiry_kernel(int* status) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(sm100::smem_u32(&bar), 1);
+    abort_flag = 0;
+    sm100::fence_mbarrier_init_cluster();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const sm100::WaitCtx wc{&abort_flag, status};
+    sm100::mbar_wait(sm100::smem_u32(&bar), 0, wc);   // phase 0 never completes
+  }
 }
 
 // ----------------------------------------------------------------- forward without a caller workspace
@@ -606,6 +625,16 @@ int mhc_fwd_static(const mhc_fwd_args* a, void* stream) {
   b.workspace = scratch;
   b.workspace_bytes = kStaticScratchBytes;
   return mhc_fwd(&b, stream);
+}
+
+int mhc_selftest_wait_expiry(void* workspace, void* stream) {
+  if (!workspace) return MHC_ERR_NULL_POINTER;
+  if (!aligned(workspace, kWsAlign)) return MHC_ERR_MISALIGNED;
+  int sms = 0;
+  int st = current_sm_count(&sms);
+  if (st) return st;
+  wait_expiry_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<int*>(workspace));
+  return after_launch();
 }
 
 int mhc_query_plan(int which, int64_t tokens, int32_t n, int32_t D, int* path, int* cluster_size, int* clusters) {

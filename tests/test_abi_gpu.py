@@ -72,3 +72,19 @@ def test_launch_counter_advances():
     mhc_forward_pre(d.x, d.phi, d.alpha, d.bias)
     torch.cuda.synchronize()
     assert _lib.launch_count() > before
+
+
+def test_bounded_wait_expiry_reports_timeout():
+    """A device wait that can never complete gives up (about a second), records
+    MHC_ERR_DEVICE_TIMEOUT in the workspace status word, and leaves the context
+    usable: the next forward call still works and the status word was cleared."""
+    lib = _lib.load()
+    stream = torch.cuda.current_stream()
+    ws = torch.zeros(1 << 12, dtype=torch.uint8, device="cuda")
+    assert lib.mhc_selftest_wait_expiry(ws.data_ptr(), stream.cuda_stream) == 0
+    assert _lib.read_device_status(ws, stream) == _lib.MHC_ERR_DEVICE_TIMEOUT
+    assert _lib.read_device_status(ws, stream) == 0          # read clears it
+    d = make_inputs(1, 16, 4, 128, seed=6).to("cuda")
+    out = mhc_forward_pre(d.x, d.phi, d.alpha, d.bias)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out[1]).all()
