@@ -1,6 +1,6 @@
 // Blackwell (sm_100a) building blocks written as inline PTX: mbarriers with
-// bounded waits, TMA tensor loads, tcgen05 (TMEM alloc, UMMA, commit, loads),
-// cluster rank / DSMEM addressing.  No TMA multicast is used anywhere.
+// bounded waits, TMA tensor loads and stores, tcgen05 (TMEM alloc, UMMA,
+// commit, loads, stores).  Every kernel here runs as plain single CTAs.
 #pragma once
 
 #include <cuda.h>
@@ -45,36 +45,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
                : "memory");
 }
 
-// Arrive on an mbarrier of CTA `cta` of this cluster (bar is the local smem address
-// of the same barrier object; mapa translates it).  Release at cluster scope orders
-// this thread's prior DSMEM stores before the arrival.
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar, uint32_t cta) {
-  asm volatile(
-      "{\n\t.reg .b32 ra;\n\t"
-      "mapa.shared::cluster.u32 ra, %0, %1;\n\t"
-      "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [ra];\n\t}" ::"r"(bar),
-      "r"(cta)
-      : "memory");
-}
-
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.b32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Acquire at cluster scope: for barriers that remote CTAs arrive on after DSMEM stores.
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.b32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
@@ -90,14 +65,13 @@ struct WaitCtx {
 
 // The clock is read once every 256 polls (the common case, a wait that ends
 // within a few polls, reads it never).
-template <bool kClusterScope = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtx& w) {
   if (*w.abort) return false;
   uint64_t t0 = 0;
   for (uint32_t spin = 0;; ++spin) {
 #pragma unroll 1
     for (int i = 0; i < 256; ++i) {
-      const bool ok = kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
+      const bool ok = mbar_try_wait(bar, parity);
       if (ok) return true;
     }
     if (*w.abort) return false;
@@ -160,45 +134,6 @@ __device__ __forceinline__ void st_global_hint(void* ptr, uint4 v, uint64_t pol)
 
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
-}
-
-// ------------------------------------------------------------------ cluster
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t cluster_id_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t nclusters_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
-  return r;
-}
-
-// Every thread of every CTA of the cluster.
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t cta) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(cta));
-  return r;
-}
-
-__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-
-__device__ __forceinline__ void st_cluster_v4_f32(uint32_t addr, float a, float b, float c, float d) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
 }
 
 // Named barrier over `count` threads (count a multiple of 32), id 1..15.
