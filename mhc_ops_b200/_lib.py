@@ -152,7 +152,8 @@ def query_plan(which: int, tokens: int, n: int, D: int) -> dict:
     if not path.value:
         return {"path": "generic"}
     if which == 0:
-        return {"path": "tensor-core", "k_slices": cs.value, "ctas": ncl.value}
+        return {"path": "tensor-core-fused" if path.value == 2 else "tensor-core", "k_slices": cs.value,
+                "ctas": ncl.value}
     return {"path": "tensor-core", "d_slices": cs.value, "token_groups": ncl.value}
 
 

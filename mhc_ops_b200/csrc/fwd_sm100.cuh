@@ -3,15 +3,23 @@
 // Math: src/forward/golden.py:34-69 (h_mix = x @ phi^T pre-RMS, inv_rms,
 // gates, h_in = sum_i h_pre[i] * x[i,:]).
 //
-// The forward is two kernels.  This one, proj_kernel, reads x once and
-// leaves per token and K-slice the partial projection (pre-RMS h_mix) and the
-// partial sum of x^2; rowdot.cuh's fwd_rows_kernel sums the partials in a
-// fixed order, forms inv_rms and the gates and streams x a second time for
-// h_in.  The partial rows of token t are parked in row t of h_in, which the
-// second kernel reads before it overwrites that row with the result.
+// proj_kernel reads x once and leaves per token and K-slice the partial
+// projection (pre-RMS h_mix) and the partial sum of x^2; the row half
+// (rowdot.cuh, fwd_row_token) sums the partials in a fixed order, forms
+// inv_rms and the gates and reads x a second time for h_in.  The partial rows
+// of token t are parked in row t of h_in, which the row half reads before it
+// overwrites that row with the result.  Two forms:
+//   * fused (proj_kernel<n, true>, cooperative launch): extra warps WG_R run
+//     the row half of every tile whose S_K units are all done (a counter per
+//     tile in global memory, release/acquire), about one round of units
+//     behind the projection, so the second read of x hits L2 (W0 loads x
+//     with an evict-last hint);
+//   * two kernels (proj_kernel<n, false> then rowdot::fwd_rows_kernel), for
+//     shapes whose h_in row cannot hold the fused form's finer K-slices.
 //
 // Work units are (128-token tile, K-slice of KB_PER 64-wide K-blocks); a
-// persistent grid walks them with no communication between CTAs.  Per unit:
+// persistent grid walks them (in the two-kernel form with no communication
+// between CTAs).  Per unit:
 //   * W0 streams x (128 x 64 bf16, 128-B swizzle) and the bf16-split phi
 //     block (NB x 64) of each K-block into an S-stage ring with TMA;
 //   * W1 issues tcgen05.mma (M=128 tokens, N=NB split-phi rows, K=16); every
@@ -21,9 +29,10 @@
 //     accumulator (all split terms) into its fp32 partials with
 //     round-to-nearest adds -- the tensor core's own accumulation across many
 //     K steps drifts (about 2^-23 per step, one-signed), across 8 it does not
-//     -- and stores the unit's partial h_mix;
+//     -- and stores the unit's partial row (h_mix and WG_S's sum x^2, whole
+//     32-byte sectors);
 //   * WG_S (4 warps, one thread per token row) sums x^2 of its row from the
-//     smem stages (tree per stage) and stores the unit's partial sum x^2.
+//     smem stages (tree per stage) and hands it to WG_F through shared memory.
 // phi is split into NT bf16 terms (hi, mid[, lo]) stacked as UMMA N rows, so
 // x (exact in bf16) times phi is exact to ~2^-(8*NT) before fp32 accumulation.
 // Three terms at n <= 5: h_in's bound (one ulp plus 2^-18 of its terms) needs
@@ -33,6 +42,7 @@
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
+#include "rowdot.cuh"
 #include "sm100.cuh"
 
 namespace mhc {
@@ -43,6 +53,9 @@ using namespace sm100;
 constexpr int kBM = 128;          // tokens per tile = UMMA M = TMEM lanes
 constexpr int kBK = 64;           // bf16 elements per 128-byte row
 constexpr int kThreads = 10 * 32; // W0, W1, WG_F(4), WG_S(4)
+constexpr int kRowWarps = 8;      // WG_R of the fused forward
+constexpr int kThreadsFused = kThreads + kRowWarps * 32;
+constexpr int kUnitSignals = 4;   // WG_F warps: arrivals on a tile's counter per unit
 constexpr int kKG = 2;            // K-blocks accumulated per TMEM accumulator
 constexpr int kSmemLimit = 232448;
 
@@ -58,14 +71,17 @@ struct Cfg {
   static constexpr int N_OUT = n * n + 2 * n;
   static constexpr int NT = (n <= 5) ? 3 : 2;              // phi split terms
   static constexpr int NB = round_up(NT * N_OUT, 16);      // UMMA N
-  static constexpr int RW = round_up(N_OUT + 1, 4);        // floats per partial row
+  static constexpr int RW = round_up(N_OUT + 1, 8);        // floats per partial row (whole 32-byte sectors)
   static constexpr int A_BYTES = kBM * 128;
   static constexpr int B_BYTES = NB * 128;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int ACC_COLS = round_up(NB, 32);
   static constexpr int NBUF = (512 / ACC_COLS) < 4 ? (512 / ACC_COLS) : 4;   // accumulator ring
   static constexpr int TMEM_COLS = pow2_at_least(NBUF * ACC_COLS);
-  static constexpr int smem_bytes(int S) { return 1024 /*align slack*/ + S * STAGE_BYTES + 512 /*barriers*/; }
+  static constexpr int SQ_BYTES = 2 * kBM * 4;              // WG_S -> WG_F hand-over of sum x^2, two units
+  static constexpr int smem_bytes(int S) {
+    return 1024 /*align slack*/ + S * STAGE_BYTES + SQ_BYTES + 512 /*barriers*/;
+  }
   static constexpr int pick_stages() {
     int s = 8;
     while (s > 2 && smem_bytes(s) > kSmemLimit) --s;
@@ -75,6 +91,7 @@ struct Cfg {
   static constexpr int SMEM = smem_bytes(S);
   static_assert(SMEM <= kSmemLimit, "forward stage ring does not fit in shared memory");
   static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 128-B swizzle atoms aligned");
+  static_assert(RW % 4 == 0, "partial rows are stored as float4");
   static_assert(NB <= 256, "UMMA N above 256");
   static_assert(NBUF >= 2 && TMEM_COLS <= 512, "TMEM accumulator ring");
 };
@@ -87,6 +104,9 @@ struct Params {
   int S_K;                // K-slices
   int KB_PER;             // K-blocks per slice
   int num_units;          // tiles * S_K
+  // fused forward only
+  int* tile_done;         // [tiles] zeroed before the launch; kUnitSignals arrivals per finished unit
+  rowdot::FwdRowArgs rows;
 };
 
 template <int n>
@@ -96,7 +116,9 @@ struct Bars {
   static constexpr int empty = full + Cf::S;
   static constexpr int acc_full = empty + Cf::S;
   static constexpr int acc_empty = acc_full + Cf::NBUF;
-  static constexpr int count = acc_empty + Cf::NBUF;
+  static constexpr int sq_full = acc_empty + Cf::NBUF;   // 2: WG_S wrote a unit's sum x^2
+  static constexpr int sq_empty = sq_full + 2;           // 2: WG_F read it
+  static constexpr int count = sq_empty + 2;
 };
 
 __device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
@@ -114,8 +136,16 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   return v;
 }
 
-template <int n>
-__global__ void __launch_bounds__(kThreads, 1)
+// One warp's arrival on its tile's counter after its partial stores: every
+// lane fences its own stores, then lane 0 adds with release semantics.
+__device__ __forceinline__ void signal_unit(int* counter, int lane) {
+  __threadfence();
+  __syncwarp();
+  if (lane == 0) red_release_add(counter, 1);
+}
+
+template <int n, bool kFused>
+__global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
     proj_kernel(const __grid_constant__ CUtensorMap map_x2d, const __grid_constant__ CUtensorMap map_phi,
                 const Params p) {
   using Cf = Cfg<n>;
@@ -125,7 +155,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + S * Cf::STAGE_BYTES);
+  float* sq_buf = reinterpret_cast<float*>(ring + S * Cf::STAGE_BYTES);   // [2][kBM]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + S * Cf::STAGE_BYTES + Cf::SQ_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + B::count);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -141,6 +172,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < Cf::NBUF; ++i) {
       mbar_init(bar(B::acc_full + i), 1);
       mbar_init(bar(B::acc_empty + i), 4);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(B::sq_full + i), 4);
+      mbar_init(bar(B::sq_empty + i), 4);
     }
     *abort_flag = 0;
     fence_mbarrier_init_cluster();
@@ -163,7 +198,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------ W0: TMA producer
     if (lane == 0) {
-      const uint64_t pol_x = l2_policy_evict_first();
+      // fused: x stays in L2 for WG_R's second read of the same rows
+      const uint64_t pol_x = kFused ? l2_policy_evict_last() : l2_policy_evict_first();
       const uint64_t pol_phi = l2_policy_evict_last();
       uint32_t it = 0;
       for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
@@ -211,8 +247,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------ WG_F: fold accumulators, store partial h_mix
     const int q = warp & 3;                   // TMEM lane quadrant of this warp
     const int row = 32 * q + lane;            // token row of the tile = TMEM lane
-    uint32_t g = 0;
-    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
+    uint32_t g = 0, uc = 0;
+    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++uc) {
       const int tile = u / p.S_K, ks = u - (u / p.S_K) * p.S_K;
       float part[N_OUT];
 #pragma unroll
@@ -256,24 +292,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B::acc_empty + ab));
       }
+      // this row's sum x^2 from WG_S, then the whole partial row (every
+      // 32-byte sector written in full) with 16-byte stores
+      const int sb = (int)(uc & 1);
+      mbar_wait(bar(B::sq_full + sb), (uc >> 1) & 1, wc);
+      const float sq = sq_buf[sb * kBM + row];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B::sq_empty + sb));
       const int64_t t = (int64_t)tile * kBM + row;
       if (t < p.T && !*abort_flag) {
-        float* dst = p.part + t * p.part_stride + (int64_t)ks * Cf::RW;
+        float rowv[Cf::RW];
 #pragma unroll
-        for (int jj = 0; jj + 4 <= N_OUT; jj += 4)
-          *reinterpret_cast<float4*>(dst + jj) = make_float4(part[jj], part[jj + 1], part[jj + 2], part[jj + 3]);
+        for (int jj = 0; jj < Cf::RW; ++jj) rowv[jj] = jj < N_OUT ? part[jj < N_OUT ? jj : 0] : (jj == N_OUT ? sq : 0.f);
+        float4* dst = reinterpret_cast<float4*>(p.part + t * p.part_stride + (int64_t)ks * Cf::RW);
 #pragma unroll
-        for (int jj = N_OUT / 4 * 4; jj < N_OUT; ++jj) dst[jj] = part[jj];
-#pragma unroll
-        for (int jj = N_OUT + 1; jj < Cf::RW; ++jj) dst[jj] = 0.f;
+        for (int c = 0; c < Cf::RW / 4; ++c)
+          dst[c] = make_float4(rowv[4 * c], rowv[4 * c + 1], rowv[4 * c + 2], rowv[4 * c + 3]);
       }
+      if constexpr (kFused) signal_unit(p.tile_done + tile, lane);
     }
-  } else {
+  } else if (warp < kThreads / 32) {
     // ------------------------------------------------ WG_S: sum of squares, store partial sum x^2
     const int row = 32 * (warp & 3) + lane;   // token row of the tile = smem row
-    uint32_t it = 0;
-    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
-      const int tile = u / p.S_K, ks = u - (u / p.S_K) * p.S_K;
+    uint32_t it = 0, uc = 0;
+    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++uc) {
       float sq = 0.f;
       for (int kb = 0; kb < KB; ++kb, ++it) {
         const int s = it % S;
@@ -295,8 +337,50 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         sq += ((c8[0] + c8[1]) + (c8[2] + c8[3])) + ((c8[4] + c8[5]) + (c8[6] + c8[7]));
       }
-      const int64_t t = (int64_t)tile * kBM + row;
-      if (t < p.T && !*abort_flag) p.part[t * p.part_stride + (int64_t)ks * Cf::RW + N_OUT] = sq;
+      // hand the unit's sum x^2 to WG_F, which stores the partial row
+      const int sb = (int)(uc & 1);
+      mbar_wait(bar(B::sq_empty + sb), ((uc >> 1) & 1) ^ 1, wc);
+      sq_buf[sb * kBM + row] = sq;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B::sq_full + sb));
+    }
+  } else {
+    if constexpr (kFused) {
+      // ---------------------------------------------- WG_R: gates, outputs and h_in of finished tiles
+      // Unit (tile, ks) of this CTA owns rows ks, ks + S_K, ... of the tile;
+      // its rows are dealt round-robin to the kRowWarps warps.  A row waits
+      // until all S_K units of its tile have stored their partials, then
+      // reads x a second time -- from L2, about one round of units after
+      // W0 brought it in.
+      const int rw = warp - kThreads / 32;
+      rowdot::FwdRow<n> k;
+      k.load(p.rows, lane);
+      const int per_unit = (kBM + p.S_K - 1) / p.S_K;
+      const int target = kUnitSignals * p.S_K;
+      int item = 0;
+      bool stop = false;
+      for (int u = blockIdx.x; u < p.num_units && !stop; u += gridDim.x) {
+        const int tile = u / p.S_K, ks = u - (u / p.S_K) * p.S_K;
+        bool ready = false;
+        for (int m = 0; m < per_unit; ++m, ++item) {
+          if (item % kRowWarps != rw) continue;
+          const int r = ks + p.S_K * m;
+          const int64_t t = (int64_t)tile * kBM + r;
+          if (r >= kBM || t >= p.T) continue;
+          if (!ready) {
+            int ok = 0;
+            if (lane == 0) ok = counter_wait(p.tile_done + tile, target, wc) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) {
+              stop = true;
+              break;
+            }
+            (void)ld_acquire(p.tile_done + tile);   // every lane acquires the partials' stores
+            ready = true;
+          }
+          rowdot::fwd_row_token<n>(p.rows, k, t, lane);
+        }
+      }
     }
   }
 
@@ -310,14 +394,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // phi [N_OUT, nD] f32 -> phis [NB, nD] bf16: rows t*N_OUT + j hold the t-th
 // bf16 term of phi[j] (hi, mid, lo: each term rounds what the previous ones
-// left), rows >= NT*N_OUT are zero.
+// left), rows >= NT*N_OUT are zero.  Also zeroes the fused forward's tile
+// counters (tile_done may be null).
 template <int n>
 __global__ void __launch_bounds__(256) split_phi_kernel(const float* __restrict__ phi, uint16_t* __restrict__ phis,
-                                                        int nD) {
+                                                        int nD, int* __restrict__ tile_done, int tiles) {
   // phis [NB][nD]: row term*N_OUT + j holds bf16 term `term` of phi[j]; rows
   // past NT*N_OUT are zero.  Each thread writes 8 consecutive k (one 16-byte
   // store); needs nD % 8 == 0.
   using Cf = Cfg<n>;
+  if (tile_done)
+    for (int64_t i = blockIdx.x * 256ll + threadIdx.x; i < tiles; i += (int64_t)gridDim.x * 256) tile_done[i] = 0;
   const int64_t per_row = nD / 8;
   const int64_t total = (int64_t)Cf::NB * per_row;
   for (int64_t idx = blockIdx.x * 256ll + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * 256) {

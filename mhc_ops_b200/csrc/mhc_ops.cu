@@ -13,6 +13,7 @@
 #include <cstdio>
 #include <string>
 
+#include <map>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -198,9 +199,13 @@ int set_smem_limit_once(Kernel kernel, int bytes) {
 }
 
 // ----------------------------------------------------------------- tensor-core forward
-// Two kernels: fwdtc::proj_kernel (tcgen05 projection -> per (token, K-slice)
-// partial rows, parked in the token's h_in row) and rowdot::fwd_rows_kernel
-// (gates, outputs, h_in).  Shapes they take: n in {4, 8}, D a multiple of 64
+// fwdtc::proj_kernel (tcgen05 projection -> per (token, K-slice) partial rows,
+// parked in the token's h_in row) and the row half (gates, outputs, h_in),
+// either fused into one cooperative launch (proj_kernel<n, true>: row warps
+// follow the projection tile by tile through per-tile counters, so x's second
+// read hits L2) or as a second kernel (rowdot::fwd_rows_kernel) when the
+// fused form's finer K-slices do not fit in an h_in row or the device cannot
+// co-schedule its grid.  Shapes they take: n in {4, 8}, D a multiple of 64
 // whose h_in row holds at least one partial row (n = 8: D >= 192), 16-byte
 // aligned x / h_in / phi, T < 2^31.  Everything else runs the generic kernels.
 int fwd_part_row_bytes(int n) { return 4 * (n == 4 ? fwdtc::Cfg<4>::RW : fwdtc::Cfg<8>::RW); }
@@ -221,28 +226,85 @@ size_t fwd_tc_phis_bytes(int n, int D) {
 }
 
 struct FwdTcPlan {
+  bool fused = false;
   int S_K = 1;      // K-slices
   int KB_PER = 1;   // 64-wide K-blocks per slice
   int units = 1;    // tiles * S_K
   int grid = 1;     // persistent CTAs of proj_kernel
 };
 
-// The fewest K-slices (a divisor of the n*D/64 K-blocks, at most 16, and no
-// more than an h_in row holds) that give every SM at least ~4 units.
+// Fused forward: a unit is at most this many K-blocks (128 KB of x), so one
+// round of units over all SMs reads ~20 MB and x is still in L2 when the row
+// warps read it again (measured on B200: a 256 KB block per SM survives ~55 MB
+// of other traffic, and misses after ~75 MB).
+constexpr int kFusedKbPer = 8;
+
+// K-slices of the fused forward: the fewest (a divisor of the n*D/64
+// K-blocks, at most 128) with units of at most kFusedKbPer K-blocks; 0 when
+// that many partial rows do not fit in an h_in row.
+int fwd_fused_slices(int n, int D) {
+  const int KB = n * D / fwdtc::kBK;
+  for (int sk = 1; sk <= std::min(KB, fwdtc::kBM); ++sk) {
+    if (KB % sk != 0 || KB / sk > kFusedKbPer) continue;
+    return sk * fwd_part_row_bytes(n) <= 2 * D ? sk : 0;
+  }
+  return 0;
+}
+
+// Whether proj_kernel<n, true> can run with one CTA on every SM at once (a
+// cooperative launch needs that); asked once per device.
+template <int n>
+bool fwd_fused_supported() {
+  static std::mutex mu;
+  static std::map<int, bool> known;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = known.find(dev);
+  if (it != known.end()) return it->second;
+  int coop = 0, blocks = 0;
+  bool ok = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) == cudaSuccess && coop &&
+            cudaFuncSetAttribute(fwdtc::proj_kernel<n, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 fwdtc::Cfg<n>::SMEM) == cudaSuccess &&
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fwdtc::proj_kernel<n, true>,
+                                                          fwdtc::kThreadsFused, fwdtc::Cfg<n>::SMEM) == cudaSuccess &&
+            blocks >= 1;
+  (void)cudaGetLastError();
+  known[dev] = ok;
+  return ok;
+}
+
+// n = 8 never qualifies (its K-slices of at most kFusedKbPer blocks need more
+// partial rows than an h_in row holds), so only n = 4 is instantiated.
+bool fwd_fused_supported(int n) { return n == 4 && fwd_fused_supported<4>(); }
+
+// Two-kernel form: the fewest K-slices (a divisor of the n*D/64 K-blocks, at
+// most 16, and no more than an h_in row holds) that give every SM at least
+// ~4 units.  Fused form: fwd_fused_slices, one CTA per SM at most.
 FwdTcPlan fwd_tc_plan(int64_t T, int n, int D, int sms) {
   FwdTcPlan P;
   const int KB = n * D / fwdtc::kBK;
   const int64_t tiles = std::max<int64_t>(1, (T + fwdtc::kBM - 1) / fwdtc::kBM);
-  const int max_sk = std::min(16, 2 * D / fwd_part_row_bytes(n));
-  for (int sk = 1; sk <= max_sk; ++sk) {
-    if (KB % sk != 0) continue;
-    P.S_K = sk;
-    if (tiles * sk >= 4 * (int64_t)sms) break;
+  const int fused_sk = fwd_fused_slices(n, D);
+  if (fused_sk > 0 && fwd_fused_supported(n)) {
+    P.fused = true;
+    P.S_K = fused_sk;
+  } else {
+    const int max_sk = std::min(16, 2 * D / fwd_part_row_bytes(n));
+    for (int sk = 1; sk <= max_sk; ++sk) {
+      if (KB % sk != 0) continue;
+      P.S_K = sk;
+      if (tiles * sk >= 4 * (int64_t)sms) break;
+    }
   }
   P.KB_PER = KB / P.S_K;
   P.units = (int)(tiles * P.S_K);
   P.grid = std::min(P.units, sms);
   return P;
+}
+
+size_t fwd_tile_counter_bytes(int64_t T) {
+  return sizeof(int) * (size_t)std::max<int64_t>(1, (T + fwdtc::kBM - 1) / fwdtc::kBM);
 }
 
 int fwd_rows_grid(int64_t T, int sms) {
@@ -251,6 +313,27 @@ int fwd_rows_grid(int64_t T, int sms) {
 
 template <int n>
 struct FwdTc {
+  // One cooperative launch of proj_kernel<n, true> (all CTAs co-resident:
+  // row warps wait on counters other CTAs advance).
+  static int launch_fused(const CUtensorMap& m_x2d, const CUtensorMap& m_phi, const fwdtc::Params& p,
+                          const FwdTcPlan& P, cudaStream_t s) {
+    using Cf = fwdtc::Cfg<n>;
+    int st;
+    if ((st = set_smem_limit_once(fwdtc::proj_kernel<n, true>, Cf::SMEM))) return st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(P.grid);
+    cfg.blockDim = dim3(fwdtc::kThreadsFused);
+    cfg.dynamicSmemBytes = Cf::SMEM;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    MHC_CUDA_TRY(cudaLaunchKernelEx(&cfg, fwdtc::proj_kernel<n, true>, m_x2d, m_phi, p));
+    return after_launch();
+  }
+
   static int run(const mhc_fwd_args* a, cudaStream_t s, int sms) {
     using Cf = fwdtc::Cfg<n>;
     const int64_t T = a->tokens;
@@ -258,11 +341,13 @@ struct FwdTc {
     const int nD = n * D;
     char* ws = static_cast<char*>(a->workspace);
     uint16_t* phis = reinterpret_cast<uint16_t*>(ws + kWsHeaderBytes);
+    int* tile_done = reinterpret_cast<int*>(ws + align_up(kWsHeaderBytes + fwd_tc_phis_bytes(n, D), kWsAlign));
     const FwdTcPlan P = fwd_tc_plan(T, n, D, sms);
+    const int tiles = (int)((T + fwdtc::kBM - 1) / fwdtc::kBM);
     int st;
 
     fwdtc::split_phi_kernel<n><<<std::min<int64_t>(((int64_t)Cf::NB * nD / 8 + 255) / 256, 4 * 148), 256, 0, s>>>(
-        a->phi, phis, nD);
+        a->phi, phis, nD, P.fused ? tile_done : nullptr, tiles);
     if ((st = after_launch())) return st;
 
     CUtensorMap m_x2d, m_phi;
@@ -286,20 +371,40 @@ struct FwdTc {
     p.S_K = P.S_K;
     p.KB_PER = P.KB_PER;
     p.num_units = P.units;
-    if ((st = set_smem_limit_once(fwdtc::proj_kernel<n>, Cf::SMEM))) return st;
-    fwdtc::proj_kernel<n><<<P.grid, fwdtc::kThreads, Cf::SMEM, s>>>(m_x2d, m_phi, p);
+    p.tile_done = tile_done;
+    p.rows.x = a->x;
+    p.rows.alpha = a->alpha;
+    p.rows.bias = a->bias;
+    p.rows.h_in = a->h_in;
+    p.rows.h_post = a->h_post;
+    p.rows.h_res = a->h_res;
+    p.rows.inv_rms = a->inv_rms;
+    p.rows.h_mix = a->h_mix;
+    p.rows.h_pre = a->h_pre;
+    p.rows.D = D;
+    p.rows.S_K = P.S_K;
+    p.rows.RW = Cf::RW;
+    p.rows.norm_eps = a->norm_eps;
+    p.rows.hc_eps = a->hc_eps;
+    if constexpr (n == 4) {
+      if (P.fused) return launch_fused(m_x2d, m_phi, p, P, s);
+    }
+    if ((st = set_smem_limit_once(fwdtc::proj_kernel<n, false>, Cf::SMEM))) return st;
+    fwdtc::proj_kernel<n, false><<<P.grid, fwdtc::kThreads, Cf::SMEM, s>>>(m_x2d, m_phi, p);
     if ((st = after_launch())) return st;
-    rowdot::fwd_rows_kernel<n><<<fwd_rows_grid(T, sms), rowdot::kThreads, 0, s>>>(
-        a->x, a->alpha, a->bias, a->h_in, a->h_post, a->h_res, a->inv_rms, a->h_mix, a->h_pre, T, D, P.S_K, Cf::RW,
-        a->norm_eps, a->hc_eps);
+    rowdot::fwd_rows_kernel<n><<<fwd_rows_grid(T, sms), rowdot::kThreads, 0, s>>>(p.rows, T);
     return after_launch();
   }
 };
 
+// Header (status word), split-phi images, then the fused form's per-tile
+// counters.
 int fwd_workspace(int64_t T, int n, int D, size_t* bytes) {
-  (void)T;
   size_t b = kWsHeaderBytes;
-  if (fwd_tc_shape(T, n, D)) b = align_up(b + fwd_tc_phis_bytes(n, D), kWsAlign);
+  if (fwd_tc_shape(T, n, D)) {
+    b = align_up(b + fwd_tc_phis_bytes(n, D), kWsAlign);
+    b = align_up(b + fwd_tile_counter_bytes(T), kWsAlign);
+  }
   *bytes = b;
   return MHC_OK;
 }
@@ -648,7 +753,7 @@ int mhc_query_plan(int which, int64_t tokens, int32_t n, int32_t D, int* path, i
   *clusters = 0;
   if (which == 0 && fwd_tc_shape(tokens, n, D)) {
     const FwdTcPlan fp = fwd_tc_plan(tokens, n, D, sms);
-    *path = 1;
+    *path = fp.fused ? 2 : 1;
     *cluster_size = fp.S_K;
     *clusters = fp.grid;
   } else if (which == 1 && bwd_tc_shape(tokens, n, D)) {

@@ -185,111 +185,140 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_rows_kernel(
   }
 }
 
-// Forward, second kernel (src/forward/golden.py:34-69).  Per token t (warp t
-// % W): sum the S_K partial rows [h_mix (N_OUT), sum x^2] the projection
-// kernel parked in h_in's row t, in slice order; inv_rms = 1/sqrt(sum x^2 / nD
-// + norm_eps); gates from h_mix * inv_rms; then h_in[t, d] = bf16(sum_i
-// h_pre[t,i] x[t,i,d]) streamed over the row (all partial loads of the warp
-// complete, through the shuffles, before its first h_in store).
-// Needs D % 8 == 0 and 16-byte aligned x / h_in.
-template <int n>
-__global__ void __launch_bounds__(kThreads, 1) fwd_rows_kernel(
-    const uint16_t* __restrict__ x, const float* __restrict__ alpha, const float* __restrict__ bias,
-    uint16_t* h_in, float* __restrict__ h_post, float* __restrict__ h_res, float* __restrict__ inv_rms,
-    float* __restrict__ h_mix, float* __restrict__ h_pre, int64_t T, int D, int S_K, int RW, float norm_eps,
-    float hc_eps) {
-  constexpr int N_OUT = n * n + 2 * n;
-  constexpr int M = (N_OUT + 1 + 31) / 32;   // partial columns per lane (N_OUT outputs + sum x^2)
-  const int lane = threadIdx.x & 31;
-  const int64_t gw = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
-  const int64_t W = (int64_t)gridDim.x * kWarps;
-  const int nD = n * D;
-  const float inv_nd = 1.0f / (float)nD;
-  const float a_pre = alpha[0], a_post = alpha[1], a_res = alpha[2];
-  float bj[M];
-#pragma unroll
-  for (int m = 0; m < M; ++m) bj[m] = (lane + 32 * m) < N_OUT ? __ldg(bias + lane + 32 * m) : 0.f;
+// Forward, row half (src/forward/golden.py:34-69), per token t: sum the S_K
+// partial rows [h_mix (N_OUT), sum x^2] the projection parked in h_in's row t,
+// in slice order; inv_rms = 1/sqrt(sum x^2 / nD + norm_eps); gates from
+// h_mix * inv_rms; then h_in[t, d] = bf16(sum_i h_pre[t,i] x[t,i,d]) streamed
+// over the row (all partial loads of the warp complete, through the
+// shuffles, before its first h_in store).  The partials are read with plain
+// (coherent) loads: in the fused forward other CTAs wrote them during the
+// same launch.  Needs D % 8 == 0 and 16-byte aligned x / h_in.
+struct FwdRowArgs {
+  const uint16_t* x;
+  const float* alpha;   // [3]
+  const float* bias;    // [N_OUT]
+  uint16_t* h_in;
+  float* h_post;
+  float* h_res;
+  float* inv_rms;   // optional
+  float* h_mix;     // optional
+  float* h_pre;     // optional
+  int D, S_K, RW;
+  float norm_eps, hc_eps;
+};
 
-  for (int64_t t = gw; t < T; t += W) {
-    // (1) partial rows of token t, summed in slice order
-    const float* pr = reinterpret_cast<const float*>(h_in + t * D);
-    float hm[M];
+// Per-warp constants: alpha and this lane's bias entries.
+template <int n>
+struct FwdRow {
+  static constexpr int N_OUT = n * n + 2 * n;
+  static constexpr int M = (N_OUT + 1 + 31) / 32;   // partial columns per lane (N_OUT outputs + sum x^2)
+  float a_pre, a_post, a_res, inv_nd;
+  float bj[M];
+  __device__ __forceinline__ void load(const FwdRowArgs& a, int lane) {
+    a_pre = __ldg(a.alpha);
+    a_post = __ldg(a.alpha + 1);
+    a_res = __ldg(a.alpha + 2);
+    inv_nd = 1.0f / (float)(n * a.D);
 #pragma unroll
-    for (int m = 0; m < M; ++m) {
-      const int c = lane + 32 * m;
-      float acc = 0.f;
-      if (c <= N_OUT)
-        for (int ks = 0; ks < S_K; ++ks) acc += pr[ks * RW + c];
-      hm[m] = acc;
-    }
-    const float sq = __shfl_sync(0xffffffffu, hm[N_OUT / 32], N_OUT % 32);
-    const float ir = 1.0f / sqrtf(sq * inv_nd + norm_eps);
-    // (2) gates and the fp32 outputs
-    float hp_lane = 0.f;
+    for (int m = 0; m < M; ++m) bj[m] = (lane + 32 * m) < N_OUT ? __ldg(a.bias + lane + 32 * m) : 0.f;
+  }
+};
+
+template <int n>
+__device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<n>& k, int64_t t, int lane) {
+  constexpr int N_OUT = FwdRow<n>::N_OUT;
+  constexpr int M = FwdRow<n>::M;
+  const int D = a.D;
+  const int64_t nD = (int64_t)n * D;
+  // (1) partial rows of token t, summed in slice order
+  const float* pr = reinterpret_cast<const float*>(a.h_in + t * D);
+  float hm[M];
 #pragma unroll
-    for (int m = 0; m < M; ++m) {
-      const int jj = lane + 32 * m;
-      if (jj < N_OUT) {
-        const float v = hm[m] * ir;
-        if (jj < n) {
-          hp_lane = sigmoid_acc(a_pre * v + bj[m]) + hc_eps;
-          if (h_pre) h_pre[t * n + jj] = hp_lane;
-        } else if (jj < 2 * n) {
-          h_post[t * n + (jj - n)] = 2.0f * sigmoid_acc(a_post * v + bj[m]);
-        } else {
-          h_res[t * (n * n) + (jj - 2 * n)] = a_res * v + bj[m];
-        }
-        if (h_mix) h_mix[t * N_OUT + jj] = hm[m];
+  for (int m = 0; m < M; ++m) {
+    const int c = lane + 32 * m;
+    float acc = 0.f;
+    if (c <= N_OUT)
+      for (int ks = 0; ks < a.S_K; ++ks) acc += pr[ks * a.RW + c];
+    hm[m] = acc;
+  }
+  const float sq = __shfl_sync(0xffffffffu, hm[N_OUT / 32], N_OUT % 32);
+  const float ir = 1.0f / sqrtf(sq * k.inv_nd + a.norm_eps);
+  // (2) gates and the fp32 outputs
+  float hp_lane = 0.f;
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    const int jj = lane + 32 * m;
+    if (jj < N_OUT) {
+      const float v = hm[m] * ir;
+      if (jj < n) {
+        hp_lane = sigmoid_acc(k.a_pre * v + k.bj[m]) + a.hc_eps;
+        if (a.h_pre) a.h_pre[t * n + jj] = hp_lane;
+      } else if (jj < 2 * n) {
+        a.h_post[t * n + (jj - n)] = 2.0f * sigmoid_acc(k.a_post * v + k.bj[m]);
+      } else {
+        a.h_res[t * (n * n) + (jj - 2 * n)] = k.a_res * v + k.bj[m];
       }
+      if (a.h_mix) a.h_mix[t * N_OUT + jj] = hm[m];
     }
-    if (lane == 0 && inv_rms) inv_rms[t] = ir;
-    // Every lane has used its partials (the stores above consume them): only
-    // now may row t of h_in, which holds them, be overwritten.
-    __syncwarp();
-    asm volatile("" ::: "memory");
-    float hp[n];
+  }
+  if (lane == 0 && a.inv_rms) a.inv_rms[t] = ir;
+  // Every lane has used its partials (the stores above consume them): only
+  // now may row t of h_in, which holds them, be overwritten.
+  __syncwarp();
+  asm volatile("" ::: "memory");
+  float hp[n];
 #pragma unroll
-    for (int i = 0; i < n; ++i) hp[i] = __shfl_sync(0xffffffffu, hp_lane, i);
-    // (3) h_in = sum_i h_pre[i] x[i, :], streamed (U 256-element chunks in flight per lane)
-    const uint16_t* xr = x + t * nD;
-    uint16_t* hr = h_in + t * D;
-    constexpr int U = n <= 4 ? 4 : 2;
-    for (int c0 = 0; c0 < D; c0 += 256 * U) {
-      uint4 xv[U][n];
+  for (int i = 0; i < n; ++i) hp[i] = __shfl_sync(0xffffffffu, hp_lane, i);
+  // (3) h_in = sum_i h_pre[i] x[i, :], streamed (U 256-element chunks in flight per lane)
+  const uint16_t* xr = a.x + t * nD;
+  uint16_t* hr = a.h_in + t * D;
+  constexpr int U = n <= 4 ? 4 : 2;
+  for (int c0 = 0; c0 < D; c0 += 256 * U) {
+    uint4 xv[U][n];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int d = c0 + u * 256 + lane * 8;
+    for (int u = 0; u < U; ++u) {
+      const int d = c0 + u * 256 + lane * 8;
 #pragma unroll
-        for (int i = 0; i < n; ++i) xv[u][i] = d < D ? ldg_stream(xr + (int64_t)i * D + d) : make_uint4(0, 0, 0, 0);
-      }
+      for (int i = 0; i < n; ++i) xv[u][i] = d < D ? ldg_stream(xr + (int64_t)i * D + d) : make_uint4(0, 0, 0, 0);
+    }
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int d = c0 + u * 256 + lane * 8;
-        if (d < D) {
-          float acc[8];
-          {
-            float f[8];
-            bf16x8(xv[u][0], f);
+    for (int u = 0; u < U; ++u) {
+      const int d = c0 + u * 256 + lane * 8;
+      if (d < D) {
+        float acc[8];
+        {
+          float f[8];
+          bf16x8(xv[u][0], f);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) acc[e] = hp[0] * f[e];
-          }
-#pragma unroll
-          for (int i = 1; i < n; ++i) {
-            float f[8];
-            bf16x8(xv[u][i], f);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc[e] = fmaf(hp[i], f[e], acc[e]);
-          }
-          uint4 o;
-          o.x = pack_bf16x2(acc[0], acc[1]);
-          o.y = pack_bf16x2(acc[2], acc[3]);
-          o.z = pack_bf16x2(acc[4], acc[5]);
-          o.w = pack_bf16x2(acc[6], acc[7]);
-          *reinterpret_cast<uint4*>(hr + d) = o;
+          for (int e = 0; e < 8; ++e) acc[e] = hp[0] * f[e];
         }
+#pragma unroll
+        for (int i = 1; i < n; ++i) {
+          float f[8];
+          bf16x8(xv[u][i], f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] = fmaf(hp[i], f[e], acc[e]);
+        }
+        uint4 o;
+        o.x = pack_bf16x2(acc[0], acc[1]);
+        o.y = pack_bf16x2(acc[2], acc[3]);
+        o.z = pack_bf16x2(acc[4], acc[5]);
+        o.w = pack_bf16x2(acc[6], acc[7]);
+        *reinterpret_cast<uint4*>(hr + d) = o;
       }
     }
   }
+}
+
+// Forward, second kernel of the two-kernel forward: warp t % W takes token t.
+template <int n>
+__global__ void __launch_bounds__(kThreads, 1) fwd_rows_kernel(const FwdRowArgs a, int64_t T) {
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int64_t W = (int64_t)gridDim.x * kWarps;
+  FwdRow<n> k;
+  k.load(a, lane);
+  for (int64_t t = gw; t < T; t += W) fwd_row_token<n>(a, k, t, lane);
 }
 
 }  // namespace rowdot

@@ -86,6 +86,43 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
   }
 }
 
+// ------------------------------------------------------------------ counters between CTAs of one launch
+__device__ __forceinline__ void red_release_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Wait until *counter >= target (written by other CTAs of the same
+// cooperative launch); same time limit and abort protocol as mbar_wait.
+// Polls back off to one per ~2 us: every poll is an L2 access, and with
+// hundreds of warps waiting, fast polling measurably slows the memory
+// streams of the kernels around them.
+__device__ __forceinline__ bool counter_wait(const int* counter, int target, const WaitCtx& w) {
+  if (*w.abort) return false;
+  if (ld_acquire(counter) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t sleep_ns = 256;
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i) {
+      __nanosleep(sleep_ns);
+      if (sleep_ns < 2048) sleep_ns *= 2;
+      if (ld_acquire(counter) >= target) return true;
+    }
+    if (*w.abort) return false;
+    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      *w.abort = 1;
+      set_device_status(w.status, MHC_ERR_DEVICE_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   uint64_t p;
