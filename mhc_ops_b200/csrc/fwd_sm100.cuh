@@ -56,6 +56,12 @@ constexpr int kThreads = 10 * 32; // W0, W1, WG_F(4), WG_S(4)
 constexpr int kRowWarps = 8;      // WG_R of the fused forward
 constexpr int kThreadsFused = kThreads + kRowWarps * 32;
 constexpr int kUnitSignals = 4;   // WG_F warps: arrivals on a tile's counter per unit
+// Fused form: W0 starts this CTA's unit j only once WG_R has finished unit
+// j - kRowLag.  Without a bound the projection can run away from the row
+// warps, whose second read of x then misses L2 and slows them further.  The
+// rows of a unit need only units of the same or the next round (a tile's
+// S_K units are consecutive), so any kRowLag >= 2 cannot deadlock.
+constexpr int kRowLag = 5;
 constexpr int kKG = 2;            // K-blocks accumulated per TMEM accumulator
 constexpr int kSmemLimit = 232448;
 
@@ -144,6 +150,29 @@ __device__ __forceinline__ void signal_unit(int* counter, int lane) {
   if (lane == 0) red_release_add(counter, 1);
 }
 
+// W0 of the fused form: wait until every WG_R warp has finished `need` units
+// (a progress hint in shared memory, no data passes); bounded like mbar_wait.
+__device__ __forceinline__ void wait_rows_done(volatile int* rows_done, int need, const WaitCtx& w) {
+  uint64_t t0 = 0;
+  for (uint32_t spin = 0;; ++spin) {
+    int m = rows_done[0];
+#pragma unroll
+    for (int i = 1; i < kRowWarps; ++i) m = min(m, rows_done[i]);
+    if (m >= need || *w.abort) return;
+    __nanosleep(128);
+    if ((spin & 255) == 0) {
+      const uint64_t now = globaltimer_ns();
+      if (spin == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitTimeoutNs) {
+        *w.abort = 1;
+        set_device_status(w.status, MHC_ERR_DEVICE_TIMEOUT);
+        return;
+      }
+    }
+  }
+}
+
 template <int n, bool kFused>
 __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
     proj_kernel(const __grid_constant__ CUtensorMap map_x2d, const __grid_constant__ CUtensorMap map_phi,
@@ -159,6 +188,7 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(ring + S * Cf::STAGE_BYTES + Cf::SQ_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + B::count);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* rows_done = reinterpret_cast<volatile int*>(tmem_slot + 2);   // fused: [kRowWarps] units done
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -178,6 +208,8 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
       mbar_init(bar(B::sq_empty + i), 4);
     }
     *abort_flag = 0;
+    if (kFused)
+      for (int i = 0; i < kRowWarps; ++i) rows_done[i] = 0;
     fence_mbarrier_init_cluster();
   }
   if (warp == 1) {
@@ -202,8 +234,12 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
       const uint64_t pol_x = kFused ? l2_policy_evict_last() : l2_policy_evict_first();
       const uint64_t pol_phi = l2_policy_evict_last();
       uint32_t it = 0;
-      for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
+      int lu = 0;   // this CTA's unit count
+      for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++lu) {
         const int tile = u / p.S_K, ks = u - (u / p.S_K) * p.S_K;
+        if constexpr (kFused) {
+          if (lu >= kRowLag) wait_rows_done(rows_done, lu - kRowLag + 1, wc);
+        }
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % S;
           const int k0 = (ks * KB + kb) * kBK;
@@ -357,9 +393,9 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
       k.load(p.rows, lane);
       const int per_unit = (kBM + p.S_K - 1) / p.S_K;
       const int target = kUnitSignals * p.S_K;
-      int item = 0;
+      int item = 0, lu = 0;
       bool stop = false;
-      for (int u = blockIdx.x; u < p.num_units && !stop; u += gridDim.x) {
+      for (int u = blockIdx.x; u < p.num_units && !stop; u += gridDim.x, ++lu) {
         const int tile = u / p.S_K, ks = u - (u / p.S_K) * p.S_K;
         bool ready = false;
         for (int m = 0; m < per_unit; ++m, ++item) {
@@ -380,7 +416,9 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
           }
           rowdot::fwd_row_token<n>(p.rows, k, t, lane);
         }
+        if (lane == 0) rows_done[rw] = lu + 1;
       }
+      if (lane == 0) rows_done[rw] = 1 << 30;   // done (or stopped): never hold W0 back again
     }
   }
 

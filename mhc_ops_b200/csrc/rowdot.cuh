@@ -224,12 +224,13 @@ struct FwdRow {
   }
 };
 
+// Steps (1) and (2) of token t; returns h_pre[t, lane] in lanes 0..n-1.
+// After it returns, every lane is done with the partials in h_in's row t.
 template <int n>
-__device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<n>& k, int64_t t, int lane) {
+__device__ __forceinline__ float fwd_row_gates(const FwdRowArgs& a, const FwdRow<n>& k, int64_t t, int lane) {
   constexpr int N_OUT = FwdRow<n>::N_OUT;
   constexpr int M = FwdRow<n>::M;
   const int D = a.D;
-  const int64_t nD = (int64_t)n * D;
   // (1) partial rows of token t, summed in slice order
   const float* pr = reinterpret_cast<const float*>(a.h_in + t * D);
   float hm[M];
@@ -266,6 +267,14 @@ __device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<
   // now may row t of h_in, which holds them, be overwritten.
   __syncwarp();
   asm volatile("" ::: "memory");
+  return hp_lane;
+}
+
+template <int n>
+__device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<n>& k, int64_t t, int lane) {
+  const int D = a.D;
+  const int64_t nD = (int64_t)n * D;
+  const float hp_lane = fwd_row_gates<n>(a, k, t, lane);
   float hp[n];
 #pragma unroll
   for (int i = 0; i < n; ++i) hp[i] = __shfl_sync(0xffffffffu, hp_lane, i);
