@@ -135,12 +135,13 @@ MHC_API int mhc_fwd(const mhc_fwd_args* args, void* stream);
  * Same arguments, validation, kernels and results as mhc_fwd, except that
  * args->workspace and args->workspace_bytes are ignored.  The scratch the
  * forward needs (the bf16 split-phi images, 160 bytes per element of phi's
- * n*D row for n = 4 and 320 for n = 8) comes from one 16 MiB device array
- * inside the library.  Every GPU that loads the library holds those 16 MiB
- * until the process exits.
- *   Limit: a shape needing more than 16 MiB returns MHC_ERR_LIMIT.  That
- *   means D > 26176 for n = 4 and D > 6528 for n = 8 (D a multiple of 64);
- *   other shapes need only the 256-byte status header.
+ * n*D row for n = 4 and 320 for n = 8, plus 4 bytes per 128 tokens) comes
+ * from one 16 MiB device array inside the library.  Every GPU that loads the
+ * library holds those 16 MiB until the process exits.
+ *   Limit: a shape needing more than 16 MiB returns MHC_ERR_LIMIT.  Up to
+ *   778,240 tokens that means D > 26176 for n = 4 and D > 6528 for n = 8
+ *   (D a multiple of 64); more tokens lower the limit by 4 bytes per 128
+ *   tokens.  Other shapes need only the 256-byte status header.
  *   The first call on each device looks up the array's device address, with
  *   that device current.  Make that first call before any stream capture.
  *   Every call on a device uses the same array.  Calls that overlap on the

@@ -580,7 +580,8 @@ __global__ void wait_expiry_kernel(int* status) {
 
 // ----------------------------------------------------------------- forward without a caller workspace
 // Scratch of mhc_fwd_static: the forward's workspace (the status word in the
-// first kWsHeaderBytes, then the bf16 split-phi images) carved from one
+// first kWsHeaderBytes, the bf16 split-phi images, the per-tile counters)
+// carved from one
 // file-scope device array instead of caller memory.  Every device that loads
 // the library holds the array until the process exits.
 constexpr size_t kStaticScratchBytes = (size_t)16 << 20;
@@ -723,9 +724,9 @@ int mhc_fwd_static(const mhc_fwd_args* a, void* stream) {
   void* scratch = nullptr;
   if ((st = static_scratch_address(&scratch))) return st;
   // Same validation and kernels as mhc_fwd; only the workspace differs.  The
-  // split-phi images are rewritten in full (padding rows included) by every
-  // call and the status word is only ever written, so nothing in the array
-  // has to start at zero.
+  // split-phi images are rewritten in full (padding rows included) and the
+  // tile counters zeroed by every call, and the status word is only ever
+  // written, so nothing in the array has to start at zero.
   mhc_fwd_args b = *a;
   b.workspace = scratch;
   b.workspace_bytes = kStaticScratchBytes;
