@@ -257,7 +257,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int Dc = p.Dc;
   const int DCH = Dc / kBK;
   const int nD = n * D;
-  const int KC = n * Dc;
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   // Tiles run last-first, so the first ones re-read what the row kernel read last.
   auto tile_of = [&](int j) { return p.num_tiles - 1 - (group + j * p.S_T); };

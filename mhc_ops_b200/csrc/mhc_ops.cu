@@ -24,6 +24,7 @@
 #include "fwd_sm100.cuh"
 #include "bwd_sm100.cuh"
 #include "rowdot.cuh"
+#include "tiled.cuh"
 
 namespace mhc {
 
@@ -551,9 +552,94 @@ int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s, int sms) {
   return after_launch();
 }
 
+// ----------------------------------------------------------------- tiled backward (CUDA cores)
+// rowdot::bwd_rows_kernel (records), tiled::dx_kernel, tiled::g_kernel, then
+// the shared finalize kernels.  Shapes: every n the tensor-core backward does
+// not take, D a multiple of 8, 16-byte aligned x / dh_in / dx / phi / gamma,
+// T < 2^31.
+struct BwdTiledLayout {
+  size_t rec, abpart, gpart, total;
+  int P;                 // token splits of the G partials
+  int64_t per_split;     // tokens per split
+  int rows_grid;
+};
+
+int rec_width(int n) {
+  const int N = n * n + 2 * n;
+  return ((N + 1 + n) + 3) / 4 * 4;
+}
+
+BwdTiledLayout bwd_tiled_layout(int64_t T, int n, int D, int sms) {
+  BwdTiledLayout L{};
+  const int N = n * n + 2 * n;
+  const int64_t nD = (int64_t)n * D;
+  const int64_t kblocks = (nD + tiled::kKT - 1) / tiled::kKT;
+  int64_t P = std::max<int64_t>(1, (4 * (int64_t)sms + kblocks - 1) / kblocks);
+  P = std::min<int64_t>(P, std::max<int64_t>(1, (T + tiled::kTC - 1) / tiled::kTC));
+  P = std::min<int64_t>(P, 64);
+  L.P = (int)P;
+  L.per_split = T > 0 ? (T + P - 1) / P : 1;
+  L.per_split = (L.per_split + tiled::kTC - 1) / tiled::kTC * tiled::kTC;
+  L.rows_grid = bwd_rows_grid(T, sms);
+  size_t off = kWsHeaderBytes;
+  L.rec = off;
+  off = align_up(off + sizeof(float) * (size_t)T * rec_width(n), kWsAlign);
+  L.abpart = off;
+  off = align_up(off + sizeof(float) * (size_t)L.rows_grid * kRowsWarps * (3 + N), kWsAlign);
+  L.gpart = off;
+  off = align_up(off + sizeof(float) * (size_t)L.P * N * nD, kWsAlign);
+  L.total = off;
+  return L;
+}
+
+bool bwd_tiled_shape(int64_t T, int n, int D) {
+  return n >= 1 && n <= 8 && D % 8 == 0 && T < ((int64_t)1 << 31);
+}
+
+bool bwd_tiled_eligible(const mhc_bwd_args* a) {
+  return bwd_tiled_shape(a->tokens, a->n, a->D) && aligned(a->x, 16) && aligned(a->dh_in, 16) &&
+         aligned(a->dx, 16) && aligned(a->phi, 16) && aligned(a->gamma, 16);
+}
+
+template <int n>
+struct BwdTiled {
+  static int run(const mhc_bwd_args* a, cudaStream_t s, int sms) {
+    using Dm = tiled::Dims<n>;
+    constexpr int N = Dm::N;
+    static_assert(Dm::RW == rowdot::Rec<n>::W && 3 + N == rowdot::Rec<n>::CW, "record layouts differ");
+    const int64_t T = a->tokens;
+    const int D = a->D;
+    const int nD = n * D;
+    const BwdTiledLayout L = bwd_tiled_layout(T, n, D, sms);
+    char* ws = static_cast<char*>(a->workspace);
+    float* rec = reinterpret_cast<float*>(ws + L.rec);
+    float* abpart = reinterpret_cast<float*>(ws + L.abpart);
+    float* gpart = reinterpret_cast<float*>(ws + L.gpart);
+    int st;
+    rowdot::bwd_rows_kernel<n><<<L.rows_grid, rowdot::kThreads, 0, s>>>(
+        a->x, a->dh_in, a->alpha, a->inv_rms, a->h_mix, a->h_pre, a->h_post, a->dh_post, a->dh_res, rec, abpart, T, D,
+        a->hc_eps);
+    if ((st = after_launch())) return st;
+    if ((st = set_smem_limit_once(tiled::dx_kernel<n>, Dm::DX_SMEM))) return st;
+    const dim3 gdx((unsigned)((T + tiled::kTT - 1) / tiled::kTT), (unsigned)((nD + tiled::kKT - 1) / tiled::kKT));
+    tiled::dx_kernel<n><<<gdx, tiled::kThreads, Dm::DX_SMEM, s>>>(a->x, a->phi, a->gamma, rec, a->dh_in, a->dx, T, D);
+    if ((st = after_launch())) return st;
+    const dim3 gg((unsigned)((nD + tiled::kKT - 1) / tiled::kKT), (unsigned)L.P);
+    tiled::g_kernel<n><<<gg, tiled::kThreads, 0, s>>>(a->x, rec, gpart, T, nD, L.per_split);
+    if ((st = after_launch())) return st;
+    generic::finalize_param_kernel<<<(nD + generic::kFinCols - 1) / generic::kFinCols, generic::kThreads, 0, s>>>(
+        gpart, L.P, N, a->phi, a->gamma, a->dphi, a->dgamma, nD);
+    if ((st = after_launch())) return st;
+    generic::reduce_columns_kernel<<<3 + N, generic::kThreads, 0, s>>>(
+        abpart, (int64_t)L.rows_grid * kRowsWarps, 3 + N, a->dalpha, a->dbias);
+    return after_launch();
+  }
+};
+
 int bwd_workspace(int64_t T, int n, int D, int sms, size_t* bytes) {
   size_t b = bwd_generic_layout(T, n, D, sms).total;
   if (bwd_tc_shape(T, n, D)) b = std::max(b, bwd_tc_layout(T, D, sms).total);
+  if (bwd_tiled_shape(T, n, D)) b = std::max(b, bwd_tiled_layout(T, n, D, sms).total);
   *bytes = b;
   return MHC_OK;
 }
@@ -709,6 +795,7 @@ int mhc_bwd(const mhc_bwd_args* a, void* stream) {
       !aligned(a->dalpha, 4) || !aligned(a->dbias, 4) || !aligned(a->dgamma, 4))
     return MHC_ERR_MISALIGNED;
   if (bwd_tc_eligible(a)) return bwd_tc_run(a, s, sms);
+  if (bwd_tiled_eligible(a)) return dispatch_n<BwdTiled>(a->n, a, s, sms);
   return dispatch_n<BwdGeneric>(a->n, a, s, sms);
 }
 
@@ -762,6 +849,9 @@ int mhc_query_plan(int which, int64_t tokens, int32_t n, int32_t D, int* path, i
     *path = 1;
     *cluster_size = bp.S_K;
     *clusters = bp.S_T;
+  } else if (which == 1 && bwd_tiled_shape(tokens, n, D)) {
+    *path = 3;
+    *cluster_size = bwd_tiled_layout(tokens, n, D, sms).P;
   } else if (which != 0 && which != 1) {
     return MHC_ERR_BAD_SHAPE;
   }

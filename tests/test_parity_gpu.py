@@ -82,6 +82,8 @@ def test_readme_backward_shapes_vs_oracle(B, S, D):
     (3, 1, 4, 64, True),         # a handful of tokens
     (1, 33, 2, 40, True),        # n=2, D not a multiple of 64
     (1, 50, 3, 24, True),        # odd n
+    (1, 300, 8, 1024, False),    # n=8 tiled backward, ragged token tiles, gamma=None
+    (1, 70, 6, 512, True),       # n=6 tiled backward
 ])
 def test_wide_rows_vs_oracle(B, S, n, D, gamma):
     _live_case(B, S, n, D, seed=12, gamma=gamma)
