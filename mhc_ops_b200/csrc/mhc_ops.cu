@@ -558,7 +558,7 @@ int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s, int sms) {
 // not take, D a multiple of 8, 16-byte aligned x / dh_in / dx / phi / gamma,
 // T < 2^31.
 struct BwdTiledLayout {
-  size_t rec, abpart, gpart, total;
+  size_t rec, abpart, gpart, dmT, total;
   int P;                 // token splits of the G partials
   int64_t per_split;     // tokens per split
   int rows_grid;
@@ -588,6 +588,8 @@ BwdTiledLayout bwd_tiled_layout(int64_t T, int n, int D, int sms) {
   off = align_up(off + sizeof(float) * (size_t)L.rows_grid * kRowsWarps * (3 + N), kWsAlign);
   L.gpart = off;
   off = align_up(off + sizeof(float) * (size_t)L.P * N * nD, kWsAlign);
+  L.dmT = off;
+  off = align_up(off + sizeof(float) * (size_t)N * tiled::padded_tokens(T), kWsAlign);
   L.total = off;
   return L;
 }
@@ -615,14 +617,20 @@ struct BwdTiled {
     float* rec = reinterpret_cast<float*>(ws + L.rec);
     float* abpart = reinterpret_cast<float*>(ws + L.abpart);
     float* gpart = reinterpret_cast<float*>(ws + L.gpart);
+    float* dmT = reinterpret_cast<float*>(ws + L.dmT);
+    const int64_t Tp = tiled::padded_tokens(T);
     int st;
     rowdot::bwd_rows_kernel<n><<<L.rows_grid, rowdot::kThreads, 0, s>>>(
         a->x, a->dh_in, a->alpha, a->inv_rms, a->h_mix, a->h_pre, a->h_post, a->dh_post, a->dh_res, rec, abpart, T, D,
         a->hc_eps);
     if ((st = after_launch())) return st;
+    const dim3 gtr((unsigned)(Tp / 32), (unsigned)((N + 31) / 32));
+    tiled::transpose_kernel<n><<<gtr, tiled::kThreads, 0, s>>>(rec, dmT, T, Tp);
+    if ((st = after_launch())) return st;
     if ((st = set_smem_limit_once(tiled::dx_kernel<n>, Dm::DX_SMEM))) return st;
-    const dim3 gdx((unsigned)((T + tiled::kTT - 1) / tiled::kTT), (unsigned)((nD + tiled::kKT - 1) / tiled::kKT));
-    tiled::dx_kernel<n><<<gdx, tiled::kThreads, Dm::DX_SMEM, s>>>(a->x, a->phi, a->gamma, rec, a->dh_in, a->dx, T, D);
+    const dim3 gdx((unsigned)(Tp / tiled::kTT), (unsigned)((nD + tiled::kKT - 1) / tiled::kKT));
+    tiled::dx_kernel<n><<<gdx, tiled::kThreads, Dm::DX_SMEM, s>>>(a->x, a->phi, a->gamma, rec, dmT, a->dh_in, a->dx,
+                                                                  T, Tp, D);
     if ((st = after_launch())) return st;
     const dim3 gg((unsigned)((nD + tiled::kKT - 1) / tiled::kKT), (unsigned)L.P);
     tiled::g_kernel<n><<<gg, tiled::kThreads, 0, s>>>(a->x, rec, gpart, T, nD, L.per_split);

@@ -4,18 +4,20 @@
 // Math: src/backward/golden.py:38-96, split as in the tensor-core backward:
 //   * rowdot::bwd_rows_kernel<n> leaves one record per token, {dh_mix[N], c,
 //     h_pre[n]} (golden.py:49-62, 74, 89), and the dalpha/dbias partials;
+//   * transpose_kernel turns the records' dh_mix into dmT [N][Tp] (token
+//     fastest), the layout the dx tiles read;
 //   * dx_kernel: dx[t,k] = (sum_j dh_mix[t,j] phi[j,k]) gamma[k] - c[t] x[t,k]
 //     + h_pre[t,i] dh_in[t,d]  (k = i*D + d; golden.py:65, 89-94) -- a
-//     [T,N] x [N,nD] product tiled through shared memory, 64 tokens x 128 k
-//     per CTA, 8 x 4 outputs per thread, the N-term sum in fp32 FMAs in
-//     ascending j (the generic kernel's order);
+//     [T,N] x [N,nD] product tiled through shared memory (cp.async), 64
+//     tokens x 128 k per CTA, 8 x 4 outputs per thread, the N-term sum in
+//     fp32 FMAs in ascending j (the generic kernel's order);
 //   * g_kernel: gpart[p][j][k] = sum over the tokens of split p of
 //     dh_mix[t,j] x[t,k] (the un-scaled dphi, golden.py:68-69), 128 k x all N
-//     per CTA, 32-token chunks through shared memory, 10 x 4 outputs per
-//     thread at n = 8, tokens summed in ascending order;
+//     per CTA, 32-token chunks double-buffered through shared memory with
+//     cp.async, tokens summed in ascending order;
 //   * generic::finalize_param_kernel / reduce_columns_kernel as in the
 //     tensor-core backward (fixed order, so results repeat bit for bit).
-// Needs D % 8 == 0 and 16-byte aligned x, dh_in, dx and phi.
+// Needs D % 8 == 0 and 16-byte aligned x, dh_in, dx, phi and gamma.
 #pragma once
 
 #include "common.cuh"
@@ -31,11 +33,27 @@ constexpr int kTC = 32;    // tokens per g_kernel chunk
 template <int n>
 struct Dims {
   static constexpr int N = n * n + 2 * n;
+  static constexpr int N4 = (N + 3) / 4 * 4;             // dh_mix floats copied per record (16-byte pieces)
   static constexpr int RW = ((N + 1 + n) + 3) / 4 * 4;   // record width (rowdot::Rec<n>::W)
   static constexpr int JW = (N + 7) / 8;                 // g_kernel: j per warp
   // dx_kernel's dynamic shared memory: dmT [N][kTT], ph [N][kKT], c [kTT], h_pre [kTT][n]
   static constexpr int DX_SMEM = 4 * (N * kTT + N * kKT + kTT + kTT * n);
+  static_assert(N4 <= RW && N4 <= 8 * JW, "record copy stays inside the record and the chunk row");
 };
+
+// Tokens of the transposed dh_mix (a whole number of dx tiles).
+inline int64_t padded_tokens(int64_t T) { return (T + kTT - 1) / kTT * kTT; }
+
+__device__ __forceinline__ void cp16(void* dst_smem, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst_smem)),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int kPending>
+__device__ __forceinline__ void cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(kPending) : "memory");
+}
 
 __device__ __forceinline__ void bf16x4(uint2 v, float (&f)[4]) {
   f[0] = __uint_as_float(v.x << 16);
@@ -44,13 +62,37 @@ __device__ __forceinline__ void bf16x4(uint2 v, float (&f)[4]) {
   f[3] = __uint_as_float(v.y & 0xFFFF0000u);
 }
 
-// grid = (ceil(T / kTT), ceil(nD / kKT)), kThreads threads, Dims<n>::DX_SMEM
-// bytes of dynamic shared memory.
+// rec [T][RW] -> dmT [N][Tp], zeros for tokens T..Tp-1.  grid = (Tp / 32,
+// ceil(N / 32)), 256 threads; a 32 x 32 tile through padded shared memory.
+template <int n>
+__global__ void __launch_bounds__(kThreads) transpose_kernel(const float* __restrict__ rec, float* __restrict__ dmT,
+                                                             int64_t T, int64_t Tp) {
+  constexpr int N = Dims<n>::N;
+  constexpr int RW = Dims<n>::RW;
+  __shared__ float tile[32][33];
+  const int64_t t0 = (int64_t)blockIdx.x * 32;
+  const int j0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int r = ty; r < 32; r += kThreads / 32) {
+    const int64_t t = t0 + r;
+    const int j = j0 + tx;
+    tile[r][tx] = (t < T && j < N) ? __ldg(rec + t * RW + j) : 0.f;
+  }
+  __syncthreads();
+  for (int r = ty; r < 32; r += kThreads / 32) {
+    const int j = j0 + r;
+    const int64_t t = t0 + tx;
+    if (j < N && t < Tp) dmT[(int64_t)j * Tp + t] = tile[tx][r];
+  }
+}
+
+// grid = (Tp / kTT, ceil(nD / kKT)), kThreads threads, Dims<n>::DX_SMEM bytes
+// of dynamic shared memory.
 template <int n>
 __global__ void __launch_bounds__(kThreads) dx_kernel(const uint16_t* __restrict__ x, const float* __restrict__ phi,
                                                       const float* __restrict__ gamma, const float* __restrict__ rec,
-                                                      const uint16_t* __restrict__ dh_in, uint16_t* __restrict__ dx,
-                                                      int64_t T, int D) {
+                                                      const float* __restrict__ dmT_g, const uint16_t* __restrict__ dh_in,
+                                                      uint16_t* __restrict__ dx, int64_t T, int64_t Tp, int D) {
   constexpr int N = Dims<n>::N;
   constexpr int RW = Dims<n>::RW;
   extern __shared__ float4 dx_smem[];
@@ -64,22 +106,26 @@ __global__ void __launch_bounds__(kThreads) dx_kernel(const uint16_t* __restrict
   const int k0 = blockIdx.y * kKT;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
-  // records of the tile's tokens (zeros past T)
-  for (int e = threadIdx.x; e < kTT * RW; e += kThreads) {
-    const int tt = e / RW, c = e - tt * RW;
-    const int64_t t = t0 + tt;
-    const float v = t < T ? __ldg(rec + t * RW + c) : 0.f;
-    if (c < N) dmT[c][tt] = v;
-    else if (c == N) c_s[tt] = v;
-    else if (c < N + 1 + n) hp_s[tt][c - N - 1] = v;
+  // dh_mix rows of the tile (Tp covers every tile) and phi rows (zeros past nD)
+  for (int e = threadIdx.x; e < N * (kTT / 4); e += kThreads) {
+    const int j = e / (kTT / 4), q = e - j * (kTT / 4);
+    cp16(&dmT[j][4 * q], dmT_g + (int64_t)j * Tp + t0 + 4 * q);
   }
-  // phi rows for the tile's k (zeros past nD)
   for (int e = threadIdx.x; e < N * (kKT / 4); e += kThreads) {
     const int j = e / (kKT / 4), q = e - j * (kKT / 4);
     const int k = k0 + 4 * q;
-    const float4 v = k < nD ? __ldg(reinterpret_cast<const float4*>(phi + (int64_t)j * nD + k)) : make_float4(0, 0, 0, 0);
-    *reinterpret_cast<float4*>(&ph[j][4 * q]) = v;
+    if (k < nD) cp16(&ph[j][4 * q], phi + (int64_t)j * nD + k);
+    else *reinterpret_cast<float4*>(&ph[j][4 * q]) = make_float4(0.f, 0.f, 0.f, 0.f);
   }
+  cp_commit();
+  for (int e = threadIdx.x; e < kTT * (1 + n); e += kThreads) {
+    const int tt = e / (1 + n), c = e - tt * (1 + n);
+    const int64_t t = t0 + tt;
+    const float v = t < T ? __ldg(rec + t * RW + N + c) : 0.f;
+    if (c == 0) c_s[tt] = v;
+    else hp_s[tt][c - 1] = v;
+  }
+  cp_wait<0>();
   __syncthreads();
 
   float acc[8][4];
@@ -136,10 +182,11 @@ template <int n>
 __global__ void __launch_bounds__(kThreads) g_kernel(const uint16_t* __restrict__ x, const float* __restrict__ rec,
                                                      float* __restrict__ gpart, int64_t T, int nD, int64_t per_split) {
   constexpr int N = Dims<n>::N;
+  constexpr int N4 = Dims<n>::N4;
   constexpr int RW = Dims<n>::RW;
   constexpr int JW = Dims<n>::JW;
-  __shared__ __align__(16) float xs[kTC][kKT];
-  __shared__ float dm[kTC][8 * JW];
+  __shared__ __align__(16) uint16_t xs[2][kTC][kKT];   // raw bf16 chunks
+  __shared__ __align__(16) float dm[2][kTC][8 * JW];
   const int k0 = blockIdx.x * kKT;
   const int p = blockIdx.y;
   const int64_t ta = (int64_t)p * per_split;
@@ -151,40 +198,56 @@ __global__ void __launch_bounds__(kThreads) g_kernel(const uint16_t* __restrict_
 #pragma unroll
     for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
 
-  for (int64_t tc = ta; tc < tb; tc += kTC) {
-    __syncthreads();   // the previous chunk is used up
-    // x chunk [kTC tokens][kKT k] as fp32 (zeros past T or nD)
+  // chunk tokens [tc, tc + kTC) into buffer b; x columns past nD and tokens
+  // past tb are not copied (their products are never summed or stored)
+  auto load = [&](int64_t tc, int b) {
     for (int e = threadIdx.x; e < kTC * (kKT / 8); e += kThreads) {
       const int tt = e / (kKT / 8), q = e - tt * (kKT / 8);
       const int64_t t = tc + tt;
       const int k = k0 + 8 * q;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (t < tb && k < nD) v = __ldg(reinterpret_cast<const uint4*>(x + t * nD + k));
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        xs[tt][8 * q + 2 * h] = __uint_as_float(w[h] << 16);
-        xs[tt][8 * q + 2 * h + 1] = __uint_as_float(w[h] & 0xFFFF0000u);
-      }
+      if (t < tb && k < nD) cp16(&xs[b][tt][8 * q], x + t * nD + k);
     }
-    // dh_mix of the chunk's tokens, j padded to 8 * JW with zeros
-    for (int e = threadIdx.x; e < kTC * 8 * JW; e += kThreads) {
-      const int tt = e / (8 * JW), j = e - tt * (8 * JW);
+    for (int e = threadIdx.x; e < kTC * (N4 / 4); e += kThreads) {
+      const int tt = e / (N4 / 4), q = e - tt * (N4 / 4);
       const int64_t t = tc + tt;
-      dm[tt][j] = (t < tb && j < N) ? __ldg(rec + t * RW + j) : 0.f;
+      if (t < tb) cp16(&dm[b][tt][4 * q], rec + t * RW + 4 * q);
     }
-    __syncthreads();
+    cp_commit();
+  };
+
+  if (ta < tb) load(ta, 0);
+  int b = 0;
+  for (int64_t tc = ta; tc < tb; tc += kTC, b ^= 1) {
+    const bool more = tc + kTC < tb;
+    if (more) {
+      load(tc + kTC, b ^ 1);
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
+    }
+    __syncthreads();   // chunk tc is in buffer b for every thread
     const int nt = (int)min((int64_t)kTC, tb - tc);
     for (int tt = 0; tt < nt; ++tt) {
-      const float4 xv = *reinterpret_cast<const float4*>(&xs[tt][4 * lane]);
-      const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
+      float xa[4];
+      bf16x4(*reinterpret_cast<const uint2*>(&xs[b][tt][4 * lane]), xa);
+      float dv[JW];   // this warp's JW values of dh_mix: float2 broadcasts when JW is even
+      if constexpr (JW % 2 == 0) {
 #pragma unroll
-      for (int a = 0; a < JW; ++a) {
-        const float dv = dm[tt][warp * JW + a];
+        for (int a = 0; a < JW; a += 2) {
+          const float2 v2 = *reinterpret_cast<const float2*>(&dm[b][tt][warp * JW + a]);
+          dv[a] = v2.x;
+          dv[a + 1] = v2.y;
+        }
+      } else {
 #pragma unroll
-        for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(dv, xa[b], acc[a][b]);
+        for (int a = 0; a < JW; ++a) dv[a] = dm[b][tt][warp * JW + a];
       }
+#pragma unroll
+      for (int a = 0; a < JW; ++a)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[a][q] = fmaf(dv[a], xa[q], acc[a][q]);
     }
+    __syncthreads();   // buffer b is used up before the next chunk refills it
   }
   const int k = k0 + 4 * lane;
   if (k >= nD) return;
