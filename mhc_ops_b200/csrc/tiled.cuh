@@ -128,22 +128,32 @@ __global__ void __launch_bounds__(kThreads) dx_kernel(const uint16_t* __restrict
   cp_wait<0>();
   __syncthreads();
 
-  float acc[8][4];
+  // acc2[a][h] holds outputs (token a, k 2h and 2h+1); __ffma2_rn rounds each
+  // half exactly as fmaf does, two FMAs per instruction
+  float2 acc2[8][2];
 #pragma unroll
-  for (int a = 0; a < 8; ++a)
-#pragma unroll
-    for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+  for (int a = 0; a < 8; ++a) acc2[a][0] = acc2[a][1] = make_float2(0.f, 0.f);
 #pragma unroll 4
   for (int j = 0; j < N; ++j) {
     const float4 d0 = *reinterpret_cast<const float4*>(&dmT[j][8 * warp]);
     const float4 d1 = *reinterpret_cast<const float4*>(&dmT[j][8 * warp + 4]);
     const float4 p = *reinterpret_cast<const float4*>(&ph[j][4 * lane]);
     const float dv[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
-    const float pv[4] = {p.x, p.y, p.z, p.w};
+    const float2 p01 = make_float2(p.x, p.y), p23 = make_float2(p.z, p.w);
 #pragma unroll
-    for (int a = 0; a < 8; ++a)
+    for (int a = 0; a < 8; ++a) {
+      const float2 dd = make_float2(dv[a], dv[a]);
+      acc2[a][0] = __ffma2_rn(dd, p01, acc2[a][0]);
+      acc2[a][1] = __ffma2_rn(dd, p23, acc2[a][1]);
+    }
+  }
+  float acc[8][4];
 #pragma unroll
-      for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(dv[a], pv[b], acc[a][b]);
+  for (int a = 0; a < 8; ++a) {
+    acc[a][0] = acc2[a][0].x;
+    acc[a][1] = acc2[a][0].y;
+    acc[a][2] = acc2[a][1].x;
+    acc[a][3] = acc2[a][1].y;
   }
 
   const int k = k0 + 4 * lane;
@@ -192,11 +202,9 @@ __global__ void __launch_bounds__(kThreads) g_kernel(const uint16_t* __restrict_
   const int64_t ta = (int64_t)p * per_split;
   const int64_t tb = min(T, ta + per_split);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float acc[JW][4];
+  float2 acc2[JW][2];   // (j, k pair): __ffma2_rn, two exact fmaf per instruction
 #pragma unroll
-  for (int a = 0; a < JW; ++a)
-#pragma unroll
-    for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+  for (int a = 0; a < JW; ++a) acc2[a][0] = acc2[a][1] = make_float2(0.f, 0.f);
 
   // chunk tokens [tc, tc + kTC) into buffer b; x columns past nD and tokens
   // past tb are not copied (their products are never summed or stored)
@@ -230,6 +238,7 @@ __global__ void __launch_bounds__(kThreads) g_kernel(const uint16_t* __restrict_
     for (int tt = 0; tt < nt; ++tt) {
       float xa[4];
       bf16x4(*reinterpret_cast<const uint2*>(&xs[b][tt][4 * lane]), xa);
+      const float2 x01 = make_float2(xa[0], xa[1]), x23 = make_float2(xa[2], xa[3]);
       float dv[JW];   // this warp's JW values of dh_mix: float2 broadcasts when JW is even
       if constexpr (JW % 2 == 0) {
 #pragma unroll
@@ -243,9 +252,11 @@ __global__ void __launch_bounds__(kThreads) g_kernel(const uint16_t* __restrict_
         for (int a = 0; a < JW; ++a) dv[a] = dm[b][tt][warp * JW + a];
       }
 #pragma unroll
-      for (int a = 0; a < JW; ++a)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) acc[a][q] = fmaf(dv[a], xa[q], acc[a][q]);
+      for (int a = 0; a < JW; ++a) {
+        const float2 dd = make_float2(dv[a], dv[a]);
+        acc2[a][0] = __ffma2_rn(dd, x01, acc2[a][0]);
+        acc2[a][1] = __ffma2_rn(dd, x23, acc2[a][1]);
+      }
     }
     __syncthreads();   // buffer b is used up before the next chunk refills it
   }
@@ -256,7 +267,7 @@ __global__ void __launch_bounds__(kThreads) g_kernel(const uint16_t* __restrict_
     const int j = warp * JW + a;
     if (j < N)
       *reinterpret_cast<float4*>(gpart + ((int64_t)p * N + j) * nD + k) =
-          make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+          make_float4(acc2[a][0].x, acc2[a][0].y, acc2[a][1].x, acc2[a][1].y);
   }
 }
 
