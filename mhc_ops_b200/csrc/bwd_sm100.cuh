@@ -631,10 +631,20 @@ __global__ void __launch_bounds__(256) phit_kernel(const float* __restrict__ phi
   constexpr int CPR = Cf::KA / 8;                  // 16-byte chunks per image row
   __shared__ float cols[Cf::N_OUT][kBK + 1];
   const int blk = blockIdx.x;
-  for (int idx = threadIdx.x; idx < Cf::N_OUT * kBK; idx += 256) {
+  // all of this thread's loads first (one round trip), then the smem stores
+  constexpr int PER = (Cf::N_OUT * kBK + 255) / 256;
+  float v[PER];
+#pragma unroll
+  for (int it = 0; it < PER; ++it) {
+    const int idx = it * 256 + (int)threadIdx.x;
     const int j = idx / kBK, kk = idx - j * kBK;
     const int64_t k = (int64_t)blk * kBK + kk;
-    cols[j][kk] = __ldg(phi + (int64_t)j * nD + k) * (gamma ? __ldg(gamma + k) : 1.0f);
+    v[it] = idx < Cf::N_OUT * kBK ? __ldg(phi + (int64_t)j * nD + k) * (gamma ? __ldg(gamma + k) : 1.0f) : 0.f;
+  }
+#pragma unroll
+  for (int it = 0; it < PER; ++it) {
+    const int idx = it * 256 + (int)threadIdx.x;
+    if (idx < Cf::N_OUT * kBK) cols[idx / kBK][idx % kBK] = v[it];
   }
   __syncthreads();
   uint8_t* out = reinterpret_cast<uint8_t*>(img) + (size_t)blk * Cf::PH_BYTES;

@@ -207,24 +207,39 @@ __global__ void __launch_bounds__(kThreads) bwd_g_kernel(const uint16_t* __restr
 // CTA = 32 columns k x 8 row groups (j = jg, jg+8, ...); the 8 dgamma partials
 // are added in a fixed order.  Launch with ceil(nD / kFinCols) CTAs of kThreads.
 constexpr int kFinCols = 32;
-__global__ void __launch_bounds__(kThreads) finalize_param_kernel(const float* __restrict__ gpart, int P, int N,
+template <int N>
+__global__ void __launch_bounds__(kThreads) finalize_param_kernel(const float* __restrict__ gpart, int P,
                                                                   const float* __restrict__ phi,
                                                                   const float* __restrict__ gamma,
                                                                   float* __restrict__ dphi,
                                                                   float* __restrict__ dgamma, int nD) {
   constexpr int JG = kThreads / kFinCols;
+  constexpr int JPER = (N + JG - 1) / JG;   // j = jg, jg + JG, ... of this thread
   __shared__ float part[JG][kFinCols];
   const int kk = threadIdx.x % kFinCols, jg = threadIdx.x / kFinCols;
   const int k = blockIdx.x * kFinCols + kk;
   float dg = 0.f;
   if (k < nD) {
     const float gm = gamma ? __ldg(gamma + k) : 1.0f;
-    for (int j = jg; j < N; j += JG) {
-      float g = 0.f;
-#pragma unroll 8
-      for (int p = 0; p < P; ++p) g += __ldg(gpart + ((int64_t)p * N + j) * nD + k);
-      dphi[(int64_t)j * nD + k] = gm * g;
-      dg = fmaf(__ldg(phi + (int64_t)j * nD + k), g, dg);
+    // splits outer, this thread's rows inner: JPER independent loads per step,
+    // each row still summed over p in ascending order
+    float g[JPER];
+#pragma unroll
+    for (int q = 0; q < JPER; ++q) g[q] = 0.f;
+    for (int p = 0; p < P; ++p) {
+#pragma unroll
+      for (int q = 0; q < JPER; ++q) {
+        const int j = jg + q * JG;
+        if (j < N) g[q] += __ldg(gpart + ((int64_t)p * N + j) * nD + k);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < JPER; ++q) {
+      const int j = jg + q * JG;
+      if (j < N) {
+        dphi[(int64_t)j * nD + k] = gm * g[q];
+        dg = fmaf(__ldg(phi + (int64_t)j * nD + k), g[q], dg);
+      }
     }
   }
   part[jg][kk] = dg;
