@@ -203,16 +203,46 @@ __global__ void __launch_bounds__(kThreads) bwd_g_kernel(const uint16_t* __restr
   }
 }
 
+// dalpha / dbias: column c of part [rows][W] summed over rows in a fixed
+// order (thread r takes rows r, r + kThreads, ...; then warps, then the 8
+// warp sums in order); c < 3 -> dalpha[c], else dbias[c - 3].
+__device__ __forceinline__ void reduce_column(const float* __restrict__ part, int64_t rows, int W, int c,
+                                              float* __restrict__ dalpha, float* __restrict__ dbias) {
+  __shared__ float red[kWarps];
+  float s = 0.f;
+#pragma unroll 4
+  for (int64_t r = threadIdx.x; r < rows; r += kThreads) s += part[r * W + c];
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int w = 0; w < kWarps; ++w) tot += red[w];
+    if (c < 3) dalpha[c] = tot;
+    else dbias[c - 3] = tot;
+  }
+}
+
 // dphi[j][k] = gamma[k] * sum_p gpart[p][j][k]; dgamma[k] = sum_j phi[j][k] * G[j][k].
 // CTA = 32 columns k x 8 row groups (j = jg, jg+8, ...); the 8 dgamma partials
-// are added in a fixed order.  Launch with ceil(nD / kFinCols) CTAs of kThreads.
+// are added in a fixed order.  Launch with ceil(nD / kFinCols) + 3 + N CTAs of
+// kThreads: the trailing 3 + N CTAs sum the dalpha / dbias columns of abpart
+// [ab_rows][3 + N] (reduce_column).
 constexpr int kFinCols = 32;
 template <int N>
 __global__ void __launch_bounds__(kThreads) finalize_param_kernel(const float* __restrict__ gpart, int P,
                                                                   const float* __restrict__ phi,
                                                                   const float* __restrict__ gamma,
                                                                   float* __restrict__ dphi,
-                                                                  float* __restrict__ dgamma, int nD) {
+                                                                  float* __restrict__ dgamma, int nD,
+                                                                  const float* __restrict__ abpart, int64_t ab_rows,
+                                                                  float* __restrict__ dalpha,
+                                                                  float* __restrict__ dbias) {
+  const int kblocks = (nD + kFinCols - 1) / kFinCols;
+  if ((int)blockIdx.x >= kblocks) {   // the 3 + N trailing CTAs: dalpha / dbias columns
+    reduce_column(abpart, ab_rows, 3 + N, (int)blockIdx.x - kblocks, dalpha, dbias);
+    return;
+  }
   constexpr int JG = kThreads / kFinCols;
   constexpr int JPER = (N + JG - 1) / JG;   // j = jg, jg + JG, ... of this thread
   __shared__ float part[JG][kFinCols];
@@ -249,26 +279,6 @@ __global__ void __launch_bounds__(kThreads) finalize_param_kernel(const float* _
 #pragma unroll
     for (int g2 = 1; g2 < JG; ++g2) s += part[g2][kk];
     dgamma[k] = s;
-  }
-}
-
-// dalpha / dbias: column c of tokpart [rows][W] summed over rows in a fixed
-// order; one CTA per column.  c < 3 -> dalpha[c], else dbias[c-3].
-__global__ void __launch_bounds__(kThreads) reduce_columns_kernel(const float* __restrict__ part, int64_t rows,
-                                                                  int W, float* __restrict__ dalpha,
-                                                                  float* __restrict__ dbias) {
-  __shared__ float red[kWarps];
-  const int c = blockIdx.x;
-  float s = 0.f;
-  for (int64_t r = threadIdx.x; r < rows; r += kThreads) s += part[r * W + c];
-  s = warp_sum(s);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float tot = 0.f;
-    for (int w = 0; w < kWarps; ++w) tot += red[w];
-    if (c < 3) dalpha[c] = tot;
-    else dbias[c - 3] = tot;
   }
 }
 

@@ -137,10 +137,9 @@ struct BwdGeneric {
     dim3 g2((nD + generic::kThreads - 1) / generic::kThreads, L.P);
     generic::bwd_g_kernel<n><<<g2, generic::kThreads, 0, s>>>(a->x, dh_mix, gpart, T, nD, L.tokens_per_split);
     if ((st = after_launch())) return st;
-    generic::finalize_param_kernel<N><<<(nD + generic::kFinCols - 1) / generic::kFinCols, generic::kThreads, 0, s>>>(
-        gpart, L.P, a->phi, a->gamma, a->dphi, a->dgamma, nD);
-    if ((st = after_launch())) return st;
-    generic::reduce_columns_kernel<<<3 + N, generic::kThreads, 0, s>>>(tokpart, T, 3 + N, a->dalpha, a->dbias);
+    generic::finalize_param_kernel<N><<<(nD + generic::kFinCols - 1) / generic::kFinCols + 3 + N, generic::kThreads, 0,
+                                        s>>>(gpart, L.P, a->phi, a->gamma, a->dphi, a->dgamma, nD, tokpart, T, a->dalpha,
+                                             a->dbias);
     return after_launch();
   }
 };
@@ -544,11 +543,10 @@ int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s, int sms) {
   bwdtc::bwd_kernel<n><<<L.plan.S_K * L.plan.S_T, bwdtc::kThreads, Cf::SMEM, s>>>(m_x2d, m_dh, m_dx, m_rec, p);
   if ((st = after_launch())) return st;
 
-  generic::finalize_param_kernel<Cf::N_OUT><<<(nD + generic::kFinCols - 1) / generic::kFinCols, generic::kThreads, 0,
-                                              s>>>(gpart, L.plan.S_T, a->phi, a->gamma, a->dphi, a->dgamma, nD);
-  if ((st = after_launch())) return st;
-  generic::reduce_columns_kernel<<<3 + Cf::N_OUT, generic::kThreads, 0, s>>>(
-      abpart, (int64_t)L.rows_grid * kRowsWarps, 3 + Cf::N_OUT, a->dalpha, a->dbias);
+  generic::finalize_param_kernel<Cf::N_OUT>
+      <<<(nD + generic::kFinCols - 1) / generic::kFinCols + 3 + Cf::N_OUT, generic::kThreads, 0, s>>>(
+          gpart, L.plan.S_T, a->phi, a->gamma, a->dphi, a->dgamma, nD, abpart, (int64_t)L.rows_grid * kRowsWarps,
+          a->dalpha, a->dbias);
   return after_launch();
 }
 
@@ -635,11 +633,9 @@ struct BwdTiled {
     const dim3 gg((unsigned)((nD + tiled::kKT - 1) / tiled::kKT), (unsigned)L.P);
     tiled::g_kernel<n><<<gg, tiled::kThreads, 0, s>>>(a->x, rec, gpart, T, nD, L.per_split);
     if ((st = after_launch())) return st;
-    generic::finalize_param_kernel<N><<<(nD + generic::kFinCols - 1) / generic::kFinCols, generic::kThreads, 0, s>>>(
-        gpart, L.P, a->phi, a->gamma, a->dphi, a->dgamma, nD);
-    if ((st = after_launch())) return st;
-    generic::reduce_columns_kernel<<<3 + N, generic::kThreads, 0, s>>>(
-        abpart, (int64_t)L.rows_grid * kRowsWarps, 3 + N, a->dalpha, a->dbias);
+    generic::finalize_param_kernel<N><<<(nD + generic::kFinCols - 1) / generic::kFinCols + 3 + N, generic::kThreads, 0,
+                                        s>>>(gpart, L.P, a->phi, a->gamma, a->dphi, a->dgamma, nD, abpart,
+                                             (int64_t)L.rows_grid * kRowsWarps, a->dalpha, a->dbias);
     return after_launch();
   }
 };

@@ -15,8 +15,9 @@
 //     dh_mix[t,j] x[t,k] (the un-scaled dphi, golden.py:68-69), 128 k x all N
 //     per CTA, 32-token chunks double-buffered through shared memory with
 //     cp.async, tokens summed in ascending order;
-//   * generic::finalize_param_kernel / reduce_columns_kernel as in the
-//     tensor-core backward (fixed order, so results repeat bit for bit).
+//   * generic::finalize_param_kernel (dphi, dgamma and the dalpha / dbias
+//     column sums) as in the tensor-core backward (fixed order, so results
+//     repeat bit for bit).
 // Needs D % 8 == 0 and 16-byte aligned x, dh_in, dx, phi and gamma.
 #pragma once
 
