@@ -40,13 +40,6 @@
 #include "common.cuh"
 #include "sm100.cuh"
 
-// Stages of look-ahead of the producer's L2 prefetch: HBM latency under full
-// load is a few microseconds, longer than the smem ring covers, so the x and
-// dh_in boxes are pulled into L2 this many stages before their TMA load.
-#ifndef MHC_BWD_PF_STAGES
-#define MHC_BWD_PF_STAGES 8
-#endif
-
 namespace mhc {
 namespace bwdtc {
 
@@ -325,18 +318,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < n; ++i, ++q) {
             const int s = q % Cf::XS;
             const int k0 = i * D + slice * Dc + dch * kBK;
-            if (MHC_BWD_PF_STAGES > 0) {
-              // L2 prefetch of the stage MHC_BWD_PF_STAGES ahead of this one
-              // (and, at the start, of the first MHC_BWD_PF_STAGES stages)
-              for (uint32_t qg = (q == 0 ? 0u : q + MHC_BWD_PF_STAGES); qg <= q + MHC_BWD_PF_STAGES; ++qg) {
-                const int jt = (int)(qg / (uint32_t)(DCH * n)), r2 = (int)(qg % (uint32_t)(DCH * n));
-                if (jt < my_tiles) {
-                  const int pd = r2 / n, pi = r2 % n, pt = tile_of(jt);
-                  tma_prefetch_2d(&map_x2d, pi * D + slice * Dc + pd * kBK, pt * kBM);
-                  if (pi == 0) tma_prefetch_2d(&map_dh, slice * Dc + pd * kBK, pt * kBM);
-                }
-              }
-            }
             mbar_wait(bar(B::x_empty + s), ((q / Cf::XS) & 1) ^ 1, wc);
             if (!*abort_flag) {
               mbar_arrive_expect_tx(bar(B::x_full + s), Cf::X_BYTES);

@@ -157,7 +157,11 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// Row-major tensor of `rank` dims (dims[0] innermost) -> tiled TMA map.
+// Row-major tensor of `rank` dims (dims[0] innermost) -> tiled TMA map.  L2
+// promotion is 128 bytes, the width of every box row here: with 256-byte
+// promotion the neighbouring lines are evicted before their own box asks for
+// them (measured on B200: the backward kernel then reads ~39% more than it
+// needs; an L2 prefetch of its boxes 8 stages ahead wastes reads the same way).
 int encode_map(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, int rank, const uint64_t* dims,
                const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz) {
   auto enc = tensor_map_encoder();
@@ -172,7 +176,7 @@ int encode_map(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, in
     if (i + 1 < rank) st[i] = strides_bytes[i];
   }
   CUresult r = enc(map, dtype, rank, const_cast<void*>(base), d, st, b, es,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? MHC_OK : MHC_ERR_CUDA;
 }
