@@ -172,11 +172,14 @@ MHC_API int mhc_bwd(const mhc_bwd_args* args, void* stream);
 MHC_API int mhc_read_device_status(void* workspace, void* stream, int* device_status);
 
 /* Self test of the device-side failure detection: launches one CTA that
- * waits, through the same bounded wait every tensor-core kernel uses, on a
- * barrier nothing completes.  After about a second the wait gives up, the
- * kernel writes MHC_ERR_DEVICE_TIMEOUT into the workspace's status word
- * (read it with mhc_read_device_status) and returns; the context stays
- * usable.  No counterpart in the reference (it has no device waits). */
+ * runs the two bounded waits the tensor-core kernels use, each on something
+ * that never completes (an mbarrier nothing arrives on; a global counter
+ * nothing increments, as the fused forward waits on other CTAs' tiles).
+ * Each wait gives up after about a second; the kernel writes
+ * MHC_ERR_DEVICE_TIMEOUT into the workspace's status word (read it with
+ * mhc_read_device_status), sets bits 0 and 1 of the second int of the
+ * workspace for the two waits that reported it, and returns; the context
+ * stays usable.  No counterpart in the reference (it has no device waits). */
 MHC_API int mhc_selftest_wait_expiry(void* workspace, void* stream);
 
 /* Launch plan the library uses for this shape on the current device:

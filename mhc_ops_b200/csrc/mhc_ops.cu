@@ -653,22 +653,31 @@ int bwd_workspace(int64_t T, int n, int D, int sms, size_t* bytes) {
 }
 
 // ----------------------------------------------------------------- bounded-wait self test
-// One thread waits, through the same bounded mbar_wait every tensor-core
-// kernel uses, on an mbarrier that nothing ever completes.  The wait gives
-// up after its limit (about a second), sets the status word to
-// MHC_ERR_DEVICE_TIMEOUT and the kernel returns.  No fault is involved.
+// One thread runs, one after the other, the two bounded waits the kernels
+// use, each on something that never completes: mbar_wait on an mbarrier
+// nothing arrives on, and counter_wait (the fused forward's wait for another
+// CTA's tile) on a global counter nothing increments.  Each gives up after
+// its limit (about a second), sets the status word to MHC_ERR_DEVICE_TIMEOUT
+// and the kernel returns; status[1] gets bit 0 / bit 1 for each wait that
+// reported the timeout.  No fault is involved.
+static __device__ int g_never_signalled = 0;
+
 __global__ void wait_expiry_kernel(int* status) {
   __shared__ uint64_t bar;
-  __shared__ int abort_flag;
+  __shared__ int abort_a, abort_b;
   if (threadIdx.x == 0) {
     sm100::mbar_init(sm100::smem_u32(&bar), 1);
-    abort_flag = 0;
+    abort_a = 0;
+    abort_b = 0;
     sm100::fence_mbarrier_init_cluster();
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    const sm100::WaitCtx wc{&abort_flag, status};
-    sm100::mbar_wait(sm100::smem_u32(&bar), 0, wc);   // phase 0 never completes
+    const sm100::WaitCtx wa{&abort_a, status};
+    const bool a_done = sm100::mbar_wait(sm100::smem_u32(&bar), 0, wa);   // phase 0 never completes
+    const sm100::WaitCtx wb{&abort_b, status};
+    const bool b_done = sm100::counter_wait(&g_never_signalled, 1, wb);   // stays 0
+    status[1] = (!a_done && abort_a ? 1 : 0) | (!b_done && abort_b ? 2 : 0);
   }
 }
 

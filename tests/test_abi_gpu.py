@@ -82,6 +82,8 @@ def test_bounded_wait_expiry_reports_timeout():
     stream = torch.cuda.current_stream()
     ws = torch.zeros(1 << 12, dtype=torch.uint8, device="cuda")
     assert lib.mhc_selftest_wait_expiry(ws.data_ptr(), stream.cuda_stream) == 0
+    torch.cuda.synchronize()
+    assert int(ws[4:8].view(torch.int32).item()) == 3, "both bounded waits (mbarrier, counter) must report"
     assert _lib.read_device_status(ws, stream) == _lib.MHC_ERR_DEVICE_TIMEOUT
     assert _lib.read_device_status(ws, stream) == 0          # read clears it
     d = make_inputs(1, 16, 4, 128, seed=6).to("cuda")

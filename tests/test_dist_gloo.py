@@ -55,7 +55,9 @@ def _oracle_bwd(x, phi, alpha, bias, inv_rms, h_mix, h_pre, h_post, dh_in, dh_po
 
 def _worker_allreduce(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    # a generous rendezvous limit: a rank's first `import torch` in a fresh
+    # container can take a minute
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=180))
     try:
         inp = make_inputs(2, 9, 4, 32, seed=7)   # 18 tokens: uneven split is fine too
         sh = {k: shard_tokens(getattr(inp, k), rank, world) for k in ("x", "dh_in", "dh_post", "dh_res")}
@@ -71,12 +73,15 @@ def _worker_allreduce(rank, world, port, q):
 
 def _worker_dies(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    # rendezvous with a generous limit (slow first imports), then a group whose
+    # collectives give up after 5 s: the survivor's error comes from that limit
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=180))
+    group = dist.new_group(ranks=list(range(world)), timeout=datetime.timedelta(seconds=5))
     if rank == 1:
         os._exit(3)          # the failing rank leaves between steps, before the collective
     flat = torch.ones(param_grad_numel(4, 8))
     try:
-        dist.all_reduce(flat)
+        dist.all_reduce(flat, group=group)
         q.put((rank, "no error"))
     except Exception as e:   # noqa: BLE001 - any collective error is the detection we want
         q.put((rank, f"error: {type(e).__name__}"))
@@ -99,7 +104,7 @@ def test_allreduced_shard_grads_equal_full_batch_grads():
     procs = [ctx.Process(target=_worker_allreduce, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    results = [q.get(timeout=120) for _ in range(world)]
+    results = [q.get(timeout=300) for _ in range(world)]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -126,7 +131,7 @@ def test_dead_rank_is_detected_by_collective_timeout():
     procs = [ctx.Process(target=_worker_dies, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    rank, msg = q.get(timeout=120)
+    rank, msg = q.get(timeout=300)
     for p in procs:
         p.join(timeout=60)
     assert rank == 0 and msg.startswith("error"), msg
