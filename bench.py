@@ -239,14 +239,24 @@ def run_ours(args):
     dh_res = torch.randn(B, S, n, n, generator=gd, device=dev)
     flat = torch.empty(param_grad_numel(n, D), device=dev)
 
+    # The parameter-gradient all-reduce of step k runs on NCCL's stream while
+    # step k+1's forward runs; step k+1's backward, which rewrites `flat`,
+    # waits for it first (a stream wait, the host does not block).
+    pending = []
+
+    def drain():
+        while pending:
+            pending.pop().wait()
+
     def step():
         out = mhc_forward_pre(x, phi, alpha, bias, outflag=True)
+        drain()
         ev[1].record()
         mhc_backward_manual(x, phi, alpha, bias, out[3], out[4], out[5], out[1], dh_in, dh_post, dh_res, gamma,
                             grad_out=flat)
         ev[2].record()
         if world > 1:
-            dist.all_reduce(flat)
+            pending.append(dist.all_reduce(flat, async_op=True))
 
     def sync_all():
         torch.cuda.synchronize()
@@ -265,6 +275,7 @@ def run_ours(args):
     for _ in range(args.warmup):
         ev[0].record()
         step()
+    drain()
     sync_all()
 
     # timed region (device-resident inputs)
@@ -278,6 +289,7 @@ def run_ours(args):
     for _ in range(args.steps):
         ev[0].record()
         step()
+    drain()   # the last step's all-reduce is inside the timed region
     stop.record()
     sync_all()
     total_ms = max_over_ranks(start.elapsed_time(stop))
@@ -294,6 +306,7 @@ def run_ours(args):
         ev = evs
         ev[0].record()
         step()
+    drain()
     torch.cuda.synchronize()
     for evs in step_evs:
         fwd_ms.append(evs[0].elapsed_time(evs[1]))
@@ -321,6 +334,7 @@ def run_ours(args):
             dh_res.copy_(hres, non_blocking=True)
             ev[0].record()
             step()
+            drain()
             hflat.copy_(flat, non_blocking=True)
         stop.record()
         sync_all()

@@ -65,6 +65,7 @@ class DataParallelMHC:
         self.fwd, self.bwd = fwd, bwd
         self.device = device
         self.flat = None
+        self.pending = None   # all-reduce still in flight (backward(..., overlap=True))
 
     def grad_buffer(self, device) -> torch.Tensor:
         numel = param_grad_numel(self.n, self.D)
@@ -76,10 +77,24 @@ class DataParallelMHC:
         return self.fwd(x, phi, alpha, bias, outflag=True, **kw)
 
     def backward(self, x, phi, alpha, bias, inv_rms, h_mix, h_pre, h_post, dh_in, dh_post, dh_res, gamma,
-                 **kw):
+                 overlap: bool = False, **kw):
+        """With ``overlap=True`` the all-reduce is left in flight (NCCL's own
+        stream) so that whatever the caller enqueues next -- typically the next
+        step's forward -- overlaps it; the returned parameter gradients are
+        valid after ``wait()``, which the next ``backward`` also calls before it
+        rewrites the buffer."""
+        self.wait()
         flat = self.grad_buffer(x.device)
         dx, dphi, dalpha, dbias, dgamma = self.bwd(x, phi, alpha, bias, inv_rms, h_mix, h_pre, h_post,
                                                    dh_in, dh_post, dh_res, gamma, grad_out=flat, **kw)
-        allreduce_param_grads(flat, self.group)
+        work = allreduce_param_grads(flat, self.group, async_op=overlap)
+        if overlap:
+            self.pending = work
         dphi, dgamma, dalpha, dbias = split_param_grads(flat, self.n, self.D)
         return dx, dphi, dalpha, dbias, dgamma
+
+    def wait(self):
+        """Order the current stream after an all-reduce left in flight (no host wait for NCCL)."""
+        if self.pending is not None:
+            self.pending.wait()
+            self.pending = None

@@ -53,7 +53,7 @@ def _oracle_bwd(x, phi, alpha, bias, inv_rms, h_mix, h_pre, h_post, dh_in, dh_po
     return dx_t, views[0], views[2], views[3], views[1]
 
 
-def _worker_allreduce(rank, world, port, q):
+def _worker_allreduce(rank, world, port, q, overlap=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     # a generous rendezvous limit: a rank's first `import torch` in a fresh
     # container can take a minute
@@ -65,7 +65,8 @@ def _worker_allreduce(rank, world, port, q):
         h_in, h_post, h_res, inv_rms, h_mix, h_pre = dp.forward(sh["x"], inp.phi, inp.alpha, inp.bias)
         dx, dphi, dalpha, dbias, dgamma = dp.backward(sh["x"], inp.phi, inp.alpha, inp.bias, inv_rms, h_mix,
                                                       h_pre, h_post, sh["dh_in"], sh["dh_post"], sh["dh_res"],
-                                                      inp.gamma)
+                                                      inp.gamma, overlap=overlap)
+        dp.wait()   # with overlap the all-reduce was left in flight
         q.put((rank, dphi.clone(), dalpha.clone(), dbias.clone(), dgamma.clone(), dx.clone()))
     finally:
         dist.destroy_process_group()
@@ -96,12 +97,13 @@ def test_shard_bounds_cover_all_tokens_once():
             assert max(b - a for a, b in spans) - min(b - a for a, b in spans) <= 1
 
 
-def test_allreduced_shard_grads_equal_full_batch_grads():
+@pytest.mark.parametrize("overlap", [False, True])
+def test_allreduced_shard_grads_equal_full_batch_grads(overlap):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker_allreduce, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker_allreduce, args=(r, world, port, q, overlap)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in range(world)]
