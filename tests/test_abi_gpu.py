@@ -66,6 +66,19 @@ def test_abi_rejects_bad_arguments():
         mhc_forward_pre(d.x, d.phi[:, :-1].contiguous(), d.alpha, d.bias)   # wrong phi shape
 
 
+@pytest.mark.parametrize("which,T,n,D,path", [
+    (0, 16384, 4, 4096, "tensor-core-fused"),   # the LLM config: one cooperative launch
+    (0, 16384, 8, 4096, "tensor-core"),         # n = 8: projection + row kernel
+    (0, 1000, 6, 512, "generic"),
+    (1, 16384, 4, 4096, "tensor-core"),
+    (1, 16384, 8, 4096, "tiled"),               # n = 8 backward on the CUDA cores
+    (1, 100, 4, 36, "generic"),                 # D not a multiple of 8
+])
+def test_launch_plan_routes_each_shape(which, T, n, D, path):
+    """The plan query names the kernels a shape runs on (no kernel is launched)."""
+    assert _lib.query_plan(which, T, n, D)["path"] == path
+
+
 def test_launch_counter_advances():
     d = make_inputs(1, 16, 4, 128, seed=5).to("cuda")
     before = _lib.launch_count()
