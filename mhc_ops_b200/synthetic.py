@@ -3,7 +3,7 @@
 Two draw orders are provided; both use the CPU torch generator so that every
 consumer (the CUDA path, the CPU oracle, the bench) sees identical bytes.
 
-``convention="survey"`` (default)
+``convention="standard"`` (default)
     ``torch.manual_seed(seed)`` then, in order: ``x ~ N(0,1)`` bf16
     ``[B,S,n,D]``; ``phi ~ N(0,1) * phi_scale`` fp32 ``[N,nD]`` (``phi_scale``
     defaults to ``1/sqrt(nD)``); ``alpha = [1.1, 0.9, 1.05]``;
@@ -49,11 +49,11 @@ class MhcInputs:
 
 
 def make_inputs(B: int, S: int, n: int, D: int, seed: int = 0, phi_scale: float | None = None,
-                convention: str = "survey", grad_seed: int = 123) -> MhcInputs:
+                convention: str = "standard", grad_seed: int = 123) -> MhcInputs:
     """Draw one seeded input set on the CPU (see module docstring for the order)."""
     N = n_out(n)
     nD = n * D
-    if convention == "survey":
+    if convention == "standard":
         if phi_scale is None:
             phi_scale = 1.0 / math.sqrt(nD)
         g = torch.Generator().manual_seed(seed)

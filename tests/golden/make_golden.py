@@ -28,18 +28,18 @@ from mhc_ops_b200.synthetic import make_inputs  # noqa: E402
 
 # (name, B, S, n, D, convention, seed, phi_scale, with_backward)
 CASES = [
-    # golden forward B=2,S=128,n=4,D=256, phi ~ N(0,1) unscaled.
-    ("fwd_cfg1_2x128x4x256", 2, 128, 4, 256, "survey", 0, 1.0, True),
+    # the golden-forward case: B=2,S=128,n=4,D=256, phi ~ N(0,1) unscaled.
+    ("fwd_cfg1_2x128x4x256", 2, 128, 4, 256, "standard", 0, 1.0, True),
     # The reference's own backward test: test/backward/test_backward.py:44-65 (seeds 42/123).
     ("refconv_2x64x4x128", 2, 64, 4, 128, "reference", 42, None, True),
     # README backward shape family with the fan-in scaled phi and gamma ~ 1 + 0.1 N(0,1).
-    ("bwd_2x64x4x256", 2, 64, 4, 256, "survey", 1, None, True),
+    ("bwd_2x64x4x256", 2, 64, 4, 256, "standard", 1, None, True),
     # Wider hyper-connection n=8 (N = 80).
-    ("n8_1x64x8x128", 1, 64, 8, 128, "survey", 2, None, True),
+    ("n8_1x64x8x128", 1, 64, 8, 128, "standard", 2, None, True),
     # quick_test.py:194 tiny printout shape B=1,S=2,n=2,D=4.
     ("tiny_1x2x2x4", 1, 2, 2, 4, "reference", 42, None, True),
     # Ragged: prime token count, D not a multiple of 128.
-    ("ragged_1x7x4x64", 1, 7, 4, 64, "survey", 3, None, True),
+    ("ragged_1x7x4x64", 1, 7, 4, 64, "standard", 3, None, True),
 ]
 
 
