@@ -9,11 +9,11 @@
 //   * dx_kernel: dx[t,k] = (sum_j dh_mix[t,j] phi[j,k]) gamma[k] - c[t] x[t,k]
 //     + h_pre[t,i] dh_in[t,d]  (k = i*D + d; golden.py:65, 89-94) -- a
 //     [T,N] x [N,nD] product tiled through shared memory (cp.async), 64
-//     tokens x 128 k per CTA, 8 x 4 outputs per thread, the N-term sum in
+//     tokens x 256 k per CTA, 8 x 8 outputs per thread, the N-term sum in
 //     fp32 FMAs in ascending j (the generic kernel's order);
 //   * g_kernel: gpart[p][j][k] = sum over the tokens of split p of
-//     dh_mix[t,j] x[t,k] (the un-scaled dphi, golden.py:68-69), 128 k x all N
-//     per CTA, 32-token chunks double-buffered through shared memory with
+//     dh_mix[t,j] x[t,k] (the un-scaled dphi, golden.py:68-69), 256 k x all N
+//     per CTA, 16-token chunks double-buffered through shared memory with
 //     cp.async, tokens summed in ascending order;
 //   * generic::finalize_param_kernel (dphi, dgamma and the dalpha / dbias
 //     column sums) as in the tensor-core backward (fixed order, so results
@@ -28,8 +28,9 @@ namespace tiled {
 
 constexpr int kThreads = 256;
 constexpr int kTT = 64;    // tokens per dx tile (8 warps x 8 tokens)
-constexpr int kKT = 128;   // k per tile (32 lanes x 4 k)
-constexpr int kTC = 32;    // tokens per g_kernel chunk
+constexpr int kKL = 8;     // consecutive k per lane (one 16-byte bf16 load)
+constexpr int kKT = 32 * kKL;   // k per tile
+constexpr int kTC = 16;    // tokens per g_kernel chunk
 
 template <int n>
 struct Dims {
@@ -129,61 +130,69 @@ __global__ void __launch_bounds__(kThreads) dx_kernel(const uint16_t* __restrict
   cp_wait<0>();
   __syncthreads();
 
-  // acc2[a][h] holds outputs (token a, k 2h and 2h+1); __ffma2_rn rounds each
-  // half exactly as fmaf does, two FMAs per instruction
-  float2 acc2[8][2];
+  // acc2[a][h] holds outputs (token a, k 2h and 2h+1 of the lane's 8);
+  // __ffma2_rn rounds each half exactly as fmaf does, two FMAs per instruction
+  float2 acc2[8][kKL / 2];
 #pragma unroll
-  for (int a = 0; a < 8; ++a) acc2[a][0] = acc2[a][1] = make_float2(0.f, 0.f);
-#pragma unroll 4
+  for (int a = 0; a < 8; ++a)
+#pragma unroll
+    for (int h = 0; h < kKL / 2; ++h) acc2[a][h] = make_float2(0.f, 0.f);
+#pragma unroll 2
   for (int j = 0; j < N; ++j) {
     const float4 d0 = *reinterpret_cast<const float4*>(&dmT[j][8 * warp]);
     const float4 d1 = *reinterpret_cast<const float4*>(&dmT[j][8 * warp + 4]);
-    const float4 p = *reinterpret_cast<const float4*>(&ph[j][4 * lane]);
+    const float4 pa = *reinterpret_cast<const float4*>(&ph[j][kKL * lane]);
+    const float4 pb = *reinterpret_cast<const float4*>(&ph[j][kKL * lane + 4]);
     const float dv[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
-    const float2 p01 = make_float2(p.x, p.y), p23 = make_float2(p.z, p.w);
+    const float2 pv[kKL / 2] = {make_float2(pa.x, pa.y), make_float2(pa.z, pa.w), make_float2(pb.x, pb.y),
+                                make_float2(pb.z, pb.w)};
 #pragma unroll
     for (int a = 0; a < 8; ++a) {
       const float2 dd = make_float2(dv[a], dv[a]);
-      acc2[a][0] = __ffma2_rn(dd, p01, acc2[a][0]);
-      acc2[a][1] = __ffma2_rn(dd, p23, acc2[a][1]);
+#pragma unroll
+      for (int h = 0; h < kKL / 2; ++h) acc2[a][h] = __ffma2_rn(dd, pv[h], acc2[a][h]);
     }
   }
-  float acc[8][4];
-#pragma unroll
-  for (int a = 0; a < 8; ++a) {
-    acc[a][0] = acc2[a][0].x;
-    acc[a][1] = acc2[a][0].y;
-    acc[a][2] = acc2[a][1].x;
-    acc[a][3] = acc2[a][1].y;
-  }
 
-  const int k = k0 + 4 * lane;
+  const int k = k0 + kKL * lane;
   if (k >= nD) return;
-  const int i = k / D, d = k - i * D;   // the 4 k share one stream (D % 4 == 0)
-  float gm[4] = {1.f, 1.f, 1.f, 1.f};
+  const int i = k / D, d = k - i * D;   // the 8 k share one stream (D % 8 == 0)
+  float gm[kKL];
+#pragma unroll
+  for (int b = 0; b < kKL; ++b) gm[b] = 1.f;
   if (gamma) {
-    const float4 g = __ldg(reinterpret_cast<const float4*>(gamma + k));
-    gm[0] = g.x;
-    gm[1] = g.y;
-    gm[2] = g.z;
-    gm[3] = g.w;
+    const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma + k));
+    const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma + k + 4));
+    gm[0] = g0.x;
+    gm[1] = g0.y;
+    gm[2] = g0.z;
+    gm[3] = g0.w;
+    gm[4] = g1.x;
+    gm[5] = g1.y;
+    gm[6] = g1.z;
+    gm[7] = g1.w;
   }
 #pragma unroll
   for (int a = 0; a < 8; ++a) {
     const int tt = 8 * warp + a;
     const int64_t t = t0 + tt;
     if (t >= T) break;
-    float xf[4], gf[4];
-    bf16x4(__ldg(reinterpret_cast<const uint2*>(x + t * nD + k)), xf);
-    bf16x4(__ldg(reinterpret_cast<const uint2*>(dh_in + t * D + d)), gf);
+    const uint4 xr = __ldg(reinterpret_cast<const uint4*>(x + t * nD + k));
+    const uint4 gr = __ldg(reinterpret_cast<const uint4*>(dh_in + t * D + d));
+    float xf[kKL], gf[kKL];
+    bf16x4(make_uint2(xr.x, xr.y), *reinterpret_cast<float(*)[4]>(&xf[0]));
+    bf16x4(make_uint2(xr.z, xr.w), *reinterpret_cast<float(*)[4]>(&xf[4]));
+    bf16x4(make_uint2(gr.x, gr.y), *reinterpret_cast<float(*)[4]>(&gf[0]));
+    bf16x4(make_uint2(gr.z, gr.w), *reinterpret_cast<float(*)[4]>(&gf[4]));
     const float c = c_s[tt], hp = hp_s[tt][i];
-    float v[4];
+    uint32_t w[kKL / 2];
 #pragma unroll
-    for (int b = 0; b < 4; ++b) v[b] = acc[a][b] * gm[b] + ((-c) * xf[b] + hp * gf[b]);
-    uint2 o;
-    o.x = (uint32_t)f32_to_bf16_bits(v[0]) | ((uint32_t)f32_to_bf16_bits(v[1]) << 16);
-    o.y = (uint32_t)f32_to_bf16_bits(v[2]) | ((uint32_t)f32_to_bf16_bits(v[3]) << 16);
-    *reinterpret_cast<uint2*>(dx + t * nD + k) = o;
+    for (int h = 0; h < kKL / 2; ++h) {
+      const float v0 = acc2[a][h].x * gm[2 * h] + ((-c) * xf[2 * h] + hp * gf[2 * h]);
+      const float v1 = acc2[a][h].y * gm[2 * h + 1] + ((-c) * xf[2 * h + 1] + hp * gf[2 * h + 1]);
+      w[h] = (uint32_t)f32_to_bf16_bits(v0) | ((uint32_t)f32_to_bf16_bits(v1) << 16);
+    }
+    *reinterpret_cast<uint4*>(dx + t * nD + k) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
@@ -203,9 +212,11 @@ __global__ void __launch_bounds__(kThreads) g_kernel(const uint16_t* __restrict_
   const int64_t ta = (int64_t)p * per_split;
   const int64_t tb = min(T, ta + per_split);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float2 acc2[JW][2];   // (j, k pair): __ffma2_rn, two exact fmaf per instruction
+  float2 acc2[JW][kKL / 2];   // (j, k pair): __ffma2_rn, two exact fmaf per instruction
 #pragma unroll
-  for (int a = 0; a < JW; ++a) acc2[a][0] = acc2[a][1] = make_float2(0.f, 0.f);
+  for (int a = 0; a < JW; ++a)
+#pragma unroll
+    for (int h = 0; h < kKL / 2; ++h) acc2[a][h] = make_float2(0.f, 0.f);
 
   // chunk tokens [tc, tc + kTC) into buffer b; x columns past nD and tokens
   // past tb are not copied (their products are never summed or stored)
@@ -237,9 +248,13 @@ __global__ void __launch_bounds__(kThreads) g_kernel(const uint16_t* __restrict_
     __syncthreads();   // chunk tc is in buffer b for every thread
     const int nt = (int)min((int64_t)kTC, tb - tc);
     for (int tt = 0; tt < nt; ++tt) {
-      float xa[4];
-      bf16x4(*reinterpret_cast<const uint2*>(&xs[b][tt][4 * lane]), xa);
-      const float2 x01 = make_float2(xa[0], xa[1]), x23 = make_float2(xa[2], xa[3]);
+      const uint4 xr = *reinterpret_cast<const uint4*>(&xs[b][tt][kKL * lane]);
+      float xa[kKL];
+      bf16x4(make_uint2(xr.x, xr.y), *reinterpret_cast<float(*)[4]>(&xa[0]));
+      bf16x4(make_uint2(xr.z, xr.w), *reinterpret_cast<float(*)[4]>(&xa[4]));
+      float2 xv[kKL / 2];
+#pragma unroll
+      for (int h = 0; h < kKL / 2; ++h) xv[h] = make_float2(xa[2 * h], xa[2 * h + 1]);
       float dv[JW];   // this warp's JW values of dh_mix: float2 broadcasts when JW is even
       if constexpr (JW % 2 == 0) {
 #pragma unroll
@@ -255,20 +270,22 @@ __global__ void __launch_bounds__(kThreads) g_kernel(const uint16_t* __restrict_
 #pragma unroll
       for (int a = 0; a < JW; ++a) {
         const float2 dd = make_float2(dv[a], dv[a]);
-        acc2[a][0] = __ffma2_rn(dd, x01, acc2[a][0]);
-        acc2[a][1] = __ffma2_rn(dd, x23, acc2[a][1]);
+#pragma unroll
+        for (int h = 0; h < kKL / 2; ++h) acc2[a][h] = __ffma2_rn(dd, xv[h], acc2[a][h]);
       }
     }
     __syncthreads();   // buffer b is used up before the next chunk refills it
   }
-  const int k = k0 + 4 * lane;
+  const int k = k0 + kKL * lane;
   if (k >= nD) return;
 #pragma unroll
   for (int a = 0; a < JW; ++a) {
     const int j = warp * JW + a;
-    if (j < N)
-      *reinterpret_cast<float4*>(gpart + ((int64_t)p * N + j) * nD + k) =
-          make_float4(acc2[a][0].x, acc2[a][0].y, acc2[a][1].x, acc2[a][1].y);
+    if (j < N) {
+      float4* o = reinterpret_cast<float4*>(gpart + ((int64_t)p * N + j) * nD + k);
+      o[0] = make_float4(acc2[a][0].x, acc2[a][0].y, acc2[a][1].x, acc2[a][1].y);
+      o[1] = make_float4(acc2[a][2].x, acc2[a][2].y, acc2[a][3].x, acc2[a][3].y);
+    }
   }
 }
 
