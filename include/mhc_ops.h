@@ -185,7 +185,8 @@ MHC_API int mhc_selftest_wait_expiry(void* workspace, void* stream);
 /* Launch plan the library uses for this shape on the current device:
  * *path = 0 generic kernels, 1 tensor-core kernels, 2 (forward only) the
  * fused tensor-core forward (one cooperative launch), 3 (backward only) the
- * tiled CUDA-core backward (n other than 4; *cluster_size = its token splits).  which = 0 forward: for
+ * backward for n other than 4 (dx on the CUDA cores, the parameter-gradient
+ * product on the tensor cores; *cluster_size = its token groups).  which = 0 forward: for
  * paths 1 and 2, *cluster_size is the number of K-slices the projection is
  * split into and *clusters the CTAs of its persistent grid.  which = 1 backward:
  * for path 1, the tensor-core kernel's grid is *clusters token groups of

@@ -155,7 +155,7 @@ def query_plan(which: int, tokens: int, n: int, D: int) -> dict:
         return {"path": "tensor-core-fused" if path.value == 2 else "tensor-core", "k_slices": cs.value,
                 "ctas": ncl.value}
     if path.value == 3:
-        return {"path": "tiled", "token_splits": cs.value}
+        return {"path": "tiled", "token_groups": cs.value}
     return {"path": "tensor-core", "d_slices": cs.value, "token_groups": ncl.value}
 
 

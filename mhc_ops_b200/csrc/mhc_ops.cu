@@ -554,15 +554,14 @@ int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s, int sms) {
   return after_launch();
 }
 
-// ----------------------------------------------------------------- tiled backward (CUDA cores)
-// rowdot::bwd_rows_kernel (records), tiled::dx_kernel, tiled::g_kernel, then
-// the shared finalize kernels.  Shapes: every n the tensor-core backward does
+// ----------------------------------------------------------------- tiled backward (n != 4)
+// rowdot::bwd_rows_kernel (records), tiled::dx_kernel (CUDA cores),
+// tiled::g_tc_kernel (tcgen05), then the shared finalize kernel.  Shapes: every n the tensor-core backward does
 // not take, D a multiple of 8, 16-byte aligned x / dh_in / dx / phi / gamma,
 // T < 2^31.
 struct BwdTiledLayout {
   size_t rec, abpart, gpart, dmT, total;
-  int P;                 // token splits of the G partials
-  int64_t per_split;     // tokens per split
+  int P;                 // token groups of the G partials (g_tc_kernel's grid.y)
   int rows_grid;
 };
 
@@ -575,13 +574,22 @@ BwdTiledLayout bwd_tiled_layout(int64_t T, int n, int D, int sms) {
   BwdTiledLayout L{};
   const int N = n * n + 2 * n;
   const int64_t nD = (int64_t)n * D;
-  const int64_t kblocks = (nD + tiled::kKT - 1) / tiled::kKT;
-  int64_t P = std::max<int64_t>(1, (4 * (int64_t)sms + kblocks - 1) / kblocks);
-  P = std::min<int64_t>(P, std::max<int64_t>(1, (T + tiled::kTC - 1) / tiled::kTC));
-  P = std::min<int64_t>(P, 64);
-  L.P = (int)P;
-  L.per_split = T > 0 ? (T + P - 1) / P : 1;
-  L.per_split = (L.per_split + tiled::kTC - 1) / tiled::kTC * tiled::kTC;
+  // token groups of the tensor-core G kernel: the fewest with the least
+  // per-CTA work, waves * ceil(tiles / S_T), over ceil(nD / 128) k-ranges
+  const int64_t kranges = (nD + 127) / 128;
+  const int64_t tiles = std::max<int64_t>(1, (T + 127) / 128);
+  int64_t best = 1;
+  double best_cost = 0.0;
+  // (at most 8 groups: the partial sums take S_T * N * nD floats; a larger
+  // S_T must save at least 3% to be taken)
+  for (int64_t st = 1; st <= std::min<int64_t>(tiles, 8); ++st) {
+    const double cost = (double)((kranges * st + sms - 1) / sms) * (double)((tiles + st - 1) / st);
+    if (st == 1 || cost < 0.97 * best_cost) {
+      best = st;
+      best_cost = cost;
+    }
+  }
+  L.P = (int)best;
   L.rows_grid = bwd_rows_grid(T, sms);
   size_t off = kWsHeaderBytes;
   L.rec = off;
@@ -634,9 +642,20 @@ struct BwdTiled {
     tiled::dx_kernel<n><<<gdx, tiled::kThreads, Dm::DX_SMEM, s>>>(a->x, a->phi, a->gamma, rec, dmT, a->dh_in, a->dx,
                                                                   T, Tp, D);
     if ((st = after_launch())) return st;
-    const dim3 gg((unsigned)((nD + tiled::kKT - 1) / tiled::kKT), (unsigned)L.P);
-    tiled::g_kernel<n><<<gg, tiled::kThreads, 0, s>>>(a->x, rec, gpart, T, nD, L.per_split);
-    if ((st = after_launch())) return st;
+    {
+      using Gc = tiled::GCfg<n>;
+      CUtensorMap m_x;
+      const uint64_t dims[2] = {(uint64_t)nD, (uint64_t)T};
+      const uint64_t strides[1] = {(uint64_t)nD * 2};
+      const uint32_t box[2] = {64, 128};
+      if ((st = encode_bf16_map(&m_x, a->x, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+      if ((st = set_smem_limit_once(tiled::g_tc_kernel<n>, Gc::SMEM))) return st;
+      const int num_tiles = (int)((T + 127) / 128);
+      const dim3 gg((unsigned)((nD + 127) / 128), (unsigned)L.P);
+      tiled::g_tc_kernel<n><<<gg, tiled::kGThreads, Gc::SMEM, s>>>(m_x, rec, gpart, reinterpret_cast<int*>(ws), T,
+                                                                   nD, L.P, num_tiles);
+      if ((st = after_launch())) return st;
+    }
     generic::finalize_param_kernel<N><<<(nD + generic::kFinCols - 1) / generic::kFinCols + 3 + N, generic::kThreads, 0,
                                         s>>>(gpart, L.P, a->phi, a->gamma, a->dphi, a->dgamma, nD, abpart,
                                              (int64_t)L.rows_grid * kRowsWarps, a->dalpha, a->dbias);

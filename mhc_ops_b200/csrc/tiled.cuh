@@ -1,5 +1,6 @@
-// Tiled backward for the shapes the tensor-core backward does not take (n other
-// than 4: the n = 8 "wide" hyper-connection above all), on the CUDA cores.
+// Backward for the shapes the n = 4 tensor-core backward does not take (n other
+// than 4: the n = 8 "wide" hyper-connection above all): dx on the CUDA cores,
+// the parameter-gradient product on the tensor cores.
 //
 // Math: src/backward/golden.py:38-96, split as in the tensor-core backward:
 //   * rowdot::bwd_rows_kernel<n> leaves one record per token, {dh_mix[N], c,
@@ -11,10 +12,9 @@
 //     [T,N] x [N,nD] product tiled through shared memory (cp.async), 64
 //     tokens x 256 k per CTA, 8 x 8 outputs per thread, the N-term sum in
 //     fp32 FMAs in ascending j (the generic kernel's order);
-//   * g_kernel: gpart[p][j][k] = sum over the tokens of split p of
-//     dh_mix[t,j] x[t,k] (the un-scaled dphi, golden.py:68-69), 256 k x all N
-//     per CTA, 16-token chunks double-buffered through shared memory with
-//     cp.async, tokens summed in ascending order;
+//   * g_tc_kernel: gpart[g][j][k] = sum over the tokens of token group g of
+//     dh_mix[t,j] x[t,k] (the un-scaled dphi, golden.py:68-69) on the tensor
+//     cores (below);
 //   * generic::finalize_param_kernel (dphi, dgamma and the dalpha / dbias
 //     column sums) as in the tensor-core backward (fixed order, so results
 //     repeat bit for bit).
@@ -22,6 +22,8 @@
 #pragma once
 
 #include "common.cuh"
+#include "bwd_sm100.cuh"
+#include "sm100.cuh"
 
 namespace mhc {
 namespace tiled {
@@ -30,17 +32,13 @@ constexpr int kThreads = 256;
 constexpr int kTT = 64;    // tokens per dx tile (8 warps x 8 tokens)
 constexpr int kKL = 8;     // consecutive k per lane (one 16-byte bf16 load)
 constexpr int kKT = 32 * kKL;   // k per tile
-constexpr int kTC = 16;    // tokens per g_kernel chunk
 
 template <int n>
 struct Dims {
   static constexpr int N = n * n + 2 * n;
-  static constexpr int N4 = (N + 3) / 4 * 4;             // dh_mix floats copied per record (16-byte pieces)
   static constexpr int RW = ((N + 1 + n) + 3) / 4 * 4;   // record width (rowdot::Rec<n>::W)
-  static constexpr int JW = (N + 7) / 8;                 // g_kernel: j per warp
   // dx_kernel's dynamic shared memory: dmT [N][kTT], ph [N][kKT], c [kTT], h_pre [kTT][n]
   static constexpr int DX_SMEM = 4 * (N * kTT + N * kKT + kTT + kTT * n);
-  static_assert(N4 <= RW && N4 <= 8 * JW, "record copy stays inside the record and the chunk row");
 };
 
 // Tokens of the transposed dh_mix (a whole number of dx tiles).
@@ -196,96 +194,210 @@ __global__ void __launch_bounds__(kThreads) dx_kernel(const uint16_t* __restrict
   }
 }
 
-// grid = (ceil(nD / kKT), P), kThreads threads; split p sums tokens
-// [p * per_split, min(T, (p + 1) * per_split)).
+// ------------------------------------------------------------------ G on the tensor cores
+// gpart[g][j][k] = sum over the tokens of token group g of (hi + mid)[t,j] x[t,k],
+// with hi and mid the first two bf16 terms of dh_mix (G needs ~2^-17, as in
+// the n = 4 tensor-core backward).  CTA (k-range of 128, token group g) walks
+// the tiles g, g + S_T, ...:
+//   * W0 loads the tile's x [128 tok x 128 k] as two 128-B-swizzled TMA boxes
+//     into a GS-deep ring;
+//   * WG_E (4 warps, thread = token row) builds DHM [128 tok x (hi | mid)]
+//     from the records (K-major interleaved, double buffered: tile j+1's
+//     during tile j);
+//   * W1 issues 8 tcgen05.mma per tile: M = 128 k (x read MN-major), N = the
+//     hi and mid segments (DHM read MN-major), K = 16 tokens each, into one
+//     of two TMEM accumulators;
+//   * WG_E (thread = k row = TMEM lane) adds each tile's hi + mid into fp32
+//     registers in tile order, and stores its row of the group's partial once.
+// Every wait is bounded (sm100::mbar_wait): a broken pipeline ends with
+// MHC_ERR_DEVICE_TIMEOUT in the status word instead of hanging.
+constexpr int kGThreads = 6 * 32;   // W0, W1, WG_E(4)
+
 template <int n>
-__global__ void __launch_bounds__(kThreads) g_kernel(const uint16_t* __restrict__ x, const float* __restrict__ rec,
-                                                     float* __restrict__ gpart, int64_t T, int nD, int64_t per_split) {
-  constexpr int N = Dims<n>::N;
-  constexpr int N4 = Dims<n>::N4;
-  constexpr int RW = Dims<n>::RW;
-  constexpr int JW = Dims<n>::JW;
-  __shared__ __align__(16) uint16_t xs[2][kTC][kKT];   // raw bf16 chunks
-  __shared__ __align__(16) float dm[2][kTC][8 * JW];
-  const int k0 = blockIdx.x * kKT;
-  const int p = blockIdx.y;
-  const int64_t ta = (int64_t)p * per_split;
-  const int64_t tb = min(T, ta + per_split);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float2 acc2[JW][kKL / 2];   // (j, k pair): __ffma2_rn, two exact fmaf per instruction
-#pragma unroll
-  for (int a = 0; a < JW; ++a)
-#pragma unroll
-    for (int h = 0; h < kKL / 2; ++h) acc2[a][h] = make_float2(0.f, 0.f);
+struct GCfg {
+  static constexpr int N_OUT = n * n + 2 * n;
+  static constexpr int SEGW = (N_OUT + 15) / 16 * 16;   // one term segment (MMA N per term)
+  static constexpr int KA = 2 * SEGW;                    // hi | mid
+  static constexpr int RG = (KA / 8) * 128;              // one 8-row group of the DHM image
+  static constexpr int DHM_BYTES = 16 * RG;              // 128 token rows
+  static constexpr int BOX_BYTES = 128 * 128;            // one {64 k, 128 tok} x box
+  static constexpr int GS = 3;                           // x tiles in flight
+  static constexpr int RW = Dims<n>::RW;
+  static constexpr int ACC_COLS = (KA + 31) / 32 * 32;
+  static constexpr int TMEM_COLS = 2 * ACC_COLS <= 32 ? 32 : 2 * ACC_COLS <= 64 ? 64 : 2 * ACC_COLS <= 128 ? 128
+                                   : 2 * ACC_COLS <= 256 ? 256 : 512;
+  static constexpr int SMEM = 1024 + GS * 2 * BOX_BYTES + 2 * DHM_BYTES + 256;
+  static_assert(KA <= 256 && KA % 16 == 0, "UMMA N");
+  static_assert(2 * ACC_COLS <= 512, "TMEM");
+  static_assert(SMEM <= 232448, "shared memory");
+};
 
-  // chunk tokens [tc, tc + kTC) into buffer b; x columns past nD and tokens
-  // past tb are not copied (their products are never summed or stored)
-  auto load = [&](int64_t tc, int b) {
-    for (int e = threadIdx.x; e < kTC * (kKT / 8); e += kThreads) {
-      const int tt = e / (kKT / 8), q = e - tt * (kKT / 8);
-      const int64_t t = tc + tt;
-      const int k = k0 + 8 * q;
-      if (t < tb && k < nD) cp16(&xs[b][tt][8 * q], x + t * nD + k);
-    }
-    for (int e = threadIdx.x; e < kTC * (N4 / 4); e += kThreads) {
-      const int tt = e / (N4 / 4), q = e - tt * (N4 / 4);
-      const int64_t t = tc + tt;
-      if (t < tb) cp16(&dm[b][tt][4 * q], rec + t * RW + 4 * q);
-    }
-    cp_commit();
-  };
+template <int n>
+__global__ void __launch_bounds__(kGThreads, 1)
+    g_tc_kernel(const __grid_constant__ CUtensorMap map_x, const float* __restrict__ rec, float* __restrict__ gpart,
+                int* status, int64_t T, int nD, int S_T, int num_tiles) {
+  using namespace sm100;
+  using Cf = GCfg<n>;
+  constexpr int N_OUT = Cf::N_OUT;
+  constexpr int GS = Cf::GS;
+  // barrier slots
+  constexpr int X_FULL = 0, X_EMPTY = GS, DHM_FULL = 2 * GS, DHM_FREE = 2 * GS + 2, ACC_FULL = 2 * GS + 4,
+                ACC_EMPTY = 2 * GS + 6, NBARS = 2 * GS + 8;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* xr = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* dhm = xr + GS * 2 * Cf::BOX_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(dhm + 2 * Cf::DHM_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  const int k0 = blockIdx.x * 128;
+  const int group = blockIdx.y;
+  const int my_tiles = group < num_tiles ? (num_tiles - 1 - group) / S_T + 1 : 0;
 
-  if (ta < tb) load(ta, 0);
-  int b = 0;
-  for (int64_t tc = ta; tc < tb; tc += kTC, b ^= 1) {
-    const bool more = tc + kTC < tb;
-    if (more) {
-      load(tc + kTC, b ^ 1);
-      cp_wait<1>();
-    } else {
-      cp_wait<0>();
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < GS; ++i) {
+      mbar_init(bar(X_FULL + i), 1);
+      mbar_init(bar(X_EMPTY + i), 1);
     }
-    __syncthreads();   // chunk tc is in buffer b for every thread
-    const int nt = (int)min((int64_t)kTC, tb - tc);
-    for (int tt = 0; tt < nt; ++tt) {
-      const uint4 xr = *reinterpret_cast<const uint4*>(&xs[b][tt][kKL * lane]);
-      float xa[kKL];
-      bf16x4(make_uint2(xr.x, xr.y), *reinterpret_cast<float(*)[4]>(&xa[0]));
-      bf16x4(make_uint2(xr.z, xr.w), *reinterpret_cast<float(*)[4]>(&xa[4]));
-      float2 xv[kKL / 2];
-#pragma unroll
-      for (int h = 0; h < kKL / 2; ++h) xv[h] = make_float2(xa[2 * h], xa[2 * h + 1]);
-      float dv[JW];   // this warp's JW values of dh_mix: float2 broadcasts when JW is even
-      if constexpr (JW % 2 == 0) {
-#pragma unroll
-        for (int a = 0; a < JW; a += 2) {
-          const float2 v2 = *reinterpret_cast<const float2*>(&dm[b][tt][warp * JW + a]);
-          dv[a] = v2.x;
-          dv[a + 1] = v2.y;
-        }
-      } else {
-#pragma unroll
-        for (int a = 0; a < JW; ++a) dv[a] = dm[b][tt][warp * JW + a];
-      }
-#pragma unroll
-      for (int a = 0; a < JW; ++a) {
-        const float2 dd = make_float2(dv[a], dv[a]);
-#pragma unroll
-        for (int h = 0; h < kKL / 2; ++h) acc2[a][h] = __ffma2_rn(dd, xv[h], acc2[a][h]);
-      }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(DHM_FULL + i), 128);
+      mbar_init(bar(DHM_FREE + i), 1);
+      mbar_init(bar(ACC_FULL + i), 1);
+      mbar_init(bar(ACC_EMPTY + i), 4);
     }
-    __syncthreads();   // buffer b is used up before the next chunk refills it
+    *abort_flag = 0;
+    fence_mbarrier_init_cluster();
   }
-  const int k = k0 + kKL * lane;
-  if (k >= nD) return;
-#pragma unroll
-  for (int a = 0; a < JW; ++a) {
-    const int j = warp * JW + a;
-    if (j < N) {
-      float4* o = reinterpret_cast<float4*>(gpart + ((int64_t)p * N + j) * nD + k);
-      o[0] = make_float4(acc2[a][0].x, acc2[a][0].y, acc2[a][1].x, acc2[a][1].y);
-      o[1] = make_float4(acc2[a][2].x, acc2[a][2].y, acc2[a][3].x, acc2[a][3].y);
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), Cf::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) prefetch_tensormap(&map_x);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const WaitCtx wc{abort_flag, status};
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- W0: x tiles
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      for (int j = 0; j < my_tiles; ++j) {
+        const int s = j % GS;
+        const int tile = group + j * S_T;
+        mbar_wait(bar(X_EMPTY + s), ((j / GS) & 1) ^ 1, wc);
+        if (*abort_flag) continue;
+        const uint32_t dst = smem_u32(xr + s * 2 * Cf::BOX_BYTES);
+        mbar_arrive_expect_tx(bar(X_FULL + s), 2 * Cf::BOX_BYTES);
+        tma_load_2d(dst, &map_x, bar(X_FULL + s), k0, tile * 128, pol);
+        tma_load_2d(dst + Cf::BOX_BYTES, &map_x, bar(X_FULL + s), k0 + 64, tile * 128, pol);
+      }
     }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- W1: MMA
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(128, Cf::KA, true, true);
+      for (int j = 0; j < my_tiles; ++j) {
+        const int s = j % GS, hb = j & 1;
+        mbar_wait(bar(DHM_FULL + hb), (j >> 1) & 1, wc);
+        mbar_wait(bar(X_FULL + s), (j / GS) & 1, wc);
+        mbar_wait(bar(ACC_EMPTY + hb), ((j >> 1) & 1) ^ 1, wc);
+        tc_fence_after();
+        if (*abort_flag) continue;
+        const uint64_t a = desc_mnmajor_sw128(smem_u32(xr + s * 2 * Cf::BOX_BYTES), Cf::BOX_BYTES, 1024);
+        const uint64_t b = bwdtc::desc_kmajor_interleave(smem_u32(dhm + hb * Cf::DHM_BYTES), Cf::RG, 128);
+        const uint32_t d = tmem_base + hb * Cf::ACC_COLS;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma_bf16(d, a + ((ks * 2048) >> 4), b + ((ks * 2 * Cf::RG) >> 4), idesc, ks != 0);
+        umma_commit(bar(X_EMPTY + s));
+        umma_commit(bar(DHM_FREE + hb));
+        umma_commit(bar(ACC_FULL + hb));
+      }
+    }
+  } else {
+    // ---------------------------------------------------------- WG_E: DHM rows, fold, store
+    const int q4 = warp & 3;
+    const int row = 32 * q4 + lane;   // token row of DHM, k row of the accumulator (TMEM lane)
+    auto build = [&](int j) {
+      const int hb = j & 1;
+      const int64_t t = (int64_t)(group + j * S_T) * 128 + row;
+      float r[Cf::SEGW];
+#pragma unroll
+      for (int c = 0; c < Cf::SEGW; ++c) r[c] = 0.f;
+      if (t < T) {
+        const float4* rp = reinterpret_cast<const float4*>(rec + t * Cf::RW);
+#pragma unroll
+        for (int c4 = 0; c4 < Cf::SEGW / 4; ++c4) {
+          if (4 * c4 < N_OUT) {
+            const float4 v = __ldg(rp + c4);
+            r[4 * c4] = v.x;
+            r[4 * c4 + 1] = v.y;
+            r[4 * c4 + 2] = v.z;
+            r[4 * c4 + 3] = v.w;
+          }
+        }
+#pragma unroll
+        for (int c = N_OUT; c < Cf::SEGW; ++c) r[c] = 0.f;   // c, h_pre and padding of the record
+      }
+      mbar_wait(bar(DHM_FREE + hb), ((j >> 1) & 1) ^ 1, wc);
+      uint8_t* dst = dhm + hb * Cf::DHM_BYTES;
+#pragma unroll
+      for (int kc = 0; kc < Cf::KA / 8; ++kc) {
+        const int e = (kc * 8) / Cf::SEGW, j0 = kc * 8 - e * Cf::SEGW;
+        uint32_t w[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const uint32_t lo = bwdtc::split_term(r[j0 + 2 * h], e);
+          const uint32_t hi = bwdtc::split_term(r[j0 + 2 * h + 1], e);
+          w[h] = lo | (hi << 16);
+        }
+        *reinterpret_cast<uint4*>(dst + bwdtc::interleave_off(row, kc * 8, Cf::RG)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(bar(DHM_FULL + hb));
+    };
+    float acc[N_OUT];
+#pragma unroll
+    for (int c = 0; c < N_OUT; ++c) acc[c] = 0.f;
+    if (my_tiles > 0) build(0);
+    for (int j = 0; j < my_tiles; ++j) {
+      if (j + 1 < my_tiles) build(j + 1);
+      const int hb = j & 1;
+      mbar_wait(bar(ACC_FULL + hb), (j >> 1) & 1, wc);
+      tc_fence_after();
+      const uint32_t ta = tmem_base + hb * Cf::ACC_COLS + ((uint32_t)(32 * q4) << 16);
+#pragma unroll
+      for (int c16 = 0; c16 < Cf::SEGW / 16; ++c16) {
+        float hi[16], mid[16];
+        tmem_ld16(ta + c16 * 16, hi);
+        tmem_ld16(ta + Cf::SEGW + c16 * 16, mid);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int jj = c16 * 16 + e;
+          if (jj < N_OUT) acc[jj] += mid[e] + hi[e];
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(ACC_EMPTY + hb));
+    }
+    const int k = k0 + row;
+    if (k < nD && !*abort_flag) {
+      float* gp = gpart + (int64_t)group * N_OUT * nD + k;
+#pragma unroll
+      for (int jj = 0; jj < N_OUT; ++jj) gp[(int64_t)jj * nD] = acc[jj];
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cf::TMEM_COLS);
   }
 }
 
