@@ -560,7 +560,10 @@ int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s, int sms) {
 // not take, D a multiple of 8, 16-byte aligned x / dh_in / dx / phi / gamma,
 // T < 2^31.
 struct BwdTiledLayout {
-  size_t rec, abpart, gpart, dmT, total;
+  size_t rec, abpart, gpart, dmT, phimg, total;
+  bool dx_tc;            // dx on the tensor cores (D % 64 == 0), else dx_kernel
+  int dx_slices;         // dx_tc_kernel: k-block ranges per token tile
+  int dx_kb_per;         // 64-k blocks per range
   int P;                 // token groups of the G partials (g_tc_kernel's grid.y)
   int rows_grid;
 };
@@ -568,6 +571,19 @@ struct BwdTiledLayout {
 int rec_width(int n) {
   const int N = n * n + 2 * n;
   return ((N + 1 + n) + 3) / 4 * 4;
+}
+
+size_t bwd_tiled_phimg_bytes(int n) {
+  switch (n) {
+    case 1: return tiled::DxCfg<1>::PH_BYTES;
+    case 2: return tiled::DxCfg<2>::PH_BYTES;
+    case 3: return tiled::DxCfg<3>::PH_BYTES;
+    case 4: return tiled::DxCfg<4>::PH_BYTES;
+    case 5: return tiled::DxCfg<5>::PH_BYTES;
+    case 6: return tiled::DxCfg<6>::PH_BYTES;
+    case 7: return tiled::DxCfg<7>::PH_BYTES;
+    default: return tiled::DxCfg<8>::PH_BYTES;
+  }
 }
 
 BwdTiledLayout bwd_tiled_layout(int64_t T, int n, int D, int sms) {
@@ -598,8 +614,27 @@ BwdTiledLayout bwd_tiled_layout(int64_t T, int n, int D, int sms) {
   off = align_up(off + sizeof(float) * (size_t)L.rows_grid * kRowsWarps * (3 + N), kWsAlign);
   L.gpart = off;
   off = align_up(off + sizeof(float) * (size_t)L.P * N * nD, kWsAlign);
-  L.dmT = off;
-  off = align_up(off + sizeof(float) * (size_t)N * tiled::padded_tokens(T), kWsAlign);
+  L.dx_tc = D % 64 == 0;
+  if (L.dx_tc) {
+    // k-block ranges per tile with the least per-CTA work, waves * blocks per range
+    const int64_t KB = nD / 64;
+    int64_t best_s = 1;
+    double best_c = 0.0;
+    for (int64_t sl = 1; sl <= std::min<int64_t>(KB, 64); ++sl) {
+      const double c = (double)((tiles * sl + sms - 1) / sms) * (double)((KB + sl - 1) / sl);
+      if (sl == 1 || c < best_c - 1e-9) {
+        best_s = sl;
+        best_c = c;
+      }
+    }
+    L.dx_slices = (int)best_s;
+    L.dx_kb_per = (int)((KB + best_s - 1) / best_s);
+    L.phimg = off;
+    off = align_up(off + (size_t)KB * bwd_tiled_phimg_bytes(n), kWsAlign);
+  } else {
+    L.dmT = off;
+    off = align_up(off + sizeof(float) * (size_t)N * tiled::padded_tokens(T), kWsAlign);
+  }
   L.total = off;
   return L;
 }
@@ -627,21 +662,48 @@ struct BwdTiled {
     float* rec = reinterpret_cast<float*>(ws + L.rec);
     float* abpart = reinterpret_cast<float*>(ws + L.abpart);
     float* gpart = reinterpret_cast<float*>(ws + L.gpart);
-    float* dmT = reinterpret_cast<float*>(ws + L.dmT);
-    const int64_t Tp = tiled::padded_tokens(T);
     int st;
     rowdot::bwd_rows_kernel<n><<<L.rows_grid, rowdot::kThreads, 0, s>>>(
         a->x, a->dh_in, a->alpha, a->inv_rms, a->h_mix, a->h_pre, a->h_post, a->dh_post, a->dh_res, rec, abpart, T, D,
         a->hc_eps);
     if ((st = after_launch())) return st;
-    const dim3 gtr((unsigned)(Tp / 32), (unsigned)((N + 31) / 32));
-    tiled::transpose_kernel<n><<<gtr, tiled::kThreads, 0, s>>>(rec, dmT, T, Tp);
-    if ((st = after_launch())) return st;
-    if ((st = set_smem_limit_once(tiled::dx_kernel<n>, Dm::DX_SMEM))) return st;
-    const dim3 gdx((unsigned)(Tp / tiled::kTT), (unsigned)((nD + tiled::kKT - 1) / tiled::kKT));
-    tiled::dx_kernel<n><<<gdx, tiled::kThreads, Dm::DX_SMEM, s>>>(a->x, a->phi, a->gamma, rec, dmT, a->dh_in, a->dx,
-                                                                  T, Tp, D);
-    if ((st = after_launch())) return st;
+    if (L.dx_tc) {
+      // dx on the tensor cores: split phi * gamma images, then one CTA per
+      // (token tile, range of 64-k blocks)
+      using Dc = tiled::DxCfg<n>;
+      uint8_t* img = reinterpret_cast<uint8_t*>(ws + L.phimg);
+      tiled::phimg_kernel<n><<<nD / 64, 256, 0, s>>>(a->phi, a->gamma, img, nD);
+      if ((st = after_launch())) return st;
+      CUtensorMap m_x, m_dh;
+      {
+        const uint64_t dims[2] = {(uint64_t)nD, (uint64_t)T};
+        const uint64_t strides[1] = {(uint64_t)nD * 2};
+        const uint32_t box[2] = {64, 128};
+        if ((st = encode_bf16_map(&m_x, a->x, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+      }
+      {
+        const uint64_t dims[2] = {(uint64_t)D, (uint64_t)T};
+        const uint64_t strides[1] = {(uint64_t)D * 2};
+        const uint32_t box[2] = {64, 128};
+        if ((st = encode_bf16_map(&m_dh, a->dh_in, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+      }
+      if ((st = set_smem_limit_once(tiled::dx_tc_kernel<n>, Dc::SMEM))) return st;
+      const dim3 gdx((unsigned)((T + 127) / 128), (unsigned)L.dx_slices);
+      tiled::dx_tc_kernel<n><<<gdx, tiled::kGThreads, Dc::SMEM, s>>>(m_x, m_dh, img, rec, a->dx,
+                                                                    reinterpret_cast<int*>(ws), T, D, L.dx_kb_per);
+      if ((st = after_launch())) return st;
+    } else {
+      float* dmT = reinterpret_cast<float*>(ws + L.dmT);
+      const int64_t Tp = tiled::padded_tokens(T);
+      const dim3 gtr((unsigned)(Tp / 32), (unsigned)((N + 31) / 32));
+      tiled::transpose_kernel<n><<<gtr, tiled::kThreads, 0, s>>>(rec, dmT, T, Tp);
+      if ((st = after_launch())) return st;
+      if ((st = set_smem_limit_once(tiled::dx_kernel<n>, Dm::DX_SMEM))) return st;
+      const dim3 gdx((unsigned)(Tp / tiled::kTT), (unsigned)((nD + tiled::kKT - 1) / tiled::kKT));
+      tiled::dx_kernel<n><<<gdx, tiled::kThreads, Dm::DX_SMEM, s>>>(a->x, a->phi, a->gamma, rec, dmT, a->dh_in,
+                                                                    a->dx, T, Tp, D);
+      if ((st = after_launch())) return st;
+    }
     {
       using Gc = tiled::GCfg<n>;
       CUtensorMap m_x;

@@ -1,6 +1,7 @@
 // Backward for the shapes the n = 4 tensor-core backward does not take (n other
-// than 4: the n = 8 "wide" hyper-connection above all): dx on the CUDA cores,
-// the parameter-gradient product on the tensor cores.
+// than 4: the n = 8 "wide" hyper-connection above all): dx and the
+// parameter-gradient product on the tensor cores (dx_tc_kernel, g_tc_kernel,
+// below), dx on the CUDA cores (dx_kernel) when D is not a multiple of 64.
 //
 // Math: src/backward/golden.py:38-96, split as in the tensor-core backward:
 //   * rowdot::bwd_rows_kernel<n> leaves one record per token, {dh_mix[N], c,
@@ -398,6 +399,271 @@ __global__ void __launch_bounds__(kGThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cf::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ dx on the tensor cores
+// dvecX = dh_mix @ (phi * gamma) as in the n = 4 tensor-core backward: dh_mix
+// and phi * gamma each split into three bf16 terms (hi, mid, lo), six term
+// products summed smallest first (m.M, l.H, h.L, m.H, h.M, h.H; exact to
+// ~2^-23), then dx = dvecX - c x + h_pre[i] dh_in in fp32 and rounded once.
+// CTA = (128-token tile, contiguous range of 64-k blocks):
+//   * WG_E (4 warps, thread = token row) builds the tile's DHM image
+//     [128 tok x 3 segments] from the records once;
+//   * W0 streams per 64-k block the x and dh_in boxes (TMA, 128-B swizzle)
+//     and the block's split phi * gamma image (bulk copy from the image
+//     phimg_kernel leaves in the workspace) into a 2-stage ring;
+//   * W1 issues 6 x SEGW/16 tcgen05.mma (M = 128 tokens, N = 64 k, K = 16)
+//     per block into one of two TMEM accumulators;
+//   * WG_E reads the accumulator (TMEM lane = token row), adds -c x + h_pre
+//     dh_in and stores the row's 64 dx values (128 bytes) to global.
+template <int n>
+struct DxCfg {
+  static constexpr int N_OUT = n * n + 2 * n;
+  static constexpr int SEGW = (N_OUT + 15) / 16 * 16;
+  static constexpr int KA = 3 * SEGW;                    // hi | mid | lo
+  static constexpr int RG = (KA / 8) * 128;              // one 8-row group of a K-major interleaved image
+  static constexpr int DHM_BYTES = 16 * RG;              // 128 token rows
+  static constexpr int PH_BYTES = 8 * RG;                // 64 k rows: split phi * gamma of one 64-k block
+  static constexpr int BOX_BYTES = 128 * 128;            // one {64, 128} bf16 box
+  static constexpr int STAGE_BYTES = 2 * BOX_BYTES + PH_BYTES;   // x, dh_in, phi image
+  static constexpr int ST = 2;
+  static constexpr int RW = Dims<n>::RW;
+  static constexpr int SMEM = 1024 + ST * STAGE_BYTES + DHM_BYTES + 256;
+  static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 128-B swizzle atoms aligned");
+  static_assert(SMEM <= 232448, "shared memory");
+};
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// Split images of phi * gamma: block kb (64 k) -> img + kb * PH_BYTES, row kk
+// (= k - 64 kb), column e * SEGW + j = bf16 term e of phi[j][k] * gamma[k]
+// (zeros for j >= N_OUT), K-major interleaved.  One CTA per block.
+template <int n>
+__global__ void __launch_bounds__(256) phimg_kernel(const float* __restrict__ phi, const float* __restrict__ gamma,
+                                                    uint8_t* __restrict__ img, int nD) {
+  using Cf = DxCfg<n>;
+  constexpr int CPR = Cf::KA / 8;
+  __shared__ float cols[Cf::N_OUT][65];
+  const int blk = blockIdx.x;
+  for (int idx = threadIdx.x; idx < Cf::N_OUT * 64; idx += 256) {
+    const int j = idx / 64, kk = idx - j * 64;
+    const int64_t k = (int64_t)blk * 64 + kk;
+    cols[j][kk] = k < nD ? __ldg(phi + (int64_t)j * nD + k) * (gamma ? __ldg(gamma + k) : 1.0f) : 0.f;
+  }
+  __syncthreads();
+  uint8_t* out = img + (size_t)blk * Cf::PH_BYTES;
+  for (int t = threadIdx.x; t < Cf::PH_BYTES / 16; t += 256) {
+    // byte offset 16*t = (kk/8)*RG + cc*128 + (kk%8)*16
+    const int grp = t / (8 * CPR), rem = t - grp * 8 * CPR;
+    const int cc = rem >> 3, kk = grp * 8 + (rem & 7);
+    const int e = (cc * 8) / Cf::SEGW, j0 = cc * 8 - e * Cf::SEGW;
+    uint32_t w[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const int ja = j0 + 2 * h, jb = ja + 1;
+      const uint32_t lo = ja < Cf::N_OUT ? bwdtc::split_term(cols[ja < Cf::N_OUT ? ja : 0][kk], e) : 0;
+      const uint32_t hi = jb < Cf::N_OUT ? bwdtc::split_term(cols[jb < Cf::N_OUT ? jb : 0][kk], e) : 0;
+      w[h] = lo | (hi << 16);
+    }
+    *reinterpret_cast<uint4*>(out + (size_t)t * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+template <int n>
+__global__ void __launch_bounds__(kGThreads, 1)
+    dx_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_dh,
+                 const uint8_t* __restrict__ img, const float* __restrict__ rec, uint16_t* __restrict__ dx,
+                 int* status, int64_t T, int D, int kb_per) {
+  using namespace sm100;
+  using Cf = DxCfg<n>;
+  constexpr int N_OUT = Cf::N_OUT;
+  constexpr int ST = Cf::ST;
+  constexpr int FULL = 0, EMPTY = ST, ACC_FULL = 2 * ST, ACC_EMPTY = 2 * ST + 2, DHM_FULL = 2 * ST + 4,
+                NBARS = 2 * ST + 5;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* dhm = stages + ST * Cf::STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(dhm + Cf::DHM_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  const int nD = n * D;
+  const int KB = nD / 64;
+  const int tile = blockIdx.x;
+  const int kb0 = blockIdx.y * kb_per;
+  const int nkb = max(0, min(kb_per, KB - kb0));
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ST; ++i) {
+      mbar_init(bar(FULL + i), 1);
+      mbar_init(bar(EMPTY + i), 1 + 4);   // MMA commit + the 4 epilogue warps
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(ACC_FULL + i), 1);
+      mbar_init(bar(ACC_EMPTY + i), 4);
+    }
+    mbar_init(bar(DHM_FULL), 128);
+    *abort_flag = 0;
+    fence_mbarrier_init_cluster();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 128);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&map_x);
+    prefetch_tensormap(&map_dh);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const WaitCtx wc{abort_flag, status};
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- W0: x, dh_in, phi image
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      for (int b = 0; b < nkb; ++b) {
+        const int s = b % ST;
+        const int kb = kb0 + b;
+        mbar_wait(bar(EMPTY + s), ((b / ST) & 1) ^ 1, wc);
+        if (*abort_flag) continue;
+        uint8_t* st = stages + s * Cf::STAGE_BYTES;
+        mbar_arrive_expect_tx(bar(FULL + s), Cf::STAGE_BYTES);
+        tma_load_2d(smem_u32(st), &map_x, bar(FULL + s), kb * 64, tile * 128, pol);
+        tma_load_2d(smem_u32(st + Cf::BOX_BYTES), &map_dh, bar(FULL + s), (kb * 64) % D, tile * 128, pol);
+        bulk_g2s(smem_u32(st + 2 * Cf::BOX_BYTES), img + (size_t)kb * Cf::PH_BYTES, Cf::PH_BYTES, bar(FULL + s));
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- W1: MMA
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(128, 64, false, false);
+      mbar_wait(bar(DHM_FULL), 0, wc);
+      const uint64_t a_dv = bwdtc::desc_kmajor_interleave(smem_u32(dhm), 128, Cf::RG);
+      for (int b = 0; b < nkb; ++b) {
+        const int s = b % ST, ab = b & 1;
+        mbar_wait(bar(FULL + s), (b / ST) & 1, wc);
+        mbar_wait(bar(ACC_EMPTY + ab), ((b >> 1) & 1) ^ 1, wc);
+        tc_fence_after();
+        if (*abort_flag) continue;
+        const uint64_t b_dv =
+            bwdtc::desc_kmajor_interleave(smem_u32(stages + s * Cf::STAGE_BYTES + 2 * Cf::BOX_BYTES), 128, Cf::RG);
+        const uint32_t d = tmem_base + ab * 64;
+#pragma unroll
+        for (int pr = 0; pr < 6; ++pr) {
+#pragma unroll
+          for (int ks = 0; ks < Cf::SEGW / 16; ++ks) {
+            const uint32_t ca = (bwdtc::prod_a_term(pr) * Cf::SEGW + ks * 16) * 16;
+            const uint32_t cb = (bwdtc::prod_b_term(pr) * Cf::SEGW + ks * 16) * 16;
+            umma_bf16(d, a_dv + (ca >> 4), b_dv + (cb >> 4), idesc, pr != 0 || ks != 0);
+          }
+        }
+        umma_commit(bar(EMPTY + s));
+        umma_commit(bar(ACC_FULL + ab));
+      }
+    }
+  } else {
+    // ---------------------------------------------------------- WG_E: DHM once, dx per block
+    const int q4 = warp & 3;
+    const int row = 32 * q4 + lane;   // token row = TMEM lane
+    const int64_t t = (int64_t)tile * 128 + row;
+    float c_t = 0.f, hp[n];
+#pragma unroll
+    for (int i = 0; i < n; ++i) hp[i] = 0.f;
+    {
+      float r[Cf::SEGW];
+#pragma unroll
+      for (int c = 0; c < Cf::SEGW; ++c) r[c] = 0.f;
+      if (t < T) {
+        const float* rp = rec + t * Cf::RW;
+#pragma unroll
+        for (int c = 0; c < N_OUT; ++c) r[c] = __ldg(rp + c);
+        c_t = __ldg(rp + N_OUT);
+#pragma unroll
+        for (int i = 0; i < n; ++i) hp[i] = __ldg(rp + N_OUT + 1 + i);
+      }
+#pragma unroll
+      for (int kc = 0; kc < Cf::KA / 8; ++kc) {
+        const int e = (kc * 8) / Cf::SEGW, j0 = kc * 8 - e * Cf::SEGW;
+        uint32_t w[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const uint32_t lo = bwdtc::split_term(r[j0 + 2 * h], e);
+          const uint32_t hi = bwdtc::split_term(r[j0 + 2 * h + 1], e);
+          w[h] = lo | (hi << 16);
+        }
+        *reinterpret_cast<uint4*>(dhm + bwdtc::interleave_off(row, kc * 8, Cf::RG)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(bar(DHM_FULL));
+    }
+    for (int b = 0; b < nkb; ++b) {
+      const int s = b % ST, ab = b & 1;
+      const int k0 = (kb0 + b) * 64;
+      const int i = k0 / D;
+      float hpi = hp[0];
+#pragma unroll
+      for (int ii = 1; ii < n; ++ii)
+        if (i == ii) hpi = hp[ii];
+      mbar_wait(bar(ACC_FULL + ab), (b >> 1) & 1, wc);
+      mbar_wait(bar(FULL + s), (b / ST) & 1, wc);   // x and dh_in of the block (already complete)
+      tc_fence_after();
+      const uint8_t* st = stages + s * Cf::STAGE_BYTES;
+      const uint32_t x_row = smem_u32(st) + row * 128;
+      const uint32_t g_row = smem_u32(st + Cf::BOX_BYTES) + row * 128;
+      const uint32_t ta = tmem_base + ab * 64 + ((uint32_t)(32 * q4) << 16);
+      uint4 outv[8];
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        float v0[16], v1[16];
+        tmem_ld16(ta + hf * 32, v0);
+        tmem_ld16(ta + hf * 32 + 16, v1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int hc = 0; hc < 4; ++hc) {
+          const int c = hf * 4 + hc;   // 16-byte chunk of the 128-byte row
+          float xf[8], gf[8];
+          bwdtc::bf16x8_to_f32(bwdtc::lds128(x_row + ((c ^ (row & 7)) << 4)), xf);
+          bwdtc::bf16x8_to_f32(bwdtc::lds128(g_row + ((c ^ (row & 7)) << 4)), gf);
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            const float a0 = (hc < 2 ? v0[(hc * 8 + e) & 15] : v1[(hc * 8 + e) & 15]);
+            const float a1 = (hc < 2 ? v0[(hc * 8 + e + 1) & 15] : v1[(hc * 8 + e + 1) & 15]);
+            const float d0 = a0 + ((-c_t) * xf[e] + hpi * gf[e]);
+            const float d1 = a1 + ((-c_t) * xf[e + 1] + hpi * gf[e + 1]);
+            o[e / 2] = pack_bf16x2(d0, d1);
+          }
+          outv[c] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(bar(ACC_EMPTY + ab));
+        mbar_arrive(bar(EMPTY + s));
+      }
+      if (t < T && !*abort_flag) {
+        uint4* dst = reinterpret_cast<uint4*>(dx + t * nD + k0);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) dst[c] = outv[c];
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 128);
   }
 }
 
