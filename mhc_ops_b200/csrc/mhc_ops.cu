@@ -555,12 +555,13 @@ int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s, int sms) {
 }
 
 // ----------------------------------------------------------------- tiled backward (n != 4)
-// rowdot::bwd_rows_kernel (records), tiled::dx_kernel (CUDA cores),
-// tiled::g_tc_kernel (tcgen05), then the shared finalize kernel.  Shapes: every n the tensor-core backward does
+// rowdot::bwd_rows_kernel (records), dx (tiled::phimg_kernel + dx_tc_kernel
+// on the tensor cores, or transpose_kernel + dx_kernel on the CUDA cores),
+// tiled::gimg_kernel + g_tc_kernel (tcgen05), then the shared finalize kernel.  Shapes: every n the tensor-core backward does
 // not take, D a multiple of 8, 16-byte aligned x / dh_in / dx / phi / gamma,
 // T < 2^31.
 struct BwdTiledLayout {
-  size_t rec, abpart, gpart, dmT, phimg, total;
+  size_t rec, abpart, gpart, gimg, dmT, phimg, total;
   bool dx_tc;            // dx on the tensor cores (D % 64 == 0), else dx_kernel
   int dx_slices;         // dx_tc_kernel: k-block ranges per token tile
   int dx_kb_per;         // 64-k blocks per range
@@ -583,6 +584,19 @@ size_t bwd_tiled_phimg_bytes(int n) {
     case 6: return tiled::DxCfg<6>::PH_BYTES;
     case 7: return tiled::DxCfg<7>::PH_BYTES;
     default: return tiled::DxCfg<8>::PH_BYTES;
+  }
+}
+
+size_t bwd_tiled_gimg_bytes(int n) {
+  switch (n) {
+    case 1: return tiled::GCfg<1>::DHM_BYTES;
+    case 2: return tiled::GCfg<2>::DHM_BYTES;
+    case 3: return tiled::GCfg<3>::DHM_BYTES;
+    case 4: return tiled::GCfg<4>::DHM_BYTES;
+    case 5: return tiled::GCfg<5>::DHM_BYTES;
+    case 6: return tiled::GCfg<6>::DHM_BYTES;
+    case 7: return tiled::GCfg<7>::DHM_BYTES;
+    default: return tiled::GCfg<8>::DHM_BYTES;
   }
 }
 
@@ -614,6 +628,8 @@ BwdTiledLayout bwd_tiled_layout(int64_t T, int n, int D, int sms) {
   off = align_up(off + sizeof(float) * (size_t)L.rows_grid * kRowsWarps * (3 + N), kWsAlign);
   L.gpart = off;
   off = align_up(off + sizeof(float) * (size_t)L.P * N * nD, kWsAlign);
+  L.gimg = off;
+  off = align_up(off + (size_t)tiles * bwd_tiled_gimg_bytes(n), kWsAlign);
   L.dx_tc = D % 64 == 0;
   if (L.dx_tc) {
     // k-block ranges per tile with the least per-CTA work, waves * blocks per range
@@ -711,11 +727,14 @@ struct BwdTiled {
       const uint64_t strides[1] = {(uint64_t)nD * 2};
       const uint32_t box[2] = {64, 128};
       if ((st = encode_bf16_map(&m_x, a->x, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
-      if ((st = set_smem_limit_once(tiled::g_tc_kernel<n>, Gc::SMEM))) return st;
       const int num_tiles = (int)((T + 127) / 128);
+      uint8_t* gimg = reinterpret_cast<uint8_t*>(ws + L.gimg);
+      tiled::gimg_kernel<n><<<num_tiles, 128, 0, s>>>(rec, gimg, T);
+      if ((st = after_launch())) return st;
+      if ((st = set_smem_limit_once(tiled::g_tc_kernel<n>, Gc::SMEM))) return st;
       const dim3 gg((unsigned)((nD + 127) / 128), (unsigned)L.P);
-      tiled::g_tc_kernel<n><<<gg, tiled::kGThreads, Gc::SMEM, s>>>(m_x, rec, gpart, reinterpret_cast<int*>(ws), T,
-                                                                   nD, L.P, num_tiles);
+      tiled::g_tc_kernel<n><<<gg, tiled::kGThreads, Gc::SMEM, s>>>(m_x, gimg, gpart, reinterpret_cast<int*>(ws), nD,
+                                                                   L.P, num_tiles);
       if ((st = after_launch())) return st;
     }
     generic::finalize_param_kernel<N><<<(nD + generic::kFinCols - 1) / generic::kFinCols + 3 + N, generic::kThreads, 0,

@@ -198,18 +198,18 @@ __global__ void __launch_bounds__(kThreads) dx_kernel(const uint16_t* __restrict
 // ------------------------------------------------------------------ G on the tensor cores
 // gpart[g][j][k] = sum over the tokens of token group g of (hi + mid)[t,j] x[t,k],
 // with hi and mid the first two bf16 terms of dh_mix (G needs ~2^-17, as in
-// the n = 4 tensor-core backward).  CTA (k-range of 128, token group g) walks
-// the tiles g, g + S_T, ...:
-//   * W0 loads the tile's x [128 tok x 128 k] as two 128-B-swizzled TMA boxes
-//     into a GS-deep ring;
-//   * WG_E (4 warps, thread = token row) builds DHM [128 tok x (hi | mid)]
-//     from the records (K-major interleaved, double buffered: tile j+1's
-//     during tile j);
-//   * W1 issues 8 tcgen05.mma per tile: M = 128 k (x read MN-major), N = the
-//     hi and mid segments (DHM read MN-major), K = 16 tokens each, into one
-//     of two TMEM accumulators;
-//   * WG_E (thread = k row = TMEM lane) adds each tile's hi + mid into fp32
-//     registers in tile order, and stores its row of the group's partial once.
+// the n = 4 tensor-core backward).
+//   * gimg_kernel writes, once per 128-token tile, the tile's DHM image
+//     [128 tok x (hi | mid)] (K-major interleaved) into the workspace;
+//   * g_tc_kernel: CTA (k-range of 128, token group g) walks the tiles g,
+//     g + S_T, ...  W0 loads per tile the x block [128 tok x 128 k] as two
+//     128-B-swizzled TMA boxes and the tile's DHM image (bulk copy, from L2:
+//     every k-range reads it) into one stage of a GS-deep ring; W1 issues 8
+//     tcgen05.mma per tile (M = 128 k, x read MN-major; N = the hi and mid
+//     segments, DHM read MN-major; K = 16 tokens each) into one of two TMEM
+//     accumulators; WG_E (thread = k row = TMEM lane) adds each tile's
+//     hi + mid into fp32 registers in tile order and stores its row of the
+//     group's partial once.
 // Every wait is bounded (sm100::mbar_wait): a broken pipeline ends with
 // MHC_ERR_DEVICE_TIMEOUT in the status word instead of hanging.
 constexpr int kGThreads = 6 * 32;   // W0, W1, WG_E(4)
@@ -222,32 +222,83 @@ struct GCfg {
   static constexpr int RG = (KA / 8) * 128;              // one 8-row group of the DHM image
   static constexpr int DHM_BYTES = 16 * RG;              // 128 token rows
   static constexpr int BOX_BYTES = 128 * 128;            // one {64 k, 128 tok} x box
-  static constexpr int GS = 3;                           // x tiles in flight
+  static constexpr int STAGE_BYTES = 2 * BOX_BYTES + DHM_BYTES;
+  static constexpr int GS = (232448 - 1024 - 256) / STAGE_BYTES < 6 ? (232448 - 1024 - 256) / STAGE_BYTES : 6;
   static constexpr int RW = Dims<n>::RW;
   static constexpr int ACC_COLS = (KA + 31) / 32 * 32;
   static constexpr int TMEM_COLS = 2 * ACC_COLS <= 32 ? 32 : 2 * ACC_COLS <= 64 ? 64 : 2 * ACC_COLS <= 128 ? 128
                                    : 2 * ACC_COLS <= 256 ? 256 : 512;
-  static constexpr int SMEM = 1024 + GS * 2 * BOX_BYTES + 2 * DHM_BYTES + 256;
+  static constexpr int SMEM = 1024 + GS * STAGE_BYTES + 256;
   static_assert(KA <= 256 && KA % 16 == 0, "UMMA N");
+  static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 128-B swizzle atoms aligned");
+  static_assert(GS >= 2, "ring depth");
   static_assert(2 * ACC_COLS <= 512, "TMEM");
   static_assert(SMEM <= 232448, "shared memory");
 };
 
+// DHM image of tile blockIdx.x: row = token, column e * SEGW + j = bf16 term
+// e (0 = hi, 1 = mid) of dh_mix[t][j] (zeros for j >= N_OUT and t >= T),
+// K-major interleaved, as g_tc_kernel's B operand reads it.  128 threads,
+// thread = token row.
+template <int n>
+__global__ void __launch_bounds__(128) gimg_kernel(const float* __restrict__ rec, uint8_t* __restrict__ img,
+                                                   int64_t T) {
+  using Cf = GCfg<n>;
+  constexpr int N_OUT = Cf::N_OUT;
+  const int row = threadIdx.x;
+  const int64_t t = (int64_t)blockIdx.x * 128 + row;
+  float r[Cf::SEGW];
+#pragma unroll
+  for (int c = 0; c < Cf::SEGW; ++c) r[c] = 0.f;
+  if (t < T) {
+    const float4* rp = reinterpret_cast<const float4*>(rec + t * Cf::RW);
+#pragma unroll
+    for (int c4 = 0; c4 < Cf::SEGW / 4; ++c4) {
+      if (4 * c4 < N_OUT) {
+        const float4 v = __ldg(rp + c4);
+        r[4 * c4] = v.x;
+        r[4 * c4 + 1] = v.y;
+        r[4 * c4 + 2] = v.z;
+        r[4 * c4 + 3] = v.w;
+      }
+    }
+#pragma unroll
+    for (int c = N_OUT; c < Cf::SEGW; ++c) r[c] = 0.f;   // c, h_pre and padding of the record
+  }
+  uint8_t* dst = img + (size_t)blockIdx.x * Cf::DHM_BYTES;
+#pragma unroll
+  for (int kc = 0; kc < Cf::KA / 8; ++kc) {
+    const int e = (kc * 8) / Cf::SEGW, j0 = kc * 8 - e * Cf::SEGW;
+    uint32_t w[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const uint32_t lo = bwdtc::split_term(r[j0 + 2 * h], e);
+      const uint32_t hi = bwdtc::split_term(r[j0 + 2 * h + 1], e);
+      w[h] = lo | (hi << 16);
+    }
+    *reinterpret_cast<uint4*>(dst + bwdtc::interleave_off(row, kc * 8, Cf::RG)) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
 template <int n>
 __global__ void __launch_bounds__(kGThreads, 1)
-    g_tc_kernel(const __grid_constant__ CUtensorMap map_x, const float* __restrict__ rec, float* __restrict__ gpart,
-                int* status, int64_t T, int nD, int S_T, int num_tiles) {
+    g_tc_kernel(const __grid_constant__ CUtensorMap map_x, const uint8_t* __restrict__ gimg, float* __restrict__ gpart,
+                int* status, int nD, int S_T, int num_tiles) {
   using namespace sm100;
   using Cf = GCfg<n>;
   constexpr int N_OUT = Cf::N_OUT;
   constexpr int GS = Cf::GS;
   // barrier slots
-  constexpr int X_FULL = 0, X_EMPTY = GS, DHM_FULL = 2 * GS, DHM_FREE = 2 * GS + 2, ACC_FULL = 2 * GS + 4,
-                ACC_EMPTY = 2 * GS + 6, NBARS = 2 * GS + 8;
+  constexpr int FULL = 0, EMPTY = GS, ACC_FULL = 2 * GS, ACC_EMPTY = 2 * GS + 2, NBARS = 2 * GS + 4;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* xr = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* dhm = xr + GS * 2 * Cf::BOX_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(dhm + 2 * Cf::DHM_BYTES);
+  uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(stages + GS * Cf::STAGE_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -258,12 +309,10 @@ __global__ void __launch_bounds__(kGThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < GS; ++i) {
-      mbar_init(bar(X_FULL + i), 1);
-      mbar_init(bar(X_EMPTY + i), 1);
+      mbar_init(bar(FULL + i), 1);
+      mbar_init(bar(EMPTY + i), 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(bar(DHM_FULL + i), 128);
-      mbar_init(bar(DHM_FREE + i), 1);
       mbar_init(bar(ACC_FULL + i), 1);
       mbar_init(bar(ACC_EMPTY + i), 4);
     }
@@ -282,18 +331,19 @@ __global__ void __launch_bounds__(kGThreads, 1)
   const WaitCtx wc{abort_flag, status};
 
   if (warp == 0) {
-    // ---------------------------------------------------------- W0: x tiles
+    // ---------------------------------------------------------- W0: x block and DHM image per tile
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
       for (int j = 0; j < my_tiles; ++j) {
         const int s = j % GS;
         const int tile = group + j * S_T;
-        mbar_wait(bar(X_EMPTY + s), ((j / GS) & 1) ^ 1, wc);
+        mbar_wait(bar(EMPTY + s), ((j / GS) & 1) ^ 1, wc);
         if (*abort_flag) continue;
-        const uint32_t dst = smem_u32(xr + s * 2 * Cf::BOX_BYTES);
-        mbar_arrive_expect_tx(bar(X_FULL + s), 2 * Cf::BOX_BYTES);
-        tma_load_2d(dst, &map_x, bar(X_FULL + s), k0, tile * 128, pol);
-        tma_load_2d(dst + Cf::BOX_BYTES, &map_x, bar(X_FULL + s), k0 + 64, tile * 128, pol);
+        const uint32_t dst = smem_u32(stages + s * Cf::STAGE_BYTES);
+        mbar_arrive_expect_tx(bar(FULL + s), Cf::STAGE_BYTES);
+        tma_load_2d(dst, &map_x, bar(FULL + s), k0, tile * 128, pol);
+        tma_load_2d(dst + Cf::BOX_BYTES, &map_x, bar(FULL + s), k0 + 64, tile * 128, pol);
+        bulk_g2s(dst + 2 * Cf::BOX_BYTES, gimg + (size_t)tile * Cf::DHM_BYTES, Cf::DHM_BYTES, bar(FULL + s));
       }
     }
   } else if (warp == 1) {
@@ -302,70 +352,29 @@ __global__ void __launch_bounds__(kGThreads, 1)
       constexpr uint32_t idesc = idesc_bf16_f32(128, Cf::KA, true, true);
       for (int j = 0; j < my_tiles; ++j) {
         const int s = j % GS, hb = j & 1;
-        mbar_wait(bar(DHM_FULL + hb), (j >> 1) & 1, wc);
-        mbar_wait(bar(X_FULL + s), (j / GS) & 1, wc);
+        mbar_wait(bar(FULL + s), (j / GS) & 1, wc);
         mbar_wait(bar(ACC_EMPTY + hb), ((j >> 1) & 1) ^ 1, wc);
         tc_fence_after();
         if (*abort_flag) continue;
-        const uint64_t a = desc_mnmajor_sw128(smem_u32(xr + s * 2 * Cf::BOX_BYTES), Cf::BOX_BYTES, 1024);
-        const uint64_t b = bwdtc::desc_kmajor_interleave(smem_u32(dhm + hb * Cf::DHM_BYTES), Cf::RG, 128);
+        const uint32_t st = smem_u32(stages + s * Cf::STAGE_BYTES);
+        const uint64_t a = desc_mnmajor_sw128(st, Cf::BOX_BYTES, 1024);
+        const uint64_t b = bwdtc::desc_kmajor_interleave(st + 2 * Cf::BOX_BYTES, Cf::RG, 128);
         const uint32_t d = tmem_base + hb * Cf::ACC_COLS;
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
           umma_bf16(d, a + ((ks * 2048) >> 4), b + ((ks * 2 * Cf::RG) >> 4), idesc, ks != 0);
-        umma_commit(bar(X_EMPTY + s));
-        umma_commit(bar(DHM_FREE + hb));
+        umma_commit(bar(EMPTY + s));
         umma_commit(bar(ACC_FULL + hb));
       }
     }
   } else {
-    // ---------------------------------------------------------- WG_E: DHM rows, fold, store
+    // ---------------------------------------------------------- WG_E: fold, store
     const int q4 = warp & 3;
-    const int row = 32 * q4 + lane;   // token row of DHM, k row of the accumulator (TMEM lane)
-    auto build = [&](int j) {
-      const int hb = j & 1;
-      const int64_t t = (int64_t)(group + j * S_T) * 128 + row;
-      float r[Cf::SEGW];
-#pragma unroll
-      for (int c = 0; c < Cf::SEGW; ++c) r[c] = 0.f;
-      if (t < T) {
-        const float4* rp = reinterpret_cast<const float4*>(rec + t * Cf::RW);
-#pragma unroll
-        for (int c4 = 0; c4 < Cf::SEGW / 4; ++c4) {
-          if (4 * c4 < N_OUT) {
-            const float4 v = __ldg(rp + c4);
-            r[4 * c4] = v.x;
-            r[4 * c4 + 1] = v.y;
-            r[4 * c4 + 2] = v.z;
-            r[4 * c4 + 3] = v.w;
-          }
-        }
-#pragma unroll
-        for (int c = N_OUT; c < Cf::SEGW; ++c) r[c] = 0.f;   // c, h_pre and padding of the record
-      }
-      mbar_wait(bar(DHM_FREE + hb), ((j >> 1) & 1) ^ 1, wc);
-      uint8_t* dst = dhm + hb * Cf::DHM_BYTES;
-#pragma unroll
-      for (int kc = 0; kc < Cf::KA / 8; ++kc) {
-        const int e = (kc * 8) / Cf::SEGW, j0 = kc * 8 - e * Cf::SEGW;
-        uint32_t w[4];
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          const uint32_t lo = bwdtc::split_term(r[j0 + 2 * h], e);
-          const uint32_t hi = bwdtc::split_term(r[j0 + 2 * h + 1], e);
-          w[h] = lo | (hi << 16);
-        }
-        *reinterpret_cast<uint4*>(dst + bwdtc::interleave_off(row, kc * 8, Cf::RG)) = make_uint4(w[0], w[1], w[2], w[3]);
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(bar(DHM_FULL + hb));
-    };
+    const int row = 32 * q4 + lane;   // k row of the accumulator (TMEM lane)
     float acc[N_OUT];
 #pragma unroll
     for (int c = 0; c < N_OUT; ++c) acc[c] = 0.f;
-    if (my_tiles > 0) build(0);
     for (int j = 0; j < my_tiles; ++j) {
-      if (j + 1 < my_tiles) build(j + 1);
       const int hb = j & 1;
       mbar_wait(bar(ACC_FULL + hb), (j >> 1) & 1, wc);
       tc_fence_after();
@@ -407,7 +416,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
 // and phi * gamma each split into three bf16 terms (hi, mid, lo), six term
 // products summed smallest first (m.M, l.H, h.L, m.H, h.M, h.H; exact to
 // ~2^-23), then dx = dvecX - c x + h_pre[i] dh_in in fp32 and rounded once.
-// CTA = (128-token tile, contiguous range of 64-k blocks):
+// CTA = (128-token tile, range of 64-k blocks taken in stream-fastest order,
+// so the n blocks that read one dh_in box run back to back and the box is
+// read from DRAM once):
 //   * WG_E (4 warps, thread = token row) builds the tile's DHM image
 //     [128 tok x 3 segments] from the records once;
 //   * W0 streams per 64-k block the x and dh_in boxes (TMA, 128-B swizzle)
@@ -434,11 +445,6 @@ struct DxCfg {
   static_assert(SMEM <= 232448, "shared memory");
 };
 
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-               "l"(src), "r"(bytes), "r"(bar)
-               : "memory");
-}
 
 // Split images of phi * gamma: block kb (64 k) -> img + kb * PH_BYTES, row kk
 // (= k - 64 kb), column e * SEGW + j = bf16 term e of phi[j][k] * gamma[k]
@@ -498,6 +504,10 @@ __global__ void __launch_bounds__(kGThreads, 1)
   const int tile = blockIdx.x;
   const int kb0 = blockIdx.y * kb_per;
   const int nkb = max(0, min(kb_per, KB - kb0));
+  // the CTA's blocks in stream-fastest order: position q -> block (q % n) *
+  // D/64 + q / n, so the n blocks that share one dh_in box follow each other
+  const int DB = D / 64;
+  auto kb_of = [&](int q) { return (q % n) * DB + q / n; };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < ST; ++i) {
@@ -530,15 +540,16 @@ __global__ void __launch_bounds__(kGThreads, 1)
     // ---------------------------------------------------------- W0: x, dh_in, phi image
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
+      const uint64_t pol_dh = l2_policy_evict_last();   // read again by the next n - 1 blocks
       for (int b = 0; b < nkb; ++b) {
         const int s = b % ST;
-        const int kb = kb0 + b;
+        const int kb = kb_of(kb0 + b);
         mbar_wait(bar(EMPTY + s), ((b / ST) & 1) ^ 1, wc);
         if (*abort_flag) continue;
         uint8_t* st = stages + s * Cf::STAGE_BYTES;
         mbar_arrive_expect_tx(bar(FULL + s), Cf::STAGE_BYTES);
         tma_load_2d(smem_u32(st), &map_x, bar(FULL + s), kb * 64, tile * 128, pol);
-        tma_load_2d(smem_u32(st + Cf::BOX_BYTES), &map_dh, bar(FULL + s), (kb * 64) % D, tile * 128, pol);
+        tma_load_2d(smem_u32(st + Cf::BOX_BYTES), &map_dh, bar(FULL + s), (kb * 64) % D, tile * 128, pol_dh);
         bulk_g2s(smem_u32(st + 2 * Cf::BOX_BYTES), img + (size_t)kb * Cf::PH_BYTES, Cf::PH_BYTES, bar(FULL + s));
       }
     }
@@ -607,7 +618,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
     }
     for (int b = 0; b < nkb; ++b) {
       const int s = b % ST, ab = b & 1;
-      const int k0 = (kb0 + b) * 64;
+      const int k0 = kb_of(kb0 + b) * 64;
       const int i = k0 / D;
       float hpi = hp[0];
 #pragma unroll
