@@ -703,9 +703,16 @@ struct BwdTiled {
         const uint32_t box[2] = {64, 128};
         if ((st = encode_bf16_map(&m_dh, a->dh_in, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
       }
+      CUtensorMap m_dx;
+      {
+        const uint64_t dims[2] = {(uint64_t)nD, (uint64_t)T};
+        const uint64_t strides[1] = {(uint64_t)nD * 2};
+        const uint32_t box[2] = {64, 128};
+        if ((st = encode_bf16_map(&m_dx, a->dx, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+      }
       if ((st = set_smem_limit_once(tiled::dx_tc_kernel<n>, Dc::SMEM))) return st;
       const dim3 gdx((unsigned)((T + 127) / 128), (unsigned)L.dx_slices);
-      tiled::dx_tc_kernel<n><<<gdx, tiled::kGThreads, Dc::SMEM, s>>>(m_x, m_dh, img, rec, a->dx,
+      tiled::dx_tc_kernel<n><<<gdx, tiled::kGThreads, Dc::SMEM, s>>>(m_x, m_dh, m_dx, img, rec,
                                                                     reinterpret_cast<int*>(ws), T, D, L.dx_kb_per);
       if ((st = after_launch())) return st;
     } else {

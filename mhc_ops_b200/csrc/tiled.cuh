@@ -419,32 +419,40 @@ __global__ void __launch_bounds__(kGThreads, 1)
 // CTA = (128-token tile, range of 64-k blocks taken in stream-fastest order,
 // so the n blocks that read one dh_in box run back to back and the box is
 // read from DRAM once):
-//   * WG_E (4 warps, thread = token row) builds the tile's DHM image
-//     [128 tok x 3 segments] from the records once;
+//   * WG_E (4 warps, thread = token row) writes the tile's DHM [128 tok x 3
+//     segments] once into tensor memory (lane = token row, two bf16 per
+//     column): the A operand of every block's products, read by the tensor
+//     core without shared-memory traffic;
 //   * W0 streams per 64-k block the x and dh_in boxes (TMA, 128-B swizzle)
 //     and the block's split phi * gamma image (bulk copy from the image
-//     phimg_kernel leaves in the workspace) into a 2-stage ring;
-//   * W1 issues 6 x SEGW/16 tcgen05.mma (M = 128 tokens, N = 64 k, K = 16)
-//     per block into one of two TMEM accumulators;
+//     phimg_kernel leaves in the workspace) into an ST-deep ring;
+//   * W1 issues 6 x SEGW/16 tcgen05.mma (M = 128 tokens, N = 64 k, K = 16,
+//     A from tensor memory) per block into one of two TMEM accumulators;
 //   * WG_E reads the accumulator (TMEM lane = token row), adds -c x + h_pre
-//     dh_in and stores the row's 64 dx values (128 bytes) to global.
+//     dh_in, writes the 64 dx values of its row into a 128-B-swizzled
+//     staging box (two, alternating) and one thread stores the box with TMA
+//     (rows past T are clipped by the tensor map).
 template <int n>
 struct DxCfg {
   static constexpr int N_OUT = n * n + 2 * n;
   static constexpr int SEGW = (N_OUT + 15) / 16 * 16;
   static constexpr int KA = 3 * SEGW;                    // hi | mid | lo
   static constexpr int RG = (KA / 8) * 128;              // one 8-row group of a K-major interleaved image
-  static constexpr int DHM_BYTES = 16 * RG;              // 128 token rows
   static constexpr int PH_BYTES = 8 * RG;                // 64 k rows: split phi * gamma of one 64-k block
   static constexpr int BOX_BYTES = 128 * 128;            // one {64, 128} bf16 box
   static constexpr int STAGE_BYTES = 2 * BOX_BYTES + PH_BYTES;   // x, dh_in, phi image
-  static constexpr int ST = 2;
+  static constexpr int OUT_BUFS = 2;                     // dx staging boxes
+  static constexpr int ST_FIT = (232448 - 1024 - 256 - OUT_BUFS * BOX_BYTES) / STAGE_BYTES;
+  static constexpr int ST = ST_FIT < 4 ? ST_FIT : 4;
+  static constexpr int DHM_COL = 128;                    // TMEM: accumulators 0..127, DHM from here
+  static constexpr int TMEM_COLS = 256;
   static constexpr int RW = Dims<n>::RW;
-  static constexpr int SMEM = 1024 + ST * STAGE_BYTES + DHM_BYTES + 256;
+  static constexpr int SMEM = 1024 + ST * STAGE_BYTES + OUT_BUFS * BOX_BYTES + 256;
   static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 128-B swizzle atoms aligned");
+  static_assert(ST >= 2, "ring depth");
+  static_assert(DHM_COL + KA / 2 <= TMEM_COLS, "TMEM");
   static_assert(SMEM <= 232448, "shared memory");
 };
-
 
 // Split images of phi * gamma: block kb (64 k) -> img + kb * PH_BYTES, row kk
 // (= k - 64 kb), column e * SEGW + j = bf16 term e of phi[j][k] * gamma[k]
@@ -483,8 +491,8 @@ __global__ void __launch_bounds__(256) phimg_kernel(const float* __restrict__ ph
 template <int n>
 __global__ void __launch_bounds__(kGThreads, 1)
     dx_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_dh,
-                 const uint8_t* __restrict__ img, const float* __restrict__ rec, uint16_t* __restrict__ dx,
-                 int* status, int64_t T, int D, int kb_per) {
+                 const __grid_constant__ CUtensorMap map_dx, const uint8_t* __restrict__ img,
+                 const float* __restrict__ rec, int* status, int64_t T, int D, int kb_per) {
   using namespace sm100;
   using Cf = DxCfg<n>;
   constexpr int N_OUT = Cf::N_OUT;
@@ -493,8 +501,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
                 NBARS = 2 * ST + 5;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* dhm = stages + ST * Cf::STAGE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(dhm + Cf::DHM_BYTES);
+  uint8_t* outb = stages + ST * Cf::STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(outb + Cf::OUT_BUFS * Cf::BOX_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -523,12 +531,13 @@ __global__ void __launch_bounds__(kGThreads, 1)
     fence_mbarrier_init_cluster();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 128);
+    tmem_alloc(smem_u32(tmem_slot), Cf::TMEM_COLS);
     tmem_relinquish();
   }
   if (warp == 0 && lane == 0) {
     prefetch_tensormap(&map_x);
     prefetch_tensormap(&map_dh);
+    prefetch_tensormap(&map_dx);
   }
   tc_fence_before();
   __syncthreads();
@@ -558,7 +567,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16_f32(128, 64, false, false);
       mbar_wait(bar(DHM_FULL), 0, wc);
-      const uint64_t a_dv = bwdtc::desc_kmajor_interleave(smem_u32(dhm), 128, Cf::RG);
+      tc_fence_after();
+      const uint32_t a_t = tmem_base + Cf::DHM_COL;
       for (int b = 0; b < nkb; ++b) {
         const int s = b % ST, ab = b & 1;
         mbar_wait(bar(FULL + s), (b / ST) & 1, wc);
@@ -572,9 +582,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
         for (int pr = 0; pr < 6; ++pr) {
 #pragma unroll
           for (int ks = 0; ks < Cf::SEGW / 16; ++ks) {
-            const uint32_t ca = (bwdtc::prod_a_term(pr) * Cf::SEGW + ks * 16) * 16;
-            const uint32_t cb = (bwdtc::prod_b_term(pr) * Cf::SEGW + ks * 16) * 16;
-            umma_bf16(d, a_dv + (ca >> 4), b_dv + (cb >> 4), idesc, pr != 0 || ks != 0);
+            const uint32_t ca = (bwdtc::prod_a_term(pr) * Cf::SEGW + ks * 16) / 2;    // TMEM column
+            const uint32_t cb = (bwdtc::prod_b_term(pr) * Cf::SEGW + ks * 16) * 16;   // image bytes
+            umma_bf16_ta(d, a_t + ca, b_dv + (cb >> 4), idesc, pr != 0 || ks != 0);
           }
         }
         umma_commit(bar(EMPTY + s));
@@ -585,6 +595,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
     // ---------------------------------------------------------- WG_E: DHM once, dx per block
     const int q4 = warp & 3;
     const int row = 32 * q4 + lane;   // token row = TMEM lane
+    const bool issuer = threadIdx.x == 64;
+    const uint32_t lane_off = (uint32_t)(32 * q4) << 16;
     const int64_t t = (int64_t)tile * 128 + row;
     float c_t = 0.f, hp[n];
 #pragma unroll
@@ -601,21 +613,26 @@ __global__ void __launch_bounds__(kGThreads, 1)
 #pragma unroll
         for (int i = 0; i < n; ++i) hp[i] = __ldg(rp + N_OUT + 1 + i);
       }
+      // term e of dh_mix[j] at TMEM column DHM_COL + (e SEGW + j) / 2 (j even: low half)
 #pragma unroll
-      for (int kc = 0; kc < Cf::KA / 8; ++kc) {
-        const int e = (kc * 8) / Cf::SEGW, j0 = kc * 8 - e * Cf::SEGW;
-        uint32_t w[4];
+      for (int e = 0; e < 3; ++e) {
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          const uint32_t lo = bwdtc::split_term(r[j0 + 2 * h], e);
-          const uint32_t hi = bwdtc::split_term(r[j0 + 2 * h + 1], e);
-          w[h] = lo | (hi << 16);
+        for (int c = 0; c < Cf::SEGW / 16; ++c) {
+          uint32_t w[8];
+#pragma unroll
+          for (int h = 0; h < 8; ++h) {
+            const uint32_t lo = bwdtc::split_term(r[16 * c + 2 * h], e);
+            const uint32_t hi = bwdtc::split_term(r[16 * c + 2 * h + 1], e);
+            w[h] = lo | (hi << 16);
+          }
+          tmem_st8(tmem_base + lane_off + Cf::DHM_COL + e * (Cf::SEGW / 2) + 8 * c, w);
         }
-        *reinterpret_cast<uint4*>(dhm + bwdtc::interleave_off(row, kc * 8, Cf::RG)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      fence_proxy_async_smem();
+      tmem_wait_st();
+      tc_fence_before();
       mbar_arrive(bar(DHM_FULL));
     }
+    const uint64_t pol_out = l2_policy_evict_first();
     for (int b = 0; b < nkb; ++b) {
       const int s = b % ST, ab = b & 1;
       const int k0 = kb_of(kb0 + b) * 64;
@@ -630,8 +647,12 @@ __global__ void __launch_bounds__(kGThreads, 1)
       const uint8_t* st = stages + s * Cf::STAGE_BYTES;
       const uint32_t x_row = smem_u32(st) + row * 128;
       const uint32_t g_row = smem_u32(st + Cf::BOX_BYTES) + row * 128;
-      const uint32_t ta = tmem_base + ab * 64 + ((uint32_t)(32 * q4) << 16);
-      uint4 outv[8];
+      const uint32_t o_buf = smem_u32(outb + ab * Cf::BOX_BYTES);
+      const uint32_t o_row = o_buf + row * 128;
+      // staging box ab is free once the store issued two blocks ago has read it
+      if (issuer) bwdtc::bulk_wait_read1();
+      named_sync(1, 128);
+      const uint32_t ta = tmem_base + ab * 64 + lane_off;
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         float v0[16], v1[16];
@@ -641,9 +662,10 @@ __global__ void __launch_bounds__(kGThreads, 1)
 #pragma unroll
         for (int hc = 0; hc < 4; ++hc) {
           const int c = hf * 4 + hc;   // 16-byte chunk of the 128-byte row
+          const uint32_t sw = (uint32_t)((c ^ (row & 7)) << 4);
           float xf[8], gf[8];
-          bwdtc::bf16x8_to_f32(bwdtc::lds128(x_row + ((c ^ (row & 7)) << 4)), xf);
-          bwdtc::bf16x8_to_f32(bwdtc::lds128(g_row + ((c ^ (row & 7)) << 4)), gf);
+          bwdtc::bf16x8_to_f32(bwdtc::lds128(x_row + sw), xf);
+          bwdtc::bf16x8_to_f32(bwdtc::lds128(g_row + sw), gf);
           uint32_t o[4];
 #pragma unroll
           for (int e = 0; e < 8; e += 2) {
@@ -653,7 +675,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
             const float d1 = a1 + ((-c_t) * xf[e + 1] + hpi * gf[e + 1]);
             o[e / 2] = pack_bf16x2(d0, d1);
           }
-          outv[c] = make_uint4(o[0], o[1], o[2], o[3]);
+          bwdtc::sts128(o_row + sw, make_uint4(o[0], o[1], o[2], o[3]));
         }
       }
       tc_fence_before();
@@ -662,19 +684,21 @@ __global__ void __launch_bounds__(kGThreads, 1)
         mbar_arrive(bar(ACC_EMPTY + ab));
         mbar_arrive(bar(EMPTY + s));
       }
-      if (t < T && !*abort_flag) {
-        uint4* dst = reinterpret_cast<uint4*>(dx + t * nD + k0);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) dst[c] = outv[c];
+      fence_proxy_async_smem();
+      named_sync(1, 128);
+      if (issuer && !*abort_flag) {
+        bwdtc::tma_store_2d(&map_dx, o_buf, k0, tile * 128, pol_out);
+        bwdtc::bulk_commit();
       }
     }
+    if (issuer) bwdtc::bulk_wait_all0();   // the dx stores have completed
   }
 
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 128);
+    tmem_dealloc(tmem_base, Cf::TMEM_COLS);
   }
 }
 
