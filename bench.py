@@ -222,8 +222,10 @@ def run_ours(args):
     from mhc_ops_b200 import _lib, mhc_backward_manual, mhc_forward_pre
     from mhc_ops_b200.backward import param_grad_numel
 
-    w = dict(WORKLOAD, B=args.batch)
+    w = dict(WORKLOAD, B=args.batch, S=args.seq, n=args.streams, D=args.hidden)
     B, S, n, D = w["B"], w["S"], w["n"], w["D"]
+    shape = f"B={B},S={S},n={n},D={D}"
+    headline = dict(w, B=WORKLOAD["B"]) == WORKLOAD   # the metric's shape (B may shrink for profiling)
     N, nD, T = n * n + 2 * n, n * D, w["B"] * w["S"]
 
     # parameters: identical on every rank; token data: per-rank seeds
@@ -347,7 +349,7 @@ def run_ours(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, cores, _ = cpu_oracle_rate(args.cpu_tokens, n, D, steps=1)
         cpu = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
-               "sample": f"{args.cpu_tokens} tokens of the B=4,S=4096,n=4,D=4096 workload, numpy restatement of "
+               "sample": f"{args.cpu_tokens} tokens of the {shape} workload, numpy restatement of "
                          f"the reference golden fwd(outflag)+bwd, {cores} spawn workers; CPU {cpu_model()}"}
 
     if world > 1:
@@ -365,14 +367,16 @@ def run_ours(args):
     step_alg = fwd_alg + bwd_alg
     dom = ("mhc_bwd", bwd_alg, bwd_ms) if bwd_ms >= fwd_ms else ("mhc_fwd", fwd_alg, fwd_ms)
     achieved = dom[1] / (dom[2] / 1e3) / 1e9
-    traffic = load_profile_traffic(dom[0])
+    traffic = load_profile_traffic(dom[0]) if headline and B == WORKLOAD["B"] else None
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"mHC pre-op fwd(outflag)+bwd, B={B},S=4096,n=4,D=4096 per GPU (LLM-scale config)",
+        "config": {"workload": f"mHC pre-op fwd(outflag)+bwd, {shape} per GPU"
+                               + (" (LLM-scale config)" if headline else ""),
                    **w, "global_tokens": world * T, "parallelism": f"dp{world} (token shards, NCCL all-reduce of "
-                   "param grads)", "l2": "inputs larger than L2 (x is 512 MiB per GPU); no flush",
+                   "param grads)",
+                   "l2": f"inputs larger than L2 (x is {T * nD * 2 / 2**20:.0f} MiB per GPU); no flush",
                    "launch_plan": plans},
         "hbm_gbs_step": step_alg / (ms_per_step / 1e3) / 1e9 / 1.0,
         "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -411,7 +415,10 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--ref-tokens", type=int, default=1024)
     ap.add_argument("--batch", type=int, default=WORKLOAD["B"],
-                    help="B per GPU (default 4, the metric's configuration; smaller only for profiling)")
+                    help="B per GPU (default 4, the metric's configuration; others only for profiling)")
+    ap.add_argument("--seq", type=int, default=WORKLOAD["S"], help="S (default 4096; others only for profiling)")
+    ap.add_argument("--streams", type=int, default=WORKLOAD["n"], help="n (default 4; others only for profiling)")
+    ap.add_argument("--hidden", type=int, default=WORKLOAD["D"], help="D (default 4096; others only for profiling)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)   # at least 3 untimed warm-up steps, whatever was asked
     if args.impl == "reference":
