@@ -563,8 +563,9 @@ int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s, int sms) {
 struct BwdTiledLayout {
   size_t rec, abpart, gpart, gimg, dmT, phimg, total;
   bool dx_tc;            // dx on the tensor cores (D % 64 == 0), else dx_kernel
-  int dx_slices;         // dx_tc_kernel: k-block ranges per token tile
-  int dx_kb_per;         // 64-k blocks per range
+  bool dx_pair;          // even n: dx_tc_pair_kernel (pairs of 64-k blocks), else dx_tc_kernel
+  int dx_slices;         // unit ranges per token tile
+  int dx_kb_per;         // units (64-k blocks, or pairs) per range
   int P;                 // token groups of the G partials (g_tc_kernel's grid.y)
   int rows_grid;
 };
@@ -632,19 +633,22 @@ BwdTiledLayout bwd_tiled_layout(int64_t T, int n, int D, int sms) {
   off = align_up(off + (size_t)tiles * bwd_tiled_gimg_bytes(n), kWsAlign);
   L.dx_tc = D % 64 == 0;
   if (L.dx_tc) {
-    // k-block ranges per tile with the least per-CTA work, waves * blocks per range
+    // ranges of work units (64-k blocks; pairs of them for even n) per tile
+    // with the least per-CTA work, waves * units per range
     const int64_t KB = nD / 64;
+    L.dx_pair = n % 2 == 0;
+    const int64_t units = L.dx_pair ? KB / 2 : KB;
     int64_t best_s = 1;
     double best_c = 0.0;
-    for (int64_t sl = 1; sl <= std::min<int64_t>(KB, 64); ++sl) {
-      const double c = (double)((tiles * sl + sms - 1) / sms) * (double)((KB + sl - 1) / sl);
+    for (int64_t sl = 1; sl <= std::min<int64_t>(units, 64); ++sl) {
+      const double c = (double)((tiles * sl + sms - 1) / sms) * (double)((units + sl - 1) / sl);
       if (sl == 1 || c < best_c - 1e-9) {
         best_s = sl;
         best_c = c;
       }
     }
     L.dx_slices = (int)best_s;
-    L.dx_kb_per = (int)((KB + best_s - 1) / best_s);
+    L.dx_kb_per = (int)((units + best_s - 1) / best_s);
     L.phimg = off;
     off = align_up(off + (size_t)KB * bwd_tiled_phimg_bytes(n), kWsAlign);
   } else {
@@ -710,10 +714,17 @@ struct BwdTiled {
         const uint32_t box[2] = {64, 128};
         if ((st = encode_bf16_map(&m_dx, a->dx, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
       }
-      if ((st = set_smem_limit_once(tiled::dx_tc_kernel<n>, Dc::SMEM))) return st;
       const dim3 gdx((unsigned)((T + 127) / 128), (unsigned)L.dx_slices);
-      tiled::dx_tc_kernel<n><<<gdx, tiled::kGThreads, Dc::SMEM, s>>>(m_x, m_dh, m_dx, img, rec,
-                                                                    reinterpret_cast<int*>(ws), T, D, L.dx_kb_per);
+      if constexpr (n % 2 == 0) {
+        using Dp = tiled::DxPairCfg<n>;
+        if ((st = set_smem_limit_once(tiled::dx_tc_pair_kernel<n>, Dp::SMEM))) return st;
+        tiled::dx_tc_pair_kernel<n><<<gdx, tiled::kGThreads, Dp::SMEM, s>>>(
+            m_x, m_dh, m_dx, img, rec, reinterpret_cast<int*>(ws), T, D, L.dx_kb_per);
+      } else {
+        if ((st = set_smem_limit_once(tiled::dx_tc_kernel<n>, Dc::SMEM))) return st;
+        tiled::dx_tc_kernel<n><<<gdx, tiled::kGThreads, Dc::SMEM, s>>>(m_x, m_dh, m_dx, img, rec,
+                                                                      reinterpret_cast<int*>(ws), T, D, L.dx_kb_per);
+      }
       if ((st = after_launch())) return st;
     } else {
       float* dmT = reinterpret_cast<float*>(ws + L.dmT);

@@ -702,5 +702,255 @@ __global__ void __launch_bounds__(kGThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------ dx on the tensor cores, stream pairs
+// For even n: the same products as dx_tc_kernel, but a unit of work is a pair
+// of 64-k blocks of streams i and i + 1 over the same d-range (consecutive in
+// the stream-fastest order), so both share one dh_in box and their two split
+// phi * gamma images stack into one 128-row B operand: 6 x SEGW/16
+// tcgen05.mma of N = 128 per pair, half the issues of two N = 64 chains (an
+// MMA costs about the same to issue at N = 64 and N = 128).  A stage holds the
+// pair's two x boxes, its dh_in box and its two images; the epilogue writes dx
+// over the x boxes it has read (each thread its own row) and one thread
+// stores them with TMA, then releases the stage once the store has read it.
+template <int n>
+struct DxPairCfg {
+  static constexpr int N_OUT = n * n + 2 * n;
+  static constexpr int SEGW = (N_OUT + 15) / 16 * 16;
+  static constexpr int KA = 3 * SEGW;
+  static constexpr int RG = (KA / 8) * 128;
+  static constexpr int PH_BYTES = 8 * RG;                // one 64-k block's image
+  static constexpr int BOX_BYTES = 128 * 128;
+  static constexpr int STAGE_BYTES = 3 * BOX_BYTES + 2 * PH_BYTES;   // x0, x1, dh_in, image0 | image1
+  static constexpr int ST_FIT = (232448 - 1024 - 256) / STAGE_BYTES;
+  static constexpr int ST = ST_FIT < 4 ? ST_FIT : 4;
+  static constexpr int DHM_COL = 256;                    // TMEM: accumulators 0..255, DHM from here
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int RW = Dims<n>::RW;
+  static constexpr int SMEM = 1024 + ST * STAGE_BYTES + 256;
+  static_assert(n % 2 == 0, "pairs of streams");
+  static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 128-B swizzle atoms aligned");
+  static_assert(ST >= 2, "ring depth");
+  static_assert(DHM_COL + KA / 2 <= TMEM_COLS, "TMEM");
+  static_assert(SMEM <= 232448, "shared memory");
+};
+
+// grid = (tiles, slices); CTA (tile, y) takes the pairs [y * kp_per, ...) of
+// the nD / 128 pairs; pair p = blocks q = 2p, 2p + 1 of the stream-fastest
+// order (block (q % n) * D/64 + q / n).
+template <int n>
+__global__ void __launch_bounds__(kGThreads, 1)
+    dx_tc_pair_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_dh,
+                      const __grid_constant__ CUtensorMap map_dx, const uint8_t* __restrict__ img,
+                      const float* __restrict__ rec, int* status, int64_t T, int D, int kp_per) {
+  using namespace sm100;
+  using Cf = DxPairCfg<n>;
+  constexpr int N_OUT = Cf::N_OUT;
+  constexpr int ST = Cf::ST;
+  constexpr int FULL = 0, EMPTY = ST, ACC_FULL = 2 * ST, ACC_EMPTY = 2 * ST + 2, DHM_FULL = 2 * ST + 4,
+                NBARS = 2 * ST + 5;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(stages + ST * Cf::STAGE_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  const int nD = n * D;
+  const int KP = nD / 128;
+  const int tile = blockIdx.x;
+  const int p0 = blockIdx.y * kp_per;
+  const int npairs = max(0, min(kp_per, KP - p0));
+  const int DB = D / 64;
+  auto kb_of = [&](int q) { return (q % n) * DB + q / n; };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ST; ++i) {
+      mbar_init(bar(FULL + i), 1);
+      mbar_init(bar(EMPTY + i), 2);   // MMA commit + the store issuer once its stores have read the stage
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(ACC_FULL + i), 1);
+      mbar_init(bar(ACC_EMPTY + i), 4);
+    }
+    mbar_init(bar(DHM_FULL), 128);
+    *abort_flag = 0;
+    fence_mbarrier_init_cluster();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), Cf::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&map_x);
+    prefetch_tensormap(&map_dh);
+    prefetch_tensormap(&map_dx);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const WaitCtx wc{abort_flag, status};
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- W0: x pair, dh_in, phi image pair
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      for (int b = 0; b < npairs; ++b) {
+        const int s = b % ST;
+        const int q = 2 * (p0 + b);
+        const int kb0 = kb_of(q), kb1 = kb_of(q + 1);
+        mbar_wait(bar(EMPTY + s), ((b / ST) & 1) ^ 1, wc);
+        if (*abort_flag) continue;
+        const uint32_t st = smem_u32(stages + s * Cf::STAGE_BYTES);
+        mbar_arrive_expect_tx(bar(FULL + s), Cf::STAGE_BYTES);
+        tma_load_2d(st, &map_x, bar(FULL + s), kb0 * 64, tile * 128, pol);
+        tma_load_2d(st + Cf::BOX_BYTES, &map_x, bar(FULL + s), kb1 * 64, tile * 128, pol);
+        tma_load_2d(st + 2 * Cf::BOX_BYTES, &map_dh, bar(FULL + s), (kb0 * 64) % D, tile * 128, pol);
+        bulk_g2s(st + 3 * Cf::BOX_BYTES, img + (size_t)kb0 * Cf::PH_BYTES, Cf::PH_BYTES, bar(FULL + s));
+        bulk_g2s(st + 3 * Cf::BOX_BYTES + Cf::PH_BYTES, img + (size_t)kb1 * Cf::PH_BYTES, Cf::PH_BYTES,
+                 bar(FULL + s));
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- W1: MMA
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(128, 128, false, false);
+      mbar_wait(bar(DHM_FULL), 0, wc);
+      tc_fence_after();
+      const uint32_t a_t = tmem_base + Cf::DHM_COL;
+      for (int b = 0; b < npairs; ++b) {
+        const int s = b % ST, ab = b & 1;
+        mbar_wait(bar(FULL + s), (b / ST) & 1, wc);
+        mbar_wait(bar(ACC_EMPTY + ab), ((b >> 1) & 1) ^ 1, wc);
+        tc_fence_after();
+        if (*abort_flag) continue;
+        // the two images stack into one 128-row K-major interleaved operand
+        const uint64_t b_dv = bwdtc::desc_kmajor_interleave(
+            smem_u32(stages + s * Cf::STAGE_BYTES + 3 * Cf::BOX_BYTES), 128, Cf::RG);
+        const uint32_t d = tmem_base + ab * 128;
+#pragma unroll
+        for (int pr = 0; pr < 6; ++pr) {
+#pragma unroll
+          for (int ks = 0; ks < Cf::SEGW / 16; ++ks) {
+            const uint32_t ca = (bwdtc::prod_a_term(pr) * Cf::SEGW + ks * 16) / 2;    // TMEM column
+            const uint32_t cb = (bwdtc::prod_b_term(pr) * Cf::SEGW + ks * 16) * 16;   // image bytes
+            umma_bf16_ta(d, a_t + ca, b_dv + (cb >> 4), idesc, pr != 0 || ks != 0);
+          }
+        }
+        umma_commit(bar(EMPTY + s));
+        umma_commit(bar(ACC_FULL + ab));
+      }
+    }
+  } else {
+    // ---------------------------------------------------------- WG_E: DHM once, dx per pair
+    const int q4 = warp & 3;
+    const int row = 32 * q4 + lane;   // token row = TMEM lane
+    const bool issuer = threadIdx.x == 64;
+    const uint32_t lane_off = (uint32_t)(32 * q4) << 16;
+    const int64_t t = (int64_t)tile * 128 + row;
+    float c_t = 0.f, hp[n];
+#pragma unroll
+    for (int i = 0; i < n; ++i) hp[i] = 0.f;
+    {
+      float r[Cf::SEGW];
+#pragma unroll
+      for (int c = 0; c < Cf::SEGW; ++c) r[c] = 0.f;
+      if (t < T) {
+        const float* rp = rec + t * Cf::RW;
+#pragma unroll
+        for (int c = 0; c < N_OUT; ++c) r[c] = __ldg(rp + c);
+        c_t = __ldg(rp + N_OUT);
+#pragma unroll
+        for (int i = 0; i < n; ++i) hp[i] = __ldg(rp + N_OUT + 1 + i);
+      }
+      // term e of dh_mix[j] at TMEM column DHM_COL + (e SEGW + j) / 2 (j even: low half)
+#pragma unroll
+      for (int e = 0; e < 3; ++e) {
+#pragma unroll
+        for (int c = 0; c < Cf::SEGW / 16; ++c) {
+          uint32_t w[8];
+#pragma unroll
+          for (int h = 0; h < 8; ++h) {
+            const uint32_t lo = bwdtc::split_term(r[16 * c + 2 * h], e);
+            const uint32_t hi = bwdtc::split_term(r[16 * c + 2 * h + 1], e);
+            w[h] = lo | (hi << 16);
+          }
+          tmem_st8(tmem_base + lane_off + Cf::DHM_COL + e * (Cf::SEGW / 2) + 8 * c, w);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(DHM_FULL));
+    }
+    const uint64_t pol_out = l2_policy_evict_first();
+    for (int b = 0; b < npairs; ++b) {
+      const int s = b % ST, ab = b & 1;
+      const int q = 2 * (p0 + b);
+      mbar_wait(bar(ACC_FULL + ab), (b >> 1) & 1, wc);
+      mbar_wait(bar(FULL + s), (b / ST) & 1, wc);   // the stage's boxes (already complete)
+      tc_fence_after();
+      const uint32_t st = smem_u32(stages + s * Cf::STAGE_BYTES);
+      const uint32_t g_row = st + 2 * Cf::BOX_BYTES + row * 128;
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        const int i = (q + h) % n;   // stream of block h
+        float hpi = hp[0];
+#pragma unroll
+        for (int ii = 1; ii < n; ++ii)
+          if (i == ii) hpi = hp[ii];
+        const uint32_t x_row = st + h * Cf::BOX_BYTES + row * 128;   // dx overwrites it in place
+        const uint32_t ta = tmem_base + ab * 128 + h * 64 + lane_off;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          float v0[16], v1[16];
+          tmem_ld16(ta + hf * 32, v0);
+          tmem_ld16(ta + hf * 32 + 16, v1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int hc = 0; hc < 4; ++hc) {
+            const int c = hf * 4 + hc;   // 16-byte chunk of the 128-byte row
+            const uint32_t sw = (uint32_t)((c ^ (row & 7)) << 4);
+            float xf[8], gf[8];
+            bwdtc::bf16x8_to_f32(bwdtc::lds128(x_row + sw), xf);
+            bwdtc::bf16x8_to_f32(bwdtc::lds128(g_row + sw), gf);
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+              const float a0 = (hc < 2 ? v0[(hc * 8 + e) & 15] : v1[(hc * 8 + e) & 15]);
+              const float a1 = (hc < 2 ? v0[(hc * 8 + e + 1) & 15] : v1[(hc * 8 + e + 1) & 15]);
+              const float d0 = a0 + ((-c_t) * xf[e] + hpi * gf[e]);
+              const float d1 = a1 + ((-c_t) * xf[e + 1] + hpi * gf[e + 1]);
+              o[e / 2] = pack_bf16x2(d0, d1);
+            }
+            bwdtc::sts128(x_row + sw, make_uint4(o[0], o[1], o[2], o[3]));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(ACC_EMPTY + ab));
+      fence_proxy_async_smem();
+      named_sync(1, 128);
+      if (issuer) {
+        if (!*abort_flag) {
+          bwdtc::tma_store_2d(&map_dx, st, kb_of(q) * 64, tile * 128, pol_out);
+          bwdtc::tma_store_2d(&map_dx, st + Cf::BOX_BYTES, kb_of(q + 1) * 64, tile * 128, pol_out);
+          bwdtc::bulk_commit();
+          bwdtc::bulk_wait_read0();   // the stores have read the stage
+        }
+        mbar_arrive(bar(EMPTY + s));
+      }
+    }
+    if (issuer) bwdtc::bulk_wait_all0();   // the dx stores have completed
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cf::TMEM_COLS);
+  }
+}
+
 }  // namespace tiled
 }  // namespace mhc

@@ -84,6 +84,8 @@ def test_readme_backward_shapes_vs_oracle(B, S, D):
     (1, 50, 3, 24, True),        # odd n
     (1, 300, 8, 1024, False),    # n=8 tiled backward, ragged token tiles, gamma=None
     (1, 70, 6, 512, True),       # n=6 tiled backward
+    (1, 200, 5, 256, True),      # odd n on the tensor cores: dx one 64-k block at a time
+    (1, 140, 2, 128, False),     # n=2: dx in stream pairs, one pair per d-block
 ])
 def test_wide_rows_vs_oracle(B, S, n, D, gamma):
     _live_case(B, S, n, D, seed=12, gamma=gamma)
