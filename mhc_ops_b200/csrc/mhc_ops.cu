@@ -718,7 +718,7 @@ struct BwdTiled {
       if constexpr (n % 2 == 0) {
         using Dp = tiled::DxPairCfg<n>;
         if ((st = set_smem_limit_once(tiled::dx_tc_pair_kernel<n>, Dp::SMEM))) return st;
-        tiled::dx_tc_pair_kernel<n><<<gdx, tiled::kGThreads, Dp::SMEM, s>>>(
+        tiled::dx_tc_pair_kernel<n><<<gdx, tiled::kPThreads, Dp::SMEM, s>>>(
             m_x, m_dh, m_dx, img, rec, reinterpret_cast<int*>(ws), T, D, L.dx_kb_per);
       } else {
         if ((st = set_smem_limit_once(tiled::dx_tc_kernel<n>, Dc::SMEM))) return st;

@@ -709,9 +709,10 @@ __global__ void __launch_bounds__(kGThreads, 1)
 // phi * gamma images stack into one 128-row B operand: 6 x SEGW/16
 // tcgen05.mma of N = 128 per pair, half the issues of two N = 64 chains (an
 // MMA costs about the same to issue at N = 64 and N = 128).  A stage holds the
-// pair's two x boxes, its dh_in box and its two images; the epilogue writes dx
-// over the x boxes it has read (each thread its own row) and one thread
-// stores them with TMA, then releases the stage once the store has read it.
+// pair's two x boxes, its dh_in box and its two images; the epilogue (two
+// groups of four warps, group h on block h of the pair) writes dx over the x
+// boxes it has read (each thread its own row), and one thread TMA-stores them
+// and releases the stage once the stores have read it.
 template <int n>
 struct DxPairCfg {
   static constexpr int N_OUT = n * n + 2 * n;
@@ -734,11 +735,13 @@ struct DxPairCfg {
   static_assert(SMEM <= 232448, "shared memory");
 };
 
+constexpr int kPThreads = 10 * 32;   // W0, W1, WG_E(8)
+
 // grid = (tiles, slices); CTA (tile, y) takes the pairs [y * kp_per, ...) of
 // the nD / 128 pairs; pair p = blocks q = 2p, 2p + 1 of the stream-fastest
 // order (block (q % n) * D/64 + q / n).
 template <int n>
-__global__ void __launch_bounds__(kGThreads, 1)
+__global__ void __launch_bounds__(kPThreads, 1)
     dx_tc_pair_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_dh,
                       const __grid_constant__ CUtensorMap map_dx, const uint8_t* __restrict__ img,
                       const float* __restrict__ rec, int* status, int64_t T, int D, int kp_per) {
@@ -770,9 +773,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(ACC_FULL + i), 1);
-      mbar_init(bar(ACC_EMPTY + i), 4);
+      mbar_init(bar(ACC_EMPTY + i), 8);   // the 8 epilogue warps
     }
-    mbar_init(bar(DHM_FULL), 128);
+    mbar_init(bar(DHM_FULL), 256);
     *abort_flag = 0;
     fence_mbarrier_init_cluster();
   }
@@ -843,7 +846,11 @@ __global__ void __launch_bounds__(kGThreads, 1)
     }
   } else {
     // ---------------------------------------------------------- WG_E: DHM once, dx per pair
+    // two groups of four warps (one per TMEM lane quadrant each); group h
+    // takes block h of every pair, so two warps per scheduler hide each
+    // other's TMEM / shared-memory latency
     const int q4 = warp & 3;
+    const int grp = (warp - 2) >> 2;
     const int row = 32 * q4 + lane;   // token row = TMEM lane
     const bool issuer = threadIdx.x == 64;
     const uint32_t lane_off = (uint32_t)(32 * q4) << 16;
@@ -864,8 +871,10 @@ __global__ void __launch_bounds__(kGThreads, 1)
         for (int i = 0; i < n; ++i) hp[i] = __ldg(rp + N_OUT + 1 + i);
       }
       // term e of dh_mix[j] at TMEM column DHM_COL + (e SEGW + j) / 2 (j even: low half)
+      // group 0 writes terms 0 and 2, group 1 term 1
 #pragma unroll
       for (int e = 0; e < 3; ++e) {
+        if ((e & 1) != grp) continue;
 #pragma unroll
         for (int c = 0; c < Cf::SEGW / 16; ++c) {
           uint32_t w[8];
@@ -891,8 +900,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
       tc_fence_after();
       const uint32_t st = smem_u32(stages + s * Cf::STAGE_BYTES);
       const uint32_t g_row = st + 2 * Cf::BOX_BYTES + row * 128;
-#pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
+      {
+        const int h = grp;
         const int i = (q + h) % n;   // stream of block h
         float hpi = hp[0];
 #pragma unroll
@@ -930,7 +939,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(ACC_EMPTY + ab));
       fence_proxy_async_smem();
-      named_sync(1, 128);
+      named_sync(1, 256);
       if (issuer) {
         if (!*abort_flag) {
           bwdtc::tma_store_2d(&map_dx, st, kb_of(q) * 64, tile * 128, pol_out);
