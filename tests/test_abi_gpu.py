@@ -71,7 +71,7 @@ def test_abi_rejects_bad_arguments():
     (0, 16384, 8, 4096, "tensor-core"),         # n = 8: projection + row kernel
     (0, 1000, 6, 512, "generic"),
     (1, 16384, 4, 4096, "tensor-core"),
-    (1, 16384, 8, 4096, "tiled"),               # n = 8 backward on the CUDA cores
+    (1, 16384, 8, 4096, "tiled"),               # n = 8 backward: the n != 4 tcgen05 kernels
     (1, 100, 4, 36, "generic"),                 # D not a multiple of 8
 ])
 def test_launch_plan_routes_each_shape(which, T, n, D, path):
