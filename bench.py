@@ -345,6 +345,8 @@ def run_ours(args):
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "path": "mhc_forward_pre + mhc_backward_manual (public API, C ABI), pinned host buffers"}
 
+    post = post_op_timing(x, dh_in, dev, n, D, T) if rank == 0 and not args.no_post else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, cores, _ = cpu_oracle_rate(args.cpu_tokens, n, D, steps=1)
@@ -385,6 +387,7 @@ def run_ours(args):
                      "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
                      "fwd_frac": fwd_alg / (fwd_ms / 1e3) / 1e9 / peak,
                      "bwd_frac": bwd_alg / (bwd_ms / 1e3) / 1e9 / peak},
+        "post_op": post,
         "gpu_launches": int(launches),
         "clocks": clk,
         "e2e": e2e,
@@ -392,6 +395,44 @@ def run_ours(args):
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def post_op_timing(x, y, dev, n, D, T, reps=10):
+    """The post-op (x_next = h_res x + h_post y, and its backward) on the same
+    streams, timed per call with CUDA events (median of `reps` after 3 warm-up
+    calls); y stands in for the sublayer output f(h_in).  Reported beside the
+    pre-op numbers, outside the timed region of the headline metric."""
+    import torch
+
+    from mhc_ops_b200 import mhc_post, mhc_post_backward
+
+    g = torch.Generator(device=dev).manual_seed(7)
+    h_res = torch.randn(*x.shape[:2], n, n, generator=g, device=dev) * 0.5
+    h_post = torch.rand(*x.shape[:2], n, generator=g, device=dev) * 2.0
+    dout = torch.randn(x.shape, generator=g, device=dev, dtype=torch.bfloat16)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        for a, b in evs:
+            a.record()
+            fn()
+            b.record()
+        torch.cuda.synchronize()
+        return statistics.median(a.elapsed_time(b) for a, b in evs)
+
+    fwd_ms = timed(lambda: mhc_post(x, h_res, h_post, y))
+    bwd_ms = timed(lambda: mhc_post_backward(x, h_res, h_post, y, dout))
+    peak, kind = measured_hbm_peak()
+    coef = 4 * n * n + 4 * n
+    fwd_b = T * (2 * n * D + 2 * D + coef + 2 * n * D)
+    bwd_b = T * (2 * n * D + 2 * n * D + 2 * D + coef + 2 * n * D + 2 * D + coef)
+    return {"fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "algorithmic_bytes": {"fwd": fwd_b, "bwd": bwd_b},
+            "fwd_gbs": fwd_b / fwd_ms / 1e6, "bwd_gbs": bwd_b / bwd_ms / 1e6,
+            "fwd_frac": fwd_b / fwd_ms / 1e6 / peak, "bwd_frac": bwd_b / bwd_ms / 1e6 / peak,
+            "peak_gbs": peak, "peak_source": kind,
+            "what": "x_next = h_res x + h_post y (mhc_post) and its backward, per call, same shape"}
 
 
 def load_profile_traffic(kernel_call: str):
@@ -412,6 +453,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-post", action="store_true", help="skip the post-op timing")
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--ref-tokens", type=int, default=1024)
     ap.add_argument("--batch", type=int, default=WORKLOAD["B"],

@@ -197,6 +197,50 @@ MHC_API int mhc_selftest_wait_expiry(void* workspace, void* stream);
 MHC_API int mhc_query_plan(int which, int64_t tokens, int32_t n, int32_t D, int* path, int* cluster_size,
                            int* clusters);
 
+/* ---------------------------------------------------------------- post-op
+ * The mHC post-op, the consumer of h_post and h_res: the next residual
+ * stream of the hyper-connection block,
+ *   out[t,i,:] = sum_j h_res[t,i,j] x[t,j,:] + h_post[t,i] y[t,:],
+ * y = f(h_in) [T,D] bf16 the sublayer's output.  No counterpart in the
+ * reference, which stops at h_post / h_res (src/forward/golden.py:65-69).
+ * Shapes as above (1 <= n <= 8, D >= 1, T >= 0); no workspace.  The bf16
+ * outputs are sums in ascending term order with each multiply and add
+ * rounded on its own, then one round-to-nearest-even to bf16.  16-byte
+ * aligned bf16 pointers with D a multiple of 8 take the vector kernels. */
+typedef struct mhc_post_fwd_args {
+  const uint16_t* x;       /* [T,n,D] bf16 */
+  const float* h_res;      /* [T,n,n] */
+  const float* h_post;     /* [T,n] */
+  const uint16_t* y;       /* [T,D] bf16 */
+  uint16_t* out;           /* [T,n,D] bf16 */
+  int64_t tokens;
+  int32_t n;
+  int32_t D;
+} mhc_post_fwd_args;
+
+/* Backward of the post-op from dout [T,n,D] bf16:
+ *   dx[t,j,:] = sum_i h_res[t,i,j] dout[t,i,:] (bf16), dy[t,:] = sum_i
+ *   h_post[t,i] dout[t,i,:] (bf16), dh_res[t,i,j] = sum_d dout[t,i,d]
+ *   x[t,j,d], dh_post[t,i] = sum_d dout[t,i,d] y[t,d] (fp32, summed in a
+ *   fixed order, so repeated calls return identical bytes). */
+typedef struct mhc_post_bwd_args {
+  const uint16_t* x;
+  const float* h_res;
+  const float* h_post;
+  const uint16_t* y;
+  const uint16_t* dout;    /* [T,n,D] bf16 */
+  uint16_t* dx;            /* [T,n,D] bf16 */
+  uint16_t* dy;            /* [T,D] bf16 */
+  float* dh_res;           /* [T,n,n] */
+  float* dh_post;          /* [T,n] */
+  int64_t tokens;
+  int32_t n;
+  int32_t D;
+} mhc_post_bwd_args;
+
+MHC_API int mhc_post_fwd(const mhc_post_fwd_args* args, void* stream);
+MHC_API int mhc_post_bwd(const mhc_post_bwd_args* args, void* stream);
+
 /* Number of kernels this library has launched in this process (all devices,
  * all threads).  No counterpart in the reference; used to report launches. */
 MHC_API uint64_t mhc_launch_count(void);

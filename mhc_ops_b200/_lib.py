@@ -46,6 +46,23 @@ class BwdArgs(ctypes.Structure):
     ]
 
 
+class PostFwdArgs(ctypes.Structure):
+    """Mirror of ``mhc_post_fwd_args`` (include/mhc_ops.h)."""
+    _fields_ = [
+        ("x", _c_void_p), ("h_res", _c_void_p), ("h_post", _c_void_p), ("y", _c_void_p), ("out", _c_void_p),
+        ("tokens", ctypes.c_int64), ("n", ctypes.c_int32), ("D", ctypes.c_int32),
+    ]
+
+
+class PostBwdArgs(ctypes.Structure):
+    """Mirror of ``mhc_post_bwd_args`` (include/mhc_ops.h)."""
+    _fields_ = [
+        ("x", _c_void_p), ("h_res", _c_void_p), ("h_post", _c_void_p), ("y", _c_void_p), ("dout", _c_void_p),
+        ("dx", _c_void_p), ("dy", _c_void_p), ("dh_res", _c_void_p), ("dh_post", _c_void_p),
+        ("tokens", ctypes.c_int64), ("n", ctypes.c_int32), ("D", ctypes.c_int32),
+    ]
+
+
 # Every symbol include/mhc_ops.h declares, with its ctypes signature.
 SIGNATURES = {
     "mhc_status_string": (ctypes.c_char_p, [ctypes.c_int]),
@@ -62,6 +79,8 @@ SIGNATURES = {
     "mhc_query_plan": (ctypes.c_int, [ctypes.c_int, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
                                       ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
                                       ctypes.POINTER(ctypes.c_int)]),
+    "mhc_post_fwd": (ctypes.c_int, [ctypes.POINTER(PostFwdArgs), _c_void_p]),
+    "mhc_post_bwd": (ctypes.c_int, [ctypes.POINTER(PostBwdArgs), _c_void_p]),
     "mhc_launch_count": (ctypes.c_uint64, []),
     "mhc_abi_version": (ctypes.c_int, []),
 }

@@ -25,6 +25,7 @@
 #include "bwd_sm100.cuh"
 #include "rowdot.cuh"
 #include "tiled.cuh"
+#include "post.cuh"
 
 namespace mhc {
 
@@ -830,6 +831,48 @@ int static_scratch_address(void** out) {
   return MHC_OK;
 }
 
+// ----------------------------------------------------------------- post-op
+bool post_vec(const void* a, const void* b, const void* c, int D) {
+  return D % 8 == 0 && aligned(a, 16) && aligned(b, 16) && aligned(c, 16);
+}
+
+template <int n>
+struct PostFwd {
+  static int run(const mhc_post_fwd_args* a, cudaStream_t s, int sms) {
+    const int64_t T = a->tokens;
+    const int D = a->D;
+    const bool vec = post_vec(a->x, a->y, a->out, D);
+    const int64_t runs = ((int64_t)(vec ? D / 8 : D) + 32 * post::kU - 1) / (32 * post::kU);
+    const int64_t blocks =
+        std::max<int64_t>(1, std::min<int64_t>((T * runs + post::kWarps - 1) / post::kWarps, (int64_t)sms * 8));
+    if (vec)
+      post::post_fwd_kernel<n, 8><<<(unsigned)blocks, post::kThreads, 0, s>>>(a->x, a->h_res, a->h_post, a->y, a->out,
+                                                                              T, D);
+    else
+      post::post_fwd_kernel<n, 1><<<(unsigned)blocks, post::kThreads, 0, s>>>(a->x, a->h_res, a->h_post, a->y, a->out,
+                                                                              T, D);
+    return after_launch();
+  }
+};
+
+template <int n>
+struct PostBwd {
+  static int run(const mhc_post_bwd_args* a, cudaStream_t s, int sms) {
+    const int64_t T = a->tokens;
+    const int D = a->D;
+    const bool vec = post_vec(a->x, a->y, a->dout, D) && aligned(a->dx, 16) && aligned(a->dy, 16);
+    const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((T + post::kWarps - 1) / post::kWarps,
+                                                                  (int64_t)sms * 8));
+    if (vec)
+      post::post_bwd_kernel<n, 8><<<(unsigned)blocks, post::kThreads, 0, s>>>(
+          a->x, a->h_res, a->h_post, a->y, a->dout, a->dx, a->dy, a->dh_res, a->dh_post, T, D);
+    else
+      post::post_bwd_kernel<n, 1><<<(unsigned)blocks, post::kThreads, 0, s>>>(
+          a->x, a->h_res, a->h_post, a->y, a->dout, a->dx, a->dy, a->dh_res, a->dh_post, T, D);
+    return after_launch();
+  }
+};
+
 }  // namespace
 }  // namespace mhc
 
@@ -991,6 +1034,36 @@ int mhc_query_plan(int which, int64_t tokens, int32_t n, int32_t D, int* path, i
     return MHC_ERR_BAD_SHAPE;
   }
   return MHC_OK;
+}
+
+int mhc_post_fwd(const mhc_post_fwd_args* a, void* stream) {
+  if (!a) return MHC_ERR_NULL_POINTER;
+  int st = check_shape(a->tokens, a->n, a->D);
+  if (st) return st;
+  int sms = 0;
+  if ((st = current_sm_count(&sms))) return st;
+  if (a->tokens == 0) return MHC_OK;
+  if (!a->x || !a->h_res || !a->h_post || !a->y || !a->out) return MHC_ERR_NULL_POINTER;
+  if (!aligned(a->x, 2) || !aligned(a->y, 2) || !aligned(a->out, 2) || !aligned(a->h_res, 4) ||
+      !aligned(a->h_post, 4))
+    return MHC_ERR_MISALIGNED;
+  return dispatch_n<PostFwd>(a->n, a, static_cast<cudaStream_t>(stream), sms);
+}
+
+int mhc_post_bwd(const mhc_post_bwd_args* a, void* stream) {
+  if (!a) return MHC_ERR_NULL_POINTER;
+  int st = check_shape(a->tokens, a->n, a->D);
+  if (st) return st;
+  int sms = 0;
+  if ((st = current_sm_count(&sms))) return st;
+  if (a->tokens == 0) return MHC_OK;
+  if (!a->x || !a->h_res || !a->h_post || !a->y || !a->dout || !a->dx || !a->dy || !a->dh_res || !a->dh_post)
+    return MHC_ERR_NULL_POINTER;
+  if (!aligned(a->x, 2) || !aligned(a->y, 2) || !aligned(a->dout, 2) || !aligned(a->dx, 2) ||
+      !aligned(a->dy, 2) || !aligned(a->h_res, 4) || !aligned(a->h_post, 4) || !aligned(a->dh_res, 4) ||
+      !aligned(a->dh_post, 4))
+    return MHC_ERR_MISALIGNED;
+  return dispatch_n<PostBwd>(a->n, a, static_cast<cudaStream_t>(stream), sms);
 }
 
 int mhc_read_device_status(void* workspace, void* stream, int* device_status) {

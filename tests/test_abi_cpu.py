@@ -56,6 +56,10 @@ int main(void) {
   F(mhc_fwd_args, tokens) F(mhc_fwd_args, n) F(mhc_fwd_args, D) F(mhc_fwd_args, norm_eps)
   F(mhc_fwd_args, workspace) F(mhc_fwd_args, workspace_bytes)
   F(mhc_bwd_args, dgamma) F(mhc_bwd_args, tokens) F(mhc_bwd_args, hc_eps) F(mhc_bwd_args, workspace_bytes)
+  printf("mhc_post_fwd_args %zu\n", sizeof(mhc_post_fwd_args));
+  printf("mhc_post_bwd_args %zu\n", sizeof(mhc_post_bwd_args));
+  F(mhc_post_fwd_args, out) F(mhc_post_fwd_args, tokens) F(mhc_post_fwd_args, D)
+  F(mhc_post_bwd_args, dh_post) F(mhc_post_bwd_args, tokens) F(mhc_post_bwd_args, D)
   return 0;
 }
 '''
@@ -66,13 +70,14 @@ int main(void) {
         subprocess.run(["gcc", "-std=c99", "-I", os.path.join(ROOT, "include"), c, "-o", exe], check=True)
         lines = subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split("\n")
     got = dict(l.split() for l in lines if l.strip())
-    assert int(got["mhc_fwd_args"]) == ctypes.sizeof(_lib.FwdArgs)
-    assert int(got["mhc_bwd_args"]) == ctypes.sizeof(_lib.BwdArgs)
+    classes = {"mhc_fwd_args": _lib.FwdArgs, "mhc_bwd_args": _lib.BwdArgs,
+               "mhc_post_fwd_args": _lib.PostFwdArgs, "mhc_post_bwd_args": _lib.PostBwdArgs}
+    for sname, cls in classes.items():
+        assert int(got[sname]) == ctypes.sizeof(cls), sname
     for key, val in got.items():
         if "." in key:
             sname, field = key.split(".")
-            cls = _lib.FwdArgs if sname == "mhc_fwd_args" else _lib.BwdArgs
-            assert getattr(cls, field).offset == int(val), key
+            assert getattr(classes[sname], field).offset == int(val), key
 
 
 def test_status_strings_and_version(lib):
