@@ -113,7 +113,7 @@ __global__ void __launch_bounds__(kThreads) post_fwd_kernel(const uint16_t* __re
 // running sums of dout[i] . x[j] and dout[i] . y over its vectors; a fixed
 // xor-shuffle tree then sums the 32 lanes and lane 0 writes dh_res, dh_post.
 template <int n, int V>
-__global__ void __launch_bounds__(kThreads) post_bwd_kernel(const uint16_t* __restrict__ x,
+__global__ void __launch_bounds__(kThreads, (n <= 4 ? 2 : 1)) post_bwd_kernel(const uint16_t* __restrict__ x,
                                                             const float* __restrict__ h_res,
                                                             const float* __restrict__ h_post,
                                                             const uint16_t* __restrict__ y,
