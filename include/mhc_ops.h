@@ -197,6 +197,16 @@ MHC_API int mhc_selftest_wait_expiry(void* workspace, void* stream);
 MHC_API int mhc_query_plan(int which, int64_t tokens, int32_t n, int32_t D, int* path, int* cluster_size,
                            int* clusters);
 
+/* The plan mhc_query_plan would report on an sm_100 device with `sms` SMs,
+ * computed on the host without a device (capacity planning, host-side
+ * tests).  It assumes the fused forward's cooperative launch fits, as it does
+ * on every sm_100 part.  1 <= sms <= 4096.  No counterpart in the reference. */
+MHC_API int mhc_query_plan_for(int which, int64_t tokens, int32_t n, int32_t D, int32_t sms, int* path,
+                               int* cluster_size, int* clusters);
+
+/* mhc_bwd_workspace_size for a device with `sms` SMs, without a device. */
+MHC_API int mhc_bwd_workspace_size_for(int64_t tokens, int32_t n, int32_t D, int32_t sms, size_t* bytes);
+
 /* ---------------------------------------------------------------- post-op
  * The mHC post-op, the consumer of h_post and h_res: the next residual
  * stream of the hyper-connection block,
@@ -245,7 +255,8 @@ MHC_API int mhc_post_bwd(const mhc_post_bwd_args* args, void* stream);
  * all threads).  No counterpart in the reference; used to report launches. */
 MHC_API uint64_t mhc_launch_count(void);
 
-/* Version of this ABI (major*10000 + minor*100 + patch). */
+/* Version of this ABI (major*10000 + minor*100 + patch).  1.1.0 added the
+ * post-op and the device-free plan queries. */
 MHC_API int mhc_abi_version(void);
 
 #ifdef __cplusplus

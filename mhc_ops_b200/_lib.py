@@ -79,6 +79,11 @@ SIGNATURES = {
     "mhc_query_plan": (ctypes.c_int, [ctypes.c_int, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
                                       ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
                                       ctypes.POINTER(ctypes.c_int)]),
+    "mhc_query_plan_for": (ctypes.c_int, [ctypes.c_int, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                          ctypes.c_int32, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
+                                          ctypes.POINTER(ctypes.c_int)]),
+    "mhc_bwd_workspace_size_for": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                                  ctypes.POINTER(ctypes.c_size_t)]),
     "mhc_post_fwd": (ctypes.c_int, [ctypes.POINTER(PostFwdArgs), _c_void_p]),
     "mhc_post_bwd": (ctypes.c_int, [ctypes.POINTER(PostBwdArgs), _c_void_p]),
     "mhc_launch_count": (ctypes.c_uint64, []),
@@ -163,11 +168,17 @@ def bwd_workspace_size(tokens: int, n: int, D: int) -> int:
     return int(out.value)
 
 
-def query_plan(which: int, tokens: int, n: int, D: int) -> dict:
-    """Launch plan for forward (which=0) or backward (1) of this shape on the current device."""
+def query_plan(which: int, tokens: int, n: int, D: int, sms: int | None = None) -> dict:
+    """Launch plan for forward (which=0) or backward (1) of this shape on the
+    current device, or, with ``sms``, on an sm_100 device with that many SMs
+    (computed on the host; no device needed)."""
     path, cs, ncl = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
-    check(load().mhc_query_plan(which, tokens, n, D, ctypes.byref(path), ctypes.byref(cs), ctypes.byref(ncl)),
-          "mhc_query_plan")
+    if sms is None:
+        check(load().mhc_query_plan(which, tokens, n, D, ctypes.byref(path), ctypes.byref(cs), ctypes.byref(ncl)),
+              "mhc_query_plan")
+    else:
+        check(load().mhc_query_plan_for(which, tokens, n, D, sms, ctypes.byref(path), ctypes.byref(cs),
+                                        ctypes.byref(ncl)), "mhc_query_plan_for")
     if not path.value:
         return {"path": "generic"}
     if which == 0:

@@ -286,12 +286,14 @@ bool fwd_fused_supported(int n) { return n == 4 && fwd_fused_supported<4>(); }
 // Two-kernel form: the fewest K-slices (a divisor of the n*D/64 K-blocks, at
 // most 16, and no more than an h_in row holds) that give every SM at least
 // ~4 units.  Fused form: fwd_fused_slices, one CTA per SM at most.
-FwdTcPlan fwd_tc_plan(int64_t T, int n, int D, int sms) {
+// fused_ok: whether the fused form's cooperative launch fits on the device
+// (fwd_fused_supported; true on every sm_100 part for n = 4).
+FwdTcPlan fwd_tc_plan_with(int64_t T, int n, int D, int sms, bool fused_ok) {
   FwdTcPlan P;
   const int KB = n * D / fwdtc::kBK;
   const int64_t tiles = std::max<int64_t>(1, (T + fwdtc::kBM - 1) / fwdtc::kBM);
   const int fused_sk = fwd_fused_slices(n, D);
-  if (fused_sk > 0 && fwd_fused_supported(n)) {
+  if (fused_sk > 0 && fused_ok) {
     P.fused = true;
     P.S_K = fused_sk;
   } else {
@@ -306,6 +308,10 @@ FwdTcPlan fwd_tc_plan(int64_t T, int n, int D, int sms) {
   P.units = (int)(tiles * P.S_K);
   P.grid = std::min(P.units, sms);
   return P;
+}
+
+FwdTcPlan fwd_tc_plan(int64_t T, int n, int D, int sms) {
+  return fwd_tc_plan_with(T, n, D, sms, fwd_fused_supported(n));
 }
 
 size_t fwd_tile_counter_bytes(int64_t T) {
@@ -873,6 +879,31 @@ struct PostBwd {
   }
 };
 
+// The plan of mhc_query_plan / mhc_query_plan_for (shape already checked).
+int query_plan_impl(int which, int64_t tokens, int n, int D, int sms, bool fused_ok, int* path, int* cluster_size,
+                    int* clusters) {
+  *path = 0;
+  *cluster_size = 0;
+  *clusters = 0;
+  if (which == 0 && fwd_tc_shape(tokens, n, D)) {
+    const FwdTcPlan fp = fwd_tc_plan_with(tokens, n, D, sms, fused_ok);
+    *path = fp.fused ? 2 : 1;
+    *cluster_size = fp.S_K;
+    *clusters = fp.grid;
+  } else if (which == 1 && bwd_tc_shape(tokens, n, D)) {
+    const BwdTcPlan bp = bwd_tc_plan(tokens, D, sms);
+    *path = 1;
+    *cluster_size = bp.S_K;
+    *clusters = bp.S_T;
+  } else if (which == 1 && bwd_tiled_shape(tokens, n, D)) {
+    *path = 3;
+    *cluster_size = bwd_tiled_layout(tokens, n, D, sms).P;
+  } else if (which != 0 && which != 1) {
+    return MHC_ERR_BAD_SHAPE;
+  }
+  return MHC_OK;
+}
+
 }  // namespace
 }  // namespace mhc
 
@@ -897,7 +928,7 @@ const char* mhc_status_string(int status) {
 
 const char* mhc_last_cuda_error(void) { return t_last_cuda_error.c_str(); }
 
-int mhc_abi_version(void) { return 10000; }
+int mhc_abi_version(void) { return 10100; }
 
 uint64_t mhc_launch_count(void) { return g_launch_count.load(std::memory_order_relaxed); }
 
@@ -1014,29 +1045,29 @@ int mhc_query_plan(int which, int64_t tokens, int32_t n, int32_t D, int* path, i
   if (st) return st;
   int sms = 0;
   if ((st = current_sm_count(&sms))) return st;
-  *path = 0;
-  *cluster_size = 0;
-  *clusters = 0;
-  if (which == 0 && fwd_tc_shape(tokens, n, D)) {
-    const FwdTcPlan fp = fwd_tc_plan(tokens, n, D, sms);
-    *path = fp.fused ? 2 : 1;
-    *cluster_size = fp.S_K;
-    *clusters = fp.grid;
-  } else if (which == 1 && bwd_tc_shape(tokens, n, D)) {
-    const BwdTcPlan bp = bwd_tc_plan(tokens, D, sms);
-    *path = 1;
-    *cluster_size = bp.S_K;
-    *clusters = bp.S_T;
-  } else if (which == 1 && bwd_tiled_shape(tokens, n, D)) {
-    *path = 3;
-    *cluster_size = bwd_tiled_layout(tokens, n, D, sms).P;
-  } else if (which != 0 && which != 1) {
-    return MHC_ERR_BAD_SHAPE;
-  }
-  return MHC_OK;
+  const bool fused_ok = which == 0 && n == 4 && fwd_fused_supported(n);
+  return query_plan_impl(which, tokens, n, D, sms, fused_ok, path, cluster_size, clusters);
+}
+
+int mhc_query_plan_for(int which, int64_t tokens, int32_t n, int32_t D, int32_t sms, int* path, int* cluster_size,
+                       int* clusters) {
+  if (!path || !cluster_size || !clusters) return MHC_ERR_NULL_POINTER;
+  int st = check_shape(tokens, n, D);
+  if (st) return st;
+  if (sms < 1 || sms > 4096) return MHC_ERR_BAD_SHAPE;
+  return query_plan_impl(which, tokens, n, D, sms, n == 4, path, cluster_size, clusters);
+}
+
+int mhc_bwd_workspace_size_for(int64_t tokens, int32_t n, int32_t D, int32_t sms, size_t* bytes) {
+  if (!bytes) return MHC_ERR_NULL_POINTER;
+  int st = check_shape(tokens, n, D);
+  if (st) return st;
+  if (sms < 1 || sms > 4096) return MHC_ERR_BAD_SHAPE;
+  return bwd_workspace(tokens, n, D, sms, bytes);
 }
 
 int mhc_post_fwd(const mhc_post_fwd_args* a, void* stream) {
+
   if (!a) return MHC_ERR_NULL_POINTER;
   int st = check_shape(a->tokens, a->n, a->D);
   if (st) return st;

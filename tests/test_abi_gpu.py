@@ -75,8 +75,12 @@ def test_abi_rejects_bad_arguments():
     (1, 100, 4, 36, "generic"),                 # D not a multiple of 8
 ])
 def test_launch_plan_routes_each_shape(which, T, n, D, path):
-    """The plan query names the kernels a shape runs on (no kernel is launched)."""
-    assert _lib.query_plan(which, T, n, D)["path"] == path
+    """The plan query names the kernels a shape runs on (no kernel is launched),
+    and the device-free query at this device's SM count gives the same plan."""
+    got = _lib.query_plan(which, T, n, D)
+    assert got["path"] == path
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert _lib.query_plan(which, T, n, D, sms=sms) == got
 
 
 def test_launch_counter_advances():
