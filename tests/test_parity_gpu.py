@@ -91,6 +91,13 @@ def test_wide_rows_vs_oracle(B, S, n, D, gamma):
     _live_case(B, S, n, D, seed=12, gamma=gamma)
 
 
+@pytest.mark.parametrize("B,S,n,D", [(1, 4096, 4, 2560), (2, 2048, 8, 1280)])
+def test_reference_forward_test_shapes_vs_oracle(B, S, n, D):
+    """The largest shapes of the reference's forward tests
+    (test/forward/test_forward.py:460-483), forward and backward, all tokens."""
+    _live_case(B, S, n, D, seed=13)
+
+
 def test_full_llm_size_properties():
     """B=4,S=4096,n=4,D=4096: sampled tokens vs oracle, shard additivity, determinism."""
     B, S, n, D = 4, 4096, 4, 4096
