@@ -187,7 +187,9 @@ MHC_API int mhc_selftest_wait_expiry(void* workspace, void* stream);
  * fused tensor-core forward (one cooperative launch), 3 (backward only) the
  * backward for n other than 4 (tcgen05 dx and parameter-gradient kernels,
  * dx on the CUDA cores when D is not a multiple of 64; *cluster_size = the
- * token groups of its parameter-gradient kernel).  which = 0 forward: for
+ * token groups of its parameter-gradient kernel, *clusters = 2 when dx runs
+ * in stream pairs (even n), 1 one 64-k block at a time, 0 on the CUDA
+ * cores).  which = 0 forward: for
  * paths 1 and 2, *cluster_size is the number of K-slices the projection is
  * split into and *clusters the CTAs of its persistent grid.  which = 1 backward:
  * for path 1, the tensor-core kernel's grid is *clusters token groups of

@@ -185,7 +185,8 @@ def query_plan(which: int, tokens: int, n: int, D: int, sms: int | None = None) 
         return {"path": "tensor-core-fused" if path.value == 2 else "tensor-core", "k_slices": cs.value,
                 "ctas": ncl.value}
     if path.value == 3:
-        return {"path": "tiled", "token_groups": cs.value}
+        dx = {2: "tensor-core-stream-pairs", 1: "tensor-core", 0: "cuda-cores"}[ncl.value]
+        return {"path": "tiled", "token_groups": cs.value, "dx": dx}
     return {"path": "tensor-core", "d_slices": cs.value, "token_groups": ncl.value}
 
 

@@ -896,8 +896,10 @@ int query_plan_impl(int which, int64_t tokens, int n, int D, int sms, bool fused
     *cluster_size = bp.S_K;
     *clusters = bp.S_T;
   } else if (which == 1 && bwd_tiled_shape(tokens, n, D)) {
+    const BwdTiledLayout L = bwd_tiled_layout(tokens, n, D, sms);
     *path = 3;
-    *cluster_size = bwd_tiled_layout(tokens, n, D, sms).P;
+    *cluster_size = L.P;
+    *clusters = L.dx_tc ? (L.dx_pair ? 2 : 1) : 0;
   } else if (which != 0 && which != 1) {
     return MHC_ERR_BAD_SHAPE;
   }

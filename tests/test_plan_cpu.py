@@ -29,6 +29,9 @@ def test_wide_and_other_shapes_route_as_documented():
     assert plan(0, 16384, 8, 4096)["path"] == "tensor-core"        # n = 8: projection + row kernel
     b = plan(1, 16384, 8, 4096)
     assert b["path"] == "tiled" and 1 <= b["token_groups"] <= 8
+    assert b["dx"] == "tensor-core-stream-pairs"                   # even n: dx in stream pairs
+    assert plan(1, 200, 5, 256)["dx"] == "tensor-core"              # odd n: one 64-k block at a time
+    assert plan(1, 33, 2, 40)["dx"] == "cuda-cores"                 # D not a multiple of 64
     assert plan(1, 70, 6, 512)["path"] == "tiled"
     assert plan(0, 1000, 6, 512)["path"] == "generic"
     assert plan(1, 100, 4, 36)["path"] == "generic"                # D not a multiple of 8
