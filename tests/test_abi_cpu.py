@@ -120,3 +120,38 @@ def test_product_path_does_not_import_the_oracle():
             if f.endswith((".py", ".cu", ".cuh")):
                 text = open(os.path.join(dirpath, f)).read()
                 assert not re.search(r"(import\s+oracle|from\s+oracle|mhc_oracle)", text), f
+
+
+def test_c_program_links_the_library_and_agrees_with_ctypes():
+    """A plain C caller (the native boundary, not ctypes) links libmhc_ops.so and
+    gets the same device-free answers as the Python binding."""
+    src = r'''
+#include <stdio.h>
+#include "mhc_ops.h"
+int main(void) {
+  size_t fw = 0, bw = 0;
+  int p = -1, c = -1, k = -1;
+  if (mhc_fwd_workspace_size(16384, 4, 4096, &fw)) return 2;
+  if (mhc_bwd_workspace_size_for(16384, 4, 4096, 148, &bw)) return 3;
+  if (mhc_query_plan_for(1, 16384, 4, 4096, 148, &p, &c, &k)) return 4;
+  printf("%d %zu %zu %d %d %d %s\n", mhc_abi_version(), fw, bw, p, c, k, mhc_status_string(MHC_ERR_LIMIT));
+  return 0;
+}
+'''
+    libdir = os.path.dirname(_lib.lib_path())
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "caller.c")
+        exe = os.path.join(d, "caller")
+        open(c, "w").write(src)
+        subprocess.run(["gcc", "-std=c99", "-I", os.path.join(ROOT, "include"), c, "-o", exe, "-L", libdir,
+                        "-lmhc_ops", f"-Wl,-rpath,{libdir}"], check=True)
+        out = subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()
+    lib = _lib.load()
+    fw, bw = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    lib.mhc_fwd_workspace_size(16384, 4, 4096, ctypes.byref(fw))
+    lib.mhc_bwd_workspace_size_for(16384, 4, 4096, 148, ctypes.byref(bw))
+    plan = _lib.query_plan(1, 16384, 4, 4096, sms=148)
+    assert int(out[0]) == lib.mhc_abi_version()
+    assert (int(out[1]), int(out[2])) == (fw.value, bw.value)
+    assert (int(out[3]), int(out[4]), int(out[5])) == (1, plan["d_slices"], plan["token_groups"])
+    assert " ".join(out[6:]).encode() == lib.mhc_status_string(8)
