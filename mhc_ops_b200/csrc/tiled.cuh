@@ -1,21 +1,24 @@
 // Backward for the shapes the n = 4 tensor-core backward does not take (n other
 // than 4: the n = 8 "wide" hyper-connection above all): dx and the
-// parameter-gradient product on the tensor cores (dx_tc_kernel, g_tc_kernel,
-// below), dx on the CUDA cores (dx_kernel) when D is not a multiple of 64.
+// parameter-gradient product on the tensor cores, dx on the CUDA cores
+// (dx_kernel) when D is not a multiple of 64.
 //
 // Math: src/backward/golden.py:38-96, split as in the tensor-core backward:
 //   * rowdot::bwd_rows_kernel<n> leaves one record per token, {dh_mix[N], c,
 //     h_pre[n]} (golden.py:49-62, 74, 89), and the dalpha/dbias partials;
-//   * transpose_kernel turns the records' dh_mix into dmT [N][Tp] (token
-//     fastest), the layout the dx tiles read;
-//   * dx_kernel: dx[t,k] = (sum_j dh_mix[t,j] phi[j,k]) gamma[k] - c[t] x[t,k]
-//     + h_pre[t,i] dh_in[t,d]  (k = i*D + d; golden.py:65, 89-94) -- a
-//     [T,N] x [N,nD] product tiled through shared memory (cp.async), 64
-//     tokens x 256 k per CTA, 8 x 8 outputs per thread, the N-term sum in
-//     fp32 FMAs in ascending j (the generic kernel's order);
-//   * g_tc_kernel: gpart[g][j][k] = sum over the tokens of token group g of
-//     dh_mix[t,j] x[t,k] (the un-scaled dphi, golden.py:68-69) on the tensor
-//     cores (below);
+//   * dx[t,k] = (sum_j dh_mix[t,j] phi[j,k]) gamma[k] - c[t] x[t,k]
+//     + h_pre[t,i] dh_in[t,d]  (k = i*D + d; golden.py:65, 89-94):
+//     - D % 64 == 0: phimg_kernel (split phi * gamma images per 64-k block),
+//       then dx_tc_pair_kernel (even n: pairs of streams over one d-range,
+//       N = 128 MMAs) or dx_tc_kernel (odd n: one 64-k block at a time),
+//       both with the tile's dh_mix terms in tensor memory (below);
+//     - otherwise transpose_kernel (the records' dh_mix into dmT [N][Tp],
+//       token fastest) and dx_kernel, a [T,N] x [N,nD] product tiled through
+//       shared memory (cp.async), 64 tokens x 256 k per CTA, 8 x 8 outputs
+//       per thread, the N-term sum in fp32 FMAs in ascending j;
+//   * gimg_kernel + g_tc_kernel: gpart[g][j][k] = sum over the tokens of
+//     token group g of dh_mix[t,j] x[t,k] (the un-scaled dphi,
+//     golden.py:68-69) on the tensor cores (below);
 //   * generic::finalize_param_kernel (dphi, dgamma and the dalpha / dbias
 //     column sums) as in the tensor-core backward (fixed order, so results
 //     repeat bit for bit).
