@@ -2,8 +2,9 @@
 //
 // Validation, workspace carving and kernel selection live here; the kernels
 // are in generic.cuh (any shape), fwd_sm100.cuh / bwd_sm100.cuh (tcgen05 +
-// TMA kernels for the shapes the tensor cores take) and rowdot.cuh (the
-// streaming whole-row kernels beside them).
+// TMA kernels for the shapes the tensor cores take), rowdot.cuh (the
+// streaming whole-row kernels beside them), tiled.cuh (the backward for n
+// other than 4) and post.cuh (the post-op that consumes h_post / h_res).
 
 #include <cuda.h>
 #include <cuda_runtime.h>
