@@ -4,10 +4,15 @@
     (N > 1: python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...)
 
 Workload (per GPU, weak scaling): B=4, S=4096, n=4, D=4096 -- the LLM-scale
-configuration the metric is quoted on.  One step = forward with the outflag
+configuration the metric is quoted on.  ``--config 8g`` instead splits
+B=8, S=4096, n=4, D=7168 over the GPUs (strong scaling).  One step = forward with the outflag
 intermediates + backward + (N > 1) one NCCL all-reduce of the flat parameter
 gradient buffer.  Inputs are synthetic, seeded, and larger than L2 (x alone is
 512 MiB per GPU), so no L2 flush is needed between steps.
+
+When the K timed steps take less than 200 ms, the same step is timed again
+over at least 200 ms and reported as ``sustained`` (the NVML clock record
+covers both regions).
 
 Prints ONE JSON line on rank 0.  `value` is whole-job tokens/s with inputs
 resident in HBM; `e2e` is the same metric through the public API with the
@@ -34,6 +39,8 @@ sys.path.insert(0, ROOT)
 
 METRIC = "fwd+bwd tokens/s and HBM GB/s (% of roofline) at n=4,D=4096, 1/2/4/8 B200"
 WORKLOAD = dict(B=4, S=4096, n=4, D=4096)
+STRONG_WORKLOAD = dict(B=8, S=4096, n=4, D=7168)   # --config 8g: the whole batch split over the ranks
+SUSTAIN_MS = 200.0
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -190,7 +197,11 @@ def run_reference(args):
     T = w["B"] * w["S"]
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * T / value,
+        "steps": args.steps, "warmup": args.warmup,
+        # a step is the timed sample (ref_tokens tokens); the full-configuration
+        # figure is extrapolated from its rate and reported apart
+        "ms_per_step": 1e3 * statistics.median(times[args.warmup:]),
+        "ms_per_full_step_extrapolated": 1e3 * T / value,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "mHC pre-op fwd+bwd, B=4,S=4096,n=4,D=4096 per GPU", **w,
                    "tokens_per_step_sampled": sample},
@@ -222,10 +233,20 @@ def run_ours(args):
     from mhc_ops_b200 import _lib, mhc_backward_manual, mhc_forward_pre
     from mhc_ops_b200.backward import param_grad_numel
 
-    w = dict(WORKLOAD, B=args.batch, S=args.seq, n=args.streams, D=args.hidden)
+    strong = args.config == "8g"
+    if strong:
+        # B=8,S=4096,n=4,D=7168 in all: each rank takes a contiguous 1/world
+        # share of the 32768 tokens (strong scaling)
+        g = STRONG_WORKLOAD
+        total = g["B"] * g["S"]
+        if total % world:
+            raise SystemExit(f"--config 8g needs a world size dividing {total}")
+        w = dict(B=1, S=total // world, n=g["n"], D=g["D"])
+    else:
+        w = dict(WORKLOAD, B=args.batch, S=args.seq, n=args.streams, D=args.hidden)
     B, S, n, D = w["B"], w["S"], w["n"], w["D"]
     shape = f"B={B},S={S},n={n},D={D}"
-    headline = dict(w, B=WORKLOAD["B"]) == WORKLOAD   # the metric's shape (B may shrink for profiling)
+    headline = not strong and dict(w, B=WORKLOAD["B"]) == WORKLOAD   # the metric's shape (B may shrink for profiling)
     N, nD, T = n * n + 2 * n, n * D, w["B"] * w["S"]
 
     # parameters: identical on every rank; token data: per-rank seeds
@@ -296,6 +317,25 @@ def run_ours(args):
     sync_all()
     total_ms = max_over_ranks(start.elapsed_time(stop))
     launches = _lib.launch_count() - launches0
+
+    # A K-step region of a few ms holds only a handful of clock samples; the
+    # same steps are timed again over at least SUSTAIN_MS (reported apart, the
+    # clock record covers both regions).
+    sustained = None
+    reps = max(0, math.ceil(SUSTAIN_MS / max(total_ms / args.steps, 1e-3)))
+    reps = int(max_over_ranks(reps))
+    if total_ms < SUSTAIN_MS and reps > args.steps:
+        sync_all()
+        start.record()
+        for _ in range(reps):
+            ev[0].record()
+            step()
+        drain()
+        stop.record()
+        sync_all()
+        sus_ms = max_over_ranks(start.elapsed_time(stop))
+        sustained = {"steps": reps, "ms_per_step": sus_ms / reps, "value": world * T * reps / (sus_ms / 1e3),
+                     "what": f"the same step timed over {reps} steps ({sus_ms:.0f} ms) after the K-step region"}
     clk = clocks.stop() if rank == 0 else None
 
     # per-call durations (separate pass, same work, events between the calls).  No
@@ -369,13 +409,17 @@ def run_ours(args):
     step_alg = fwd_alg + bwd_alg
     dom = ("mhc_bwd", bwd_alg, bwd_ms) if bwd_ms >= fwd_ms else ("mhc_fwd", fwd_alg, fwd_ms)
     achieved = dom[1] / (dom[2] / 1e3) / 1e9
-    traffic = load_profile_traffic(dom[0]) if headline and B == WORKLOAD["B"] else None
+    traffic, traffic_src = (load_profile_traffic(dom[0]) if headline and B == WORKLOAD["B"]
+                            else (None, "no capture for this shape"))
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "strong" if strong else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"mHC pre-op fwd(outflag)+bwd, {shape} per GPU"
-                               + (" (LLM-scale config)" if headline else ""),
+        "config": {"workload": (f"mHC pre-op fwd(outflag)+bwd, B=8,S=4096,n=4,D=7168 split over {world} GPUs "
+                                f"({shape} per GPU, 8-GPU config)" if strong else
+                                f"mHC pre-op fwd(outflag)+bwd, {shape} per GPU"
+                                + (" (LLM-scale config)" if headline else "")),
                    **w, "global_tokens": world * T, "parallelism": f"dp{world} (token shards, NCCL all-reduce of "
                    "param grads)",
                    "l2": f"inputs larger than L2 (x is {T * nD * 2 / 2**20:.0f} MiB per GPU); no flush",
@@ -383,10 +427,12 @@ def run_ours(args):
         "hbm_gbs_step": step_alg / (ms_per_step / 1e3) / 1e9 / 1.0,
         "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": peak_kind, "traffic": traffic,
+                     "traffic_source": traffic_src,
                      "algorithmic_bytes": dom[1], "ms": dom[2],
                      "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
                      "fwd_frac": fwd_alg / (fwd_ms / 1e3) / 1e9 / peak,
                      "bwd_frac": bwd_alg / (bwd_ms / 1e3) / 1e9 / peak},
+        "sustained": sustained,
         "post_op": post,
         "gpu_launches": int(launches),
         "clocks": clk,
@@ -435,14 +481,34 @@ def post_op_timing(x, y, dev, n, D, T, reps=10):
             "what": "x_next = h_res x + h_post y (mhc_post) and its backward, per call, same shape"}
 
 
+def kernel_sources_sha16() -> str:
+    """Hash of the device code (mhc_ops_b200/csrc/*.cuh): the DRAM traffic of
+    a committed ncu capture is reported only while the kernels it measured are
+    the ones being timed."""
+    import glob
+    import hashlib
+    h = hashlib.sha256()
+    for f in sorted(glob.glob(os.path.join(ROOT, "mhc_ops_b200", "csrc", "*.cuh"))):
+        h.update(os.path.basename(f).encode())
+        with open(f, "rb") as fh:
+            h.update(fh.read())
+    return h.hexdigest()[:16]
+
+
 def load_profile_traffic(kernel_call: str):
-    """DRAM bytes per launch of the dominant call from the committed ncu summary, if any."""
+    """DRAM bytes per launch of the dominant call from the committed ncu summary
+    (profiles/traffic.json), with its provenance; None when the capture was
+    taken on other kernel sources than the ones timed now."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         with open(p) as f:
-            return json.load(f).get(kernel_call)
+            rec = json.load(f)
     except Exception:  # noqa: BLE001
-        return None
+        return None, "no profiles/traffic.json"
+    if rec.get("sources_sha16") != kernel_sources_sha16():
+        return None, "profiles/traffic.json was captured on other kernel sources (stale); not reported"
+    return rec.get(kernel_call), (f"profiles/traffic.json: one ncu capture ({rec.get('captured', '?')}) of these "
+                                  f"kernel sources (sha16 {rec['sources_sha16']})")
 
 
 def main():
@@ -461,6 +527,9 @@ def main():
     ap.add_argument("--seq", type=int, default=WORKLOAD["S"], help="S (default 4096; others only for profiling)")
     ap.add_argument("--streams", type=int, default=WORKLOAD["n"], help="n (default 4; others only for profiling)")
     ap.add_argument("--hidden", type=int, default=WORKLOAD["D"], help="D (default 4096; others only for profiling)")
+    ap.add_argument("--config", choices=["llm", "8g"], default="llm",
+                    help="llm: B=4,S=4096,n=4,D=4096 per GPU (weak scaling, the metric's configuration); "
+                         "8g: B=8,S=4096,n=4,D=7168 split over the GPUs (strong scaling)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)   # at least 3 untimed warm-up steps, whatever was asked
     if args.impl == "reference":

@@ -142,8 +142,9 @@ MHC_API int mhc_fwd(const mhc_fwd_args* args, void* stream);
  *   778,240 tokens that means D > 26176 for n = 4 and D > 6528 for n = 8
  *   (D a multiple of 64); more tokens lower the limit by 4 bytes per 128
  *   tokens.  Other shapes need only the 256-byte status header.
- *   The first call on each device looks up the array's device address, with
- *   that device current.  Make that first call before any stream capture.
+ *   The first call in each CUDA context (one per device; a new one after a
+ *   device reset) looks up the array's device address in that context.  Make
+ *   that first call before any stream capture.
  *   Every call on a device uses the same array.  Calls that overlap on the
  *   GPU (two streams, or two host threads) race on it and may return wrong
  *   results.  Order them on one stream, or use mhc_fwd with a workspace per

@@ -138,22 +138,82 @@ def ptr(t: torch.Tensor | None) -> int | None:
 
 
 # ------------------------------------------------------------------ workspaces
+class Workspace:
+    """A cached device workspace plus the watch over its device status word.
+
+    The first bytes of every workspace hold the status word that a kernel sets
+    to MHC_ERR_DEVICE_TIMEOUT when one of its bounded waits expires (its
+    outputs are then invalid).  After each call ``watch`` copies that word into
+    pinned host memory on a side stream, ordered after the call's kernels but
+    without making the caller's stream wait; the next call through the same
+    workspace (``raise_if_timed_out``), or ``check_device_status``, looks at
+    the copy and raises ``MhcError(MHC_ERR_DEVICE_TIMEOUT)``.
+    """
+
+    def __init__(self, nbytes: int, device: torch.device):
+        self.buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+        self.device = device
+        self.host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self.side = torch.cuda.Stream(device=device)
+        self.done = None          # event recorded on the side stream after the copy
+        self.where = ""
+
+    def watch(self, stream: torch.cuda.Stream, where: str) -> None:
+        if torch.cuda.is_current_stream_capturing():
+            return                # no host-visible copy inside a graph capture
+        self.where = where
+        self.side.wait_stream(stream)
+        with torch.cuda.stream(self.side):
+            self.host.copy_(self.buf[:4].view(torch.int32), non_blocking=True)
+            self.done = torch.cuda.Event()
+            self.done.record(self.side)
+
+    def raise_if_timed_out(self, wait: bool = False) -> None:
+        """Raise if an earlier call through this workspace reported a device
+        timeout; the word is cleared first, so the next call starts clean.
+        With ``wait`` the copy of the last call is waited for."""
+        if self.done is None:
+            return
+        if wait:
+            self.done.synchronize()
+        elif not self.done.query():
+            return                # the last call has not finished yet: look next time
+        self.done = None
+        code = int(self.host.item())
+        if code != MHC_OK:
+            self.buf[:4].zero_()
+            self.host.zero_()
+            raise MhcError(code, f"{self.where} (an earlier call; its outputs are invalid)")
+
+
 _ws_cache: dict = {}
 
 
-def workspace(nbytes: int, device: torch.device, stream: torch.cuda.Stream) -> torch.Tensor:
-    """A zero-initialised byte workspace of >= nbytes, cached per (device, stream).
+def workspace(nbytes: int, device: torch.device, stream: torch.cuda.Stream) -> Workspace:
+    """A zero-initialised workspace of >= nbytes, cached per (device, stream).
 
-    The first bytes hold the device status word, so new workspaces are zero
-    filled once; later calls reuse the buffer, ordered by the stream.
+    New workspaces are zero filled once (the first bytes hold the device
+    status word); later calls reuse the buffer, ordered by the stream.  A
+    timeout an earlier call on this workspace reported is raised here.
     """
     key = (device.index, stream.cuda_stream)
-    buf = _ws_cache.get(key)
-    if buf is None or buf.numel() < nbytes:
-        size = max(nbytes, 1 << 16)
-        buf = torch.zeros(size, dtype=torch.uint8, device=device)
-        _ws_cache[key] = buf
-    return buf
+    ws = _ws_cache.get(key)
+    if ws is not None:
+        # a workspace about to be replaced reports its last call first
+        ws.raise_if_timed_out(wait=ws.buf.numel() < nbytes)
+    if ws is None or ws.buf.numel() < nbytes:
+        ws = Workspace(nbytes, device)
+        _ws_cache[key] = ws
+    return ws
+
+
+def check_device_status(device=None) -> None:
+    """Wait for the status copies of every cached workspace on ``device``
+    (all devices when None) and raise ``MhcError(MHC_ERR_DEVICE_TIMEOUT)`` if
+    any call reported an expired device wait."""
+    for (idx, _), ws in list(_ws_cache.items()):
+        if device is None or torch.device(device).index in (None, idx):
+            ws.raise_if_timed_out(wait=True)
 
 
 def fwd_workspace_size(tokens: int, n: int, D: int) -> int:

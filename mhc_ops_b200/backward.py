@@ -89,8 +89,9 @@ def mhc_backward_manual(x, phi, alpha, bias, inv_rms, h_mix, h_pre, h_post, dh_i
             dh_in=_lib.ptr(dh_in), dh_post=_lib.ptr(dh_post), dh_res=_lib.ptr(dh_res), gamma=_lib.ptr(gamma),
             dx=_lib.ptr(dx), dphi=_lib.ptr(dphi), dalpha=_lib.ptr(dalpha), dbias=_lib.ptr(dbias),
             dgamma=_lib.ptr(dgamma), tokens=T, n=n, D=D, norm_eps=float(norm_eps), hc_eps=float(hc_eps),
-            workspace=ws.data_ptr(), workspace_bytes=ws.numel())
+            workspace=ws.buf.data_ptr(), workspace_bytes=ws.buf.numel())
         _lib.check(lib.mhc_bwd(args, stream.cuda_stream), "mhc_bwd")
+        ws.watch(stream, "mhc_bwd")
     return dx, dphi, dalpha, dbias, dgamma
 
 

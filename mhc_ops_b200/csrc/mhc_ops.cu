@@ -146,16 +146,19 @@ struct BwdGeneric {
   }
 };
 
-// ----------------------------------------------------------------- TMA maps
+// ----------------------------------------------------------------- driver entry points, TMA maps
+// A CUDA driver function looked up through the runtime (NULL if unavailable).
+void* driver_entry_point(const char* name) {
+  void* ptr = nullptr;
+  cudaDriverEntryPointQueryResult q{};
+  if (cudaGetDriverEntryPoint(name, &ptr, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess)
+    ptr = nullptr;
+  return ptr;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      ptr = nullptr;
-    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  }();
+  static PFN_cuTensorMapEncodeTiled_v12000 fn =
+      reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(driver_entry_point("cuTensorMapEncodeTiled"));
   return fn;
 }
 
@@ -814,27 +817,45 @@ __global__ void wait_expiry_kernel(int* status) {
 // file-scope device array instead of caller memory.  Every device that loads
 // the library holds the array until the process exits.
 constexpr size_t kStaticScratchBytes = (size_t)16 << 20;
-constexpr int kStaticMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
-// Device address of g_static_scratch on the current device.  In host code the
-// symbol names a host-side shadow, so the address comes from
-// cudaGetSymbolAddress, asked once per device with that device current.
+// Device address of g_static_scratch in the current CUDA context.  In host
+// code the symbol names a host-side shadow, so the address comes from
+// cudaGetSymbolAddress, asked once per context with that context current.
+// The cache is keyed by the driver's unique context id, not the device
+// ordinal: after a device reset the module is loaded again into a new
+// context, possibly at another address, and the old one must not be reused.
 int static_scratch_address(void** out) {
   static std::mutex mu;
-  static void* addr[kStaticMaxDevices] = {};
-  int dev = 0;
-  MHC_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= kStaticMaxDevices) return MHC_ERR_LIMIT;
+  static std::map<unsigned long long, void*> by_ctx;
+  // Driver entry points through the runtime, so the library keeps no link-time
+  // dependency on libcuda (it loads on machines without a driver).
+  using GetCurrentFn = CUresult (*)(CUcontext*);
+  using GetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrentFn get_current = reinterpret_cast<GetCurrentFn>(driver_entry_point("cuCtxGetCurrent"));
+  static GetIdFn get_id = reinterpret_cast<GetIdFn>(driver_entry_point("cuCtxGetId"));
+  auto current_id = [](unsigned long long* id) {
+    CUcontext ctx = nullptr;
+    return get_current && get_id && get_current(&ctx) == CUDA_SUCCESS && ctx != nullptr &&
+           get_id(ctx, id) == CUDA_SUCCESS;
+  };
+  unsigned long long id = 0;
+  const bool known_ctx = current_id(&id);
   std::lock_guard<std::mutex> g(mu);
-  if (!addr[dev]) {
-    void* p = nullptr;
-    MHC_CUDA_TRY(cudaGetSymbolAddress(&p, g_static_scratch));
-    if (!p) return MHC_ERR_CUDA;
-    addr[dev] = p;
+  if (known_ctx) {
+    auto it = by_ctx.find(id);
+    if (it != by_ctx.end()) {
+      *out = it->second;
+      return MHC_OK;
+    }
   }
-  *out = addr[dev];
+  void* p = nullptr;
+  MHC_CUDA_TRY(cudaGetSymbolAddress(&p, g_static_scratch));   // creates the primary context if none is current
+  if (!p) return MHC_ERR_CUDA;
+  if (!known_ctx && !current_id(&id)) return MHC_ERR_CUDA;
+  by_ctx[id] = p;
+  *out = p;
   return MHC_OK;
 }
 

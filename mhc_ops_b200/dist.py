@@ -78,11 +78,19 @@ class DataParallelMHC:
 
     def backward(self, x, phi, alpha, bias, inv_rms, h_mix, h_pre, h_post, dh_in, dh_post, dh_res, gamma,
                  overlap: bool = False, **kw):
-        """With ``overlap=True`` the all-reduce is left in flight (NCCL's own
-        stream) so that whatever the caller enqueues next -- typically the next
-        step's forward -- overlaps it; the returned parameter gradients are
-        valid after ``wait()``, which the next ``backward`` also calls before it
-        rewrites the buffer."""
+        """Returns ``(dx_local, dphi, dalpha, dbias, dgamma)``.
+
+        The four parameter gradients are views into one flat buffer owned by
+        this object, which every ``backward`` call rewrites.  With
+        ``overlap=False`` they hold the sums over all ranks when this returns
+        (in stream order).  With ``overlap=True`` the all-reduce is left in
+        flight on NCCL's own stream so that whatever the caller enqueues next
+        -- typically the next step's forward -- overlaps it: the views then
+        hold this rank's partial sums until ``wait()`` has been called, and
+        reading them before that gives partial or mixed values.  The next
+        ``backward`` calls ``wait()`` itself and then overwrites the buffer, so
+        a caller that keeps the gradients across steps must ``wait()`` and
+        copy them first."""
         self.wait()
         flat = self.grad_buffer(x.device)
         dx, dphi, dalpha, dbias, dgamma = self.bwd(x, phi, alpha, bias, inv_rms, h_mix, h_pre, h_post,

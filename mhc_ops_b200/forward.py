@@ -75,8 +75,9 @@ def mhc_forward_pre(x, phi, alpha, bias, outflag: bool = False, norm_eps: float 
             h_in=_lib.ptr(h_in), h_post=_lib.ptr(h_post), h_res=_lib.ptr(h_res),
             inv_rms=_lib.ptr(inv_rms), h_mix=_lib.ptr(h_mix), h_pre=_lib.ptr(h_pre),
             tokens=T, n=n, D=D, norm_eps=float(norm_eps), hc_eps=float(hc_eps),
-            workspace=ws.data_ptr(), workspace_bytes=ws.numel())
+            workspace=ws.buf.data_ptr(), workspace_bytes=ws.buf.numel())
         _lib.check(lib.mhc_fwd(args, stream.cuda_stream), "mhc_fwd")
+        ws.watch(stream, "mhc_fwd")
 
     if not outflag:
         return h_in, h_post, h_res

@@ -30,6 +30,8 @@ __all__ = [
     "n_out",
     "forward",
     "backward",
+    "bf16_stats",
+    "bf16_within",
 ]
 
 
@@ -227,6 +229,36 @@ def backward_term_scale(x_bf16, phi, alpha, inv_rms, h_mix, h_pre, h_post,
             + np.abs(h_pre[..., None] * dh[:, :, None, :]))
 
 
+def bf16_stats(ours_bf16, ref_bf16, term_scale, ulps=1.0, fp32_floor=2.0 ** -18) -> dict:
+    """How far bf16 results are from the reference value, element by element.
+
+    Keys: ``n`` elements; ``exact`` equal bit patterns (value-equal, so +0/-0
+    count); ``within_ulp`` |ours - ref| <= ulps * ulp(ref) (exact included);
+    ``floor_needed`` beyond that but within the fp32 accumulation floor
+    ``fp32_floor * term_scale``; ``bad`` beyond both; ``worst_ulps`` the
+    largest distance in ulps of ref; ``worst_ulps_no_floor`` the same over the
+    elements that needed no floor (at most ``ulps`` when ``within_ulp`` holds
+    everywhere else).
+    """
+    a = bf16_to_f32(ours_bf16)
+    b = bf16_to_f32(ref_bf16)
+    d = np.abs(a - b)
+    u = bf16_ulp(b)
+    in_ulp = d <= ulps * u
+    floor = np.float32(fp32_floor) * np.asarray(term_scale, np.float32)
+    ok = d <= ulps * u + floor
+    dist = d / u
+    return {
+        "n": int(d.size),
+        "exact": int((a == b).sum()),
+        "within_ulp": int(in_ulp.sum()),
+        "floor_needed": int((ok & ~in_ulp).sum()),
+        "bad": int((~ok).sum()),
+        "worst_ulps": float(dist.max()) if d.size else 0.0,
+        "worst_ulps_no_floor": float(dist[in_ulp].max()) if in_ulp.any() else 0.0,
+    }
+
+
 def bf16_within(ours_bf16, ref_bf16, term_scale, ulps=1.0, fp32_floor=2.0 ** -18):
     """Elementwise check |ours - ref| <= ulps * ulp(ref) + fp32_floor * term_scale.
 
@@ -234,10 +266,5 @@ def bf16_within(ours_bf16, ref_bf16, term_scale, ulps=1.0, fp32_floor=2.0 ** -18
     of the same terms may differ by a few 2^-24 * sum|terms|, which is many bf16
     ulps of a result produced by cancellation.  Returns (ok, worst_ulps, n_bad).
     """
-    a = bf16_to_f32(ours_bf16)
-    b = bf16_to_f32(ref_bf16)
-    d = np.abs(a - b)
-    tol = ulps * bf16_ulp(b) + np.float32(fp32_floor) * np.asarray(term_scale, np.float32)
-    bad = d > tol
-    worst = float((d / bf16_ulp(b)).max()) if d.size else 0.0
-    return (not bad.any()), worst, int(bad.sum())
+    st = bf16_stats(ours_bf16, ref_bf16, term_scale, ulps, fp32_floor)
+    return st["bad"] == 0, st["worst_ulps"], st["bad"]

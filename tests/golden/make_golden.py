@@ -7,9 +7,11 @@ their files (no Triton import), run on the CPU on seeded inputs, and the
 inputs plus every output are stored as ``<case>.npz`` (bf16 as uint16 bits).
 
 The reference checkout is only available where the fixtures are generated;
-the committed ``.npz`` files are what the tests read.
+the committed ``.npz`` files are what the tests read.  Its location is
+required: ``--reference <checkout>`` or the ``MHC_REFERENCE_ROOT``
+environment variable.
 
-Usage:  python tests/golden/make_golden.py [--reference /root/reference]
+Usage:  python tests/golden/make_golden.py --reference <path to the reference checkout>
 """
 from __future__ import annotations
 
@@ -56,8 +58,11 @@ def _bits(t: torch.Tensor) -> np.ndarray:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("MHC_REFERENCE_ROOT"),
+                    help="root of the reference checkout (default: $MHC_REFERENCE_ROOT)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference <checkout root> or set MHC_REFERENCE_ROOT")
     fwd_mod = _load(os.path.join(args.reference, "src/forward/golden.py"), "ref_fwd_golden")
     bwd_mod = _load(os.path.join(args.reference, "src/backward/golden.py"), "ref_bwd_golden")
     torch.set_num_threads(max(1, os.cpu_count() or 1))

@@ -107,3 +107,25 @@ def test_bounded_wait_expiry_reports_timeout():
     out = mhc_forward_pre(d.x, d.phi, d.alpha, d.bias)
     torch.cuda.synchronize()
     assert torch.isfinite(out[1]).all()
+
+
+def test_timeout_reported_through_the_python_api():
+    """The Python API surfaces a device timeout: the status word of the cached
+    workspace is set (by the bounded-wait self test, which gives up after
+    about a second, no fault), the next forward through mhc_forward_pre copies
+    it, and check_device_status raises MHC_ERR_DEVICE_TIMEOUT.  The word is
+    cleared by the raise, so the calls after it run clean."""
+    lib = _lib.load()
+    stream = torch.cuda.current_stream()
+    d = make_inputs(1, 16, 4, 128, seed=7).to("cuda")
+    mhc_forward_pre(d.x, d.phi, d.alpha, d.bias)
+    _lib.check_device_status()
+    ws = _lib._ws_cache[(torch.cuda.current_device(), stream.cuda_stream)]
+    assert lib.mhc_selftest_wait_expiry(ws.buf.data_ptr(), stream.cuda_stream) == 0
+    mhc_forward_pre(d.x, d.phi, d.alpha, d.bias)
+    with pytest.raises(_lib.MhcError) as err:
+        _lib.check_device_status()
+    assert err.value.status == _lib.MHC_ERR_DEVICE_TIMEOUT
+    out = mhc_forward_pre(d.x, d.phi, d.alpha, d.bias)
+    _lib.check_device_status()
+    assert torch.isfinite(out[1]).all()

@@ -6,8 +6,12 @@
 * at the full LLM size, size-independent properties: per-token outputs of a
   random token sample against the oracle, shard additivity of the parameter
   gradients, bitwise determinism.
+* the wide configuration (n=8, D=4096, B=2, S=8192) and the 8-GPU row width
+  (n=4, D=7168, 4096 tokens) over every token, in shards against the oracle.
 Tolerances: fp32 outputs max|a-b|/max|ref| <= 1e-4; bf16 h_in/dx within 1 bf16
-ulp of the golden value plus the fp32 accumulation floor 2^-18 * sum|terms|.
+ulp of the golden value, or, for at most 0.1% of the elements (cancellation),
+within the fp32 accumulation floor 2^-18 * sum|terms|; the counts are printed
+at the end of the run.
 """
 import numpy as np
 import pytest
@@ -17,7 +21,8 @@ from mhc_ops_b200 import mhc_backward_manual, mhc_forward_pre
 from mhc_ops_b200.synthetic import make_inputs
 from oracle import mhc_oracle as O
 from tests._golden import fixture_names, load_fixture
-from tests._gpu import DEV, FP32_TOL, assert_bwd_close, assert_fwd_close, bits, from_bits, rel
+from tests._gpu import (BF16_REPORT, DEV, FLOOR_FRAC, FP32_TOL, assert_bwd_close, assert_fwd_close, bits, check_bf16,
+                        from_bits, oracle_shards, rel)
 
 pytestmark = pytest.mark.gpu
 
@@ -129,8 +134,7 @@ def test_full_llm_size_properties():
                                   inp.dh_post.reshape(T, n)[idx][None].numpy(),
                                   inp.dh_res.reshape(T, n, n)[idx][None].numpy(), inp.gamma.numpy())
     dx_s = bw[0].reshape(T, n, D)[torch.as_tensor(idx, device=DEV)]
-    ok, worst, nbad = O.bf16_within(bits(dx_s), ref_b[0].reshape(-1, n, D), scale.reshape(-1, n, D))
-    assert ok, f"llm-sample dx: {nbad} beyond tolerance (worst {worst:.1f} ulp)"
+    check_bf16("llm-sample", "dx", bits(dx_s), ref_b[0].reshape(-1, n, D), scale.reshape(-1, n, D))
 
     # parameter gradients are sums over tokens: 4 shards must add up to the whole
     parts = []
@@ -177,3 +181,61 @@ def test_outflag_false_returns_three():
     full = mhc_forward_pre(inp.x, inp.phi, inp.alpha, inp.bias, outflag=True)
     for a, b in zip(out, full[:3]):
         assert torch.equal(a, b)
+
+
+def _full_batch_vs_oracle(B, S, n, D, seed, shard, tag):
+    """Forward and backward of the whole batch on the GPU; every token checked
+    against the oracle, shard by shard in worker processes (the oracle's
+    backward runs from the GPU's forward intermediates, so both backward
+    implementations see the same inputs); parameter gradients against the
+    float64 sum of the oracle's per-shard gradients."""
+    inp = make_inputs(B, S, n, D, seed=seed)
+    d = inp.to(DEV)
+    out = mhc_forward_pre(d.x, d.phi, d.alpha, d.bias, outflag=True)
+    bw = mhc_backward_manual(d.x, d.phi, d.alpha, d.bias, out[3], out[4], out[5], out[1], d.dh_in, d.dh_post,
+                             d.dh_res, d.gamma)
+    torch.cuda.synchronize()
+    T = B * S
+    N = n * n + 2 * n
+    phi, alpha, bias, gamma = inp.phi.numpy(), inp.alpha.numpy(), inp.bias.numpy(), inp.gamma.numpy()
+    xb = bits(inp.x).reshape(T, n, D)
+    dhb = bits(inp.dh_in).reshape(T, D)
+    dpost = inp.dh_post.reshape(T, n).numpy()
+    dres = inp.dh_res.reshape(T, n, n).numpy()
+    h_in_b = bits(out[0]).reshape(T, D)
+    f_np = [o.reshape(T, *o.shape[2:]).cpu().numpy() for o in out[1:]]
+    dx_b = bits(bw[0]).reshape(T, n, D)
+    jobs, bounds = [], []
+    for a in range(0, T, shard):
+        sl = slice(a, min(T, a + shard))
+        bounds.append((a, sl.stop))
+        jobs.append((xb[sl][None], dhb[sl][None], dpost[sl][None], dres[sl][None], phi, alpha, bias, gamma,
+                     h_in_b[sl][None], tuple(o[sl][None] for o in f_np), dx_b[sl][None]))
+    sums = [np.zeros((N, n * D)), np.zeros(3), np.zeros(N), np.zeros(n * D)]
+    for (a, b), res in zip(bounds, oracle_shards(jobs)):
+        for nm, e in res["fwd_rel"].items():
+            assert e <= FP32_TOL, f"{tag} [{a}:{b}] {nm}: rel err {e:.3g}"
+        for nm in ("h_in", "dx"):
+            st = res[nm]
+            BF16_REPORT.append((f"{tag} [{a}:{b}]", nm, st))
+            assert st["bad"] == 0, f"{tag} [{a}:{b}] {nm}: {st['bad']} beyond tolerance ({st})"
+            assert st["floor_needed"] <= FLOOR_FRAC * st["n"] + 8, f"{tag} [{a}:{b}] {nm}: {st}"
+        for acc, r in zip(sums, res["param"]):
+            acc += r.reshape(acc.shape)
+    for name, o, r in zip(("dphi", "dalpha", "dbias", "dgamma"), bw[1:], sums):
+        e = rel(o, r)
+        assert e <= FP32_TOL, f"{tag} {name}: rel err {e:.3g}"
+
+
+def test_wide_config_full_size_vs_oracle():
+    """The wide configuration, n=8, D=4096, B=2, S=8192 (16384 tokens, N=80):
+    every token's forward outputs and dx against the oracle, and the parameter
+    gradients of the whole batch (the tiled backward with its multi-group
+    parameter-gradient partials)."""
+    _full_batch_vs_oracle(2, 8192, 8, 4096, seed=21, shard=1024, tag="wide n8 D4096")
+
+
+def test_eight_gpu_row_width_vs_oracle():
+    """The 8-GPU configuration's row width, n=4, D=7168, over 4096 tokens
+    (one GPU's share of B=8,S=4096 at 8 GPUs): every token against the oracle."""
+    _full_batch_vs_oracle(1, 4096, 4, 7168, seed=22, shard=1024, tag="8gpu n4 D7168")
