@@ -466,6 +466,23 @@ BwdTcPlan bwd_tc_plan(int64_t T, int D, int sms) {
   return best;
 }
 
+rowdot::BwdRowArgs bwd_row_args(const mhc_bwd_args* a, float* rec) {
+  rowdot::BwdRowArgs r;
+  r.x = a->x;
+  r.dh_in = a->dh_in;
+  r.alpha = a->alpha;
+  r.inv_rms = a->inv_rms;
+  r.h_mix = a->h_mix;
+  r.h_pre = a->h_pre;
+  r.h_post = a->h_post;
+  r.dh_post = a->dh_post;
+  r.dh_res = a->dh_res;
+  r.rec = rec;
+  r.D = a->D;
+  r.hc_eps = a->hc_eps;
+  return r;
+}
+
 int bwd_rows_grid(int64_t T, int sms) {
   return (int)std::max<int64_t>(1, std::min<int64_t>(sms, (T + kRowsWarps - 1) / kRowsWarps));
 }
@@ -516,9 +533,7 @@ int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s, int sms) {
   bwdtc::phit_kernel<n><<<nD / bwdtc::kBK, 256, 0, s>>>(a->phi, a->gamma, reinterpret_cast<uint16_t*>(ws + L.phit),
                                                         nD);
   if ((st = after_launch())) return st;
-  rowdot::bwd_rows_kernel<n><<<L.rows_grid, rowdot::kThreads, 0, s>>>(
-      a->x, a->dh_in, a->alpha, a->inv_rms, a->h_mix, a->h_pre, a->h_post, a->dh_post, a->dh_res, rec, abpart, T, D,
-      a->hc_eps);
+  rowdot::bwd_rows_kernel<n><<<L.rows_grid, rowdot::kThreads, 0, s>>>(bwd_row_args(a, rec), abpart, T);
   if ((st = after_launch())) return st;
 
   CUtensorMap m_x2d, m_dh, m_dx, m_rec;
@@ -694,9 +709,7 @@ struct BwdTiled {
     float* abpart = reinterpret_cast<float*>(ws + L.abpart);
     float* gpart = reinterpret_cast<float*>(ws + L.gpart);
     int st;
-    rowdot::bwd_rows_kernel<n><<<L.rows_grid, rowdot::kThreads, 0, s>>>(
-        a->x, a->dh_in, a->alpha, a->inv_rms, a->h_mix, a->h_pre, a->h_post, a->dh_post, a->dh_res, rec, abpart, T, D,
-        a->hc_eps);
+    rowdot::bwd_rows_kernel<n><<<L.rows_grid, rowdot::kThreads, 0, s>>>(bwd_row_args(a, rec), abpart, T);
     if ((st = after_launch())) return st;
     if (L.dx_tc) {
       // dx on the tensor cores: split phi * gamma images, then one CTA per

@@ -36,153 +36,182 @@ __device__ __forceinline__ void bf16x8(const uint4& v, float (&f)[8]) {
   }
 }
 
-// B1: per token t (src/backward/golden.py:51-62, 74, 77-86, 89):
+// Running dalpha / dbias sums of the tokens one warp has processed.
+template <int n>
+struct RowAcc {
+  static constexpr int N_OUT = Rec<n>::N_OUT;
+  static constexpr int M = (N_OUT + 31) / 32;   // output columns per lane
+  float al0 = 0.f, al1 = 0.f, al2 = 0.f;        // lane 0
+  float b[M];                                   // lane l: dbias[l + 32 m]
+  __device__ __forceinline__ RowAcc() {
+#pragma unroll
+    for (int m = 0; m < M; ++m) b[m] = 0.f;
+  }
+  // this warp's partial row abpart[CW]: dalpha (3), then dbias (N_OUT)
+  __device__ __forceinline__ void store(float* ap, int lane) const {
+    if (lane == 0) {
+      ap[0] = al0;
+      ap[1] = al1;
+      ap[2] = al2;
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const int jj = lane + 32 * m;
+      if (jj < N_OUT) ap[3 + jj] = b[m];
+    }
+  }
+};
+
+struct BwdRowArgs {
+  const uint16_t* x;
+  const uint16_t* dh_in;
+  const float* alpha;
+  const float* inv_rms;
+  const float* h_mix;
+  const float* h_pre;
+  const float* h_post;
+  const float* dh_post;
+  const float* dh_res;
+  float* rec;
+  int D;
+  float hc_eps;
+};
+
+// B1 for one token t, one warp (src/backward/golden.py:51-62, 74, 77-86, 89):
 //   dh_pre[i] = sum_d dh_in[d] x[i,d]; dh_pre2, dh_post2; dh_mix = tmp * inv_rms;
 //   c = (sum_j tmp_j h_mix_j) inv_rms^3 / nD
-// writes rec[t] = {dh_mix[0..N), c, h_pre[0..n), 0...} and, per warp, the
-// running dalpha (3) and dbias (N) sums of its tokens to abpart[warp][CW].
-// Token t is owned by global warp t % W, so every sum has a fixed order.
-// Needs D % 8 == 0 and 16-byte aligned x / dh_in.
+// writes rec[t] = {dh_mix[0..N), c, h_pre[0..n), 0...} and adds the token's
+// dalpha (3) and dbias (N) terms to the warp's running sums.  Needs
+// D % 8 == 0 and 16-byte aligned x / dh_in.
 template <int n>
-__global__ void __launch_bounds__(kThreads, 1) bwd_rows_kernel(
-    const uint16_t* __restrict__ x, const uint16_t* __restrict__ dh_in, const float* __restrict__ alpha,
-    const float* __restrict__ inv_rms, const float* __restrict__ h_mix, const float* __restrict__ h_pre,
-    const float* __restrict__ h_post, const float* __restrict__ dh_post, const float* __restrict__ dh_res,
-    float* __restrict__ rec, float* __restrict__ abpart, int64_t T, int D, float hc_eps) {
+__device__ __forceinline__ void bwd_row_token(const BwdRowArgs& a, int64_t t, int lane, RowAcc<n>& acc) {
   using R = Rec<n>;
   constexpr int N_OUT = R::N_OUT;
-  constexpr int M = (N_OUT + 31) / 32;   // output columns per lane
-  const int lane = threadIdx.x & 31;
-  const int64_t gw = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
-  const int64_t W = (int64_t)gridDim.x * kWarps;
+  constexpr int M = RowAcc<n>::M;
+  const int D = a.D;
   const int nD = n * D;
-  const float inv_nd = 1.0f / (float)nD;
-  const float a_pre = alpha[0], a_post = alpha[1], a_res = alpha[2];
-  float acc_al0 = 0.f, acc_al1 = 0.f, acc_al2 = 0.f;   // lane 0
-  float acc_b[M];                                      // lane l: dbias[l + 32 m]
-#pragma unroll
-  for (int m = 0; m < M; ++m) acc_b[m] = 0.f;
-
-  for (int64_t t = gw; t < T; t += W) {
-    // small per-token inputs first, so they are in flight during the row stream
-    float hm[M], gin[M], dpo[M];
-#pragma unroll
-    for (int m = 0; m < M; ++m) {
-      const int jj = lane + 32 * m;
-      hm[m] = gin[m] = dpo[m] = 0.f;
-      if (jj < N_OUT) {
-        hm[m] = __ldg(h_mix + t * N_OUT + jj);
-        if (jj < n) {
-          gin[m] = __ldg(h_pre + t * n + jj);
-        } else if (jj < 2 * n) {
-          gin[m] = __ldg(h_post + t * n + (jj - n));
-          dpo[m] = __ldg(dh_post + t * n + (jj - n));
-        } else {
-          gin[m] = __ldg(dh_res + t * (n * n) + (jj - 2 * n));
-        }
-      }
-    }
-    const float ir = __ldg(inv_rms + t);
-
-    const uint16_t* xr = x + t * nD;
-    const uint16_t* gr = dh_in + t * D;
-    float p[n];
-#pragma unroll
-    for (int i = 0; i < n; ++i) p[i] = 0.f;
-    constexpr int U = 4;   // 256-element chunks in flight per lane
-    for (int c0 = 0; c0 < D; c0 += 256 * U) {
-      uint4 g[U], xv[U][n];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int d = c0 + u * 256 + lane * 8;
-        if (d < D) {
-          g[u] = ldg_stream(gr + d);
-#pragma unroll
-          for (int i = 0; i < n; ++i) xv[u][i] = ldg_stream(xr + i * D + d);
-        } else {
-          g[u] = make_uint4(0, 0, 0, 0);
-#pragma unroll
-          for (int i = 0; i < n; ++i) xv[u][i] = make_uint4(0, 0, 0, 0);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        float gf[8];
-        bf16x8(g[u], gf);
-#pragma unroll
-        for (int i = 0; i < n; ++i) {
-          float xf[8];
-          bf16x8(xv[u][i], xf);
-          float s0 = gf[0] * xf[0], s1 = gf[1] * xf[1];
-          s0 = fmaf(gf[2], xf[2], s0);
-          s1 = fmaf(gf[3], xf[3], s1);
-          s0 = fmaf(gf[4], xf[4], s0);
-          s1 = fmaf(gf[5], xf[5], s1);
-          s0 = fmaf(gf[6], xf[6], s0);
-          s1 = fmaf(gf[7], xf[7], s1);
-          p[i] += s0 + s1;
-        }
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < n; ++i) p[i] = warp_sum(p[i]);
-
-    float* rt = rec + t * R::W;
-    float dinv = 0.f, dal0 = 0.f, dal1 = 0.f, dal2 = 0.f;
-#pragma unroll
-    for (int m = 0; m < M; ++m) {
-      const int jj = lane + 32 * m;
-      if (jj < N_OUT) {
-        float g2, tmp;
-        if (jj < n) {
-          float dp = p[0];
-#pragma unroll
-          for (int i = 1; i < n; ++i)
-            if (jj == i) dp = p[i];
-          const float s = gin[m] - hc_eps;
-          g2 = dp * s * (1.0f - s);                 // golden.py:54
-          tmp = a_pre * g2;
-        } else if (jj < 2 * n) {
-          const float hq = gin[m];
-          g2 = dpo[m] * hq * (1.0f - hq / 2.0f);    // golden.py:55
-          tmp = a_post * g2;
-        } else {
-          g2 = gin[m];
-          tmp = a_res * g2;
-        }
-        rt[jj] = tmp * ir;                          // dh_mix (golden.py:62)
-        acc_b[m] += g2;                             // dbias terms (golden.py:83-85)
-        const float dal = g2 * (hm[m] * ir);        // dalpha terms (golden.py:77-79)
-        if (jj < n) dal0 += dal;
-        else if (jj < 2 * n) dal1 += dal;
-        else dal2 += dal;
-        dinv += tmp * hm[m];
-      }
-    }
-    dinv = warp_sum(dinv);                          // golden.py:74
-    dal0 = warp_sum(dal0);
-    dal1 = warp_sum(dal1);
-    dal2 = warp_sum(dal2);
-    if (lane == 0) {
-      rt[N_OUT] = dinv * (ir * ir * ir) * inv_nd;   // c (golden.py:89)
-      acc_al0 += dal0;
-      acc_al1 += dal1;
-      acc_al2 += dal2;
-    }
-    for (int w = N_OUT + 1 + lane; w < R::W; w += 32)
-      rt[w] = (w - N_OUT - 1 < n) ? __ldg(h_pre + t * n + (w - N_OUT - 1)) : 0.f;
-  }
-  float* ap = abpart + gw * R::CW;
-  if (lane == 0) {
-    ap[0] = acc_al0;
-    ap[1] = acc_al1;
-    ap[2] = acc_al2;
-  }
+  const float a_pre = __ldg(a.alpha), a_post = __ldg(a.alpha + 1), a_res = __ldg(a.alpha + 2);
+  // small per-token inputs first, so they are in flight during the row stream
+  float hm[M], gin[M], dpo[M];
 #pragma unroll
   for (int m = 0; m < M; ++m) {
     const int jj = lane + 32 * m;
-    if (jj < N_OUT) ap[3 + jj] = acc_b[m];
+    hm[m] = gin[m] = dpo[m] = 0.f;
+    if (jj < N_OUT) {
+      hm[m] = __ldg(a.h_mix + t * N_OUT + jj);
+      if (jj < n) {
+        gin[m] = __ldg(a.h_pre + t * n + jj);
+      } else if (jj < 2 * n) {
+        gin[m] = __ldg(a.h_post + t * n + (jj - n));
+        dpo[m] = __ldg(a.dh_post + t * n + (jj - n));
+      } else {
+        gin[m] = __ldg(a.dh_res + t * (n * n) + (jj - 2 * n));
+      }
+    }
   }
+  const float ir = __ldg(a.inv_rms + t);
+
+  const uint16_t* xr = a.x + t * nD;
+  const uint16_t* gr = a.dh_in + t * D;
+  float p[n];
+#pragma unroll
+  for (int i = 0; i < n; ++i) p[i] = 0.f;
+  constexpr int U = 4;   // 256-element chunks in flight per lane
+  for (int c0 = 0; c0 < D; c0 += 256 * U) {
+    uint4 g[U], xv[U][n];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int d = c0 + u * 256 + lane * 8;
+      if (d < D) {
+        g[u] = ldg_stream(gr + d);
+#pragma unroll
+        for (int i = 0; i < n; ++i) xv[u][i] = ldg_stream(xr + i * D + d);
+      } else {
+        g[u] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int i = 0; i < n; ++i) xv[u][i] = make_uint4(0, 0, 0, 0);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      float gf[8];
+      bf16x8(g[u], gf);
+#pragma unroll
+      for (int i = 0; i < n; ++i) {
+        float xf[8];
+        bf16x8(xv[u][i], xf);
+        float s0 = gf[0] * xf[0], s1 = gf[1] * xf[1];
+        s0 = fmaf(gf[2], xf[2], s0);
+        s1 = fmaf(gf[3], xf[3], s1);
+        s0 = fmaf(gf[4], xf[4], s0);
+        s1 = fmaf(gf[5], xf[5], s1);
+        s0 = fmaf(gf[6], xf[6], s0);
+        s1 = fmaf(gf[7], xf[7], s1);
+        p[i] += s0 + s1;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < n; ++i) p[i] = warp_sum(p[i]);
+
+  float* rt = a.rec + t * R::W;
+  float dinv = 0.f, dal0 = 0.f, dal1 = 0.f, dal2 = 0.f;
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    const int jj = lane + 32 * m;
+    if (jj < N_OUT) {
+      float g2, tmp;
+      if (jj < n) {
+        float dp = p[0];
+#pragma unroll
+        for (int i = 1; i < n; ++i)
+          if (jj == i) dp = p[i];
+        const float s = gin[m] - a.hc_eps;
+        g2 = dp * s * (1.0f - s);                 // golden.py:54
+        tmp = a_pre * g2;
+      } else if (jj < 2 * n) {
+        const float hq = gin[m];
+        g2 = dpo[m] * hq * (1.0f - hq / 2.0f);    // golden.py:55
+        tmp = a_post * g2;
+      } else {
+        g2 = gin[m];
+        tmp = a_res * g2;
+      }
+      rt[jj] = tmp * ir;                          // dh_mix (golden.py:62)
+      acc.b[m] += g2;                             // dbias terms (golden.py:83-85)
+      const float dal = g2 * (hm[m] * ir);        // dalpha terms (golden.py:77-79)
+      if (jj < n) dal0 += dal;
+      else if (jj < 2 * n) dal1 += dal;
+      else dal2 += dal;
+      dinv += tmp * hm[m];
+    }
+  }
+  dinv = warp_sum(dinv);                          // golden.py:74
+  dal0 = warp_sum(dal0);
+  dal1 = warp_sum(dal1);
+  dal2 = warp_sum(dal2);
+  if (lane == 0) {
+    rt[N_OUT] = dinv * (ir * ir * ir) * (1.0f / (float)nD);   // c (golden.py:89)
+    acc.al0 += dal0;
+    acc.al1 += dal1;
+    acc.al2 += dal2;
+  }
+  for (int w = N_OUT + 1 + lane; w < R::W; w += 32)
+    rt[w] = (w - N_OUT - 1 < n) ? __ldg(a.h_pre + t * n + (w - N_OUT - 1)) : 0.f;
+}
+
+// B1 over all tokens: token t is owned by global warp t % W, so every sum
+// has a fixed order; each warp writes its dalpha / dbias partial row to
+// abpart[warp][CW].
+template <int n>
+__global__ void __launch_bounds__(kThreads, 1) bwd_rows_kernel(const BwdRowArgs a, float* __restrict__ abpart,
+                                                                int64_t T) {
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int64_t W = (int64_t)gridDim.x * kWarps;
+  RowAcc<n> acc;
+  for (int64_t t = gw; t < T; t += W) bwd_row_token<n>(a, t, lane, acc);
+  acc.store(abpart + gw * Rec<n>::CW, lane);
 }
 
 // Forward, row half (src/forward/golden.py:34-69), per token t: sum the S_K

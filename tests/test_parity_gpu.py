@@ -91,6 +91,7 @@ def test_readme_backward_shapes_vs_oracle(B, S, D):
     (1, 70, 6, 512, True),       # n=6 tiled backward
     (1, 200, 5, 256, True),      # odd n on the tensor cores: dx one 64-k block at a time
     (1, 140, 2, 128, False),     # n=2: dx in stream pairs, one pair per d-block
+    (1, 200, 4, 9536, True),     # n=4, a row wider than the 8-GPU config's (149 64-wide d-blocks per stream)
 ])
 def test_wide_rows_vs_oracle(B, S, n, D, gamma):
     _live_case(B, S, n, D, seed=12, gamma=gamma)
