@@ -11,13 +11,16 @@ backward is exactly the gradient of the forward evaluated with
 projection only; the RMS uses plain x.  So the autograd forward folds gamma
 into phi and the backward returns gradients for x, phi, alpha, bias and gamma.
 With ``gamma=None`` the fold is skipped and no gamma gradient is produced.
+
+Both directions run as the registered operators ``torch.ops.mhc.fwd`` /
+``torch.ops.mhc.bwd`` (``mhc_ops_b200.ops``), so ``torch.compile`` traces
+``mhc_pre`` with each direction as one graph node.
 """
 from __future__ import annotations
 
 import torch
 
-from .backward import mhc_backward_manual
-from .forward import mhc_forward_pre
+from . import ops
 
 __all__ = ["MHCPreFunction", "mhc_pre"]
 
@@ -27,8 +30,7 @@ class MHCPreFunction(torch.autograd.Function):
     def forward(ctx, x, phi, alpha, bias, gamma=None, norm_eps=1e-6, hc_eps=1e-6):
         n, D = x.shape[2], x.shape[3]
         phi_eff = phi if gamma is None else phi * gamma.reshape(1, n * D).to(phi.dtype)
-        h_in, h_post, h_res, inv_rms, h_mix, h_pre = mhc_forward_pre(
-            x, phi_eff, alpha, bias, outflag=True, norm_eps=norm_eps, hc_eps=hc_eps)
+        h_in, h_post, h_res, inv_rms, h_mix, h_pre = ops.fwd(x, phi_eff, alpha, bias, norm_eps, hc_eps)
         ctx.save_for_backward(x, phi, alpha, bias, gamma, inv_rms, h_mix, h_pre, h_post)
         ctx.eps = (norm_eps, hc_eps)
         ctx.shapes = (phi.dtype, alpha.dtype, bias.dtype)
@@ -45,9 +47,9 @@ class MHCPreFunction(torch.autograd.Function):
         if dh_res is None:
             n = x.shape[2]
             dh_res = torch.zeros(x.shape[0], x.shape[1], n, n, dtype=torch.float32, device=x.device)
-        dx, dphi, dalpha, dbias, dgamma = mhc_backward_manual(
-            x, phi, alpha, bias, inv_rms, h_mix, h_pre, h_post, dh_in.to(torch.bfloat16), dh_post, dh_res,
-            gamma, norm_eps=norm_eps, hc_eps=hc_eps)
+        dx, dphi, dalpha, dbias, dgamma = ops.bwd(
+            x, phi, alpha, inv_rms, h_mix, h_pre, h_post, dh_in.to(torch.bfloat16), dh_post, dh_res, gamma,
+            norm_eps, hc_eps)
         g_gamma = None if gamma is None else dgamma.reshape(gamma.shape).to(gamma.dtype)
         return (dx, dphi.to(phi.dtype), dalpha.to(alpha.dtype), dbias.to(bias.dtype), g_gamma, None, None)
 

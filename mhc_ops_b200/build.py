@@ -1,9 +1,13 @@
-"""Build libmhc_ops.so in-tree with nvcc for sm_100a.
+"""Build the in-tree libraries.
 
     python -m mhc_ops_b200.build        (or mhc_ops_b200.build.build())
 
-Output: mhc_ops_b200/lib/libmhc_ops.so.  The build is skipped when the .so is
-newer than every source under csrc/ and include/ unless force=True.
+* mhc_ops_b200/lib/libmhc_ops.so -- the kernels and the C ABI, nvcc for sm_100a;
+* mhc_ops_b200/lib/libmhc_torch.so -- the TORCH_LIBRARY(mhc, ...) operators
+  over that C ABI (csrc/torch_ops.cpp), g++ against the installed torch.
+
+A build is skipped when its .so is newer than every source it depends on,
+unless force=True.
 """
 from __future__ import annotations
 
@@ -33,16 +37,47 @@ def _nvcc() -> str:
     raise RuntimeError("nvcc not found: set NVCC or put the CUDA toolkit on PATH")
 
 
+TORCH_LIB = os.path.join(LIBDIR, "libmhc_torch.so")
+TORCH_SRC = os.path.join(CSRC, "torch_ops.cpp")
+
+
 def _sources() -> list[str]:
     return sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cuh"))
                   + glob.glob(os.path.join(ROOT, "include", "*.h")))
 
 
-def up_to_date() -> bool:
-    if not os.path.exists(LIB):
+def up_to_date(lib: str = LIB, sources: list[str] | None = None) -> bool:
+    if not os.path.exists(lib):
         return False
-    t = os.path.getmtime(LIB)
-    return all(os.path.getmtime(s) <= t for s in _sources())
+    t = os.path.getmtime(lib)
+    return all(os.path.getmtime(s) <= t for s in (sources if sources is not None else _sources()))
+
+
+def build_torch_ops(force: bool = False, verbose: bool = False) -> str:
+    """Compile csrc/torch_ops.cpp into lib/libmhc_torch.so (links libmhc_ops.so
+    next to it and the installed torch); returns the library path."""
+    deps = [TORCH_SRC, LIB] + glob.glob(os.path.join(ROOT, "include", "*.h"))
+    if not force and up_to_date(TORCH_LIB, deps):
+        return TORCH_LIB
+    import torch
+    from torch.utils import cpp_extension as ce
+    cxx = os.environ.get("CXX") or shutil.which("g++") or "g++"
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    inc = [f"-I{p}" for p in ce.include_paths(device_type="cuda")] + ["-I", os.path.join(ROOT, "include")]
+    libdirs = ce.library_paths(device_type="cuda")
+    torch_lib = libdirs[0]
+    tmp = TORCH_LIB + ".tmp"
+    cmd = [cxx, "-O2", "-std=c++17", "-shared", "-fPIC", f"-D_GLIBCXX_USE_CXX11_ABI={abi}", *inc, TORCH_SRC,
+           "-o", tmp, "-L", LIBDIR, "-lmhc_ops", *[f"-L{p}" for p in libdirs],
+           "-lc10", "-lc10_cuda", "-ltorch_cpu", "-ltorch_cuda", "-ltorch", "-lcudart",
+           "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{torch_lib}"]
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"building the torch operators failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+    os.replace(tmp, TORCH_LIB)
+    return TORCH_LIB
 
 
 def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | None = None) -> str:
@@ -67,3 +102,4 @@ def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | N
 if __name__ == "__main__":
     force = "--force" in sys.argv
     print(build(force=force, verbose=True))
+    print(build_torch_ops(force=force, verbose=True))

@@ -50,3 +50,24 @@ def test_autograd_matches_fp64_torch(use_gamma, n, D):
     assert rel(x.grad.float(), xr.grad) < 1e-2
     if not use_gamma:
         assert leaves["gamma"].grad is None
+
+
+def test_torch_compile_of_mhc_pre_matches_eager_bit_for_bit():
+    """mhc_pre under torch.compile: dynamo traces the registered operators
+    (torch.ops.mhc.fwd / bwd, Meta kernels for the shapes) as graph nodes; the
+    compiled forward and backward run the same kernels and must give the
+    eager results bit for bit."""
+    inp = make_inputs(2, 64, 4, 256, seed=23).to("cuda")
+
+    def run(fn):
+        leaves = {k: getattr(inp, k).clone().requires_grad_(True) for k in ("phi", "alpha", "bias", "gamma")}
+        x = inp.x.clone().requires_grad_(True)
+        h_in, h_post, h_res = fn(x, leaves["phi"], leaves["alpha"], leaves["bias"], leaves["gamma"])
+        loss = (h_in.float() * inp.dh_in.float()).sum() + (h_post * inp.dh_post).sum() + (h_res * inp.dh_res).sum()
+        loss.backward()
+        return (h_in, h_post, h_res, x.grad) + tuple(leaves[k].grad for k in ("phi", "alpha", "bias", "gamma"))
+
+    eager = run(mhc_pre)
+    compiled = run(torch.compile(mhc_pre, fullgraph=True))
+    for i, (a, b) in enumerate(zip(eager, compiled)):
+        assert torch.equal(a, b), f"output {i} differs under torch.compile"
