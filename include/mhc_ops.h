@@ -83,7 +83,16 @@ typedef struct mhc_fwd_args {
  *                       dh_in, dh_post, dh_res, gamma, norm_eps=1e-6, hc_eps=1e-6)
  * of the reference (src/backward/golden.py:10-13, returns at :96; Triton twin
  * src/backward/mhc_backward_triton.py:467-473).  gamma may be NULL (all ones).
- * bias and norm_eps are unused by the math, as in the reference. */
+ * bias and norm_eps are unused by the math, as in the reference, except in
+ * the recompute form: with inv_rms, h_mix and h_pre all NULL, mhc_bwd first
+ * runs the forward (the kernels of mhc_fwd, with these phi, alpha, bias and
+ * eps) to recompute them -- a forward that did not store its outflag outputs
+ * (116 bytes per token at n = 4) pays one more read of x and the projection
+ * instead -- and h_post may then be NULL as well.  The recomputed values are
+ * bit for bit those mhc_fwd returns, so the results equal the stored form's.
+ * That form needs mhc_bwd_recompute_workspace_size bytes of workspace and
+ * uses dx as scratch before writing it.  (The reference contract returns
+ * the intermediates from the forward, src/forward/golden.py:65-69.) */
 typedef struct mhc_bwd_args {
   const uint16_t* x;
   const float* phi;
@@ -166,6 +175,9 @@ MHC_API int mhc_bwd_workspace_size(int64_t tokens, int32_t n, int32_t D, size_t*
  * repeated calls return identical bytes. */
 MHC_API int mhc_bwd(const mhc_bwd_args* args, void* stream);
 
+/* Workspace bytes mhc_bwd needs when it recomputes the forward's
+ * intermediates (inv_rms, h_mix and h_pre all NULL), on the current device. */
+MHC_API int mhc_bwd_recompute_workspace_size(int64_t tokens, int32_t n, int32_t D, size_t* bytes);
 /* Reads (and clears) the device status word a previous mhc_fwd / mhc_bwd
  * left in `workspace`; synchronizes `stream`.  *device_status receives
  * MHC_OK or MHC_ERR_DEVICE_TIMEOUT.  No counterpart in the reference, which
@@ -259,7 +271,8 @@ MHC_API int mhc_post_bwd(const mhc_post_bwd_args* args, void* stream);
 MHC_API uint64_t mhc_launch_count(void);
 
 /* Version of this ABI (major*10000 + minor*100 + patch).  1.1.0 added the
- * post-op and the device-free plan queries. */
+ * post-op and the device-free plan queries, 1.2.0 the backward that
+ * recomputes the forward's intermediates. */
 MHC_API int mhc_abi_version(void);
 
 #ifdef __cplusplus

@@ -74,6 +74,8 @@ SIGNATURES = {
     "mhc_bwd_workspace_size": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
                                               ctypes.POINTER(ctypes.c_size_t)]),
     "mhc_bwd": (ctypes.c_int, [ctypes.POINTER(BwdArgs), _c_void_p]),
+    "mhc_bwd_recompute_workspace_size": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                                        ctypes.POINTER(ctypes.c_size_t)]),
     "mhc_read_device_status": (ctypes.c_int, [_c_void_p, _c_void_p, ctypes.POINTER(ctypes.c_int)]),
     "mhc_selftest_wait_expiry": (ctypes.c_int, [_c_void_p, _c_void_p]),
     "mhc_query_plan": (ctypes.c_int, [ctypes.c_int, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
@@ -222,9 +224,13 @@ def fwd_workspace_size(tokens: int, n: int, D: int) -> int:
     return int(out.value)
 
 
-def bwd_workspace_size(tokens: int, n: int, D: int) -> int:
+def bwd_workspace_size(tokens: int, n: int, D: int, recompute: bool = False) -> int:
     out = ctypes.c_size_t(0)
-    check(load().mhc_bwd_workspace_size(tokens, n, D, ctypes.byref(out)), "mhc_bwd_workspace_size")
+    if recompute:
+        check(load().mhc_bwd_recompute_workspace_size(tokens, n, D, ctypes.byref(out)),
+              "mhc_bwd_recompute_workspace_size")
+    else:
+        check(load().mhc_bwd_workspace_size(tokens, n, D, ctypes.byref(out)), "mhc_bwd_workspace_size")
     return int(out.value)
 
 

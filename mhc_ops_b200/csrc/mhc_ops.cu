@@ -794,6 +794,41 @@ int bwd_workspace(int64_t T, int n, int D, int sms, size_t* bytes) {
   return MHC_OK;
 }
 
+// ----------------------------------------------------------------- backward that recomputes the forward's intermediates
+// mhc_bwd with inv_rms, h_mix and h_pre NULL runs the forward first (the same
+// kernels as mhc_fwd, so the intermediates are the ones a forward with outflag
+// would have returned, bit for bit), then the backward.  Workspace: [0,
+// shared) serves the forward and then the backward (used one after the other
+// on the stream, so they share their bytes and their status word), then
+// inv_rms [T], h_mix [T][N], h_pre [T][n], h_post [T][n], h_res [T][n][n].
+// The forward's h_in goes to the first T*D elements of dx, which the backward
+// then overwrites.
+struct BwdRecomputeLayout {
+  size_t shared, inv_rms, h_mix, h_pre, h_post, h_res, total;
+};
+
+BwdRecomputeLayout bwd_recompute_layout(int64_t T, int n, int D, int sms) {
+  BwdRecomputeLayout L{};
+  size_t fw = 0, bw = 0;
+  fwd_workspace(T, n, D, &fw);
+  bwd_workspace(T, n, D, sms, &bw);
+  const size_t N = (size_t)n * n + 2 * (size_t)n;
+  size_t off = align_up(std::max(fw, bw), kWsAlign);
+  L.shared = off;
+  L.inv_rms = off;
+  off = align_up(off + sizeof(float) * (size_t)T, kWsAlign);
+  L.h_mix = off;
+  off = align_up(off + sizeof(float) * (size_t)T * N, kWsAlign);
+  L.h_pre = off;
+  off = align_up(off + sizeof(float) * (size_t)T * n, kWsAlign);
+  L.h_post = off;
+  off = align_up(off + sizeof(float) * (size_t)T * n, kWsAlign);
+  L.h_res = off;
+  off = align_up(off + sizeof(float) * (size_t)T * n * n, kWsAlign);
+  L.total = off;
+  return L;
+}
+
 // ----------------------------------------------------------------- bounded-wait self test
 // One thread runs, one after the other, the two bounded waits the kernels
 // use, each on something that never completes: mbar_wait on an mbarrier
@@ -965,7 +1000,7 @@ const char* mhc_status_string(int status) {
 
 const char* mhc_last_cuda_error(void) { return t_last_cuda_error.c_str(); }
 
-int mhc_abi_version(void) { return 10100; }
+int mhc_abi_version(void) { return 10200; }
 
 uint64_t mhc_launch_count(void) { return g_launch_count.load(std::memory_order_relaxed); }
 
@@ -1018,8 +1053,10 @@ int mhc_bwd(const mhc_bwd_args* a, void* stream) {
   if (!a->workspace) return MHC_ERR_NULL_POINTER;
   int sms = 0;
   if ((st = current_sm_count(&sms))) return st;
+  const bool recompute = !a->inv_rms && !a->h_mix && !a->h_pre;
   size_t need = 0;
-  if ((st = bwd_workspace(a->tokens, a->n, a->D, sms, &need))) return st;
+  if (recompute) need = bwd_recompute_layout(a->tokens, a->n, a->D, sms).total;
+  else if ((st = bwd_workspace(a->tokens, a->n, a->D, sms, &need))) return st;
   if (a->workspace_bytes < need) return MHC_ERR_WORKSPACE_TOO_SMALL;
   if (!aligned(a->workspace, kWsAlign)) return MHC_ERR_MISALIGNED;
   if (!a->dphi || !a->dalpha || !a->dbias || !a->dgamma || !a->alpha || !a->phi) return MHC_ERR_NULL_POINTER;
@@ -1031,6 +1068,38 @@ int mhc_bwd(const mhc_bwd_args* a, void* stream) {
     MHC_CUDA_TRY(cudaMemsetAsync(a->dalpha, 0, sizeof(float) * 3, s));
     MHC_CUDA_TRY(cudaMemsetAsync(a->dbias, 0, sizeof(float) * (size_t)N, s));
     return MHC_OK;
+  }
+  if (recompute) {
+    // the forward into the workspace, then the backward from its intermediates
+    if (!a->x || !a->bias || !a->dx) return MHC_ERR_NULL_POINTER;
+    const BwdRecomputeLayout L = bwd_recompute_layout(a->tokens, a->n, a->D, sms);
+    char* ws = static_cast<char*>(a->workspace);
+    mhc_fwd_args f{};
+    f.x = a->x;
+    f.phi = a->phi;
+    f.alpha = a->alpha;
+    f.bias = a->bias;
+    f.h_in = a->dx;
+    f.h_post = reinterpret_cast<float*>(ws + L.h_post);
+    f.h_res = reinterpret_cast<float*>(ws + L.h_res);
+    f.inv_rms = reinterpret_cast<float*>(ws + L.inv_rms);
+    f.h_mix = reinterpret_cast<float*>(ws + L.h_mix);
+    f.h_pre = reinterpret_cast<float*>(ws + L.h_pre);
+    f.tokens = a->tokens;
+    f.n = a->n;
+    f.D = a->D;
+    f.norm_eps = a->norm_eps;
+    f.hc_eps = a->hc_eps;
+    f.workspace = a->workspace;
+    f.workspace_bytes = L.shared;
+    if ((st = mhc_fwd(&f, stream))) return st;
+    mhc_bwd_args b = *a;
+    b.inv_rms = f.inv_rms;
+    b.h_mix = f.h_mix;
+    b.h_pre = f.h_pre;
+    if (!b.h_post) b.h_post = f.h_post;
+    b.workspace_bytes = L.shared;
+    return mhc_bwd(&b, stream);
   }
   if (!a->x || !a->inv_rms || !a->h_mix || !a->h_pre || !a->h_post || !a->dh_in || !a->dh_post ||
       !a->dh_res || !a->dx)
@@ -1093,6 +1162,16 @@ int mhc_query_plan_for(int which, int64_t tokens, int32_t n, int32_t D, int32_t 
   if (st) return st;
   if (sms < 1 || sms > 4096) return MHC_ERR_BAD_SHAPE;
   return query_plan_impl(which, tokens, n, D, sms, n == 4, path, cluster_size, clusters);
+}
+
+int mhc_bwd_recompute_workspace_size(int64_t tokens, int32_t n, int32_t D, size_t* bytes) {
+  if (!bytes) return MHC_ERR_NULL_POINTER;
+  int st = check_shape(tokens, n, D);
+  if (st) return st;
+  int sms = 0;
+  if ((st = current_sm_count(&sms))) return st;
+  *bytes = bwd_recompute_layout(tokens, n, D, sms).total;
+  return MHC_OK;
 }
 
 int mhc_bwd_workspace_size_for(int64_t tokens, int32_t n, int32_t D, int32_t sms, size_t* bytes) {

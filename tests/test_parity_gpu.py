@@ -240,3 +240,31 @@ def test_eight_gpu_row_width_vs_oracle():
     """The 8-GPU configuration's row width, n=4, D=7168, over 4096 tokens
     (one GPU's share of B=8,S=4096 at 8 GPUs): every token against the oracle."""
     _full_batch_vs_oracle(1, 4096, 4, 7168, seed=22, shard=1024, tag="8gpu n4 D7168")
+
+
+@pytest.mark.parametrize("B,S,n,D", [(4, 4096, 4, 4096), (1, 300, 8, 1024), (1, 50, 3, 24), (1, 130, 4, 1024)])
+def test_backward_recomputing_intermediates_equals_stored_form(B, S, n, D):
+    """mhc_backward_manual with inv_rms, h_mix, h_pre (and h_post) None runs the
+    forward kernels first: the gradients must equal, bit for bit, those of the
+    backward given the intermediates mhc_forward_pre(outflag=True) stored
+    (src/forward/golden.py:65-69 is the stored contract); and, on a token
+    sample, the oracle."""
+    inp = make_inputs(B, S, n, D, seed=31)
+    d = inp.to(DEV)
+    out = mhc_forward_pre(d.x, d.phi, d.alpha, d.bias, outflag=True)
+    stored = mhc_backward_manual(d.x, d.phi, d.alpha, d.bias, out[3], out[4], out[5], out[1], d.dh_in, d.dh_post,
+                                 d.dh_res, d.gamma)
+    recomputed = mhc_backward_manual(d.x, d.phi, d.alpha, d.bias, None, None, None, None, d.dh_in, d.dh_post,
+                                     d.dh_res, d.gamma)
+    torch.cuda.synchronize()
+    for i, (a, b) in enumerate(zip(stored, recomputed)):
+        assert torch.equal(a, b), f"output {i} of the recomputing backward differs"
+    if B * S <= 2048:
+        ref_f = O.forward(bits(inp.x), inp.phi.numpy(), inp.alpha.numpy(), inp.bias.numpy(), outflag=True)
+        ref_b = O.backward(bits(inp.x), inp.phi.numpy(), inp.alpha.numpy(), inp.bias.numpy(), ref_f[3], ref_f[4],
+                           ref_f[5], ref_f[1], bits(inp.dh_in), inp.dh_post.numpy(), inp.dh_res.numpy(),
+                           inp.gamma.numpy())
+        scale = O.backward_term_scale(bits(inp.x), inp.phi.numpy(), inp.alpha.numpy(), ref_f[3], ref_f[4], ref_f[5],
+                                      ref_f[1], bits(inp.dh_in), inp.dh_post.numpy(), inp.dh_res.numpy(),
+                                      inp.gamma.numpy())
+        assert_bwd_close(recomputed, ref_b, scale, tag=f"recompute {B}x{S}x{n}x{D}")
