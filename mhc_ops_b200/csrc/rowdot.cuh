@@ -267,8 +267,19 @@ __device__ __forceinline__ float fwd_row_gates(const FwdRowArgs& a, const FwdRow
   for (int m = 0; m < M; ++m) {
     const int c = lane + 32 * m;
     float acc = 0.f;
-    if (c <= N_OUT)
-      for (int ks = 0; ks < a.S_K; ++ks) acc += pr[ks * a.RW + c];
+    if (c <= N_OUT) {
+      // kBatch loads in flight before their adds (still in slice order): the
+      // partials come from L2, and one round trip per slice would dominate
+      // the token's time.  Slices past S_K add an exact 0.
+      constexpr int kBatch = 16;
+      for (int k0 = 0; k0 < a.S_K; k0 += kBatch) {
+        float v[kBatch];
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) v[b] = k0 + b < a.S_K ? pr[(k0 + b) * a.RW + c] : 0.f;
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) acc += v[b];
+      }
+    }
     hm[m] = acc;
   }
   const float sq = __shfl_sync(0xffffffffu, hm[N_OUT / 32], N_OUT % 32);
