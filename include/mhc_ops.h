@@ -163,6 +163,27 @@ MHC_API int mhc_fwd(const mhc_fwd_args* args, void* stream);
  *   point returns.  Use mhc_fwd and mhc_read_device_status when you need it. */
 MHC_API int mhc_fwd_static(const mhc_fwd_args* args, void* stream);
 
+/* Options of mhc_fwd_ex.  Each is off when its pointer is NULL.
+ *   phi_bf16: phi given as bf16 bit patterns [N, nD] instead of fp32
+ *     (args->phi is then ignored and may be NULL).  A bf16 phi is exact in
+ *     one bf16 term, so the projection runs one tensor-core product per
+ *     K-step instead of the three (n <= 5) or two of an fp32 phi.
+ *   h_in_rstd: [T] f32 output, 1 / sqrt(mean_d(h_in[t,d]^2) + h_in_eps) over
+ *     the bf16 h_in row: the factor of the RMSNorm that opens the next
+ *     sublayer, computed while h_in is written, so that sublayer need not
+ *     read h_in once more to reduce it.
+ * No counterpart in the reference (its forward takes fp32 phi and stops at
+ * h_in, src/forward/golden.py:41,62-63). */
+typedef struct mhc_fwd_ex_args {
+  const uint16_t* phi_bf16;
+  float* h_in_rstd;
+  float h_in_eps;
+} mhc_fwd_ex_args;
+/* Workspace bytes mhc_fwd_ex needs with these options (ex may be NULL). */
+MHC_API int mhc_fwd_ex_workspace_size(const mhc_fwd_ex_args* ex, int64_t tokens, int32_t n, int32_t D,
+                                      size_t* bytes);
+/* mhc_fwd with the options above (ex may be NULL: then exactly mhc_fwd). */
+MHC_API int mhc_fwd_ex(const mhc_fwd_args* args, const mhc_fwd_ex_args* ex, void* stream);
 /* Workspace bytes mhc_bwd needs for this shape on the current device.
  * Replaces the intermediates the Triton backward allocates
  * (src/backward/mhc_backward_triton.py:509-510). */
@@ -272,7 +293,7 @@ MHC_API uint64_t mhc_launch_count(void);
 
 /* Version of this ABI (major*10000 + minor*100 + patch).  1.1.0 added the
  * post-op and the device-free plan queries, 1.2.0 the backward that
- * recomputes the forward's intermediates. */
+ * recomputes the forward's intermediates and mhc_fwd_ex. */
 MHC_API int mhc_abi_version(void);
 
 #ifdef __cplusplus

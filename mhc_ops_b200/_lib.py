@@ -32,6 +32,11 @@ class FwdArgs(ctypes.Structure):
     ]
 
 
+class FwdExArgs(ctypes.Structure):
+    """Mirror of ``mhc_fwd_ex_args`` (include/mhc_ops.h)."""
+    _fields_ = [("phi_bf16", _c_void_p), ("h_in_rstd", _c_void_p), ("h_in_eps", ctypes.c_float)]
+
+
 class BwdArgs(ctypes.Structure):
     """Mirror of ``mhc_bwd_args`` (include/mhc_ops.h)."""
     _fields_ = [
@@ -71,6 +76,9 @@ SIGNATURES = {
                                               ctypes.POINTER(ctypes.c_size_t)]),
     "mhc_fwd": (ctypes.c_int, [ctypes.POINTER(FwdArgs), _c_void_p]),
     "mhc_fwd_static": (ctypes.c_int, [ctypes.POINTER(FwdArgs), _c_void_p]),
+    "mhc_fwd_ex_workspace_size": (ctypes.c_int, [ctypes.POINTER(FwdExArgs), ctypes.c_int64, ctypes.c_int32,
+                                                 ctypes.c_int32, ctypes.POINTER(ctypes.c_size_t)]),
+    "mhc_fwd_ex": (ctypes.c_int, [ctypes.POINTER(FwdArgs), ctypes.POINTER(FwdExArgs), _c_void_p]),
     "mhc_bwd_workspace_size": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
                                               ctypes.POINTER(ctypes.c_size_t)]),
     "mhc_bwd": (ctypes.c_int, [ctypes.POINTER(BwdArgs), _c_void_p]),
@@ -218,9 +226,13 @@ def check_device_status(device=None) -> None:
             ws.raise_if_timed_out(wait=True)
 
 
-def fwd_workspace_size(tokens: int, n: int, D: int) -> int:
+def fwd_workspace_size(tokens: int, n: int, D: int, ex: "FwdExArgs | None" = None) -> int:
     out = ctypes.c_size_t(0)
-    check(load().mhc_fwd_workspace_size(tokens, n, D, ctypes.byref(out)), "mhc_fwd_workspace_size")
+    if ex is None:
+        check(load().mhc_fwd_workspace_size(tokens, n, D, ctypes.byref(out)), "mhc_fwd_workspace_size")
+    else:
+        check(load().mhc_fwd_ex_workspace_size(ctypes.byref(ex), tokens, n, D, ctypes.byref(out)),
+              "mhc_fwd_ex_workspace_size")
     return int(out.value)
 
 

@@ -72,10 +72,14 @@ constexpr int pow2_at_least(int v) {
   return p;
 }
 
-template <int n>
+// Split terms of an fp32 phi: three at n <= 5, two above (see the top of
+// this file).  A phi given in bf16 is exact in one term.
+constexpr int default_terms(int n) { return n <= 5 ? 3 : 2; }
+
+template <int n, int kNT = default_terms(n)>
 struct Cfg {
   static constexpr int N_OUT = n * n + 2 * n;
-  static constexpr int NT = (n <= 5) ? 3 : 2;              // phi split terms
+  static constexpr int NT = kNT;                           // phi split terms
   static constexpr int NB = round_up(NT * N_OUT, 16);      // UMMA N
   static constexpr int RW = round_up(N_OUT + 1, 8);        // floats per partial row (whole 32-byte sectors)
   static constexpr int A_BYTES = kBM * 128;
@@ -115,9 +119,9 @@ struct Params {
   rowdot::FwdRowArgs rows;
 };
 
-template <int n>
+template <int n, int kNT>
 struct Bars {
-  using Cf = Cfg<n>;
+  using Cf = Cfg<n, kNT>;
   static constexpr int full = 0;
   static constexpr int empty = full + Cf::S;
   static constexpr int acc_full = empty + Cf::S;
@@ -173,12 +177,12 @@ __device__ __forceinline__ void wait_rows_done(volatile int* rows_done, int need
   }
 }
 
-template <int n, bool kFused>
+template <int n, bool kFused, int kNT = default_terms(n)>
 __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
     proj_kernel(const __grid_constant__ CUtensorMap map_x2d, const __grid_constant__ CUtensorMap map_phi,
                 const Params p) {
-  using Cf = Cfg<n>;
-  using B = Bars<n>;
+  using Cf = Cfg<n, kNT>;
+  using B = Bars<n, kNT>;
   constexpr int N_OUT = Cf::N_OUT;
   constexpr int S = Cf::S;
 
@@ -432,15 +436,18 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
 
 // phi [N_OUT, nD] f32 -> phis [NB, nD] bf16: rows t*N_OUT + j hold the t-th
 // bf16 term of phi[j] (hi, mid, lo: each term rounds what the previous ones
-// left), rows >= NT*N_OUT are zero.  Also zeroes the fused forward's tile
-// counters (tile_done may be null).
-template <int n>
-__global__ void __launch_bounds__(256) split_phi_kernel(const float* __restrict__ phi, uint16_t* __restrict__ phis,
-                                                        int nD, int* __restrict__ tile_done, int tiles) {
+// left), rows >= NT*N_OUT are zero.  With phi_bf16 given (phi unused) the
+// rows are its bits: one exact term (NT = 1).  Also zeroes the fused
+// forward's tile counters (tile_done may be null).
+template <int n, int kNT = default_terms(n)>
+__global__ void __launch_bounds__(256) split_phi_kernel(const float* __restrict__ phi,
+                                                        const uint16_t* __restrict__ phi_bf16,
+                                                        uint16_t* __restrict__ phis, int nD,
+                                                        int* __restrict__ tile_done, int tiles) {
   // phis [NB][nD]: row term*N_OUT + j holds bf16 term `term` of phi[j]; rows
   // past NT*N_OUT are zero.  Each thread writes 8 consecutive k (one 16-byte
   // store); needs nD % 8 == 0.
-  using Cf = Cfg<n>;
+  using Cf = Cfg<n, kNT>;
   if (tile_done)
     for (int64_t i = blockIdx.x * 256ll + threadIdx.x; i < tiles; i += (int64_t)gridDim.x * 256) tile_done[i] = 0;
   const int64_t per_row = nD / 8;
@@ -449,7 +456,15 @@ __global__ void __launch_bounds__(256) split_phi_kernel(const float* __restrict_
     const int r = (int)(idx / per_row);
     const int64_t k = (idx - (int64_t)r * per_row) * 8;
     uint32_t w[4] = {0, 0, 0, 0};
-    if (r < Cf::NT * Cf::N_OUT) {
+    if (phi_bf16 != nullptr) {
+      if (r < Cf::N_OUT) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(phi_bf16 + (int64_t)r * nD + k));
+        w[0] = v.x;
+        w[1] = v.y;
+        w[2] = v.z;
+        w[3] = v.w;
+      }
+    } else if (r < Cf::NT * Cf::N_OUT) {
       const int term = r / Cf::N_OUT, j = r - term * Cf::N_OUT;
       const float4 a = __ldg(reinterpret_cast<const float4*>(phi + (int64_t)j * nD + k));
       const float4 b = __ldg(reinterpret_cast<const float4*>(phi + (int64_t)j * nD + k + 4));

@@ -47,7 +47,8 @@ __global__ void __launch_bounds__(kThreads) fwd_kernel(
     const uint16_t* __restrict__ x, const float* __restrict__ phi, const float* __restrict__ alpha,
     const float* __restrict__ bias, uint16_t* __restrict__ h_in, float* __restrict__ h_post,
     float* __restrict__ h_res, float* __restrict__ inv_rms_out, float* __restrict__ h_mix_out,
-    float* __restrict__ h_pre_out, int64_t T, int D, float norm_eps, float hc_eps) {
+    float* __restrict__ h_pre_out, int64_t T, int D, float norm_eps, float hc_eps,
+    float* __restrict__ h_in_rstd = nullptr, float h_in_eps = 0.f) {
   constexpr int N = Dims<n>::N;
   const int nD = n * D;
   __shared__ float red[kWarps * (N + 1)];
@@ -82,13 +83,22 @@ __global__ void __launch_bounds__(kThreads) fwd_kernel(
       for (int m = 0; m < n * n; ++m) h_res[t * n * n + m] = a_res * (tot[2 * n + m] * ir) + bias[2 * n + m];
     }
     __syncthreads();
+    float sq[1] = {0.f};   // sum of the bf16 h_in values squared (h_in_rstd)
     for (int d = threadIdx.x; d < D; d += kThreads) {
       float s = 0.f;
 #pragma unroll
       for (int i = 0; i < n; ++i) s = fmaf(hpre_s[i], bf16_bits_to_f32(xr[i * D + d]), s);
-      h_in[t * D + d] = f32_to_bf16_bits(s);
+      const uint16_t b = f32_to_bf16_bits(s);
+      h_in[t * D + d] = b;
+      const float r = bf16_bits_to_f32(b);
+      sq[0] = fmaf(r, r, sq[0]);
     }
     __syncthreads();
+    if (h_in_rstd) {
+      block_sum<1>(sq, red, tot);
+      if (threadIdx.x == 0) h_in_rstd[t] = 1.0f / sqrtf(tot[0] / (float)D + h_in_eps);
+      __syncthreads();
+    }
   }
 }
 

@@ -107,17 +107,31 @@ BwdGenericLayout bwd_generic_layout(int64_t T, int n, int D, int sms) {
 }
 
 // ----------------------------------------------------------------- generic runners
+// Options of mhc_fwd_ex (all off for mhc_fwd): phi given as bf16 instead of
+// fp32; the per-token RMSNorm factor of h_in for the next sublayer.
+struct FwdEx {
+  const uint16_t* phi_bf16 = nullptr;
+  float* h_in_rstd = nullptr;
+  float h_in_eps = 0.f;
+};
+
 template <int n>
 struct FwdGeneric {
-  static int run(const mhc_fwd_args* a, cudaStream_t s, int sms) {
+  static int run(const mhc_fwd_args* a, const float* phi, const FwdEx& ex, cudaStream_t s, int sms) {
     const int64_t T = a->tokens;
     const int grid = (int)std::min<int64_t>(T, (int64_t)sms * 8);
     generic::fwd_kernel<n><<<grid, generic::kThreads, 0, s>>>(
-        a->x, a->phi, a->alpha, a->bias, a->h_in, a->h_post, a->h_res, a->inv_rms, a->h_mix, a->h_pre, T,
-        a->D, a->norm_eps, a->hc_eps);
+        a->x, phi, a->alpha, a->bias, a->h_in, a->h_post, a->h_res, a->inv_rms, a->h_mix, a->h_pre, T,
+        a->D, a->norm_eps, a->hc_eps, ex.h_in_rstd, ex.h_in_eps);
     return after_launch();
   }
 };
+
+// bf16 phi -> an fp32 copy, for the generic forward (exact widening).
+__global__ void phi_widen_kernel(const uint16_t* __restrict__ src, float* __restrict__ dst, int64_t count) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = bf16_bits_to_f32(src[i]);
+}
 
 template <int n>
 struct BwdGeneric {
@@ -225,12 +239,15 @@ bool fwd_tc_shape(int64_t T, int n, int D) {
   return 2 * D >= fwd_part_row_bytes(n);
 }
 
-bool fwd_tc_eligible(const mhc_fwd_args* a) {
-  return fwd_tc_shape(a->tokens, a->n, a->D) && aligned(a->x, 16) && aligned(a->h_in, 16) && aligned(a->phi, 16);
+bool fwd_tc_eligible(const mhc_fwd_args* a, const FwdEx& ex) {
+  const void* phi = ex.phi_bf16 ? static_cast<const void*>(ex.phi_bf16) : static_cast<const void*>(a->phi);
+  return fwd_tc_shape(a->tokens, a->n, a->D) && aligned(a->x, 16) && aligned(a->h_in, 16) && aligned(phi, 16);
 }
 
-size_t fwd_tc_phis_bytes(int n, int D) {
-  const int NB = n == 4 ? fwdtc::Cfg<4>::NB : fwdtc::Cfg<8>::NB;
+// Bytes of the bf16 term images of phi (one term when phi comes in bf16).
+size_t fwd_tc_phis_bytes(int n, int D, bool bf16_phi) {
+  const int NB = n == 4 ? (bf16_phi ? fwdtc::Cfg<4, 1>::NB : fwdtc::Cfg<4>::NB)
+                        : (bf16_phi ? fwdtc::Cfg<8, 1>::NB : fwdtc::Cfg<8>::NB);
   return (size_t)NB * n * D * sizeof(uint16_t);
 }
 
@@ -260,9 +277,9 @@ int fwd_fused_slices(int n, int D) {
   return 0;
 }
 
-// Whether proj_kernel<n, true> can run with one CTA on every SM at once (a
-// cooperative launch needs that); asked once per device.
-template <int n>
+// Whether proj_kernel<n, true, NT> can run with one CTA on every SM at once
+// (a cooperative launch needs that); asked once per device.
+template <int n, int NT>
 bool fwd_fused_supported() {
   static std::mutex mu;
   static std::map<int, bool> known;
@@ -273,10 +290,10 @@ bool fwd_fused_supported() {
   if (it != known.end()) return it->second;
   int coop = 0, blocks = 0;
   bool ok = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) == cudaSuccess && coop &&
-            cudaFuncSetAttribute(fwdtc::proj_kernel<n, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 fwdtc::Cfg<n>::SMEM) == cudaSuccess &&
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fwdtc::proj_kernel<n, true>,
-                                                          fwdtc::kThreadsFused, fwdtc::Cfg<n>::SMEM) == cudaSuccess &&
+            cudaFuncSetAttribute(fwdtc::proj_kernel<n, true, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 fwdtc::Cfg<n, NT>::SMEM) == cudaSuccess &&
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fwdtc::proj_kernel<n, true, NT>,
+                                                          fwdtc::kThreadsFused, fwdtc::Cfg<n, NT>::SMEM) == cudaSuccess &&
             blocks >= 1;
   (void)cudaGetLastError();
   known[dev] = ok;
@@ -285,7 +302,9 @@ bool fwd_fused_supported() {
 
 // n = 8 never qualifies (its K-slices of at most kFusedKbPer blocks need more
 // partial rows than an h_in row holds), so only n = 4 is instantiated.
-bool fwd_fused_supported(int n) { return n == 4 && fwd_fused_supported<4>(); }
+bool fwd_fused_supported(int n, bool bf16_phi = false) {
+  return n == 4 && (bf16_phi ? fwd_fused_supported<4, 1>() : fwd_fused_supported<4, fwdtc::default_terms(4)>());
+}
 
 // Two-kernel form: the fewest K-slices (a divisor of the n*D/64 K-blocks, at
 // most 16, and no more than an h_in row holds) that give every SM at least
@@ -314,8 +333,8 @@ FwdTcPlan fwd_tc_plan_with(int64_t T, int n, int D, int sms, bool fused_ok) {
   return P;
 }
 
-FwdTcPlan fwd_tc_plan(int64_t T, int n, int D, int sms) {
-  return fwd_tc_plan_with(T, n, D, sms, fwd_fused_supported(n));
+FwdTcPlan fwd_tc_plan(int64_t T, int n, int D, int sms, bool bf16_phi) {
+  return fwd_tc_plan_with(T, n, D, sms, fwd_fused_supported(n, bf16_phi));
 }
 
 size_t fwd_tile_counter_bytes(int64_t T) {
@@ -326,15 +345,15 @@ int fwd_rows_grid(int64_t T, int sms) {
   return (int)std::max<int64_t>(1, std::min<int64_t>(sms, (T + rowdot::kWarps - 1) / rowdot::kWarps));
 }
 
-template <int n>
+template <int n, int NT>
 struct FwdTc {
-  // One cooperative launch of proj_kernel<n, true> (all CTAs co-resident:
+  // One cooperative launch of proj_kernel<n, true, NT> (all CTAs co-resident:
   // row warps wait on counters other CTAs advance).
   static int launch_fused(const CUtensorMap& m_x2d, const CUtensorMap& m_phi, const fwdtc::Params& p,
                           const FwdTcPlan& P, cudaStream_t s) {
-    using Cf = fwdtc::Cfg<n>;
+    using Cf = fwdtc::Cfg<n, NT>;
     int st;
-    if ((st = set_smem_limit_once(fwdtc::proj_kernel<n, true>, Cf::SMEM))) return st;
+    if ((st = set_smem_limit_once(fwdtc::proj_kernel<n, true, NT>, Cf::SMEM))) return st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
@@ -345,24 +364,27 @@ struct FwdTc {
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    MHC_CUDA_TRY(cudaLaunchKernelEx(&cfg, fwdtc::proj_kernel<n, true>, m_x2d, m_phi, p));
+    MHC_CUDA_TRY(cudaLaunchKernelEx(&cfg, fwdtc::proj_kernel<n, true, NT>, m_x2d, m_phi, p));
     return after_launch();
   }
 
-  static int run(const mhc_fwd_args* a, cudaStream_t s, int sms) {
-    using Cf = fwdtc::Cfg<n>;
+  static int run(const mhc_fwd_args* a, const FwdEx& ex, cudaStream_t s, int sms) {
+    using Cf = fwdtc::Cfg<n, NT>;
+    const bool bf16_phi = ex.phi_bf16 != nullptr;
     const int64_t T = a->tokens;
     const int D = a->D;
     const int nD = n * D;
     char* ws = static_cast<char*>(a->workspace);
     uint16_t* phis = reinterpret_cast<uint16_t*>(ws + kWsHeaderBytes);
-    int* tile_done = reinterpret_cast<int*>(ws + align_up(kWsHeaderBytes + fwd_tc_phis_bytes(n, D), kWsAlign));
-    const FwdTcPlan P = fwd_tc_plan(T, n, D, sms);
+    int* tile_done =
+        reinterpret_cast<int*>(ws + align_up(kWsHeaderBytes + fwd_tc_phis_bytes(n, D, bf16_phi), kWsAlign));
+    const FwdTcPlan P = fwd_tc_plan(T, n, D, sms, bf16_phi);
     const int tiles = (int)((T + fwdtc::kBM - 1) / fwdtc::kBM);
     int st;
 
-    fwdtc::split_phi_kernel<n><<<std::min<int64_t>(((int64_t)Cf::NB * nD / 8 + 255) / 256, 4 * 148), 256, 0, s>>>(
-        a->phi, phis, nD, P.fused ? tile_done : nullptr, tiles);
+    fwdtc::split_phi_kernel<n, NT>
+        <<<std::min<int64_t>(((int64_t)Cf::NB * nD / 8 + 255) / 256, 4 * 148), 256, 0, s>>>(
+            a->phi, ex.phi_bf16, phis, nD, P.fused ? tile_done : nullptr, tiles);
     if ((st = after_launch())) return st;
 
     CUtensorMap m_x2d, m_phi;
@@ -399,13 +421,15 @@ struct FwdTc {
     p.rows.D = D;
     p.rows.S_K = P.S_K;
     p.rows.RW = Cf::RW;
+    p.rows.h_in_rstd = ex.h_in_rstd;
     p.rows.norm_eps = a->norm_eps;
     p.rows.hc_eps = a->hc_eps;
+    p.rows.h_in_eps = ex.h_in_eps;
     if constexpr (n == 4) {
       if (P.fused) return launch_fused(m_x2d, m_phi, p, P, s);
     }
-    if ((st = set_smem_limit_once(fwdtc::proj_kernel<n, false>, Cf::SMEM))) return st;
-    fwdtc::proj_kernel<n, false><<<P.grid, fwdtc::kThreads, Cf::SMEM, s>>>(m_x2d, m_phi, p);
+    if ((st = set_smem_limit_once(fwdtc::proj_kernel<n, false, NT>, Cf::SMEM))) return st;
+    fwdtc::proj_kernel<n, false, NT><<<P.grid, fwdtc::kThreads, Cf::SMEM, s>>>(m_x2d, m_phi, p);
     if ((st = after_launch())) return st;
     rowdot::fwd_rows_kernel<n><<<fwd_rows_grid(T, sms), rowdot::kThreads, 0, s>>>(p.rows, T);
     return after_launch();
@@ -413,15 +437,42 @@ struct FwdTc {
 };
 
 // Header (status word), split-phi images, then the fused form's per-tile
-// counters.
-int fwd_workspace(int64_t T, int n, int D, size_t* bytes) {
+// counters; with a bf16 phi, last, the fp32 copy the generic kernels read.
+size_t fwd_phi_copy_offset(int64_t T, int n, int D, bool bf16_phi) {
   size_t b = kWsHeaderBytes;
   if (fwd_tc_shape(T, n, D)) {
-    b = align_up(b + fwd_tc_phis_bytes(n, D), kWsAlign);
+    b = align_up(b + fwd_tc_phis_bytes(n, D, bf16_phi), kWsAlign);
     b = align_up(b + fwd_tile_counter_bytes(T), kWsAlign);
   }
+  return b;
+}
+
+int fwd_workspace(int64_t T, int n, int D, size_t* bytes, bool bf16_phi = false) {
+  size_t b = fwd_phi_copy_offset(T, n, D, bf16_phi);
+  if (bf16_phi) b = align_up(b + sizeof(float) * (size_t)(n * n + 2 * n) * n * D, kWsAlign);
   *bytes = b;
   return MHC_OK;
+}
+
+// The forward, any shape (arguments already validated).
+int fwd_run(const mhc_fwd_args* a, const FwdEx& ex, cudaStream_t s, int sms) {
+  const bool bf16_phi = ex.phi_bf16 != nullptr;
+  if (fwd_tc_eligible(a, ex)) {
+    if (a->n == 4) return bf16_phi ? FwdTc<4, 1>::run(a, ex, s, sms) : FwdTc<4, 3>::run(a, ex, s, sms);
+    return bf16_phi ? FwdTc<8, 1>::run(a, ex, s, sms) : FwdTc<8, 2>::run(a, ex, s, sms);
+  }
+  const float* phi = a->phi;
+  if (bf16_phi) {
+    float* copy = reinterpret_cast<float*>(static_cast<char*>(a->workspace) +
+                                           fwd_phi_copy_offset(a->tokens, a->n, a->D, true));
+    const int64_t count = (int64_t)(a->n * a->n + 2 * a->n) * a->n * a->D;
+    phi_widen_kernel<<<(int)std::min<int64_t>((count + 255) / 256, 4 * (int64_t)sms), 256, 0, s>>>(ex.phi_bf16, copy,
+                                                                                                  count);
+    int st = after_launch();
+    if (st) return st;
+    phi = copy;
+  }
+  return dispatch_n<FwdGeneric>(a->n, a, phi, ex, s, sms);
 }
 
 // ----------------------------------------------------------------- tensor-core backward
@@ -1020,30 +1071,54 @@ int mhc_bwd_workspace_size(int64_t tokens, int32_t n, int32_t D, size_t* bytes) 
   return bwd_workspace(tokens, n, D, sms, bytes);
 }
 
-int mhc_fwd(const mhc_fwd_args* a, void* stream) {
+}  // extern "C"
+
+namespace mhc {
+namespace {
+// mhc_fwd and mhc_fwd_ex: validation, then fwd_run.
+int fwd_entry(const mhc_fwd_args* a, const FwdEx& ex, void* stream) {
   if (!a) return MHC_ERR_NULL_POINTER;
   int st = check_shape(a->tokens, a->n, a->D);
   if (st) return st;
   if (!a->workspace) return MHC_ERR_NULL_POINTER;
+  const bool bf16_phi = ex.phi_bf16 != nullptr;
   size_t need = 0;
-  fwd_workspace(a->tokens, a->n, a->D, &need);
+  fwd_workspace(a->tokens, a->n, a->D, &need, bf16_phi);
   if (a->workspace_bytes < need) return MHC_ERR_WORKSPACE_TOO_SMALL;
   if (!aligned(a->workspace, kWsAlign)) return MHC_ERR_MISALIGNED;
   int sms = 0;
   if ((st = current_sm_count(&sms))) return st;
   if (a->tokens == 0) return MHC_OK;
-  if (!a->x || !a->phi || !a->alpha || !a->bias || !a->h_in || !a->h_post || !a->h_res)
+  if (!a->x || (!a->phi && !bf16_phi) || !a->alpha || !a->bias || !a->h_in || !a->h_post || !a->h_res)
     return MHC_ERR_NULL_POINTER;
   if (!aligned(a->x, 2) || !aligned(a->h_in, 2) || !aligned(a->phi, 4) || !aligned(a->alpha, 4) ||
       !aligned(a->bias, 4) || !aligned(a->h_post, 4) || !aligned(a->h_res, 4) || !aligned(a->inv_rms, 4) ||
-      !aligned(a->h_mix, 4) || !aligned(a->h_pre, 4))
+      !aligned(a->h_mix, 4) || !aligned(a->h_pre, 4) || !aligned(ex.phi_bf16, 2) || !aligned(ex.h_in_rstd, 4))
     return MHC_ERR_MISALIGNED;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (fwd_tc_eligible(a)) {
-    if (a->n == 4) return FwdTc<4>::run(a, s, sms);
-    return FwdTc<8>::run(a, s, sms);
+  return fwd_run(a, ex, static_cast<cudaStream_t>(stream), sms);
+}
+}  // namespace
+}  // namespace mhc
+
+extern "C" {
+
+int mhc_fwd(const mhc_fwd_args* a, void* stream) { return fwd_entry(a, FwdEx{}, stream); }
+
+int mhc_fwd_ex_workspace_size(const mhc_fwd_ex_args* ex, int64_t tokens, int32_t n, int32_t D, size_t* bytes) {
+  if (!bytes) return MHC_ERR_NULL_POINTER;
+  int st = check_shape(tokens, n, D);
+  if (st) return st;
+  return fwd_workspace(tokens, n, D, bytes, ex != nullptr && ex->phi_bf16 != nullptr);
+}
+
+int mhc_fwd_ex(const mhc_fwd_args* a, const mhc_fwd_ex_args* ex, void* stream) {
+  FwdEx e;
+  if (ex) {
+    e.phi_bf16 = ex->phi_bf16;
+    e.h_in_rstd = ex->h_in_rstd;
+    e.h_in_eps = ex->h_in_eps;
   }
-  return dispatch_n<FwdGeneric>(a->n, a, s, sms);
+  return fwd_entry(a, e, stream);
 }
 
 int mhc_bwd(const mhc_bwd_args* a, void* stream) {

@@ -232,8 +232,9 @@ struct FwdRowArgs {
   float* inv_rms;   // optional
   float* h_mix;     // optional
   float* h_pre;     // optional
+  float* h_in_rstd; // optional: 1/sqrt(mean(h_in^2) + h_in_eps) over the bf16 row, the next RMSNorm's factor
   int D, S_K, RW;
-  float norm_eps, hc_eps;
+  float norm_eps, hc_eps, h_in_eps;
 };
 
 // Per-warp constants: alpha and this lane's bias entries.
@@ -322,6 +323,7 @@ __device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<
   const uint16_t* xr = a.x + t * nD;
   uint16_t* hr = a.h_in + t * D;
   constexpr int U = n <= 4 ? 4 : 2;
+  float sq = 0.f;   // sum of the bf16 h_in values squared (when h_in_rstd is asked for)
   for (int c0 = 0; c0 < D; c0 += 256 * U) {
     uint4 xv[U][n];
 #pragma unroll
@@ -354,8 +356,18 @@ __device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<
         o.z = pack_bf16x2(acc[4], acc[5]);
         o.w = pack_bf16x2(acc[6], acc[7]);
         *reinterpret_cast<uint4*>(hr + d) = o;
+        if (a.h_in_rstd) {
+          float r[8];
+          bf16x8(o, r);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) sq = fmaf(r[e], r[e], sq);
+        }
       }
     }
+  }
+  if (a.h_in_rstd) {
+    sq = warp_sum(sq);
+    if (lane == 0) a.h_in_rstd[t] = 1.0f / sqrtf(sq / (float)D + a.h_in_eps);
   }
 }
 

@@ -19,7 +19,8 @@ import torch
 
 from . import _lib
 
-__all__ = ["mhc_forward_pre", "mhc_forward_pre_triton", "mhc_forward_pre_triton_optimized"]
+__all__ = ["mhc_forward_pre", "mhc_forward_pre_triton", "mhc_forward_pre_triton_optimized",
+           "mhc_forward_pre_fused_norm"]
 
 
 def _as_f32(t, device, name):
@@ -39,15 +40,16 @@ def _check_x(x: torch.Tensor) -> None:
         raise TypeError(f"x must be bfloat16, got {x.dtype}")
 
 
-def mhc_forward_pre(x, phi, alpha, bias, outflag: bool = False, norm_eps: float = 1e-6,
-                    hc_eps: float = 1e-6):
-    """mHC pre-op forward; see the module docstring."""
+def _forward(x, phi, alpha, bias, outflag, norm_eps, hc_eps, h_in_norm_eps):
     _check_x(x)
     B, S, n, D = x.shape
     N = n * n + 2 * n
     dev = x.device
     x = x.contiguous()
-    phi = _as_f32(phi, dev, "phi")
+    if not torch.is_tensor(phi) or phi.device != dev:
+        raise ValueError(f"phi must be a tensor on {dev}")
+    bf16_phi = phi.dtype == torch.bfloat16
+    phi = phi.contiguous() if bf16_phi else _as_f32(phi, dev, "phi")
     alpha = _as_f32(alpha, dev, "alpha")
     bias = _as_f32(bias, dev, "bias")
     if tuple(phi.shape) != (N, n * D):
@@ -64,24 +66,56 @@ def mhc_forward_pre(x, phi, alpha, bias, outflag: bool = False, norm_eps: float 
         inv_rms = torch.empty((B, S), dtype=torch.float32, device=dev)
         h_mix = torch.empty((B, S, N), dtype=torch.float32, device=dev)
         h_pre = torch.empty((B, S, n), dtype=torch.float32, device=dev)
+    h_in_rstd = None if h_in_norm_eps is None else torch.empty((B, S), dtype=torch.float32, device=dev)
+    ex = None
+    if bf16_phi or h_in_rstd is not None:
+        ex = _lib.FwdExArgs(phi_bf16=_lib.ptr(phi) if bf16_phi else None, h_in_rstd=_lib.ptr(h_in_rstd),
+                            h_in_eps=float(h_in_norm_eps or 0.0))
 
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev)
         lib = _lib.load()
-        nbytes = _lib.fwd_workspace_size(T, n, D)
+        nbytes = _lib.fwd_workspace_size(T, n, D, ex)
         ws = _lib.workspace(nbytes, dev, stream)
         args = _lib.FwdArgs(
-            x=_lib.ptr(x), phi=_lib.ptr(phi), alpha=_lib.ptr(alpha), bias=_lib.ptr(bias),
+            x=_lib.ptr(x), phi=None if bf16_phi else _lib.ptr(phi), alpha=_lib.ptr(alpha), bias=_lib.ptr(bias),
             h_in=_lib.ptr(h_in), h_post=_lib.ptr(h_post), h_res=_lib.ptr(h_res),
             inv_rms=_lib.ptr(inv_rms), h_mix=_lib.ptr(h_mix), h_pre=_lib.ptr(h_pre),
             tokens=T, n=n, D=D, norm_eps=float(norm_eps), hc_eps=float(hc_eps),
             workspace=ws.buf.data_ptr(), workspace_bytes=ws.buf.numel())
-        _lib.check(lib.mhc_fwd(args, stream.cuda_stream), "mhc_fwd")
+        if ex is None:
+            _lib.check(lib.mhc_fwd(args, stream.cuda_stream), "mhc_fwd")
+        else:
+            _lib.check(lib.mhc_fwd_ex(args, ex, stream.cuda_stream), "mhc_fwd_ex")
         ws.watch(stream, "mhc_fwd")
+    return h_in, h_in_rstd, h_post, h_res, inv_rms, h_mix, h_pre
 
+
+def mhc_forward_pre(x, phi, alpha, bias, outflag: bool = False, norm_eps: float = 1e-6,
+                    hc_eps: float = 1e-6):
+    """mHC pre-op forward; see the module docstring.  ``phi`` may be fp32 (the
+    reference's type) or bf16 (then exact in one bf16 term: one tensor-core
+    product per K-step instead of three)."""
+    h_in, _, h_post, h_res, inv_rms, h_mix, h_pre = _forward(x, phi, alpha, bias, outflag, norm_eps, hc_eps, None)
     if not outflag:
         return h_in, h_post, h_res
     return h_in, h_post, h_res, inv_rms, h_mix, h_pre
+
+
+def mhc_forward_pre_fused_norm(x, phi, alpha, bias, h_in_norm_eps: float = 1e-6, outflag: bool = False,
+                               norm_eps: float = 1e-6, hc_eps: float = 1e-6):
+    """The forward fused with the statistic of the RMSNorm that opens the next
+    sublayer: returns ``(h_in, h_in_rstd, h_post, h_res)`` (plus the outflag
+    outputs), ``h_in_rstd [B,S] = 1 / sqrt(mean_d(h_in^2) + h_in_norm_eps)``
+    over the bf16 ``h_in`` row, computed while ``h_in`` is written.  The next
+    sublayer's ``RMSNorm(h_in) = h_in * h_in_rstd * weight`` then needs no
+    reduction pass over ``h_in``.  No counterpart in the reference, whose
+    forward stops at ``h_in`` (``src/forward/golden.py:62-63``)."""
+    h_in, rstd, h_post, h_res, inv_rms, h_mix, h_pre = _forward(x, phi, alpha, bias, outflag, norm_eps, hc_eps,
+                                                                h_in_norm_eps)
+    if not outflag:
+        return h_in, rstd, h_post, h_res
+    return h_in, rstd, h_post, h_res, inv_rms, h_mix, h_pre
 
 
 # The reference exposes the same call under its Triton names
