@@ -225,10 +225,18 @@ def run_ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
         torch.cuda.set_device(local)
+        opts = dist.ProcessGroupNCCL.Options()
+        if args.nccl_ctas > 0:
+            opts.config.max_ctas = args.nccl_ctas   # the all-reduce's SMs; the forward leaves them free
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+                                device_id=torch.device("cuda", local), pg_options=opts)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    # With the all-reduce of step k left running while step k+1's forward is
+    # launched, the forward (one cooperative launch, a CTA per SM) would wait
+    # for it; with the all-reduce's CTAs capped, the forward takes the rest.
+    fwd_budget = sms - args.nccl_ctas if world > 1 and args.nccl_ctas > 0 else None
 
     from mhc_ops_b200 import _lib, mhc_backward_manual, mhc_forward_pre
     from mhc_ops_b200.backward import param_grad_numel
@@ -272,7 +280,7 @@ def run_ours(args):
             pending.pop().wait()
 
     def step():
-        out = mhc_forward_pre(x, phi, alpha, bias, outflag=True)
+        out = mhc_forward_pre(x, phi, alpha, bias, outflag=True, sm_budget=fwd_budget)
         drain()
         ev[1].record()
         mhc_backward_manual(x, phi, alpha, bias, out[3], out[4], out[5], out[1], dh_in, dh_post, dh_res, gamma,
@@ -433,6 +441,11 @@ def run_ours(args):
                      "fwd_frac": fwd_alg / (fwd_ms / 1e3) / 1e9 / peak,
                      "bwd_frac": bwd_alg / (bwd_ms / 1e3) / 1e9 / peak},
         "sustained": sustained,
+        "comm": None if world == 1 else {
+            "allreduce_bytes": flat.numel() * 4, "nccl_max_ctas": args.nccl_ctas or "default",
+            "fwd_sm_budget": fwd_budget,
+            "what": "one NCCL all-reduce (SUM) of the flat parameter gradients per step, left running while the "
+                    "next step's forward runs"},
         "post_op": post,
         "gpu_launches": int(launches),
         "clocks": clk,
@@ -527,6 +540,9 @@ def main():
     ap.add_argument("--seq", type=int, default=WORKLOAD["S"], help="S (default 4096; others only for profiling)")
     ap.add_argument("--streams", type=int, default=WORKLOAD["n"], help="n (default 4; others only for profiling)")
     ap.add_argument("--hidden", type=int, default=WORKLOAD["D"], help="D (default 4096; others only for profiling)")
+    ap.add_argument("--nccl-ctas", type=int, default=8,
+                    help="N > 1: cap on the all-reduce's CTAs (NCCL max_ctas); the forward's grids leave that many "
+                         "SMs free so both run at once (0: NCCL's default, forward on every SM)")
     ap.add_argument("--config", choices=["llm", "8g"], default="llm",
                     help="llm: B=4,S=4096,n=4,D=4096 per GPU (weak scaling, the metric's configuration); "
                          "8g: B=8,S=4096,n=4,D=7168 split over the GPUs (strong scaling)")

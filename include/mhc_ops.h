@@ -172,12 +172,18 @@ MHC_API int mhc_fwd_static(const mhc_fwd_args* args, void* stream);
  *     the bf16 h_in row: the factor of the RMSNorm that opens the next
  *     sublayer, computed while h_in is written, so that sublayer need not
  *     read h_in once more to reduce it.
+ *   sm_budget: when > 0, the most SMs the forward's grids occupy.  The
+ *     fused forward is one cooperative launch with a CTA on every SM, so a
+ *     collective still running on a few SMs (a data-parallel all-reduce of
+ *     the previous step's gradients) would hold it back until it ends; with
+ *     the SMs that collective uses left out, the two run side by side.
  * No counterpart in the reference (its forward takes fp32 phi and stops at
  * h_in, src/forward/golden.py:41,62-63). */
 typedef struct mhc_fwd_ex_args {
   const uint16_t* phi_bf16;
   float* h_in_rstd;
   float h_in_eps;
+  int32_t sm_budget;
 } mhc_fwd_ex_args;
 /* Workspace bytes mhc_fwd_ex needs with these options (ex may be NULL). */
 MHC_API int mhc_fwd_ex_workspace_size(const mhc_fwd_ex_args* ex, int64_t tokens, int32_t n, int32_t D,

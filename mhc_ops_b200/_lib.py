@@ -34,7 +34,8 @@ class FwdArgs(ctypes.Structure):
 
 class FwdExArgs(ctypes.Structure):
     """Mirror of ``mhc_fwd_ex_args`` (include/mhc_ops.h)."""
-    _fields_ = [("phi_bf16", _c_void_p), ("h_in_rstd", _c_void_p), ("h_in_eps", ctypes.c_float)]
+    _fields_ = [("phi_bf16", _c_void_p), ("h_in_rstd", _c_void_p), ("h_in_eps", ctypes.c_float),
+                ("sm_budget", ctypes.c_int32)]
 
 
 class BwdArgs(ctypes.Structure):

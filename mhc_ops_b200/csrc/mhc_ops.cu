@@ -113,6 +113,7 @@ struct FwdEx {
   const uint16_t* phi_bf16 = nullptr;
   float* h_in_rstd = nullptr;
   float h_in_eps = 0.f;
+  int sm_budget = 0;   // > 0: grids use at most this many SMs
 };
 
 template <int n>
@@ -1088,6 +1089,8 @@ int fwd_entry(const mhc_fwd_args* a, const FwdEx& ex, void* stream) {
   if (!aligned(a->workspace, kWsAlign)) return MHC_ERR_MISALIGNED;
   int sms = 0;
   if ((st = current_sm_count(&sms))) return st;
+  if (ex.sm_budget < 0) return MHC_ERR_BAD_SHAPE;
+  if (ex.sm_budget > 0) sms = std::min(sms, ex.sm_budget);
   if (a->tokens == 0) return MHC_OK;
   if (!a->x || (!a->phi && !bf16_phi) || !a->alpha || !a->bias || !a->h_in || !a->h_post || !a->h_res)
     return MHC_ERR_NULL_POINTER;
@@ -1117,6 +1120,7 @@ int mhc_fwd_ex(const mhc_fwd_args* a, const mhc_fwd_ex_args* ex, void* stream) {
     e.phi_bf16 = ex->phi_bf16;
     e.h_in_rstd = ex->h_in_rstd;
     e.h_in_eps = ex->h_in_eps;
+    e.sm_budget = ex->sm_budget;
   }
   return fwd_entry(a, e, stream);
 }

@@ -40,7 +40,7 @@ def _check_x(x: torch.Tensor) -> None:
         raise TypeError(f"x must be bfloat16, got {x.dtype}")
 
 
-def _forward(x, phi, alpha, bias, outflag, norm_eps, hc_eps, h_in_norm_eps):
+def _forward(x, phi, alpha, bias, outflag, norm_eps, hc_eps, h_in_norm_eps, sm_budget=None):
     _check_x(x)
     B, S, n, D = x.shape
     N = n * n + 2 * n
@@ -68,9 +68,9 @@ def _forward(x, phi, alpha, bias, outflag, norm_eps, hc_eps, h_in_norm_eps):
         h_pre = torch.empty((B, S, n), dtype=torch.float32, device=dev)
     h_in_rstd = None if h_in_norm_eps is None else torch.empty((B, S), dtype=torch.float32, device=dev)
     ex = None
-    if bf16_phi or h_in_rstd is not None:
+    if bf16_phi or h_in_rstd is not None or sm_budget:
         ex = _lib.FwdExArgs(phi_bf16=_lib.ptr(phi) if bf16_phi else None, h_in_rstd=_lib.ptr(h_in_rstd),
-                            h_in_eps=float(h_in_norm_eps or 0.0))
+                            h_in_eps=float(h_in_norm_eps or 0.0), sm_budget=int(sm_budget or 0))
 
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev)
@@ -92,11 +92,14 @@ def _forward(x, phi, alpha, bias, outflag, norm_eps, hc_eps, h_in_norm_eps):
 
 
 def mhc_forward_pre(x, phi, alpha, bias, outflag: bool = False, norm_eps: float = 1e-6,
-                    hc_eps: float = 1e-6):
+                    hc_eps: float = 1e-6, sm_budget: int | None = None):
     """mHC pre-op forward; see the module docstring.  ``phi`` may be fp32 (the
     reference's type) or bf16 (then exact in one bf16 term: one tensor-core
-    product per K-step instead of three)."""
-    h_in, _, h_post, h_res, inv_rms, h_mix, h_pre = _forward(x, phi, alpha, bias, outflag, norm_eps, hc_eps, None)
+    product per K-step instead of three).  ``sm_budget`` (not in the
+    reference): the most SMs the forward's grids take, so that a collective
+    left running on the other SMs overlaps it."""
+    h_in, _, h_post, h_res, inv_rms, h_mix, h_pre = _forward(x, phi, alpha, bias, outflag, norm_eps, hc_eps, None,
+                                                             sm_budget)
     if not outflag:
         return h_in, h_post, h_res
     return h_in, h_post, h_res, inv_rms, h_mix, h_pre
