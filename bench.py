@@ -332,7 +332,7 @@ def run_ours(args):
     sustained = None
     reps = max(0, math.ceil(SUSTAIN_MS / max(total_ms / args.steps, 1e-3)))
     reps = int(max_over_ranks(reps))
-    if total_ms < SUSTAIN_MS and reps > args.steps:
+    if total_ms < SUSTAIN_MS and reps > args.steps and not args.no_sustain:
         sync_all()
         start.record()
         for _ in range(reps):
@@ -533,6 +533,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-post", action="store_true", help="skip the post-op timing")
+    ap.add_argument("--no-sustain", action="store_true",
+                    help="skip the second, >= 200 ms timing region (for profiler launch lists)")
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--ref-tokens", type=int, default=1024)
     ap.add_argument("--batch", type=int, default=WORKLOAD["B"],
