@@ -177,13 +177,23 @@ MHC_API int mhc_fwd_static(const mhc_fwd_args* args, void* stream);
  *     collective still running on a few SMs (a data-parallel all-reduce of
  *     the previous step's gradients) would hold it back until it ends; with
  *     the SMs that collective uses left out, the two run side by side.
- * No counterpart in the reference (its forward takes fp32 phi and stops at
- * h_in, src/forward/golden.py:41,62-63). */
+ *   x_fp8, x_exp: x given as e4m3 bytes [T, n, D] (args->x is then ignored
+ *     and may be NULL) with a power-of-two scale per token:
+ *     x[t,:] = x_fp8[t,:] * 2^x_exp[t] (x_exp may be NULL: exponent 0).
+ *     Every such value is exact in bf16, and the outputs are bit for bit
+ *     those of mhc_fwd on that bf16 x; the forward reads half the bytes of
+ *     x.  For inference (the backward takes bf16 x).  Tensor-core shapes
+ *     only (n in {4, 8}, D a multiple of 64, x_fp8 16-byte aligned; others
+ *     return MHC_ERR_BAD_SHAPE); keep x * 2^e inside the bf16 range. 
+ * No counterpart in the reference (its forward takes bf16 x and fp32 phi and
+ * stops at h_in, src/forward/golden.py:38,41,62-63). */
 typedef struct mhc_fwd_ex_args {
   const uint16_t* phi_bf16;
   float* h_in_rstd;
   float h_in_eps;
   int32_t sm_budget;
+  const uint8_t* x_fp8;
+  const int8_t* x_exp;
 } mhc_fwd_ex_args;
 /* Workspace bytes mhc_fwd_ex needs with these options (ex may be NULL). */
 MHC_API int mhc_fwd_ex_workspace_size(const mhc_fwd_ex_args* ex, int64_t tokens, int32_t n, int32_t D,

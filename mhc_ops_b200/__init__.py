@@ -12,8 +12,8 @@ code does not run).
 
 __version__ = "0.2.0"
 
-from .forward import (mhc_forward_pre, mhc_forward_pre_fused_norm, mhc_forward_pre_triton,  # noqa: E402
-                      mhc_forward_pre_triton_optimized)
+from .forward import (mhc_forward_pre, mhc_forward_pre_fp8, mhc_forward_pre_fused_norm,  # noqa: E402
+                      mhc_forward_pre_triton, mhc_forward_pre_triton_optimized, quantize_fp8_pow2)
 from .backward import mhc_backward_manual, mhc_backward_triton  # noqa: E402
 from .autograd import MHCPreFunction, mhc_pre  # noqa: E402
 from .post import MHCPostFunction, mhc_post, mhc_post_backward, mhc_post_fn  # noqa: E402
@@ -23,6 +23,8 @@ __all__ = [
     "mhc_forward_pre_triton",
     "mhc_forward_pre_triton_optimized",
     "mhc_forward_pre_fused_norm",
+    "mhc_forward_pre_fp8",
+    "quantize_fp8_pow2",
     "mhc_backward_manual",
     "mhc_backward_triton",
     "MHCPreFunction",

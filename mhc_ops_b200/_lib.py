@@ -35,7 +35,7 @@ class FwdArgs(ctypes.Structure):
 class FwdExArgs(ctypes.Structure):
     """Mirror of ``mhc_fwd_ex_args`` (include/mhc_ops.h)."""
     _fields_ = [("phi_bf16", _c_void_p), ("h_in_rstd", _c_void_p), ("h_in_eps", ctypes.c_float),
-                ("sm_budget", ctypes.c_int32)]
+                ("sm_budget", ctypes.c_int32), ("x_fp8", _c_void_p), ("x_exp", _c_void_p)]
 
 
 class BwdArgs(ctypes.Structure):

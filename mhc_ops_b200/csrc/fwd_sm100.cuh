@@ -39,6 +39,7 @@
 // the gates to ~2^-18, which two terms miss when |h_mix| is large.
 #pragma once
 
+#include <cuda_fp8.h>
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -76,7 +77,11 @@ constexpr int pow2_at_least(int v) {
 // this file).  A phi given in bf16 is exact in one term.
 constexpr int default_terms(int n) { return n <= 5 ? 3 : 2; }
 
-template <int n, int kNT = default_terms(n)>
+// kFp8: x comes as e4m3 bytes with a power-of-two scale per token; each
+// stage also holds the raw fp8 box, which the sum-of-squares warps widen
+// into the bf16 operand tile (exactly: every e4m3 value times a power of two
+// is a bf16 value).
+template <int n, int kNT = default_terms(n), bool kFp8 = false>
 struct Cfg {
   static constexpr int N_OUT = n * n + 2 * n;
   static constexpr int NT = kNT;                           // phi split terms
@@ -84,7 +89,8 @@ struct Cfg {
   static constexpr int RW = round_up(N_OUT + 1, 8);        // floats per partial row (whole 32-byte sectors)
   static constexpr int A_BYTES = kBM * 128;
   static constexpr int B_BYTES = NB * 128;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int RAW_BYTES = kFp8 ? kBM * kBK : 0;   // fp8 box [128 tok x 64 k], after A and B
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + RAW_BYTES;
   static constexpr int ACC_COLS = round_up(NB, 32);
   static constexpr int NBUF = (512 / ACC_COLS) < 4 ? (512 / ACC_COLS) : 4;   // accumulator ring
   static constexpr int TMEM_COLS = pow2_at_least(NBUF * ACC_COLS);
@@ -119,12 +125,13 @@ struct Params {
   rowdot::FwdRowArgs rows;
 };
 
-template <int n, int kNT>
+template <int n, int kNT, bool kFp8>
 struct Bars {
-  using Cf = Cfg<n, kNT>;
+  using Cf = Cfg<n, kNT, kFp8>;
   static constexpr int full = 0;
   static constexpr int empty = full + Cf::S;
-  static constexpr int acc_full = empty + Cf::S;
+  static constexpr int conv = empty + Cf::S;               // fp8: the stage's bf16 tile is written
+  static constexpr int acc_full = conv + Cf::S;
   static constexpr int acc_empty = acc_full + Cf::NBUF;
   static constexpr int sq_full = acc_empty + Cf::NBUF;   // 2: WG_S wrote a unit's sum x^2
   static constexpr int sq_empty = sq_full + 2;           // 2: WG_F read it
@@ -144,6 +151,11 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
   return v;
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
 }
 
 // One warp's arrival on its tile's counter after its partial stores: every
@@ -177,12 +189,12 @@ __device__ __forceinline__ void wait_rows_done(volatile int* rows_done, int need
   }
 }
 
-template <int n, bool kFused, int kNT = default_terms(n)>
+template <int n, bool kFused, int kNT = default_terms(n), bool kFp8 = false>
 __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
     proj_kernel(const __grid_constant__ CUtensorMap map_x2d, const __grid_constant__ CUtensorMap map_phi,
                 const Params p) {
-  using Cf = Cfg<n, kNT>;
-  using B = Bars<n, kNT>;
+  using Cf = Cfg<n, kNT, kFp8>;
+  using B = Bars<n, kNT, kFp8>;
   constexpr int N_OUT = Cf::N_OUT;
   constexpr int S = Cf::S;
 
@@ -202,6 +214,7 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
     for (int i = 0; i < S; ++i) {
       mbar_init(bar(B::full + i), 1);
       mbar_init(bar(B::empty + i), 1 + 4);   // MMA commit + the 4 WG_S warps
+      mbar_init(bar(B::conv + i), 4);        // fp8: the 4 WG_S warps wrote the bf16 tile
     }
     for (int i = 0; i < Cf::NBUF; ++i) {
       mbar_init(bar(B::acc_full + i), 1);
@@ -250,8 +263,13 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
           mbar_wait(bar(B::empty + s), ((it / S) & 1) ^ 1, wc);
           if (*abort_flag) continue;
           uint8_t* st = ring + s * Cf::STAGE_BYTES;
-          mbar_arrive_expect_tx(bar(B::full + s), Cf::STAGE_BYTES);
-          tma_load_2d(smem_u32(st), &map_x2d, bar(B::full + s), k0, tile * kBM, pol_x);
+          if constexpr (kFp8) {
+            mbar_arrive_expect_tx(bar(B::full + s), Cf::B_BYTES + Cf::RAW_BYTES);
+            tma_load_2d(smem_u32(st + Cf::A_BYTES + Cf::B_BYTES), &map_x2d, bar(B::full + s), k0, tile * kBM, pol_x);
+          } else {
+            mbar_arrive_expect_tx(bar(B::full + s), Cf::STAGE_BYTES);
+            tma_load_2d(smem_u32(st), &map_x2d, bar(B::full + s), k0, tile * kBM, pol_x);
+          }
           tma_load_2d(smem_u32(st + Cf::A_BYTES), &map_phi, bar(B::full + s), k0, 0, pol_phi);
         }
       }
@@ -266,7 +284,7 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
           const int s = it % S;
           const int ab = g % Cf::NBUF;
           const bool first = (kb % kKG) == 0, last = (kb % kKG) == kKG - 1 || kb == KB - 1;
-          mbar_wait(bar(B::full + s), (it / S) & 1, wc);
+          mbar_wait(bar((kFp8 ? B::conv : B::full) + s), (it / S) & 1, wc);
           if (first) mbar_wait(bar(B::acc_empty + ab), ((g / Cf::NBUF) & 1) ^ 1, wc);
           tc_fence_after();
           if (!*abort_flag) {
@@ -357,15 +375,56 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
     uint32_t it = 0, uc = 0;
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++uc) {
       float sq = 0.f;
+      float scale = 1.f;   // fp8: 2^e of this row's token (rows past the batch are zero anyway)
+      if constexpr (kFp8) {
+        const int64_t t = (int64_t)(u / p.S_K) * kBM + row;
+        if (p.rows.x_exp != nullptr && t < p.T) scale = ldexpf(1.0f, (int)__ldg(p.rows.x_exp + t));
+      }
       for (int kb = 0; kb < KB; ++kb, ++it) {
         const int s = it % S;
         mbar_wait(bar(B::full + s), (it / S) & 1, wc);
         const uint32_t base = smem_u32(ring + s * Cf::STAGE_BYTES) + row * 128;
         uint4 xv[8];
+        if constexpr (kFp8) {
+          // widen the row's 64 e4m3 values into the bf16 tile, 128-B swizzled
+          // as a TMA load would have written it (16-byte chunk c of row r at
+          // chunk c ^ (r & 7)), then read the row back in the bf16 path's
+          // order, so the sum of squares adds the same values in the same order
+          const uint32_t raw = smem_u32(ring + s * Cf::STAGE_BYTES + Cf::A_BYTES + Cf::B_BYTES) + row * kBK;
+          uint4 lx[8];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) xv[c] = lds128(base + (((c + row) & 7) << 4));
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B::empty + s));
+          for (int h = 0; h < 4; ++h) {
+            const uint4 r = lds128(raw + h * 16);
+            const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int c2 = 0; c2 < 2; ++c2) {
+              uint32_t o[4];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const uint32_t pair = w[2 * c2 + q / 2] >> (16 * (q & 1));
+                const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(pair & 0xFFFFu), __NV_E4M3);
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+                o[q] = pack_bf16x2(f.x * scale, f.y * scale);
+              }
+              lx[2 * h + c2] = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < 8; ++c) sts128(base + ((c ^ (row & 7)) << 4), lx[c]);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) xv[c] = lds128(base + (((c + row) & 7) << 4));   // the bf16 path's order
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(bar(B::conv + s));
+            mbar_arrive(bar(B::empty + s));
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) xv[c] = lds128(base + (((c + row) & 7) << 4));
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(B::empty + s));
+        }
         float c8[8];
 #pragma unroll
         for (int c = 0; c < 8; ++c) {

@@ -113,7 +113,9 @@ struct FwdEx {
   const uint16_t* phi_bf16 = nullptr;
   float* h_in_rstd = nullptr;
   float h_in_eps = 0.f;
-  int sm_budget = 0;   // > 0: grids use at most this many SMs
+  int sm_budget = 0;               // > 0: grids use at most this many SMs
+  const uint8_t* x_fp8 = nullptr;  // x as e4m3 bytes (then args->x is unused) ...
+  const int8_t* x_exp = nullptr;   // ... times 2^x_exp[t] per token
 };
 
 template <int n>
@@ -242,7 +244,8 @@ bool fwd_tc_shape(int64_t T, int n, int D) {
 
 bool fwd_tc_eligible(const mhc_fwd_args* a, const FwdEx& ex) {
   const void* phi = ex.phi_bf16 ? static_cast<const void*>(ex.phi_bf16) : static_cast<const void*>(a->phi);
-  return fwd_tc_shape(a->tokens, a->n, a->D) && aligned(a->x, 16) && aligned(a->h_in, 16) && aligned(phi, 16);
+  const void* x = ex.x_fp8 ? static_cast<const void*>(ex.x_fp8) : static_cast<const void*>(a->x);
+  return fwd_tc_shape(a->tokens, a->n, a->D) && aligned(x, 16) && aligned(a->h_in, 16) && aligned(phi, 16);
 }
 
 // Bytes of the bf16 term images of phi (one term when phi comes in bf16).
@@ -280,7 +283,7 @@ int fwd_fused_slices(int n, int D) {
 
 // Whether proj_kernel<n, true, NT> can run with one CTA on every SM at once
 // (a cooperative launch needs that); asked once per device.
-template <int n, int NT>
+template <int n, int NT, bool FP8 = false>
 bool fwd_fused_supported() {
   static std::mutex mu;
   static std::map<int, bool> known;
@@ -291,10 +294,11 @@ bool fwd_fused_supported() {
   if (it != known.end()) return it->second;
   int coop = 0, blocks = 0;
   bool ok = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) == cudaSuccess && coop &&
-            cudaFuncSetAttribute(fwdtc::proj_kernel<n, true, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 fwdtc::Cfg<n, NT>::SMEM) == cudaSuccess &&
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fwdtc::proj_kernel<n, true, NT>,
-                                                          fwdtc::kThreadsFused, fwdtc::Cfg<n, NT>::SMEM) == cudaSuccess &&
+            cudaFuncSetAttribute(fwdtc::proj_kernel<n, true, NT, FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 fwdtc::Cfg<n, NT, FP8>::SMEM) == cudaSuccess &&
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fwdtc::proj_kernel<n, true, NT, FP8>,
+                                                          fwdtc::kThreadsFused,
+                                                          fwdtc::Cfg<n, NT, FP8>::SMEM) == cudaSuccess &&
             blocks >= 1;
   (void)cudaGetLastError();
   known[dev] = ok;
@@ -303,8 +307,10 @@ bool fwd_fused_supported() {
 
 // n = 8 never qualifies (its K-slices of at most kFusedKbPer blocks need more
 // partial rows than an h_in row holds), so only n = 4 is instantiated.
-bool fwd_fused_supported(int n, bool bf16_phi = false) {
-  return n == 4 && (bf16_phi ? fwd_fused_supported<4, 1>() : fwd_fused_supported<4, fwdtc::default_terms(4)>());
+bool fwd_fused_supported(int n, bool bf16_phi = false, bool fp8_x = false) {
+  if (n != 4) return false;
+  if (fp8_x) return bf16_phi ? fwd_fused_supported<4, 1, true>() : fwd_fused_supported<4, 3, true>();
+  return bf16_phi ? fwd_fused_supported<4, 1>() : fwd_fused_supported<4, fwdtc::default_terms(4)>();
 }
 
 // Two-kernel form: the fewest K-slices (a divisor of the n*D/64 K-blocks, at
@@ -334,8 +340,8 @@ FwdTcPlan fwd_tc_plan_with(int64_t T, int n, int D, int sms, bool fused_ok) {
   return P;
 }
 
-FwdTcPlan fwd_tc_plan(int64_t T, int n, int D, int sms, bool bf16_phi) {
-  return fwd_tc_plan_with(T, n, D, sms, fwd_fused_supported(n, bf16_phi));
+FwdTcPlan fwd_tc_plan(int64_t T, int n, int D, int sms, bool bf16_phi, bool fp8_x) {
+  return fwd_tc_plan_with(T, n, D, sms, fwd_fused_supported(n, bf16_phi, fp8_x));
 }
 
 size_t fwd_tile_counter_bytes(int64_t T) {
@@ -346,15 +352,15 @@ int fwd_rows_grid(int64_t T, int sms) {
   return (int)std::max<int64_t>(1, std::min<int64_t>(sms, (T + rowdot::kWarps - 1) / rowdot::kWarps));
 }
 
-template <int n, int NT>
+template <int n, int NT, bool FP8>
 struct FwdTc {
   // One cooperative launch of proj_kernel<n, true, NT> (all CTAs co-resident:
   // row warps wait on counters other CTAs advance).
   static int launch_fused(const CUtensorMap& m_x2d, const CUtensorMap& m_phi, const fwdtc::Params& p,
                           const FwdTcPlan& P, cudaStream_t s) {
-    using Cf = fwdtc::Cfg<n, NT>;
+    using Cf = fwdtc::Cfg<n, NT, FP8>;
     int st;
-    if ((st = set_smem_limit_once(fwdtc::proj_kernel<n, true, NT>, Cf::SMEM))) return st;
+    if ((st = set_smem_limit_once(fwdtc::proj_kernel<n, true, NT, FP8>, Cf::SMEM))) return st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
@@ -365,12 +371,12 @@ struct FwdTc {
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    MHC_CUDA_TRY(cudaLaunchKernelEx(&cfg, fwdtc::proj_kernel<n, true, NT>, m_x2d, m_phi, p));
+    MHC_CUDA_TRY(cudaLaunchKernelEx(&cfg, fwdtc::proj_kernel<n, true, NT, FP8>, m_x2d, m_phi, p));
     return after_launch();
   }
 
   static int run(const mhc_fwd_args* a, const FwdEx& ex, cudaStream_t s, int sms) {
-    using Cf = fwdtc::Cfg<n, NT>;
+    using Cf = fwdtc::Cfg<n, NT, FP8>;
     const bool bf16_phi = ex.phi_bf16 != nullptr;
     const int64_t T = a->tokens;
     const int D = a->D;
@@ -379,7 +385,7 @@ struct FwdTc {
     uint16_t* phis = reinterpret_cast<uint16_t*>(ws + kWsHeaderBytes);
     int* tile_done =
         reinterpret_cast<int*>(ws + align_up(kWsHeaderBytes + fwd_tc_phis_bytes(n, D, bf16_phi), kWsAlign));
-    const FwdTcPlan P = fwd_tc_plan(T, n, D, sms, bf16_phi);
+    const FwdTcPlan P = fwd_tc_plan(T, n, D, sms, bf16_phi, FP8);
     const int tiles = (int)((T + fwdtc::kBM - 1) / fwdtc::kBM);
     int st;
 
@@ -393,7 +399,16 @@ struct FwdTc {
       const uint64_t dims[2] = {(uint64_t)nD, (uint64_t)T};
       const uint64_t strides[1] = {(uint64_t)nD * 2};
       const uint32_t box[2] = {fwdtc::kBK, fwdtc::kBM};
-      if ((st = encode_bf16_map(&m_x2d, a->x, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+      if constexpr (FP8) {
+        // [128 tok x 64 k] e4m3 bytes, unswizzled: the sum-of-squares warps
+        // read their row of it and write the swizzled bf16 tile
+        const uint64_t strides8[1] = {(uint64_t)nD};
+        if ((st = encode_map(&m_x2d, CU_TENSOR_MAP_DATA_TYPE_UINT8, ex.x_fp8, 2, dims, strides8, box,
+                             CU_TENSOR_MAP_SWIZZLE_NONE)))
+          return st;
+      } else {
+        if ((st = encode_bf16_map(&m_x2d, a->x, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+      }
     }
     {
       const uint64_t dims[2] = {(uint64_t)nD, (uint64_t)Cf::NB};
@@ -423,14 +438,16 @@ struct FwdTc {
     p.rows.S_K = P.S_K;
     p.rows.RW = Cf::RW;
     p.rows.h_in_rstd = ex.h_in_rstd;
+    p.rows.x8 = ex.x_fp8;
+    p.rows.x_exp = ex.x_exp;
     p.rows.norm_eps = a->norm_eps;
     p.rows.hc_eps = a->hc_eps;
     p.rows.h_in_eps = ex.h_in_eps;
     if constexpr (n == 4) {
       if (P.fused) return launch_fused(m_x2d, m_phi, p, P, s);
     }
-    if ((st = set_smem_limit_once(fwdtc::proj_kernel<n, false, NT>, Cf::SMEM))) return st;
-    fwdtc::proj_kernel<n, false, NT><<<P.grid, fwdtc::kThreads, Cf::SMEM, s>>>(m_x2d, m_phi, p);
+    if ((st = set_smem_limit_once(fwdtc::proj_kernel<n, false, NT, FP8>, Cf::SMEM))) return st;
+    fwdtc::proj_kernel<n, false, NT, FP8><<<P.grid, fwdtc::kThreads, Cf::SMEM, s>>>(m_x2d, m_phi, p);
     if ((st = after_launch())) return st;
     rowdot::fwd_rows_kernel<n><<<fwd_rows_grid(T, sms), rowdot::kThreads, 0, s>>>(p.rows, T);
     return after_launch();
@@ -459,9 +476,14 @@ int fwd_workspace(int64_t T, int n, int D, size_t* bytes, bool bf16_phi = false)
 int fwd_run(const mhc_fwd_args* a, const FwdEx& ex, cudaStream_t s, int sms) {
   const bool bf16_phi = ex.phi_bf16 != nullptr;
   if (fwd_tc_eligible(a, ex)) {
-    if (a->n == 4) return bf16_phi ? FwdTc<4, 1>::run(a, ex, s, sms) : FwdTc<4, 3>::run(a, ex, s, sms);
-    return bf16_phi ? FwdTc<8, 1>::run(a, ex, s, sms) : FwdTc<8, 2>::run(a, ex, s, sms);
+    if (ex.x_fp8) {
+      if (a->n == 4) return bf16_phi ? FwdTc<4, 1, true>::run(a, ex, s, sms) : FwdTc<4, 3, true>::run(a, ex, s, sms);
+      return bf16_phi ? FwdTc<8, 1, true>::run(a, ex, s, sms) : FwdTc<8, 2, true>::run(a, ex, s, sms);
+    }
+    if (a->n == 4) return bf16_phi ? FwdTc<4, 1, false>::run(a, ex, s, sms) : FwdTc<4, 3, false>::run(a, ex, s, sms);
+    return bf16_phi ? FwdTc<8, 1, false>::run(a, ex, s, sms) : FwdTc<8, 2, false>::run(a, ex, s, sms);
   }
+  if (ex.x_fp8) return MHC_ERR_BAD_SHAPE;   // fp8 x: tensor-core shapes only
   const float* phi = a->phi;
   if (bf16_phi) {
     float* copy = reinterpret_cast<float*>(static_cast<char*>(a->workspace) +
@@ -1092,8 +1114,11 @@ int fwd_entry(const mhc_fwd_args* a, const FwdEx& ex, void* stream) {
   if (ex.sm_budget < 0) return MHC_ERR_BAD_SHAPE;
   if (ex.sm_budget > 0) sms = std::min(sms, ex.sm_budget);
   if (a->tokens == 0) return MHC_OK;
-  if (!a->x || (!a->phi && !bf16_phi) || !a->alpha || !a->bias || !a->h_in || !a->h_post || !a->h_res)
+  if ((!a->x && !ex.x_fp8) || (!a->phi && !bf16_phi) || !a->alpha || !a->bias || !a->h_in || !a->h_post ||
+      !a->h_res)
     return MHC_ERR_NULL_POINTER;
+  if (ex.x_fp8 && !(fwd_tc_shape(a->tokens, a->n, a->D) && aligned(ex.x_fp8, 16) && aligned(a->h_in, 16)))
+    return MHC_ERR_BAD_SHAPE;
   if (!aligned(a->x, 2) || !aligned(a->h_in, 2) || !aligned(a->phi, 4) || !aligned(a->alpha, 4) ||
       !aligned(a->bias, 4) || !aligned(a->h_post, 4) || !aligned(a->h_res, 4) || !aligned(a->inv_rms, 4) ||
       !aligned(a->h_mix, 4) || !aligned(a->h_pre, 4) || !aligned(ex.phi_bf16, 2) || !aligned(ex.h_in_rstd, 4))
@@ -1121,6 +1146,8 @@ int mhc_fwd_ex(const mhc_fwd_args* a, const mhc_fwd_ex_args* ex, void* stream) {
     e.h_in_rstd = ex->h_in_rstd;
     e.h_in_eps = ex->h_in_eps;
     e.sm_budget = ex->sm_budget;
+    e.x_fp8 = ex->x_fp8;
+    e.x_exp = ex->x_exp;
   }
   return fwd_entry(a, e, stream);
 }

@@ -4,6 +4,9 @@
 // is 512 contiguous bytes per warp, many loads in flight per lane.
 #pragma once
 
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+
 #include "common.cuh"
 
 namespace mhc {
@@ -233,6 +236,8 @@ struct FwdRowArgs {
   float* h_mix;     // optional
   float* h_pre;     // optional
   float* h_in_rstd; // optional: 1/sqrt(mean(h_in^2) + h_in_eps) over the bf16 row, the next RMSNorm's factor
+  const uint8_t* x8;     // optional: x as e4m3 bytes [T, n, D] (then x is unused) ...
+  const int8_t* x_exp;   // ... with x = x8 * 2^x_exp[t] (NULL: exponent 0)
   int D, S_K, RW;
   float norm_eps, hc_eps, h_in_eps;
 };
@@ -319,11 +324,74 @@ __device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<
   float hp[n];
 #pragma unroll
   for (int i = 0; i < n; ++i) hp[i] = __shfl_sync(0xffffffffu, hp_lane, i);
+  uint16_t* hr = a.h_in + t * D;
+  float sq = 0.f;   // sum of the bf16 h_in values squared (when h_in_rstd is asked for)
+  if (a.x8 != nullptr) {
+    // (3, fp8 x) h_in = sum_i (h_pre[i] 2^e) x8[i, :]: scaling the weights by
+    // the power of two instead of each x value gives the same products, so
+    // the result is the one of the bf16 forward on x = x8 2^e, bit for bit
+    const float sc = a.x_exp ? ldexpf(1.0f, (int)__ldg(a.x_exp + t)) : 1.0f;
+#pragma unroll
+    for (int i = 0; i < n; ++i) hp[i] *= sc;
+    const uint8_t* xr8 = a.x8 + t * nD;
+    constexpr int U8 = n <= 4 ? 2 : 1;   // 512-element chunks in flight per lane (16 bytes per stream)
+    for (int c0 = 0; c0 < D; c0 += 512 * U8) {
+      uint4 xv[U8][n];
+#pragma unroll
+      for (int u = 0; u < U8; ++u) {
+        const int d = c0 + u * 512 + lane * 16;
+#pragma unroll
+        for (int i = 0; i < n; ++i) xv[u][i] = d < D ? ldg_stream(xr8 + (int64_t)i * D + d) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < U8; ++u) {
+        const int d = c0 + u * 512 + lane * 16;
+        if (d < D) {
+          float acc[16];
+#pragma unroll
+          for (int i = 0; i < n; ++i) {
+            const uint32_t w[4] = {xv[u][i].x, xv[u][i].y, xv[u][i].z, xv[u][i].w};
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const uint32_t pair = w[q / 2] >> (16 * (q & 1));
+              const __half2_raw h2 = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(pair & 0xFFFFu), __NV_E4M3);
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+              if (i == 0) {
+                acc[2 * q] = hp[0] * f.x;
+                acc[2 * q + 1] = hp[0] * f.y;
+              } else {
+                acc[2 * q] = fmaf(hp[i], f.x, acc[2 * q]);
+                acc[2 * q + 1] = fmaf(hp[i], f.y, acc[2 * q + 1]);
+              }
+            }
+          }
+          uint4 o[2];
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            o[hh].x = pack_bf16x2(acc[8 * hh], acc[8 * hh + 1]);
+            o[hh].y = pack_bf16x2(acc[8 * hh + 2], acc[8 * hh + 3]);
+            o[hh].z = pack_bf16x2(acc[8 * hh + 4], acc[8 * hh + 5]);
+            o[hh].w = pack_bf16x2(acc[8 * hh + 6], acc[8 * hh + 7]);
+            *reinterpret_cast<uint4*>(hr + d + 8 * hh) = o[hh];
+            if (a.h_in_rstd) {
+              float r[8];
+              bf16x8(o[hh], r);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) sq = fmaf(r[e], r[e], sq);
+            }
+          }
+        }
+      }
+    }
+    if (a.h_in_rstd) {
+      sq = warp_sum(sq);
+      if (lane == 0) a.h_in_rstd[t] = 1.0f / sqrtf(sq / (float)D + a.h_in_eps);
+    }
+    return;
+  }
   // (3) h_in = sum_i h_pre[i] x[i, :], streamed (U 256-element chunks in flight per lane)
   const uint16_t* xr = a.x + t * nD;
-  uint16_t* hr = a.h_in + t * D;
   constexpr int U = n <= 4 ? 4 : 2;
-  float sq = 0.f;   // sum of the bf16 h_in values squared (when h_in_rstd is asked for)
   for (int c0 = 0; c0 < D; c0 += 256 * U) {
     uint4 xv[U][n];
 #pragma unroll

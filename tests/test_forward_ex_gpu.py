@@ -53,3 +53,37 @@ def test_h_in_rstd_is_the_rmsnorm_factor_of_h_in(B, S, n, D):
     err = ((rstd.double() - want).abs() / want).max().item()
     assert err <= 1e-5, f"h_in_rstd rel err {err:.3g}"
     assert rstd.shape == (B, S) and np.isfinite(rstd.cpu().numpy()).all()
+
+
+@pytest.mark.parametrize("B,S,n,D", [(4, 1024, 4, 4096), (1, 300, 8, 1024), (1, 130, 4, 64), (2, 64, 4, 256)])
+@pytest.mark.parametrize("bf16_phi", [False, True])
+def test_fp8_x_forward_equals_bf16_forward_on_the_dequantized_x(B, S, n, D, bf16_phi):
+    """x as e4m3 with a power-of-two scale per token: x8 * 2^e is exact in
+    bf16, and the fp8 forward must give, bit for bit, the outputs of the bf16
+    forward on that x (and so match the oracle on it)."""
+    from mhc_ops_b200 import mhc_forward_pre_fp8, quantize_fp8_pow2
+    inp = make_inputs(B, S, n, D, seed=43)
+    d = inp.to(DEV)
+    # spread the per-token magnitudes so the exponents differ from token to token
+    x = (d.x.float() * torch.exp2(torch.randint(-6, 7, (B, S, 1, 1), device=DEV).float())).to(torch.bfloat16)
+    x8, e = quantize_fp8_pow2(x)
+    x_hat = (x8.float() * torch.exp2(e.float())[:, :, None, None]).to(torch.bfloat16)
+    assert torch.equal(x_hat.float(), x8.float() * torch.exp2(e.float())[:, :, None, None])   # exact in bf16
+    phi = d.phi.to(torch.bfloat16) if bf16_phi else d.phi
+    a = mhc_forward_pre_fp8(x8, e, phi, d.alpha, d.bias, outflag=True)
+    b = mhc_forward_pre(x_hat, phi, d.alpha, d.bias, outflag=True)
+    torch.cuda.synchronize()
+    for i, (u, v) in enumerate(zip(a, b)):
+        assert torch.equal(u, v), f"output {i}: fp8 forward differs from the bf16 forward on x8 * 2^e"
+    if B * S <= 512 and not bf16_phi:
+        xb = bits(x_hat)
+        ref = O.forward(xb, inp.phi.numpy(), inp.alpha.numpy(), inp.bias.numpy(), outflag=True)
+        assert_fwd_close(a, ref, xb, tag=f"fp8 x {B}x{S}x{n}x{D}")
+
+
+def test_fp8_x_forward_refuses_shapes_off_the_tensor_cores():
+    from mhc_ops_b200 import _lib, mhc_forward_pre_fp8, quantize_fp8_pow2
+    d = make_inputs(1, 20, 3, 24, seed=44).to(DEV)
+    x8, e = quantize_fp8_pow2(d.x)
+    with pytest.raises(_lib.MhcError):
+        mhc_forward_pre_fp8(x8, e, d.phi, d.alpha, d.bias)
