@@ -477,7 +477,7 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
             (void)ld_acquire(p.tile_done + tile);   // every lane acquires the partials' stores
             ready = true;
           }
-          rowdot::fwd_row_token<n>(p.rows, k, t, lane);
+          rowdot::fwd_row_token<n, kFp8>(p.rows, k, t, lane);
         }
         if (lane == 0) rows_done[rw] = lu + 1;
       }

@@ -449,7 +449,7 @@ struct FwdTc {
     if ((st = set_smem_limit_once(fwdtc::proj_kernel<n, false, NT, FP8>, Cf::SMEM))) return st;
     fwdtc::proj_kernel<n, false, NT, FP8><<<P.grid, fwdtc::kThreads, Cf::SMEM, s>>>(m_x2d, m_phi, p);
     if ((st = after_launch())) return st;
-    rowdot::fwd_rows_kernel<n><<<fwd_rows_grid(T, sms), rowdot::kThreads, 0, s>>>(p.rows, T);
+    rowdot::fwd_rows_kernel<n, FP8><<<fwd_rows_grid(T, sms), rowdot::kThreads, 0, s>>>(p.rows, T);
     return after_launch();
   }
 };

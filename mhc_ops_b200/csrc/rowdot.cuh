@@ -316,7 +316,8 @@ __device__ __forceinline__ float fwd_row_gates(const FwdRowArgs& a, const FwdRow
   return hp_lane;
 }
 
-template <int n>
+// kFp8: x comes as e4m3 bytes (a.x8, scaled by 2^a.x_exp[t]) instead of bf16.
+template <int n, bool kFp8 = false>
 __device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<n>& k, int64_t t, int lane) {
   const int D = a.D;
   const int64_t nD = (int64_t)n * D;
@@ -326,7 +327,7 @@ __device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<
   for (int i = 0; i < n; ++i) hp[i] = __shfl_sync(0xffffffffu, hp_lane, i);
   uint16_t* hr = a.h_in + t * D;
   float sq = 0.f;   // sum of the bf16 h_in values squared (when h_in_rstd is asked for)
-  if (a.x8 != nullptr) {
+  if constexpr (kFp8) {
     // (3, fp8 x) h_in = sum_i (h_pre[i] 2^e) x8[i, :]: scaling the weights by
     // the power of two instead of each x value gives the same products, so
     // the result is the one of the bf16 forward on x = x8 2^e, bit for bit
@@ -387,8 +388,7 @@ __device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<
       sq = warp_sum(sq);
       if (lane == 0) a.h_in_rstd[t] = 1.0f / sqrtf(sq / (float)D + a.h_in_eps);
     }
-    return;
-  }
+  } else {
   // (3) h_in = sum_i h_pre[i] x[i, :], streamed (U 256-element chunks in flight per lane)
   const uint16_t* xr = a.x + t * nD;
   constexpr int U = n <= 4 ? 4 : 2;
@@ -437,17 +437,18 @@ __device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<
     sq = warp_sum(sq);
     if (lane == 0) a.h_in_rstd[t] = 1.0f / sqrtf(sq / (float)D + a.h_in_eps);
   }
+  }
 }
 
 // Forward, second kernel of the two-kernel forward: warp t % W takes token t.
-template <int n>
+template <int n, bool kFp8 = false>
 __global__ void __launch_bounds__(kThreads, 1) fwd_rows_kernel(const FwdRowArgs a, int64_t T) {
   const int lane = threadIdx.x & 31;
   const int64_t gw = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
   const int64_t W = (int64_t)gridDim.x * kWarps;
   FwdRow<n> k;
   k.load(a, lane);
-  for (int64_t t = gw; t < T; t += W) fwd_row_token<n>(a, k, t, lane);
+  for (int64_t t = gw; t < T; t += W) fwd_row_token<n, kFp8>(a, k, t, lane);
 }
 
 }  // namespace rowdot
