@@ -97,7 +97,7 @@ typedef struct mhc_bwd_args {
   const uint16_t* x;
   const float* phi;
   const float* alpha;
-  const float* bias;     /* unused, may be NULL */
+  const float* bias;     /* read by the recompute form only; else may be NULL */
   const float* inv_rms;
   const float* h_mix;
   const float* h_pre;
