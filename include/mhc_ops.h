@@ -50,7 +50,9 @@ typedef enum mhc_status {
   MHC_ERR_CUDA = 5,                /* a CUDA runtime/driver call failed (see mhc_last_cuda_error) */
   MHC_ERR_DEVICE_TIMEOUT = 6,      /* a kernel's bounded wait expired (read by mhc_read_device_status) */
   MHC_ERR_NO_DEVICE = 7,           /* no sm_100 device is current */
-  MHC_ERR_LIMIT = 8                /* a size beyond a fixed limit of the entry point */
+  MHC_ERR_LIMIT = 8,               /* a size beyond a fixed limit of the entry point */
+  MHC_ERR_OUT_OF_BOUNDS = 9,       /* a debug-bounds build saw an access outside the call's buffers */
+  MHC_ERR_UNSUPPORTED = 10         /* the entry point is not part of this build */
 } mhc_status;
 
 /* Forward arguments.  Replaces the Python signature
@@ -309,8 +311,30 @@ MHC_API uint64_t mhc_launch_count(void);
 
 /* Version of this ABI (major*10000 + minor*100 + patch).  1.1.0 added the
  * post-op and the device-free plan queries, 1.2.0 the backward that
- * recomputes the forward's intermediates and mhc_fwd_ex. */
+ * recomputes the forward's intermediates and mhc_fwd_ex, 1.3.0 the
+ * debug-bounds entry points. */
 MHC_API int mhc_abi_version(void);
+
+/* Debug-bounds builds (compiled with -DMHC_DEBUG_BOUNDS: lib/libmhc_ops_dbg.so
+ * from `python -m mhc_ops_b200.build --debug-bounds`).  Every entry point
+ * registers the buffers it was given (argument arrays with their byte sizes
+ * and the workspace) before it launches, and every checked global access of
+ * the kernels must lie inside one of them; one that does not is skipped --
+ * nothing traps -- and the first is recorded.  mhc_debug_bounds synchronizes
+ * the device, copies the record {count, site, address, bytes} of the calls
+ * since the last clear into record[4] (site = file id * 100000 + source line
+ * of the check) and clears it when clear != 0; it returns MHC_OK when count
+ * is 0 and MHC_ERR_OUT_OF_BOUNDS otherwise.  One call at a time per process
+ * (the buffer table is global), and not under stream capture.  Normal builds
+ * check nothing and return MHC_ERR_UNSUPPORTED.  No counterpart in the
+ * reference, which has no sanitizer path. */
+MHC_API int mhc_debug_bounds(uint64_t* record, int clear);
+
+/* Debug-bounds builds: runs one kernel that checks an address one byte past a
+ * 256-byte buffer it registers inside `workspace` (no memory is accessed: the
+ * check alone fails and is recorded), so a test can see the record path work.
+ * Normal builds return MHC_ERR_UNSUPPORTED. */
+MHC_API int mhc_debug_bounds_selftest(void* workspace, void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,8 +1,10 @@
 """ctypes binding of libmhc_ops.so (the C ABI declared in include/mhc_ops.h).
 
 The library is built in-tree (``python -m mhc_ops_b200.build``) and loaded
-from ``mhc_ops_b200/lib/libmhc_ops.so``.  There is no fallback: if the library
-is missing or no sm_100 GPU is current, the calls raise.
+from ``mhc_ops_b200/lib/libmhc_ops.so``, or from the path in the environment
+variable MHC_OPS_LIBRARY (e.g. the debug-bounds build
+``lib/libmhc_ops_dbg.so``).  There is no fallback: if the library is missing
+or no sm_100 GPU is current, the calls raise.
 """
 from __future__ import annotations
 
@@ -12,10 +14,13 @@ import threading
 
 import torch
 
-_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libmhc_ops.so")
+_LIB_PATH = os.environ.get("MHC_OPS_LIBRARY") or os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib",
+                                                                "libmhc_ops.so")
 
 MHC_OK = 0
 MHC_ERR_DEVICE_TIMEOUT = 6
+MHC_ERR_OUT_OF_BOUNDS = 9
+MHC_ERR_UNSUPPORTED = 10
 
 _c_void_p = ctypes.c_void_p
 
@@ -99,6 +104,8 @@ SIGNATURES = {
     "mhc_post_bwd": (ctypes.c_int, [ctypes.POINTER(PostBwdArgs), _c_void_p]),
     "mhc_launch_count": (ctypes.c_uint64, []),
     "mhc_abi_version": (ctypes.c_int, []),
+    "mhc_debug_bounds": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint64), ctypes.c_int]),
+    "mhc_debug_bounds_selftest": (ctypes.c_int, [_c_void_p, _c_void_p]),
 }
 
 _lib = None
@@ -271,6 +278,21 @@ def query_plan(which: int, tokens: int, n: int, D: int, sms: int | None = None) 
 
 def launch_count() -> int:
     return int(load().mhc_launch_count())
+
+
+def debug_bounds(clear: bool = True, raise_on_hit: bool = True) -> dict:
+    """The debug-bounds record of the calls since the last clear (synchronizes
+    the device): ``{"count", "site", "address", "bytes"}``, site = file id *
+    100000 + source line of the failed check.  Raises MhcError when an access
+    fell outside its call's buffers (unless ``raise_on_hit`` is False), and
+    MhcError(MHC_ERR_UNSUPPORTED) with a normal build loaded."""
+    rec = (ctypes.c_uint64 * 4)()
+    st = load().mhc_debug_bounds(rec, 1 if clear else 0)
+    out = {"count": int(rec[0]), "site": int(rec[1]), "address": int(rec[2]), "bytes": int(rec[3])}
+    if st == MHC_ERR_OUT_OF_BOUNDS and not raise_on_hit:
+        return out
+    check(st, f"mhc_debug_bounds {out}")
+    return out
 
 
 def read_device_status(ws: torch.Tensor, stream: torch.cuda.Stream) -> int:

@@ -4,7 +4,11 @@
 
 * mhc_ops_b200/lib/libmhc_ops.so -- the kernels and the C ABI, nvcc for sm_100a;
 * mhc_ops_b200/lib/libmhc_torch.so -- the TORCH_LIBRARY(mhc, ...) operators
-  over that C ABI (csrc/torch_ops.cpp), g++ against the installed torch.
+  over that C ABI (csrc/torch_ops.cpp), g++ against the installed torch;
+* mhc_ops_b200/lib/libmhc_ops_dbg.so (``--debug-bounds``) -- the same
+  sources with -DMHC_DEBUG_BOUNDS: every checked global access must fall in
+  the buffers of its call, or it is skipped and recorded (mhc_debug_bounds).
+  Load it by setting MHC_OPS_LIBRARY to its path before importing the package.
 
 A build is skipped when its .so is newer than every source it depends on,
 unless force=True.
@@ -22,6 +26,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIBDIR = os.path.join(PKG, "lib")
 LIB = os.path.join(LIBDIR, "libmhc_ops.so")
+DBG_LIB = os.path.join(LIBDIR, "libmhc_ops_dbg.so")
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
@@ -80,13 +85,17 @@ def build_torch_ops(force: bool = False, verbose: bool = False) -> str:
     return TORCH_LIB
 
 
-def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | None = None) -> str:
-    """Compile csrc/mhc_ops.cu into lib/libmhc_ops.so; returns the library path."""
-    if not force and up_to_date():
-        return LIB
+def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | None = None,
+          debug_bounds: bool = False) -> str:
+    """Compile csrc/mhc_ops.cu into lib/libmhc_ops.so (lib/libmhc_ops_dbg.so
+    with debug_bounds); returns the library path."""
+    lib = DBG_LIB if debug_bounds else LIB
+    if not force and up_to_date(lib):
+        return lib
     os.makedirs(LIBDIR, exist_ok=True)
-    tmp = LIB + ".tmp"
-    cmd = [_nvcc(), *ARCH_FLAGS, *NVCC_FLAGS, *(extra_flags or []),
+    tmp = lib + ".tmp"
+    flags = (["-DMHC_DEBUG_BOUNDS"] if debug_bounds else []) + list(extra_flags or [])
+    cmd = [_nvcc(), *ARCH_FLAGS, *NVCC_FLAGS, *flags,
            "-I", os.path.join(ROOT, "include"), os.path.join(CSRC, "mhc_ops.cu"), "-o", tmp, "-lcuda"]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
@@ -95,11 +104,14 @@ def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | N
         raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
     if verbose and (res.stdout or res.stderr):
         print(res.stdout + res.stderr, file=sys.stderr)
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib)
+    return lib
 
 
 if __name__ == "__main__":
     force = "--force" in sys.argv
-    print(build(force=force, verbose=True))
-    print(build_torch_ops(force=force, verbose=True))
+    if "--debug-bounds" in sys.argv:
+        print(build(force=force, verbose=True, debug_bounds=True))
+    else:
+        print(build(force=force, verbose=True))
+        print(build_torch_ops(force=force, verbose=True))

@@ -40,6 +40,9 @@
 #include "common.cuh"
 #include "sm100.cuh"
 
+#undef MHC_FILE_ID
+#define MHC_FILE_ID 5   // debug-bounds site ids: 5 * 100000 + line
+
 namespace mhc {
 namespace bwdtc {
 
@@ -156,6 +159,7 @@ __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.
 __device__ __forceinline__ void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  src = MHC_LDP(src, 16);
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
@@ -163,6 +167,7 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
 }
 
 __device__ __forceinline__ void red_add_f32(float* addr, float v) {
+  addr = MHC_STP(addr, 4);
   asm volatile("red.global.add.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
 }
 
@@ -572,7 +577,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int jj = c16 * 16 + e;
                 if (jj < N_OUT) {
                   const float v = mid[e] + hi[e];
-                  if (j == 0) gp[(int64_t)jj * nD] = v;
+                  if (j == 0) MHC_ST(gp + (int64_t)jj * nD, v);
                   else red_add_f32(gp + (int64_t)jj * nD, v);
                 }
               }
@@ -621,7 +626,7 @@ __global__ void __launch_bounds__(256) phit_kernel(const float* __restrict__ phi
     const int idx = it * 256 + (int)threadIdx.x;
     const int j = idx / kBK, kk = idx - j * kBK;
     const int64_t k = (int64_t)blk * kBK + kk;
-    v[it] = idx < Cf::N_OUT * kBK ? __ldg(phi + (int64_t)j * nD + k) * (gamma ? __ldg(gamma + k) : 1.0f) : 0.f;
+    v[it] = idx < Cf::N_OUT * kBK ? MHC_LDG(phi + (int64_t)j * nD + k) * (gamma ? MHC_LDG(gamma + k) : 1.0f) : 0.f;
   }
 #pragma unroll
   for (int it = 0; it < PER; ++it) {
@@ -643,7 +648,7 @@ __global__ void __launch_bounds__(256) phit_kernel(const float* __restrict__ phi
       const uint32_t hi = jb < Cf::N_OUT ? split_term(cols[jb][kk], e) : 0;
       w[h] = lo | (hi << 16);
     }
-    *reinterpret_cast<uint4*>(out + (size_t)t * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    MHC_ST(reinterpret_cast<uint4*>(out + (size_t)t * 16), make_uint4(w[0], w[1], w[2], w[3]));
   }
 }
 

@@ -6,6 +6,7 @@
 #include <stdint.h>
 #include <atomic>
 #include <cstring>
+#include <type_traits>
 
 #include "../../include/mhc_ops.h"
 
@@ -75,5 +76,70 @@ __device__ __forceinline__ float warp_sum(float v) {
 __device__ __forceinline__ void set_device_status(int* status, int code) {
   if (status != nullptr) atomicExch(status, code);
 }
+
+// ------------------------------------------------------------------ debug-bounds builds
+// Built with -DMHC_DEBUG_BOUNDS (python -m mhc_ops_b200.build --debug-bounds,
+// lib/libmhc_ops_dbg.so), every global access written through MHC_CHK /
+// MHC_LD / MHC_LDG / MHC_ST / MHC_LDP / MHC_STP is checked against the buffers
+// of the current call, which each entry point registers before it launches
+// (the argument tensors and the workspace, with their byte sizes).  An access
+// that does not lie inside one of them is not made -- nothing traps -- and the
+// first one is recorded
+// {count, site, address, bytes}; mhc_debug_bounds() returns the record.  The
+// site is file id * 100000 + source line.  TMA accesses need no check: the
+// tensor maps clip them.  One call at a time per process in these builds (the
+// buffer table is global).  In normal builds the macros are the bare access.
+constexpr int kDbgBufs = 32;
+struct DbgBuf {
+  unsigned long long lo, hi;   // [lo, hi) bytes
+};
+#ifdef MHC_DEBUG_BOUNDS
+__device__ DbgBuf g_dbg_bufs[kDbgBufs];
+__device__ int g_dbg_nbufs;
+__device__ unsigned long long g_dbg_oob[4];
+__device__ uint4 g_dbg_zero;   // what a failed checked load reads (never written)
+__device__ uint4 g_dbg_sink;   // where a failed checked store goes
+
+__device__ __noinline__ bool dbg_check(const void* p, unsigned bytes, unsigned site) {
+  const unsigned long long a = reinterpret_cast<unsigned long long>(p), b = a + bytes;
+  const int nb = g_dbg_nbufs;
+  for (int i = 0; i < nb && i < kDbgBufs; ++i)
+    if (a >= g_dbg_bufs[i].lo && b <= g_dbg_bufs[i].hi) return true;
+  if (atomicAdd(&g_dbg_oob[0], 1ull) == 0ull) {
+    g_dbg_oob[1] = site;
+    g_dbg_oob[2] = a;
+    g_dbg_oob[3] = bytes;
+  }
+  return false;
+}
+// A failed check redirects the access (loads read zeros, stores land in a
+// sink) instead of branching around it, so the arithmetic around a checked
+// access compiles as in a normal build (same FMA contractions, same bits).
+template <class T>
+__device__ __forceinline__ T* dbg_ld_ptr(T* p, unsigned bytes, unsigned site) {
+  return dbg_check(p, bytes, site) ? p : reinterpret_cast<T*>(&g_dbg_zero);
+}
+template <class T>
+__device__ __forceinline__ T* dbg_st_ptr(T* p, unsigned bytes, unsigned site) {
+  return dbg_check(p, bytes, site) ? p : reinterpret_cast<T*>(&g_dbg_sink);
+}
+#define MHC_SITE ((unsigned)(MHC_FILE_ID * 100000 + __LINE__))
+#define MHC_CHK(p, bytes) ::mhc::dbg_check((p), (unsigned)(bytes), MHC_SITE)
+#define MHC_LDP(p, bytes) ::mhc::dbg_ld_ptr((p), (unsigned)(bytes), MHC_SITE)   // at most 16 bytes
+#define MHC_STP(p, bytes) ::mhc::dbg_st_ptr((p), (unsigned)(bytes), MHC_SITE)   // at most 16 bytes
+#define MHC_LDG(p) __ldg(MHC_LDP((p), sizeof(*(p))))
+#define MHC_LD(p) (*MHC_LDP((p), sizeof(*(p))))
+#define MHC_ST(p, v) (void)(*MHC_STP((p), sizeof(*(p))) = (v))
+#else
+#define MHC_CHK(p, bytes) true
+#define MHC_LDP(p, bytes) (p)
+#define MHC_STP(p, bytes) (p)
+#define MHC_LDG(p) __ldg(p)
+#define MHC_LD(p) (*(p))
+#define MHC_ST(p, v) (void)(*(p) = (v))
+#endif
+#ifndef MHC_FILE_ID
+#define MHC_FILE_ID 0
+#endif
 
 }  // namespace mhc

@@ -46,6 +46,9 @@
 #include "rowdot.cuh"
 #include "sm100.cuh"
 
+#undef MHC_FILE_ID
+#define MHC_FILE_ID 6   // debug-bounds site ids: 6 * 100000 + line
+
 namespace mhc {
 namespace fwdtc {
 
@@ -365,7 +368,7 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
         float4* dst = reinterpret_cast<float4*>(p.part + t * p.part_stride + (int64_t)ks * Cf::RW);
 #pragma unroll
         for (int c = 0; c < Cf::RW / 4; ++c)
-          dst[c] = make_float4(rowv[4 * c], rowv[4 * c + 1], rowv[4 * c + 2], rowv[4 * c + 3]);
+          MHC_ST(dst + c, make_float4(rowv[4 * c], rowv[4 * c + 1], rowv[4 * c + 2], rowv[4 * c + 3]));
       }
       if constexpr (kFused) signal_unit(p.tile_done + tile, lane);
     }
@@ -378,7 +381,7 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
       float scale = 1.f;   // fp8: 2^e of this row's token (rows past the batch are zero anyway)
       if constexpr (kFp8) {
         const int64_t t = (int64_t)(u / p.S_K) * kBM + row;
-        if (p.rows.x_exp != nullptr && t < p.T) scale = ldexpf(1.0f, (int)__ldg(p.rows.x_exp + t));
+        if (p.rows.x_exp != nullptr && t < p.T) scale = ldexpf(1.0f, (int)MHC_LDG(p.rows.x_exp + t));
       }
       for (int kb = 0; kb < KB; ++kb, ++it) {
         const int s = it % S;
@@ -508,7 +511,7 @@ __global__ void __launch_bounds__(256) split_phi_kernel(const float* __restrict_
   // store); needs nD % 8 == 0.
   using Cf = Cfg<n, kNT>;
   if (tile_done)
-    for (int64_t i = blockIdx.x * 256ll + threadIdx.x; i < tiles; i += (int64_t)gridDim.x * 256) tile_done[i] = 0;
+    for (int64_t i = blockIdx.x * 256ll + threadIdx.x; i < tiles; i += (int64_t)gridDim.x * 256) MHC_ST(tile_done + i, 0);
   const int64_t per_row = nD / 8;
   const int64_t total = (int64_t)Cf::NB * per_row;
   for (int64_t idx = blockIdx.x * 256ll + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * 256) {
@@ -517,7 +520,7 @@ __global__ void __launch_bounds__(256) split_phi_kernel(const float* __restrict_
     uint32_t w[4] = {0, 0, 0, 0};
     if (phi_bf16 != nullptr) {
       if (r < Cf::N_OUT) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(phi_bf16 + (int64_t)r * nD + k));
+        const uint4 v = MHC_LDG(reinterpret_cast<const uint4*>(phi_bf16 + (int64_t)r * nD + k));
         w[0] = v.x;
         w[1] = v.y;
         w[2] = v.z;
@@ -525,8 +528,8 @@ __global__ void __launch_bounds__(256) split_phi_kernel(const float* __restrict_
       }
     } else if (r < Cf::NT * Cf::N_OUT) {
       const int term = r / Cf::N_OUT, j = r - term * Cf::N_OUT;
-      const float4 a = __ldg(reinterpret_cast<const float4*>(phi + (int64_t)j * nD + k));
-      const float4 b = __ldg(reinterpret_cast<const float4*>(phi + (int64_t)j * nD + k + 4));
+      const float4 a = MHC_LDG(reinterpret_cast<const float4*>(phi + (int64_t)j * nD + k));
+      const float4 b = MHC_LDG(reinterpret_cast<const float4*>(phi + (int64_t)j * nD + k + 4));
       const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
@@ -544,7 +547,7 @@ __global__ void __launch_bounds__(256) split_phi_kernel(const float* __restrict_
         w[h] = t2[0] | (t2[1] << 16);
       }
     }
-    *reinterpret_cast<uint4*>(phis + (int64_t)r * nD + k) = make_uint4(w[0], w[1], w[2], w[3]);
+    MHC_ST(reinterpret_cast<uint4*>(phis + (int64_t)r * nD + k), make_uint4(w[0], w[1], w[2], w[3]));
   }
 }
 

@@ -9,6 +9,9 @@
 
 #include "common.cuh"
 
+#undef MHC_FILE_ID
+#define MHC_FILE_ID 1   // debug-bounds site ids: 1 * 100000 + line
+
 namespace mhc {
 namespace generic {
 
@@ -61,42 +64,42 @@ __global__ void __launch_bounds__(kThreads) fwd_kernel(
 #pragma unroll
     for (int j = 0; j <= N; ++j) acc[j] = 0.f;
     for (int k = threadIdx.x; k < nD; k += kThreads) {
-      const float xv = bf16_bits_to_f32(xr[k]);
+      const float xv = bf16_bits_to_f32(MHC_LD(&xr[k]));
       acc[N] = fmaf(xv, xv, acc[N]);
 #pragma unroll
-      for (int j = 0; j < N; ++j) acc[j] = fmaf(xv, __ldg(phi + (int64_t)j * nD + k), acc[j]);
+      for (int j = 0; j < N; ++j) acc[j] = fmaf(xv, MHC_LDG(phi + (int64_t)j * nD + k), acc[j]);
     }
     block_sum<N + 1>(acc, red, tot);
 
     if (threadIdx.x == 0) {
       const float ir = 1.0f / sqrtf(tot[N] / (float)nD + norm_eps);
-      const float a_pre = alpha[0], a_post = alpha[1], a_res = alpha[2];
-      if (inv_rms_out) inv_rms_out[t] = ir;
+      const float a_pre = MHC_LD(&alpha[0]), a_post = MHC_LD(&alpha[1]), a_res = MHC_LD(&alpha[2]);
+      if (inv_rms_out) MHC_ST(&inv_rms_out[t], ir);
       for (int j = 0; j < N; ++j)
-        if (h_mix_out) h_mix_out[t * N + j] = tot[j];
+        if (h_mix_out) MHC_ST(&h_mix_out[t * N + j], tot[j]);
       for (int i = 0; i < n; ++i) {
-        const float hp = sigmoid_acc(a_pre * (tot[i] * ir) + bias[i]) + hc_eps;
+        const float hp = sigmoid_acc(a_pre * (tot[i] * ir) + MHC_LD(&bias[i])) + hc_eps;
         hpre_s[i] = hp;
-        if (h_pre_out) h_pre_out[t * n + i] = hp;
-        h_post[t * n + i] = 2.0f * sigmoid_acc(a_post * (tot[n + i] * ir) + bias[n + i]);
+        if (h_pre_out) MHC_ST(&h_pre_out[t * n + i], hp);
+        MHC_ST(&h_post[t * n + i], 2.0f * sigmoid_acc(a_post * (tot[n + i] * ir) + MHC_LD(&bias[n + i])));
       }
-      for (int m = 0; m < n * n; ++m) h_res[t * n * n + m] = a_res * (tot[2 * n + m] * ir) + bias[2 * n + m];
+      for (int m = 0; m < n * n; ++m) MHC_ST(&h_res[t * n * n + m], a_res * (tot[2 * n + m] * ir) + MHC_LD(&bias[2 * n + m]));
     }
     __syncthreads();
     float sq[1] = {0.f};   // sum of the bf16 h_in values squared (h_in_rstd)
     for (int d = threadIdx.x; d < D; d += kThreads) {
       float s = 0.f;
 #pragma unroll
-      for (int i = 0; i < n; ++i) s = fmaf(hpre_s[i], bf16_bits_to_f32(xr[i * D + d]), s);
+      for (int i = 0; i < n; ++i) s = fmaf(hpre_s[i], bf16_bits_to_f32(MHC_LD(&xr[i * D + d])), s);
       const uint16_t b = f32_to_bf16_bits(s);
-      h_in[t * D + d] = b;
+      MHC_ST(&h_in[t * D + d], b);
       const float r = bf16_bits_to_f32(b);
       sq[0] = fmaf(r, r, sq[0]);
     }
     __syncthreads();
     if (h_in_rstd) {
       block_sum<1>(sq, red, tot);
-      if (threadIdx.x == 0) h_in_rstd[t] = 1.0f / sqrtf(tot[0] / (float)D + h_in_eps);
+      if (threadIdx.x == 0) MHC_ST(&h_in_rstd[t], 1.0f / sqrtf(tot[0] / (float)D + h_in_eps));
       __syncthreads();
     }
   }
@@ -129,47 +132,47 @@ __global__ void __launch_bounds__(kThreads) bwd_token_kernel(
 #pragma unroll
     for (int i = 0; i < n; ++i) p[i] = 0.f;
     for (int d = threadIdx.x; d < D; d += kThreads) {
-      const float g = bf16_bits_to_f32(gr[d]);
+      const float g = bf16_bits_to_f32(MHC_LD(&gr[d]));
 #pragma unroll
-      for (int i = 0; i < n; ++i) p[i] = fmaf(g, bf16_bits_to_f32(xr[i * D + d]), p[i]);
+      for (int i = 0; i < n; ++i) p[i] = fmaf(g, bf16_bits_to_f32(MHC_LD(&xr[i * D + d])), p[i]);
     }
     block_sum<n>(p, red, tot);
 
     if (threadIdx.x == 0) {
-      const float a_pre = alpha[0], a_post = alpha[1], a_res = alpha[2];
-      const float ir = inv_rms[t];
+      const float a_pre = MHC_LD(&alpha[0]), a_post = MHC_LD(&alpha[1]), a_res = MHC_LD(&alpha[2]);
+      const float ir = MHC_LD(&inv_rms[t]);
       float tmp[N];
       float dal0 = 0.f, dal1 = 0.f, dal2 = 0.f, dinv = 0.f;
       float* tp = tokpart + t * W;
       for (int i = 0; i < n; ++i) {
-        const float hp = h_pre[t * n + i];
+        const float hp = MHC_LD(&h_pre[t * n + i]);
         hpre_s[i] = hp;
         const float s = hp - hc_eps;
         const float dpre2 = tot[i] * s * (1.0f - s);
-        const float hq = h_post[t * n + i];
-        const float dpost2 = dh_post[t * n + i] * hq * (1.0f - hq / 2.0f);
+        const float hq = MHC_LD(&h_post[t * n + i]);
+        const float dpost2 = MHC_LD(&dh_post[t * n + i]) * hq * (1.0f - hq / 2.0f);
         tmp[i] = a_pre * dpre2;
         tmp[n + i] = a_post * dpost2;
-        dal0 += dpre2 * (h_mix[t * N + i] * ir);
-        dal1 += dpost2 * (h_mix[t * N + n + i] * ir);
-        tp[3 + i] = dpre2;
-        tp[3 + n + i] = dpost2;
+        dal0 += dpre2 * (MHC_LD(&h_mix[t * N + i]) * ir);
+        dal1 += dpost2 * (MHC_LD(&h_mix[t * N + n + i]) * ir);
+        MHC_ST(&tp[3 + i], dpre2);
+        MHC_ST(&tp[3 + n + i], dpost2);
       }
       for (int m = 0; m < n * n; ++m) {
-        const float dr = dh_res[t * n * n + m];
+        const float dr = MHC_LD(&dh_res[t * n * n + m]);
         tmp[2 * n + m] = a_res * dr;
-        dal2 += dr * (h_mix[t * N + 2 * n + m] * ir);
-        tp[3 + 2 * n + m] = dr;
+        dal2 += dr * (MHC_LD(&h_mix[t * N + 2 * n + m]) * ir);
+        MHC_ST(&tp[3 + 2 * n + m], dr);
       }
       for (int j = 0; j < N; ++j) {
-        dinv += tmp[j] * h_mix[t * N + j];
+        dinv += tmp[j] * MHC_LD(&h_mix[t * N + j]);
         const float dm = tmp[j] * ir;
         dmix_s[j] = dm;
-        dh_mix_ws[t * N + j] = dm;
+        MHC_ST(&dh_mix_ws[t * N + j], dm);
       }
-      tp[0] = dal0;
-      tp[1] = dal1;
-      tp[2] = dal2;
+      MHC_ST(&tp[0], dal0);
+      MHC_ST(&tp[1], dal1);
+      MHC_ST(&tp[2], dal2);
       c_s = dinv * (ir * ir * ir) / (float)nD;
     }
     __syncthreads();
@@ -178,10 +181,10 @@ __global__ void __launch_bounds__(kThreads) bwd_token_kernel(
       const int i = k / D, d = k - i * D;
       float mm = 0.f;
 #pragma unroll
-      for (int j = 0; j < N; ++j) mm = fmaf(dmix_s[j], __ldg(phi + (int64_t)j * nD + k), mm);
-      const float gmm = gamma ? gamma[k] : 1.0f;
-      const float v = mm * gmm + ((-c) * bf16_bits_to_f32(xr[k]) + hpre_s[i] * bf16_bits_to_f32(gr[d]));
-      dx[t * (int64_t)nD + k] = f32_to_bf16_bits(v);
+      for (int j = 0; j < N; ++j) mm = fmaf(dmix_s[j], MHC_LDG(phi + (int64_t)j * nD + k), mm);
+      const float gmm = gamma ? MHC_LD(&gamma[k]) : 1.0f;
+      const float v = mm * gmm + ((-c) * bf16_bits_to_f32(MHC_LD(&xr[k])) + hpre_s[i] * bf16_bits_to_f32(MHC_LD(&gr[d])));
+      MHC_ST(&dx[t * (int64_t)nD + k], f32_to_bf16_bits(v));
     }
     __syncthreads();
   }
@@ -204,12 +207,12 @@ __global__ void __launch_bounds__(kThreads) bwd_g_kernel(const uint16_t* __restr
   for (int j = 0; j < N; ++j) acc[j] = 0.f;
   if (k < nD) {
     for (int64_t t = t0; t < t1; ++t) {
-      const float xv = bf16_bits_to_f32(x[t * nD + k]);
+      const float xv = bf16_bits_to_f32(MHC_LD(&x[t * nD + k]));
 #pragma unroll
-      for (int j = 0; j < N; ++j) acc[j] = fmaf(__ldg(dh_mix_ws + t * N + j), xv, acc[j]);
+      for (int j = 0; j < N; ++j) acc[j] = fmaf(MHC_LDG(dh_mix_ws + t * N + j), xv, acc[j]);
     }
 #pragma unroll
-    for (int j = 0; j < N; ++j) gpart[((int64_t)p * N + j) * nD + k] = acc[j];
+    for (int j = 0; j < N; ++j) MHC_ST(&gpart[((int64_t)p * N + j) * nD + k], acc[j]);
   }
 }
 
@@ -221,15 +224,15 @@ __device__ __forceinline__ void reduce_column(const float* __restrict__ part, in
   __shared__ float red[kWarps];
   float s = 0.f;
 #pragma unroll 4
-  for (int64_t r = threadIdx.x; r < rows; r += kThreads) s += part[r * W + c];
+  for (int64_t r = threadIdx.x; r < rows; r += kThreads) s += MHC_LD(&part[r * W + c]);
   s = warp_sum(s);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
   __syncthreads();
   if (threadIdx.x == 0) {
     float tot = 0.f;
     for (int w = 0; w < kWarps; ++w) tot += red[w];
-    if (c < 3) dalpha[c] = tot;
-    else dbias[c - 3] = tot;
+    if (c < 3) MHC_ST(&dalpha[c], tot);
+    else MHC_ST(&dbias[c - 3], tot);
   }
 }
 
@@ -260,7 +263,7 @@ __global__ void __launch_bounds__(kThreads) finalize_param_kernel(const float* _
   const int k = blockIdx.x * kFinCols + kk;
   float dg = 0.f;
   if (k < nD) {
-    const float gm = gamma ? __ldg(gamma + k) : 1.0f;
+    const float gm = gamma ? MHC_LDG(gamma + k) : 1.0f;
     // splits outer, this thread's rows inner: JPER independent loads per step,
     // each row still summed over p in ascending order
     float g[JPER];
@@ -270,15 +273,15 @@ __global__ void __launch_bounds__(kThreads) finalize_param_kernel(const float* _
 #pragma unroll
       for (int q = 0; q < JPER; ++q) {
         const int j = jg + q * JG;
-        if (j < N) g[q] += __ldg(gpart + ((int64_t)p * N + j) * nD + k);
+        if (j < N) g[q] += MHC_LDG(gpart + ((int64_t)p * N + j) * nD + k);
       }
     }
 #pragma unroll
     for (int q = 0; q < JPER; ++q) {
       const int j = jg + q * JG;
       if (j < N) {
-        dphi[(int64_t)j * nD + k] = gm * g[q];
-        dg = fmaf(__ldg(phi + (int64_t)j * nD + k), g[q], dg);
+        MHC_ST(&dphi[(int64_t)j * nD + k], gm * g[q]);
+        dg = fmaf(MHC_LDG(phi + (int64_t)j * nD + k), g[q], dg);
       }
     }
   }
@@ -288,7 +291,7 @@ __global__ void __launch_bounds__(kThreads) finalize_param_kernel(const float* _
     float s = part[0][kk];
 #pragma unroll
     for (int g2 = 1; g2 < JG; ++g2) s += part[g2][kk];
-    dgamma[k] = s;
+    MHC_ST(&dgamma[k], s);
   }
 }
 

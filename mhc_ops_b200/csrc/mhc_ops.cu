@@ -28,6 +28,9 @@
 #include "tiled.cuh"
 #include "post.cuh"
 
+#undef MHC_FILE_ID
+#define MHC_FILE_ID 7   // debug-bounds site ids: 7 * 100000 + line
+
 namespace mhc {
 
 std::atomic<uint64_t> g_launch_count{0};
@@ -133,7 +136,7 @@ struct FwdGeneric {
 // bf16 phi -> an fp32 copy, for the generic forward (exact widening).
 __global__ void phi_widen_kernel(const uint16_t* __restrict__ src, float* __restrict__ dst, int64_t count) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x)
-    dst[i] = bf16_bits_to_f32(src[i]);
+    MHC_ST(dst + i, bf16_bits_to_f32(MHC_LD(src + i)));
 }
 
 template <int n>
@@ -1068,13 +1071,15 @@ const char* mhc_status_string(int status) {
     case MHC_ERR_DEVICE_TIMEOUT: return "a kernel's bounded wait expired";
     case MHC_ERR_NO_DEVICE: return "the current device is not an sm_100 GPU";
     case MHC_ERR_LIMIT: return "a size is beyond this entry point's fixed limit";
+    case MHC_ERR_OUT_OF_BOUNDS: return "a debug-bounds build saw an access outside the call's buffers";
+    case MHC_ERR_UNSUPPORTED: return "the entry point is not part of this build";
     default: return "unknown mhc status";
   }
 }
 
 const char* mhc_last_cuda_error(void) { return t_last_cuda_error.c_str(); }
 
-int mhc_abi_version(void) { return 10200; }
+int mhc_abi_version(void) { return 10300; }
 
 uint64_t mhc_launch_count(void) { return g_launch_count.load(std::memory_order_relaxed); }
 
@@ -1098,6 +1103,85 @@ int mhc_bwd_workspace_size(int64_t tokens, int32_t n, int32_t D, size_t* bytes) 
 
 namespace mhc {
 namespace {
+// Debug-bounds builds: the buffers of the current call, copied to the
+// device's table in stream order before its kernels (common.cuh).  Absent
+// from normal builds.
+#ifdef MHC_DEBUG_BOUNDS
+struct DbgTable {
+  DbgBuf b[kDbgBufs];
+  int n = 0;
+  void add(const void* p, size_t bytes) {
+    if (!p || bytes == 0 || n >= kDbgBufs) return;
+    const unsigned long long lo = reinterpret_cast<unsigned long long>(p);
+    b[n++] = DbgBuf{lo, lo + bytes};
+  }
+  // the source is pageable host memory: the copy has taken it when the call returns
+  int upload(cudaStream_t s) const {
+    MHC_CUDA_TRY(cudaMemcpyToSymbolAsync(g_dbg_bufs, b, sizeof(DbgBuf) * kDbgBufs, 0, cudaMemcpyHostToDevice, s));
+    MHC_CUDA_TRY(cudaMemcpyToSymbolAsync(g_dbg_nbufs, &n, sizeof(int), 0, cudaMemcpyHostToDevice, s));
+    return MHC_OK;
+  }
+};
+
+int dbg_register_fwd(const mhc_fwd_args* a, const FwdEx& ex, cudaStream_t s) {
+  const size_t T = (size_t)a->tokens, n = (size_t)a->n, D = (size_t)a->D, N = n * n + 2 * n;
+  DbgTable t;
+  t.add(a->x, T * n * D * 2);
+  t.add(ex.x_fp8, T * n * D);
+  t.add(ex.x_exp, T);
+  t.add(a->phi, N * n * D * 4);
+  t.add(ex.phi_bf16, N * n * D * 2);
+  t.add(a->alpha, 3 * 4);
+  t.add(a->bias, N * 4);
+  t.add(a->h_in, T * D * 2);
+  t.add(a->h_post, T * n * 4);
+  t.add(a->h_res, T * n * n * 4);
+  t.add(a->inv_rms, T * 4);
+  t.add(a->h_mix, T * N * 4);
+  t.add(a->h_pre, T * n * 4);
+  t.add(ex.h_in_rstd, T * 4);
+  t.add(a->workspace, a->workspace_bytes);
+  return t.upload(s);
+}
+
+int dbg_register_bwd(const mhc_bwd_args* a, cudaStream_t s) {
+  const size_t T = (size_t)a->tokens, n = (size_t)a->n, D = (size_t)a->D, N = n * n + 2 * n;
+  DbgTable t;
+  t.add(a->x, T * n * D * 2);
+  t.add(a->phi, N * n * D * 4);
+  t.add(a->alpha, 3 * 4);
+  t.add(a->bias, N * 4);
+  t.add(a->inv_rms, T * 4);
+  t.add(a->h_mix, T * N * 4);
+  t.add(a->h_pre, T * n * 4);
+  t.add(a->h_post, T * n * 4);
+  t.add(a->dh_in, T * D * 2);
+  t.add(a->dh_post, T * n * 4);
+  t.add(a->dh_res, T * n * n * 4);
+  t.add(a->gamma, n * D * 4);
+  t.add(a->dx, T * n * D * 2);
+  t.add(a->dphi, N * n * D * 4);
+  t.add(a->dalpha, 3 * 4);
+  t.add(a->dbias, N * 4);
+  t.add(a->dgamma, n * D * 4);
+  t.add(a->workspace, a->workspace_bytes);
+  return t.upload(s);
+}
+
+template <class A>
+int dbg_register_post(const A* a, const void* const* ptrs, const size_t* sizes, int count, cudaStream_t s) {
+  (void)a;
+  DbgTable t;
+  for (int i = 0; i < count; ++i) t.add(ptrs[i], sizes[i]);
+  return t.upload(s);
+}
+
+__global__ void dbg_selftest_kernel(const char* buf) {
+  // one byte past the registered 256 bytes: the check fails, nothing is read
+  (void)MHC_CHK(buf + 256, 1);
+}
+#endif
+
 // mhc_fwd and mhc_fwd_ex: validation, then fwd_run.
 int fwd_entry(const mhc_fwd_args* a, const FwdEx& ex, void* stream) {
   if (!a) return MHC_ERR_NULL_POINTER;
@@ -1123,6 +1207,9 @@ int fwd_entry(const mhc_fwd_args* a, const FwdEx& ex, void* stream) {
       !aligned(a->bias, 4) || !aligned(a->h_post, 4) || !aligned(a->h_res, 4) || !aligned(a->inv_rms, 4) ||
       !aligned(a->h_mix, 4) || !aligned(a->h_pre, 4) || !aligned(ex.phi_bf16, 2) || !aligned(ex.h_in_rstd, 4))
     return MHC_ERR_MISALIGNED;
+#ifdef MHC_DEBUG_BOUNDS
+  if ((st = dbg_register_fwd(a, ex, static_cast<cudaStream_t>(stream)))) return st;
+#endif
   return fwd_run(a, ex, static_cast<cudaStream_t>(stream), sms);
 }
 }  // namespace
@@ -1215,6 +1302,9 @@ int mhc_bwd(const mhc_bwd_args* a, void* stream) {
       !aligned(a->dh_post, 4) || !aligned(a->dh_res, 4) || !aligned(a->gamma, 4) || !aligned(a->dphi, 4) ||
       !aligned(a->dalpha, 4) || !aligned(a->dbias, 4) || !aligned(a->dgamma, 4))
     return MHC_ERR_MISALIGNED;
+#ifdef MHC_DEBUG_BOUNDS
+  if ((st = dbg_register_bwd(a, s))) return st;
+#endif
   if (bwd_tc_eligible(a)) return bwd_tc_run(a, s, sms);
   if (bwd_tiled_eligible(a)) return dispatch_n<BwdTiled>(a->n, a, s, sms);
   return dispatch_n<BwdGeneric>(a->n, a, s, sms);
@@ -1300,6 +1390,14 @@ int mhc_post_fwd(const mhc_post_fwd_args* a, void* stream) {
   if (!aligned(a->x, 2) || !aligned(a->y, 2) || !aligned(a->out, 2) || !aligned(a->h_res, 4) ||
       !aligned(a->h_post, 4))
     return MHC_ERR_MISALIGNED;
+#ifdef MHC_DEBUG_BOUNDS
+  {
+    const size_t T = (size_t)a->tokens, n = (size_t)a->n, D = (size_t)a->D;
+    const void* ptrs[5] = {a->x, a->h_res, a->h_post, a->y, a->out};
+    const size_t sizes[5] = {T * n * D * 2, T * n * n * 4, T * n * 4, T * D * 2, T * n * D * 2};
+    if ((st = dbg_register_post(a, ptrs, sizes, 5, static_cast<cudaStream_t>(stream)))) return st;
+  }
+#endif
   return dispatch_n<PostFwd>(a->n, a, static_cast<cudaStream_t>(stream), sms);
 }
 
@@ -1316,7 +1414,52 @@ int mhc_post_bwd(const mhc_post_bwd_args* a, void* stream) {
       !aligned(a->dy, 2) || !aligned(a->h_res, 4) || !aligned(a->h_post, 4) || !aligned(a->dh_res, 4) ||
       !aligned(a->dh_post, 4))
     return MHC_ERR_MISALIGNED;
+#ifdef MHC_DEBUG_BOUNDS
+  {
+    const size_t T = (size_t)a->tokens, n = (size_t)a->n, D = (size_t)a->D;
+    const void* ptrs[9] = {a->x, a->h_res, a->h_post, a->y, a->dout, a->dx, a->dy, a->dh_res, a->dh_post};
+    const size_t sizes[9] = {T * n * D * 2, T * n * n * 4, T * n * 4, T * D * 2, T * n * D * 2,
+                             T * n * D * 2, T * D * 2,     T * n * n * 4, T * n * 4};
+    if ((st = dbg_register_post(a, ptrs, sizes, 9, static_cast<cudaStream_t>(stream)))) return st;
+  }
+#endif
   return dispatch_n<PostBwd>(a->n, a, static_cast<cudaStream_t>(stream), sms);
+}
+
+int mhc_debug_bounds(uint64_t* record, int clear) {
+  if (!record) return MHC_ERR_NULL_POINTER;
+  for (int i = 0; i < 4; ++i) record[i] = 0;
+#ifdef MHC_DEBUG_BOUNDS
+  MHC_CUDA_TRY(cudaDeviceSynchronize());
+  unsigned long long r[4] = {0, 0, 0, 0};
+  MHC_CUDA_TRY(cudaMemcpyFromSymbol(r, g_dbg_oob, sizeof(r)));
+  if (clear) {
+    const unsigned long long z[4] = {0, 0, 0, 0};
+    MHC_CUDA_TRY(cudaMemcpyToSymbol(g_dbg_oob, z, sizeof(z)));
+  }
+  for (int i = 0; i < 4; ++i) record[i] = r[i];
+  return r[0] == 0 ? MHC_OK : MHC_ERR_OUT_OF_BOUNDS;
+#else
+  (void)clear;
+  return MHC_ERR_UNSUPPORTED;
+#endif
+}
+
+int mhc_debug_bounds_selftest(void* workspace, void* stream) {
+#ifdef MHC_DEBUG_BOUNDS
+  if (!workspace) return MHC_ERR_NULL_POINTER;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DbgTable t;
+  t.add(workspace, 256);
+  int st;
+  if ((st = t.upload(s))) return st;
+  dbg_selftest_kernel<<<1, 1, 0, s>>>(static_cast<const char*>(workspace));
+  return after_launch();
+#else
+  (void)workspace;
+  (void)stream;
+  return MHC_ERR_UNSUPPORTED;
+#endif
 }
 
 int mhc_read_device_status(void* workspace, void* stream, int* device_status) {

@@ -21,6 +21,9 @@
 
 #include "common.cuh"
 
+#undef MHC_FILE_ID
+#define MHC_FILE_ID 3   // debug-bounds site ids: 3 * 100000 + line
+
 namespace mhc {
 namespace post {
 
@@ -32,7 +35,7 @@ constexpr int kU = 4;   // vectors per lane of one forward warp task
 template <int V>
 __device__ __forceinline__ void load_bf16(const uint16_t* p, float (&f)[V]) {
   if constexpr (V == 8) {
-    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint4 u = MHC_LDG(reinterpret_cast<const uint4*>(p));
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
@@ -41,18 +44,18 @@ __device__ __forceinline__ void load_bf16(const uint16_t* p, float (&f)[V]) {
     }
   } else {
 #pragma unroll
-    for (int e = 0; e < V; ++e) f[e] = bf16_bits_to_f32(__ldg(p + e));
+    for (int e = 0; e < V; ++e) f[e] = bf16_bits_to_f32(MHC_LDG(p + e));
   }
 }
 
 template <int V>
 __device__ __forceinline__ void store_bf16(uint16_t* p, const float (&f)[V]) {
   if constexpr (V == 8) {
-    *reinterpret_cast<uint4*>(p) =
-        make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+    MHC_ST(reinterpret_cast<uint4*>(p),
+           make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7])));
   } else {
 #pragma unroll
-    for (int e = 0; e < V; ++e) p[e] = f32_to_bf16_bits(f[e]);
+    for (int e = 0; e < V; ++e) MHC_ST(p + e, f32_to_bf16_bits(f[e]));
   }
 }
 
@@ -77,9 +80,9 @@ __global__ void __launch_bounds__(kThreads) post_fwd_kernel(const uint16_t* __re
     float cr[n][n], cp[n];
 #pragma unroll
     for (int i = 0; i < n; ++i) {
-      cp[i] = __ldg(h_post + t * n + i);
+      cp[i] = MHC_LDG(h_post + t * n + i);
 #pragma unroll
-      for (int j = 0; j < n; ++j) cr[i][j] = __ldg(h_res + (t * n + i) * n + j);
+      for (int j = 0; j < n; ++j) cr[i][j] = MHC_LDG(h_res + (t * n + i) * n + j);
     }
     const uint16_t* xt = x + t * n * D;
     uint16_t* ot = out + t * n * D;
@@ -127,9 +130,9 @@ __global__ void __launch_bounds__(kThreads, (n <= 4 ? 2 : 1)) post_bwd_kernel(co
     float cr[n][n], cp[n];
 #pragma unroll
     for (int i = 0; i < n; ++i) {
-      cp[i] = __ldg(h_post + t * n + i);
+      cp[i] = MHC_LDG(h_post + t * n + i);
 #pragma unroll
-      for (int j = 0; j < n; ++j) cr[i][j] = __ldg(h_res + (t * n + i) * n + j);
+      for (int j = 0; j < n; ++j) cr[i][j] = MHC_LDG(h_res + (t * n + i) * n + j);
     }
     float sr[n][n], sp[n];
 #pragma unroll
@@ -189,9 +192,9 @@ __global__ void __launch_bounds__(kThreads, (n <= 4 ? 2 : 1)) post_bwd_kernel(co
     if (lane == 0) {
 #pragma unroll
       for (int i = 0; i < n; ++i) {
-        dh_post[t * n + i] = sp[i];
+        MHC_ST(dh_post + t * n + i, sp[i]);
 #pragma unroll
-        for (int j = 0; j < n; ++j) dh_res[(t * n + i) * n + j] = sr[i][j];
+        for (int j = 0; j < n; ++j) MHC_ST(dh_res + (t * n + i) * n + j, sr[i][j]);
       }
     }
   }

@@ -9,6 +9,9 @@
 
 #include "common.cuh"
 
+#undef MHC_FILE_ID
+#define MHC_FILE_ID 2   // debug-bounds site ids: 2 * 100000 + line
+
 namespace mhc {
 namespace rowdot {
 
@@ -23,6 +26,7 @@ struct Rec {
 };
 
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  p = MHC_LDP(p, 16);
   uint4 v;
   asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
@@ -53,14 +57,14 @@ struct RowAcc {
   // this warp's partial row abpart[CW]: dalpha (3), then dbias (N_OUT)
   __device__ __forceinline__ void store(float* ap, int lane) const {
     if (lane == 0) {
-      ap[0] = al0;
-      ap[1] = al1;
-      ap[2] = al2;
+      MHC_ST(ap + 0, al0);
+      MHC_ST(ap + 1, al1);
+      MHC_ST(ap + 2, al2);
     }
 #pragma unroll
     for (int m = 0; m < M; ++m) {
       const int jj = lane + 32 * m;
-      if (jj < N_OUT) ap[3 + jj] = b[m];
+      if (jj < N_OUT) MHC_ST(ap + 3 + jj, b[m]);
     }
   }
 };
@@ -93,7 +97,7 @@ __device__ __forceinline__ void bwd_row_token(const BwdRowArgs& a, int64_t t, in
   constexpr int M = RowAcc<n>::M;
   const int D = a.D;
   const int nD = n * D;
-  const float a_pre = __ldg(a.alpha), a_post = __ldg(a.alpha + 1), a_res = __ldg(a.alpha + 2);
+  const float a_pre = MHC_LDG(a.alpha), a_post = MHC_LDG(a.alpha + 1), a_res = MHC_LDG(a.alpha + 2);
   // small per-token inputs first, so they are in flight during the row stream
   float hm[M], gin[M], dpo[M];
 #pragma unroll
@@ -101,18 +105,18 @@ __device__ __forceinline__ void bwd_row_token(const BwdRowArgs& a, int64_t t, in
     const int jj = lane + 32 * m;
     hm[m] = gin[m] = dpo[m] = 0.f;
     if (jj < N_OUT) {
-      hm[m] = __ldg(a.h_mix + t * N_OUT + jj);
+      hm[m] = MHC_LDG(a.h_mix + t * N_OUT + jj);
       if (jj < n) {
-        gin[m] = __ldg(a.h_pre + t * n + jj);
+        gin[m] = MHC_LDG(a.h_pre + t * n + jj);
       } else if (jj < 2 * n) {
-        gin[m] = __ldg(a.h_post + t * n + (jj - n));
-        dpo[m] = __ldg(a.dh_post + t * n + (jj - n));
+        gin[m] = MHC_LDG(a.h_post + t * n + (jj - n));
+        dpo[m] = MHC_LDG(a.dh_post + t * n + (jj - n));
       } else {
-        gin[m] = __ldg(a.dh_res + t * (n * n) + (jj - 2 * n));
+        gin[m] = MHC_LDG(a.dh_res + t * (n * n) + (jj - 2 * n));
       }
     }
   }
-  const float ir = __ldg(a.inv_rms + t);
+  const float ir = MHC_LDG(a.inv_rms + t);
 
   const uint16_t* xr = a.x + t * nD;
   const uint16_t* gr = a.dh_in + t * D;
@@ -180,7 +184,7 @@ __device__ __forceinline__ void bwd_row_token(const BwdRowArgs& a, int64_t t, in
         g2 = gin[m];
         tmp = a_res * g2;
       }
-      rt[jj] = tmp * ir;                          // dh_mix (golden.py:62)
+      MHC_ST(rt + jj, tmp * ir);                  // dh_mix (golden.py:62)
       acc.b[m] += g2;                             // dbias terms (golden.py:83-85)
       const float dal = g2 * (hm[m] * ir);        // dalpha terms (golden.py:77-79)
       if (jj < n) dal0 += dal;
@@ -194,13 +198,13 @@ __device__ __forceinline__ void bwd_row_token(const BwdRowArgs& a, int64_t t, in
   dal1 = warp_sum(dal1);
   dal2 = warp_sum(dal2);
   if (lane == 0) {
-    rt[N_OUT] = dinv * (ir * ir * ir) * (1.0f / (float)nD);   // c (golden.py:89)
+    MHC_ST(rt + N_OUT, dinv * (ir * ir * ir) * (1.0f / (float)nD));   // c (golden.py:89)
     acc.al0 += dal0;
     acc.al1 += dal1;
     acc.al2 += dal2;
   }
   for (int w = N_OUT + 1 + lane; w < R::W; w += 32)
-    rt[w] = (w - N_OUT - 1 < n) ? __ldg(a.h_pre + t * n + (w - N_OUT - 1)) : 0.f;
+    MHC_ST(rt + w, (w - N_OUT - 1 < n) ? MHC_LDG(a.h_pre + t * n + (w - N_OUT - 1)) : 0.f);
 }
 
 // B1 over all tokens: token t is owned by global warp t % W, so every sum
@@ -250,12 +254,12 @@ struct FwdRow {
   float a_pre, a_post, a_res, inv_nd;
   float bj[M];
   __device__ __forceinline__ void load(const FwdRowArgs& a, int lane) {
-    a_pre = __ldg(a.alpha);
-    a_post = __ldg(a.alpha + 1);
-    a_res = __ldg(a.alpha + 2);
+    a_pre = MHC_LDG(a.alpha);
+    a_post = MHC_LDG(a.alpha + 1);
+    a_res = MHC_LDG(a.alpha + 2);
     inv_nd = 1.0f / (float)(n * a.D);
 #pragma unroll
-    for (int m = 0; m < M; ++m) bj[m] = (lane + 32 * m) < N_OUT ? __ldg(a.bias + lane + 32 * m) : 0.f;
+    for (int m = 0; m < M; ++m) bj[m] = (lane + 32 * m) < N_OUT ? MHC_LDG(a.bias + lane + 32 * m) : 0.f;
   }
 };
 
@@ -281,7 +285,7 @@ __device__ __forceinline__ float fwd_row_gates(const FwdRowArgs& a, const FwdRow
       for (int k0 = 0; k0 < a.S_K; k0 += kBatch) {
         float v[kBatch];
 #pragma unroll
-        for (int b = 0; b < kBatch; ++b) v[b] = k0 + b < a.S_K ? pr[(k0 + b) * a.RW + c] : 0.f;
+        for (int b = 0; b < kBatch; ++b) v[b] = k0 + b < a.S_K ? MHC_LD(pr + (k0 + b) * a.RW + c) : 0.f;
 #pragma unroll
         for (int b = 0; b < kBatch; ++b) acc += v[b];
       }
@@ -299,16 +303,16 @@ __device__ __forceinline__ float fwd_row_gates(const FwdRowArgs& a, const FwdRow
       const float v = hm[m] * ir;
       if (jj < n) {
         hp_lane = sigmoid_acc(k.a_pre * v + k.bj[m]) + a.hc_eps;
-        if (a.h_pre) a.h_pre[t * n + jj] = hp_lane;
+        if (a.h_pre) MHC_ST(a.h_pre + t * n + jj, hp_lane);
       } else if (jj < 2 * n) {
-        a.h_post[t * n + (jj - n)] = 2.0f * sigmoid_acc(k.a_post * v + k.bj[m]);
+        MHC_ST(a.h_post + t * n + (jj - n), 2.0f * sigmoid_acc(k.a_post * v + k.bj[m]));
       } else {
-        a.h_res[t * (n * n) + (jj - 2 * n)] = k.a_res * v + k.bj[m];
+        MHC_ST(a.h_res + t * (n * n) + (jj - 2 * n), k.a_res * v + k.bj[m]);
       }
-      if (a.h_mix) a.h_mix[t * N_OUT + jj] = hm[m];
+      if (a.h_mix) MHC_ST(a.h_mix + t * N_OUT + jj, hm[m]);
     }
   }
-  if (lane == 0 && a.inv_rms) a.inv_rms[t] = ir;
+  if (lane == 0 && a.inv_rms) MHC_ST(a.inv_rms + t, ir);
   // Every lane has used its partials (the stores above consume them): only
   // now may row t of h_in, which holds them, be overwritten.
   __syncwarp();
@@ -331,7 +335,7 @@ __device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<
     // (3, fp8 x) h_in = sum_i (h_pre[i] 2^e) x8[i, :]: scaling the weights by
     // the power of two instead of each x value gives the same products, so
     // the result is the one of the bf16 forward on x = x8 2^e, bit for bit
-    const float sc = a.x_exp ? ldexpf(1.0f, (int)__ldg(a.x_exp + t)) : 1.0f;
+    const float sc = a.x_exp ? ldexpf(1.0f, (int)MHC_LDG(a.x_exp + t)) : 1.0f;
 #pragma unroll
     for (int i = 0; i < n; ++i) hp[i] *= sc;
     const uint8_t* xr8 = a.x8 + t * nD;
@@ -373,7 +377,7 @@ __device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<
             o[hh].y = pack_bf16x2(acc[8 * hh + 2], acc[8 * hh + 3]);
             o[hh].z = pack_bf16x2(acc[8 * hh + 4], acc[8 * hh + 5]);
             o[hh].w = pack_bf16x2(acc[8 * hh + 6], acc[8 * hh + 7]);
-            *reinterpret_cast<uint4*>(hr + d + 8 * hh) = o[hh];
+            MHC_ST(reinterpret_cast<uint4*>(hr + d + 8 * hh), o[hh]);
             if (a.h_in_rstd) {
               float r[8];
               bf16x8(o[hh], r);
@@ -386,7 +390,7 @@ __device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<
     }
     if (a.h_in_rstd) {
       sq = warp_sum(sq);
-      if (lane == 0) a.h_in_rstd[t] = 1.0f / sqrtf(sq / (float)D + a.h_in_eps);
+      if (lane == 0) MHC_ST(a.h_in_rstd + t, 1.0f / sqrtf(sq / (float)D + a.h_in_eps));
     }
   } else {
   // (3) h_in = sum_i h_pre[i] x[i, :], streamed (U 256-element chunks in flight per lane)
@@ -423,7 +427,7 @@ __device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<
         o.y = pack_bf16x2(acc[2], acc[3]);
         o.z = pack_bf16x2(acc[4], acc[5]);
         o.w = pack_bf16x2(acc[6], acc[7]);
-        *reinterpret_cast<uint4*>(hr + d) = o;
+        MHC_ST(reinterpret_cast<uint4*>(hr + d), o);
         if (a.h_in_rstd) {
           float r[8];
           bf16x8(o, r);
@@ -435,7 +439,7 @@ __device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<
   }
   if (a.h_in_rstd) {
     sq = warp_sum(sq);
-    if (lane == 0) a.h_in_rstd[t] = 1.0f / sqrtf(sq / (float)D + a.h_in_eps);
+    if (lane == 0) MHC_ST(a.h_in_rstd + t, 1.0f / sqrtf(sq / (float)D + a.h_in_eps));
   }
   }
 }

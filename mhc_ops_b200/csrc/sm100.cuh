@@ -9,6 +9,9 @@
 
 #include "common.cuh"
 
+#undef MHC_FILE_ID
+#define MHC_FILE_ID 8   // debug-bounds site ids: 8 * 100000 + line
+
 namespace mhc {
 namespace sm100 {
 
@@ -88,10 +91,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
 
 // ------------------------------------------------------------------ counters between CTAs of one launch
 __device__ __forceinline__ void red_release_add(int* p, int v) {
+  p = MHC_STP(p, 4);
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ int ld_acquire(const int* p) {
+  p = MHC_LDP(p, 4);   // a failed check reads 0: a counter wait then ends in its time limit
   int v;
   asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
@@ -156,6 +161,7 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
 
 // 16-byte global store with an L2 eviction-priority hint.
 __device__ __forceinline__ void st_global_hint(void* ptr, uint4 v, uint64_t pol) {
+  ptr = MHC_STP(ptr, 16);
   asm volatile("st.global.L2::cache_hint.v4.u32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(ptr), "r"(v.x), "r"(v.y), "r"(v.z),
                "r"(v.w), "l"(pol)
                : "memory");

@@ -29,6 +29,9 @@
 #include "bwd_sm100.cuh"
 #include "sm100.cuh"
 
+#undef MHC_FILE_ID
+#define MHC_FILE_ID 4   // debug-bounds site ids: 4 * 100000 + line
+
 namespace mhc {
 namespace tiled {
 
@@ -49,6 +52,7 @@ struct Dims {
 inline int64_t padded_tokens(int64_t T) { return (T + kTT - 1) / kTT * kTT; }
 
 __device__ __forceinline__ void cp16(void* dst_smem, const void* src) {
+  src = MHC_LDP(src, 16);
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst_smem)),
                "l"(src)
                : "memory");
@@ -80,13 +84,13 @@ __global__ void __launch_bounds__(kThreads) transpose_kernel(const float* __rest
   for (int r = ty; r < 32; r += kThreads / 32) {
     const int64_t t = t0 + r;
     const int j = j0 + tx;
-    tile[r][tx] = (t < T && j < N) ? __ldg(rec + t * RW + j) : 0.f;
+    tile[r][tx] = (t < T && j < N) ? MHC_LDG(rec + t * RW + j) : 0.f;
   }
   __syncthreads();
   for (int r = ty; r < 32; r += kThreads / 32) {
     const int j = j0 + r;
     const int64_t t = t0 + tx;
-    if (j < N && t < Tp) dmT[(int64_t)j * Tp + t] = tile[tx][r];
+    if (j < N && t < Tp) MHC_ST(dmT + (int64_t)j * Tp + t, tile[tx][r]);
   }
 }
 
@@ -125,7 +129,7 @@ __global__ void __launch_bounds__(kThreads) dx_kernel(const uint16_t* __restrict
   for (int e = threadIdx.x; e < kTT * (1 + n); e += kThreads) {
     const int tt = e / (1 + n), c = e - tt * (1 + n);
     const int64_t t = t0 + tt;
-    const float v = t < T ? __ldg(rec + t * RW + N + c) : 0.f;
+    const float v = t < T ? MHC_LDG(rec + t * RW + N + c) : 0.f;
     if (c == 0) c_s[tt] = v;
     else hp_s[tt][c - 1] = v;
   }
@@ -163,8 +167,8 @@ __global__ void __launch_bounds__(kThreads) dx_kernel(const uint16_t* __restrict
 #pragma unroll
   for (int b = 0; b < kKL; ++b) gm[b] = 1.f;
   if (gamma) {
-    const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma + k));
-    const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma + k + 4));
+    const float4 g0 = MHC_LDG(reinterpret_cast<const float4*>(gamma + k));
+    const float4 g1 = MHC_LDG(reinterpret_cast<const float4*>(gamma + k + 4));
     gm[0] = g0.x;
     gm[1] = g0.y;
     gm[2] = g0.z;
@@ -179,8 +183,8 @@ __global__ void __launch_bounds__(kThreads) dx_kernel(const uint16_t* __restrict
     const int tt = 8 * warp + a;
     const int64_t t = t0 + tt;
     if (t >= T) break;
-    const uint4 xr = __ldg(reinterpret_cast<const uint4*>(x + t * nD + k));
-    const uint4 gr = __ldg(reinterpret_cast<const uint4*>(dh_in + t * D + d));
+    const uint4 xr = MHC_LDG(reinterpret_cast<const uint4*>(x + t * nD + k));
+    const uint4 gr = MHC_LDG(reinterpret_cast<const uint4*>(dh_in + t * D + d));
     float xf[kKL], gf[kKL];
     bf16x4(make_uint2(xr.x, xr.y), *reinterpret_cast<float(*)[4]>(&xf[0]));
     bf16x4(make_uint2(xr.z, xr.w), *reinterpret_cast<float(*)[4]>(&xf[4]));
@@ -194,7 +198,7 @@ __global__ void __launch_bounds__(kThreads) dx_kernel(const uint16_t* __restrict
       const float v1 = acc2[a][h].y * gm[2 * h + 1] + ((-c) * xf[2 * h + 1] + hp * gf[2 * h + 1]);
       w[h] = (uint32_t)f32_to_bf16_bits(v0) | ((uint32_t)f32_to_bf16_bits(v1) << 16);
     }
-    *reinterpret_cast<uint4*>(dx + t * nD + k) = make_uint4(w[0], w[1], w[2], w[3]);
+    MHC_ST(reinterpret_cast<uint4*>(dx + t * nD + k), make_uint4(w[0], w[1], w[2], w[3]));
   }
 }
 
@@ -258,7 +262,7 @@ __global__ void __launch_bounds__(128) gimg_kernel(const float* __restrict__ rec
 #pragma unroll
     for (int c4 = 0; c4 < Cf::SEGW / 4; ++c4) {
       if (4 * c4 < N_OUT) {
-        const float4 v = __ldg(rp + c4);
+        const float4 v = MHC_LDG(rp + c4);
         r[4 * c4] = v.x;
         r[4 * c4 + 1] = v.y;
         r[4 * c4 + 2] = v.z;
@@ -279,11 +283,12 @@ __global__ void __launch_bounds__(128) gimg_kernel(const float* __restrict__ rec
       const uint32_t hi = bwdtc::split_term(r[j0 + 2 * h + 1], e);
       w[h] = lo | (hi << 16);
     }
-    *reinterpret_cast<uint4*>(dst + bwdtc::interleave_off(row, kc * 8, Cf::RG)) = make_uint4(w[0], w[1], w[2], w[3]);
+    MHC_ST(reinterpret_cast<uint4*>(dst + bwdtc::interleave_off(row, kc * 8, Cf::RG)), make_uint4(w[0], w[1], w[2], w[3]));
   }
 }
 
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  if (!MHC_CHK(src, bytes)) return;   // the barrier's expect_tx then runs into its bounded wait
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                "l"(src), "r"(bytes), "r"(bar)
                : "memory");
@@ -402,7 +407,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
     if (k < nD && !*abort_flag) {
       float* gp = gpart + (int64_t)group * N_OUT * nD + k;
 #pragma unroll
-      for (int jj = 0; jj < N_OUT; ++jj) gp[(int64_t)jj * nD] = acc[jj];
+      for (int jj = 0; jj < N_OUT; ++jj) MHC_ST(gp + (int64_t)jj * nD, acc[jj]);
     }
   }
 
@@ -470,7 +475,7 @@ __global__ void __launch_bounds__(256) phimg_kernel(const float* __restrict__ ph
   for (int idx = threadIdx.x; idx < Cf::N_OUT * 64; idx += 256) {
     const int j = idx / 64, kk = idx - j * 64;
     const int64_t k = (int64_t)blk * 64 + kk;
-    cols[j][kk] = k < nD ? __ldg(phi + (int64_t)j * nD + k) * (gamma ? __ldg(gamma + k) : 1.0f) : 0.f;
+    cols[j][kk] = k < nD ? MHC_LDG(phi + (int64_t)j * nD + k) * (gamma ? MHC_LDG(gamma + k) : 1.0f) : 0.f;
   }
   __syncthreads();
   uint8_t* out = img + (size_t)blk * Cf::PH_BYTES;
@@ -487,7 +492,7 @@ __global__ void __launch_bounds__(256) phimg_kernel(const float* __restrict__ ph
       const uint32_t hi = jb < Cf::N_OUT ? bwdtc::split_term(cols[jb < Cf::N_OUT ? jb : 0][kk], e) : 0;
       w[h] = lo | (hi << 16);
     }
-    *reinterpret_cast<uint4*>(out + (size_t)t * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    MHC_ST(reinterpret_cast<uint4*>(out + (size_t)t * 16), make_uint4(w[0], w[1], w[2], w[3]));
   }
 }
 
@@ -611,10 +616,10 @@ __global__ void __launch_bounds__(kGThreads, 1)
       if (t < T) {
         const float* rp = rec + t * Cf::RW;
 #pragma unroll
-        for (int c = 0; c < N_OUT; ++c) r[c] = __ldg(rp + c);
-        c_t = __ldg(rp + N_OUT);
+        for (int c = 0; c < N_OUT; ++c) r[c] = MHC_LDG(rp + c);
+        c_t = MHC_LDG(rp + N_OUT);
 #pragma unroll
-        for (int i = 0; i < n; ++i) hp[i] = __ldg(rp + N_OUT + 1 + i);
+        for (int i = 0; i < n; ++i) hp[i] = MHC_LDG(rp + N_OUT + 1 + i);
       }
       // term e of dh_mix[j] at TMEM column DHM_COL + (e SEGW + j) / 2 (j even: low half)
 #pragma unroll
@@ -868,10 +873,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
       if (t < T) {
         const float* rp = rec + t * Cf::RW;
 #pragma unroll
-        for (int c = 0; c < N_OUT; ++c) r[c] = __ldg(rp + c);
-        c_t = __ldg(rp + N_OUT);
+        for (int c = 0; c < N_OUT; ++c) r[c] = MHC_LDG(rp + c);
+        c_t = MHC_LDG(rp + N_OUT);
 #pragma unroll
-        for (int i = 0; i < n; ++i) hp[i] = __ldg(rp + N_OUT + 1 + i);
+        for (int i = 0; i < n; ++i) hp[i] = MHC_LDG(rp + N_OUT + 1 + i);
       }
       // term e of dh_mix[j] at TMEM column DHM_COL + (e SEGW + j) / 2 (j even: low half)
       // group 0 writes terms 0 and 2, group 1 term 1

@@ -81,9 +81,9 @@ int main(void) {
 
 
 def test_status_strings_and_version(lib):
-    assert lib.mhc_abi_version() == 10200
+    assert lib.mhc_abi_version() == 10300
     assert lib.mhc_status_string(0) == b"ok"
-    for code in range(1, 9):
+    for code in range(1, 11):
         assert lib.mhc_status_string(code) != b"unknown mhc status"
     assert lib.mhc_status_string(99) == b"unknown mhc status"
 
@@ -155,3 +155,21 @@ int main(void) {
     assert (int(out[1]), int(out[2])) == (fw.value, bw.value)
     assert (int(out[3]), int(out[4]), int(out[5])) == (1, plan["d_slices"], plan["token_groups"])
     assert " ".join(out[6:]).encode() == lib.mhc_status_string(8)
+
+
+def test_normal_build_has_no_bounds_checks(lib):
+    """mhc_debug_bounds answers without a device in a normal build: unsupported, zero record."""
+    rec = (ctypes.c_uint64 * 4)(1, 2, 3, 4)
+    assert lib.mhc_debug_bounds(rec, 1) == _lib.MHC_ERR_UNSUPPORTED
+    assert list(rec) == [0, 0, 0, 0]
+    assert lib.mhc_debug_bounds(None, 0) == 1
+    assert lib.mhc_debug_bounds_selftest(None, None) == _lib.MHC_ERR_UNSUPPORTED
+
+
+def test_debug_bounds_build_exports_every_declared_symbol():
+    """The -DMHC_DEBUG_BOUNDS library builds from the same sources and exports the same ABI."""
+    from mhc_ops_b200 import build
+    path = build.build(debug_bounds=True)
+    out = subprocess.run(["nm", "-D", "--defined-only", path], capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (mhc_\w+)$", out, flags=re.M))
+    assert not [s for s in _declared_symbols() if s not in exported]
