@@ -123,7 +123,10 @@ __device__ __forceinline__ void bwd_row_token(const BwdRowArgs& a, int64_t t, in
   float p[n];
 #pragma unroll
   for (int i = 0; i < n; ++i) p[i] = 0.f;
-  constexpr int U = 4;   // 256-element chunks in flight per lane
+  // 256-element chunks in flight per lane: U (n + 1) 16-byte loads, ~300
+  // bytes per lane whatever n, inside the 128 registers a 512-thread CTA
+  // allows (U = 4 at n = 8 alone took them all and spilled)
+  constexpr int U = n <= 6 ? 4 : (n == 7 ? 3 : 2);
   for (int c0 = 0; c0 < D; c0 += 256 * U) {
     uint4 g[U], xv[U][n];
 #pragma unroll
