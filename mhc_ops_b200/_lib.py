@@ -212,10 +212,20 @@ def workspace(nbytes: int, device: torch.device, stream: torch.cuda.Stream) -> W
 
     New workspaces are zero filled once (the first bytes hold the device
     status word); later calls reuse the buffer, ordered by the stream.  A
-    timeout an earlier call on this workspace reported is raised here.
+    timeout an earlier call on this workspace reported is raised here.  While
+    the stream captures a CUDA graph the cached workspace is used as it is
+    (one made by an earlier call on the stream; none is created).
     """
     key = (device.index, stream.cuda_stream)
     ws = _ws_cache.get(key)
+    if torch.cuda.is_current_stream_capturing():
+        # inside a CUDA graph capture nothing may be allocated or synchronised:
+        # the workspace must come from a call on this stream before the capture
+        if ws is None or ws.buf.numel() < nbytes:
+            raise RuntimeError(
+                "mhc: no workspace for this stream while it is capturing a CUDA graph; run the same call "
+                "once on the capturing stream before the capture (as torch's own warm-up advice says)")
+        return ws
     if ws is not None:
         # a workspace about to be replaced reports its last call first
         ws.raise_if_timed_out(wait=ws.buf.numel() < nbytes)

@@ -113,6 +113,16 @@ std::map<std::pair<int, cudaStream_t>, std::unique_ptr<Workspace>> g_ws;
 Workspace& workspace(int64_t nbytes, const at::Device& dev, cudaStream_t stream) {
   std::lock_guard<std::mutex> lk(g_ws_mu);
   auto& slot = g_ws[{dev.index(), stream}];
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  check_cuda(cudaStreamIsCapturing(stream, &cap), "cudaStreamIsCapturing");
+  if (cap != cudaStreamCaptureStatusNone) {
+    // inside a CUDA graph capture nothing may be allocated or synchronised:
+    // the workspace must come from a call on this stream before the capture
+    TORCH_CHECK(slot && slot->buf.defined() && slot->buf.numel() >= nbytes,
+                "mhc: no workspace for this stream while it is capturing a CUDA graph; run the same call once "
+                "on the capturing stream before the capture");
+    return *slot;
+  }
   if (!slot) slot = std::make_unique<Workspace>();
   if (slot->buf.defined()) slot->raise_if_timed_out(stream, /*wait=*/slot->buf.numel() < nbytes);
   if (!slot->buf.defined() || slot->buf.numel() < nbytes) slot->init(nbytes, dev);
