@@ -52,7 +52,7 @@ typedef enum mhc_status {
   MHC_ERR_NO_DEVICE = 7,           /* no sm_100 device is current */
   MHC_ERR_LIMIT = 8,               /* a size beyond a fixed limit of the entry point */
   MHC_ERR_OUT_OF_BOUNDS = 9,       /* a debug-bounds build saw an access outside the call's buffers */
-  MHC_ERR_UNSUPPORTED = 10         /* the entry point is not part of this build */
+  MHC_ERR_UNSUPPORTED = 10         /* the entry point is not compiled into this library */
 } mhc_status;
 
 /* Forward arguments.  Replaces the Python signature

@@ -1072,7 +1072,7 @@ const char* mhc_status_string(int status) {
     case MHC_ERR_NO_DEVICE: return "the current device is not an sm_100 GPU";
     case MHC_ERR_LIMIT: return "a size is beyond this entry point's fixed limit";
     case MHC_ERR_OUT_OF_BOUNDS: return "a debug-bounds build saw an access outside the call's buffers";
-    case MHC_ERR_UNSUPPORTED: return "the entry point is not part of this build";
+    case MHC_ERR_UNSUPPORTED: return "the entry point is not compiled into this library";
     default: return "unknown mhc status";
   }
 }

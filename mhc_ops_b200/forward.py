@@ -9,7 +9,7 @@ keeps the reference signature and return convention (``src/forward/golden.py:10-
 
 It runs the sm_100a kernels of libmhc_ops.so through the C ABI on the current
 CUDA stream.  CPU tensors raise (the reference's Triton wrapper silently fell
-back to the golden, ``mhc_forward_pre_triton.py:423-425``; this build has no
+back to the golden, ``mhc_forward_pre_triton.py:423-425``; this library has no
 fallback).  ``h_pre`` returned with ``outflag`` is the true gate value
 (``golden.py:58``), not the reconstruction the reference's Triton wrappers used.
 """

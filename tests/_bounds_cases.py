@@ -1,10 +1,10 @@
 """The cases the debug-bounds test runs twice: in a child process on the
 -DMHC_DEBUG_BOUNDS library (MHC_OPS_LIBRARY set), where the record of
 out-of-buffer accesses must stay empty after every call, and in the test
-process on the normal library.  Odd shapes on purpose (SURVEY's plan for the
-race/bounds diagnostic): one token, prime token counts, D not a multiple of
-8, n = 2, 3, 4, 8, every forward option, the recompute backward, the
-post-op and the static forward.
+process on the normal library.  Odd shapes on purpose (a bounds diagnostic
+is only as good as the edges it visits): one token, prime token counts, D
+not a multiple of 8, n = 2, 3, 4, 5, 8, every forward option, both backward
+forms, the post-op and the static forward.
 
     python -m tests._bounds_cases OUT.npz     (child: writes every output)
 """
