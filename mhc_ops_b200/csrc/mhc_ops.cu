@@ -234,13 +234,18 @@ int set_smem_limit_once(Kernel kernel, int bytes) {
 // follow the projection tile by tile through per-tile counters, so x's second
 // read hits L2) or as a second kernel (rowdot::fwd_rows_kernel) when the
 // fused form's finer K-slices do not fit in an h_in row or the device cannot
-// co-schedule its grid.  Shapes they take: n in {4, 8}, D a multiple of 64
-// whose h_in row holds at least one partial row (n = 8: D >= 192), 16-byte
-// aligned x / h_in / phi, T < 2^31.  Everything else runs the generic kernels.
-int fwd_part_row_bytes(int n) { return 4 * (n == 4 ? fwdtc::Cfg<4>::RW : fwdtc::Cfg<8>::RW); }
+// co-schedule its grid.  Shapes they take: any n, D a multiple of 64 whose
+// h_in row holds at least one partial row (n = 8: D >= 192), 16-byte aligned
+// x / h_in / phi, T < 2^31; the fused form n = 4 only, an fp8 x n in {4, 8}.
+// Everything else runs the generic kernels.
+template <int n>
+struct FwdPartRowBytes {
+  static int run() { return 4 * fwdtc::Cfg<n>::RW; }
+};
+int fwd_part_row_bytes(int n) { return dispatch_n<FwdPartRowBytes>(n); }
 
 bool fwd_tc_shape(int64_t T, int n, int D) {
-  if (!(n == 4 || n == 8)) return false;
+  if (n < 1 || n > 8) return false;
   if (D % 64 != 0 || T >= ((int64_t)1 << 31)) return false;
   return 2 * D >= fwd_part_row_bytes(n);
 }
@@ -252,9 +257,12 @@ bool fwd_tc_eligible(const mhc_fwd_args* a, const FwdEx& ex) {
 }
 
 // Bytes of the bf16 term images of phi (one term when phi comes in bf16).
+template <int n>
+struct FwdTermRows {
+  static int run(bool bf16_phi) { return bf16_phi ? fwdtc::Cfg<n, 1>::NB : fwdtc::Cfg<n>::NB; }
+};
 size_t fwd_tc_phis_bytes(int n, int D, bool bf16_phi) {
-  const int NB = n == 4 ? (bf16_phi ? fwdtc::Cfg<4, 1>::NB : fwdtc::Cfg<4>::NB)
-                        : (bf16_phi ? fwdtc::Cfg<8, 1>::NB : fwdtc::Cfg<8>::NB);
+  const int NB = dispatch_n<FwdTermRows>(n, bf16_phi);
   return (size_t)NB * n * D * sizeof(uint16_t);
 }
 
@@ -475,16 +483,26 @@ int fwd_workspace(int64_t T, int n, int D, size_t* bytes, bool bf16_phi = false)
   return MHC_OK;
 }
 
+// Tensor-core forward of a bf16 x for stream count n (one phi term when phi
+// comes in bf16).
+template <int n>
+struct FwdTcBf16 {
+  static int run(const mhc_fwd_args* a, const FwdEx& ex, cudaStream_t s, int sms) {
+    return ex.phi_bf16 ? FwdTc<n, 1, false>::run(a, ex, s, sms)
+                       : FwdTc<n, fwdtc::default_terms(n), false>::run(a, ex, s, sms);
+  }
+};
+
 // The forward, any shape (arguments already validated).
 int fwd_run(const mhc_fwd_args* a, const FwdEx& ex, cudaStream_t s, int sms) {
   const bool bf16_phi = ex.phi_bf16 != nullptr;
   if (fwd_tc_eligible(a, ex)) {
     if (ex.x_fp8) {
       if (a->n == 4) return bf16_phi ? FwdTc<4, 1, true>::run(a, ex, s, sms) : FwdTc<4, 3, true>::run(a, ex, s, sms);
-      return bf16_phi ? FwdTc<8, 1, true>::run(a, ex, s, sms) : FwdTc<8, 2, true>::run(a, ex, s, sms);
+      if (a->n == 8) return bf16_phi ? FwdTc<8, 1, true>::run(a, ex, s, sms) : FwdTc<8, 2, true>::run(a, ex, s, sms);
+      return MHC_ERR_BAD_SHAPE;
     }
-    if (a->n == 4) return bf16_phi ? FwdTc<4, 1, false>::run(a, ex, s, sms) : FwdTc<4, 3, false>::run(a, ex, s, sms);
-    return bf16_phi ? FwdTc<8, 1, false>::run(a, ex, s, sms) : FwdTc<8, 2, false>::run(a, ex, s, sms);
+    return dispatch_n<FwdTcBf16>(a->n, a, ex, s, sms);
   }
   if (ex.x_fp8) return MHC_ERR_BAD_SHAPE;   // fp8 x: tensor-core shapes only
   const float* phi = a->phi;
@@ -1201,7 +1219,8 @@ int fwd_entry(const mhc_fwd_args* a, const FwdEx& ex, void* stream) {
   if ((!a->x && !ex.x_fp8) || (!a->phi && !bf16_phi) || !a->alpha || !a->bias || !a->h_in || !a->h_post ||
       !a->h_res)
     return MHC_ERR_NULL_POINTER;
-  if (ex.x_fp8 && !(fwd_tc_shape(a->tokens, a->n, a->D) && aligned(ex.x_fp8, 16) && aligned(a->h_in, 16)))
+  if (ex.x_fp8 && !((a->n == 4 || a->n == 8) && fwd_tc_shape(a->tokens, a->n, a->D) && aligned(ex.x_fp8, 16) &&
+                    aligned(a->h_in, 16)))
     return MHC_ERR_BAD_SHAPE;
   if (!aligned(a->x, 2) || !aligned(a->h_in, 2) || !aligned(a->phi, 4) || !aligned(a->alpha, 4) ||
       !aligned(a->bias, 4) || !aligned(a->h_post, 4) || !aligned(a->h_res, 4) || !aligned(a->inv_rms, 4) ||

@@ -69,7 +69,8 @@ def test_abi_rejects_bad_arguments():
 @pytest.mark.parametrize("which,T,n,D,path", [
     (0, 16384, 4, 4096, "tensor-core-fused"),   # the LLM config: one cooperative launch
     (0, 16384, 8, 4096, "tensor-core"),         # n = 8: projection + row kernel
-    (0, 1000, 6, 512, "generic"),
+    (0, 1000, 6, 512, "tensor-core"),          # every n: projection + row kernel
+    (0, 1000, 6, 100, "generic"),              # D not a multiple of 64
     (1, 16384, 4, 4096, "tensor-core"),
     (1, 16384, 8, 4096, "tiled"),               # n = 8 backward: the n != 4 tcgen05 kernels
     (1, 100, 4, 36, "generic"),                 # D not a multiple of 8

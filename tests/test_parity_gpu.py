@@ -17,7 +17,7 @@ import numpy as np
 import pytest
 import torch
 
-from mhc_ops_b200 import mhc_backward_manual, mhc_forward_pre
+from mhc_ops_b200 import _lib, mhc_backward_manual, mhc_forward_pre
 from mhc_ops_b200.synthetic import make_inputs
 from oracle import mhc_oracle as O
 from tests._golden import fixture_names, load_fixture
@@ -95,6 +95,16 @@ def test_readme_backward_shapes_vs_oracle(B, S, D):
 ])
 def test_wide_rows_vs_oracle(B, S, n, D, gamma):
     _live_case(B, S, n, D, seed=12, gamma=gamma)
+
+
+@pytest.mark.parametrize("B,S,n,D", [(1, 64, 1, 64), (1, 200, 2, 256), (2, 75, 3, 512), (1, 130, 5, 256),
+                                     (1, 100, 6, 128), (1, 70, 7, 192)])
+def test_every_stream_count_on_the_tensor_core_forward_vs_oracle(B, S, n, D):
+    """n outside {4, 8} with D a multiple of 64: the projection on the tensor
+    cores and the row kernel (the generic kernels only for other D), ragged
+    token tiles; forward and backward against the oracle."""
+    assert _lib.query_plan(0, B * S, n, D)["path"] == "tensor-core"
+    _live_case(B, S, n, D, seed=17)
 
 
 @pytest.mark.parametrize("B,S,n,D", [(1, 4096, 4, 2560), (2, 2048, 8, 1280)])

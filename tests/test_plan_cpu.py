@@ -33,7 +33,9 @@ def test_wide_and_other_shapes_route_as_documented():
     assert plan(1, 200, 5, 256)["dx"] == "tensor-core"              # odd n: one 64-k block at a time
     assert plan(1, 33, 2, 40)["dx"] == "cuda-cores"                 # D not a multiple of 64
     assert plan(1, 70, 6, 512)["path"] == "tiled"
-    assert plan(0, 1000, 6, 512)["path"] == "generic"
+    for n in (1, 2, 3, 5, 6, 7):                                    # every n: projection + row kernel
+        assert plan(0, 1000, n, 512)["path"] == "tensor-core"
+    assert plan(0, 1000, 6, 100)["path"] == "generic"              # D not a multiple of 64
     assert plan(1, 100, 4, 36)["path"] == "generic"                # D not a multiple of 8
     assert plan(1, 100, 4, 40)["path"] == "tiled"                  # n = 4, D % 64 != 0: the n != 4 kernels
     assert plan(0, 16384, 4, 7168)["path"] == "tensor-core-fused"  # the 8-GPU row width
