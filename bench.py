@@ -315,9 +315,15 @@ def run_ours(args):
         clocks.start()
     launches0 = _lib.launch_count()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # Per-call durations come from events recorded between the calls of these
+    # same timed steps (one triple per step).  No synchronize inside the loop:
+    # the host stays ahead of the GPU, so each pair of events brackets device
+    # time only, not the host's enqueue of the next call.
+    step_evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     sync_all()
     start.record()
-    for _ in range(args.steps):
+    for evs in step_evs:
+        ev = evs
         ev[0].record()
         step()
     drain()   # the last step's all-reduce is inside the timed region
@@ -325,6 +331,8 @@ def run_ours(args):
     sync_all()
     total_ms = max_over_ranks(start.elapsed_time(stop))
     launches = _lib.launch_count() - launches0
+    fwd_ms = max_over_ranks(statistics.median(e[0].elapsed_time(e[1]) for e in step_evs))
+    bwd_ms = max_over_ranks(statistics.median(e[1].elapsed_time(e[2]) for e in step_evs))
 
     # A K-step region of a few ms holds only a handful of clock samples; the
     # same steps are timed again over at least SUSTAIN_MS (reported apart, the
@@ -333,6 +341,7 @@ def run_ours(args):
     reps = max(0, math.ceil(SUSTAIN_MS / max(total_ms / args.steps, 1e-3)))
     reps = int(max_over_ranks(reps))
     if total_ms < SUSTAIN_MS and reps > args.steps and not args.no_sustain:
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         sync_all()
         start.record()
         for _ in range(reps):
@@ -345,24 +354,6 @@ def run_ours(args):
         sustained = {"steps": reps, "ms_per_step": sus_ms / reps, "value": world * T * reps / (sus_ms / 1e3),
                      "what": f"the same step timed over {reps} steps ({sus_ms:.0f} ms) after the K-step region"}
     clk = clocks.stop() if rank == 0 else None
-
-    # per-call durations (separate pass, same work, events between the calls).  No
-    # synchronize inside the loop: the host stays ahead of the GPU, so each pair of
-    # events brackets device time only, not the host's enqueue of the next call.
-    fwd_ms, bwd_ms = [], []
-    step_evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(max(3, args.steps))]
-    sync_all()
-    for evs in step_evs:
-        ev = evs
-        ev[0].record()
-        step()
-    drain()
-    torch.cuda.synchronize()
-    for evs in step_evs:
-        fwd_ms.append(evs[0].elapsed_time(evs[1]))
-        bwd_ms.append(evs[1].elapsed_time(evs[2]))
-    fwd_ms = max_over_ranks(statistics.median(fwd_ms))
-    bwd_ms = max_over_ranks(statistics.median(bwd_ms))
 
     # e2e: host buffers, copies inside the timed region
     e2e = None

@@ -258,6 +258,16 @@ MHC_API int mhc_query_plan(int which, int64_t tokens, int32_t n, int32_t D, int*
 MHC_API int mhc_query_plan_for(int which, int64_t tokens, int32_t n, int32_t D, int32_t sms, int* path,
                                int* cluster_size, int* clusters);
 
+/* The grid of the n = 4 tensor-core backward (path 1 above) on a device with
+ * `sms` SMs (sms = 0: the current device), written to grid[0..5]:
+ * {Dc, S_K, S_T, J, E, R}.  S_K d-slices of Dc columns per stream times S_T
+ * token groups of 128-token tiles; when the tiles do not split evenly and SMs
+ * are left over, E > 0 more CTAs take the R leftover tiles (whole d-slices
+ * each) and the S_K * S_T main CTAs J tiles each (E = J = R = 0: every tile
+ * round robin over the token groups).  MHC_ERR_BAD_SHAPE for shapes that do
+ * not take that path.  No counterpart in the reference (ABI 1.4.0). */
+MHC_API int mhc_query_bwd_grid(int64_t tokens, int32_t n, int32_t D, int32_t sms, int32_t* grid);
+
 /* mhc_bwd_workspace_size for a device with `sms` SMs, without a device. */
 MHC_API int mhc_bwd_workspace_size_for(int64_t tokens, int32_t n, int32_t D, int32_t sms, size_t* bytes);
 
@@ -312,7 +322,7 @@ MHC_API uint64_t mhc_launch_count(void);
 /* Version of this ABI (major*10000 + minor*100 + patch).  1.1.0 added the
  * post-op and the device-free plan queries, 1.2.0 the backward that
  * recomputes the forward's intermediates and mhc_fwd_ex, 1.3.0 the
- * debug-bounds entry points. */
+ * debug-bounds entry points, 1.4.0 mhc_query_bwd_grid. */
 MHC_API int mhc_abi_version(void);
 
 /* Debug-bounds builds (compiled with -DMHC_DEBUG_BOUNDS: lib/libmhc_ops_dbg.so

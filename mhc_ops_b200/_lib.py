@@ -98,6 +98,8 @@ SIGNATURES = {
     "mhc_query_plan_for": (ctypes.c_int, [ctypes.c_int, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
                                           ctypes.c_int32, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
                                           ctypes.POINTER(ctypes.c_int)]),
+    "mhc_query_bwd_grid": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                          ctypes.POINTER(ctypes.c_int32)]),
     "mhc_bwd_workspace_size_for": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                                   ctypes.POINTER(ctypes.c_size_t)]),
     "mhc_post_fwd": (ctypes.c_int, [ctypes.POINTER(PostFwdArgs), _c_void_p]),
@@ -283,7 +285,10 @@ def query_plan(which: int, tokens: int, n: int, D: int, sms: int | None = None) 
     if path.value == 3:
         dx = {2: "tensor-core-stream-pairs", 1: "tensor-core", 0: "cuda-cores"}[ncl.value]
         return {"path": "tiled", "token_groups": cs.value, "dx": dx}
-    return {"path": "tensor-core", "d_slices": cs.value, "token_groups": ncl.value}
+    g = (ctypes.c_int32 * 6)()
+    check(load().mhc_query_bwd_grid(tokens, n, D, 0 if sms is None else sms, g), "mhc_query_bwd_grid")
+    return {"path": "tensor-core", "d_slices": cs.value, "token_groups": ncl.value, "leftover_ctas": g[4],
+            "leftover_tiles": g[5], "ctas": g[1] * g[2] + g[4]}
 
 
 def launch_count() -> int:

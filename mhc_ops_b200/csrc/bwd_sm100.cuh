@@ -13,7 +13,10 @@
 // streaming kernel (rowdot.cuh, bwd_rows_kernel) that leaves one record per
 // token {dh_mix, c, h_pre}.  This kernel does the rest.  CTA (s, g) owns the
 // d-slice [s*Dc, (s+1)*Dc) of every stream and the 128-token tiles g, g+S_T,
-// ... of the batch; CTAs never talk to each other.  Per tile:
+// ... of the batch; CTAs never talk to each other.  When the tiles do not
+// split evenly over the token groups and SMs are left over, the leftover
+// tiles go to extra CTAs that each take whole d-slices of them (their own
+// slot of the G partials), so the busiest CTA has the fewest tiles.  Per tile:
 //   * W3 loads the tile's records (TMA, 16 KB); W0 streams the slice's x
 //     blocks [128 tok x 64 k] and dh_in blocks (TMA, 128-B swizzle); W2 streams
 //     the pre-laid-out split-phi images (3 bf16 terms of phi per k);
@@ -101,6 +104,12 @@ struct Params {
   int Dc;                 // d-slice width (multiple of 64)
   int S_K;                // d-slices: D / Dc
   int S_T;                // token groups
+  // leftover tiles (E > 0): main CTAs take J tiles each, E extra CTAs take
+  // tiles 0 .. R-1 of ES whole d-slices each, into G-partial slot S_T
+  int J;
+  int E;
+  int ES;
+  int R;
   int num_tiles;
 };
 
@@ -250,15 +259,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int slice = (int)blockIdx.x % p.S_K;
-  const int group = (int)blockIdx.x / p.S_K;
+  // This CTA's units (tile, d-slice), u = 0 .. my_tiles-1.  Main CTA (s, g):
+  // d-slice s of tiles tiles-1-g, tiles-1-g-S_T, ... (last-first, so the first
+  // ones re-read what the row kernel read last).  Extra CTA e: d-slices
+  // e*ES .. e*ES+ES-1, each over the leftover tiles R-1 .. 0.
+  const int nmain = p.S_K * p.S_T;
+  const bool extra = (int)blockIdx.x >= nmain;
+  const int slice0 = extra ? ((int)blockIdx.x - nmain) * p.ES : (int)blockIdx.x % p.S_K;
+  const int group = extra ? p.S_T : (int)blockIdx.x / p.S_K;
   const int D = p.D;
   const int Dc = p.Dc;
   const int DCH = Dc / kBK;
   const int nD = n * D;
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  // Tiles run last-first, so the first ones re-read what the row kernel read last.
-  auto tile_of = [&](int j) { return p.num_tiles - 1 - (group + j * p.S_T); };
+  auto tile_of = [&](int u) { return extra ? p.R - 1 - u % p.R : p.num_tiles - 1 - (group + u * p.S_T); };
+  auto slice_of = [&](int u) { return extra ? slice0 + u / p.R : slice0; };
+  // the unit opens this CTA's G partial of its d-slice: stored, not added
+  auto first_of = [&](int u) { return extra ? u % p.R == 0 : u == 0; };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < Cf::XS; ++i) {
@@ -303,7 +320,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_g = tmem_base;                        // 2 x G_BUF: G of a stage pair
   const uint32_t tmem_dv = tmem_base + Cf::G_COLS;          // 2 x DV_COLS: dvecX of a stage pair
   const WaitCtx wc{abort_flag, p.status};
-  const int my_tiles = group < p.num_tiles ? (p.num_tiles - 1 - group) / p.S_T + 1 : 0;
+  const int my_tiles = extra ? p.ES * p.R
+                             : p.E > 0 ? p.J : (group < p.num_tiles ? (p.num_tiles - 1 - group) / p.S_T + 1 : 0);
   const bool producer = (lane == 0);
 
   if (warp == 0) {
@@ -313,6 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t q = 0, dq = 0;
       for (int j = 0; j < my_tiles; ++j) {
         const int tile = tile_of(j);
+        const int slice = slice_of(j);
         for (int dch = 0; dch < DCH; ++dch, ++dq) {
           const int ds = dq % Cf::DS;
           mbar_wait(bar(B::dh_empty + ds), ((dq / Cf::DS) & 1) ^ 1, wc);
@@ -401,6 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the TMA engine only carries x, dh_in, the records and the dx stores.
     uint32_t pq = 0;
     for (int j = 0; j < my_tiles; ++j) {
+      const int slice = slice_of(j);
       for (int dch = 0; dch < DCH; ++dch) {
         for (int ip = 0; ip < NP; ++ip, ++pq) {
           const int pb = (int)(pq & 1);
@@ -476,6 +496,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t q = 0, dq = 0;
     for (int j = 0; j < my_tiles; ++j) {
       const int tile = tile_of(j);
+      const int slice = slice_of(j);
+      const bool first = first_of(j);
       float c_nxt = 0.f, hp_nxt[n];
 #pragma unroll
       for (int i = 0; i < n; ++i) hp_nxt[i] = 0.f;
@@ -577,7 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int jj = c16 * 16 + e;
                 if (jj < N_OUT) {
                   const float v = mid[e] + hi[e];
-                  if (j == 0) MHC_ST(gp + (int64_t)jj * nD, v);
+                  if (first) MHC_ST(gp + (int64_t)jj * nD, v);
                   else red_add_f32(gp + (int64_t)jj * nD, v);
                 }
               }

@@ -531,6 +531,16 @@ struct BwdTcPlan {
   int Dc = 0;     // d-slice width
   int S_K = 0;    // d-slices
   int S_T = 0;    // token groups
+  // Leftover tiles: with E > 0 the S_K * S_T main CTAs take J tiles each
+  // (tiles R .. tiles-1) and E more CTAs take the R leftover tiles (0 .. R-1)
+  // of ES whole d-slices each, so no CTA does more than max(J, R * ES) units
+  // of (tile, d-slice).  E = 0: the main CTAs share every tile round robin.
+  int J = 0;
+  int E = 0;
+  int ES = 0;
+  int R = 0;
+  int ctas() const { return S_K * S_T + E; }
+  int gpart_slots() const { return S_T + (E > 0 ? 1 : 0); }
 };
 
 struct BwdTcLayout {
@@ -540,8 +550,13 @@ struct BwdTcLayout {
 };
 
 // Slice width Dc (multiple of 64 dividing D, n*Dc <= MAX_KC) with the least
-// per-CTA work: waves * ceil(tiles / S_T) * Dc, with S_T = sms / S_K token
-// groups; ties go to the wider slice (fewer, longer CTAs).
+// per-CTA work in units of (tile, d-slice) times Dc; S_T = sms / S_K token
+// groups.  Round robin: waves * ceil(tiles / S_T) units for the busiest CTA.
+// With SMs to spare (sms > S_K * S_T) and tiles % S_T = R > 0, the leftover
+// tiles may go to E' extra CTAs instead (E' the largest divisor of S_K that
+// fits, so each takes whole d-slices and owns its slot of the G partials):
+// max(tiles / S_T, R * S_K / E') units.  Ties go to the wider slice (fewer,
+// longer CTAs), then to round robin.
 BwdTcPlan bwd_tc_plan(int64_t T, int D, int sms) {
   using Cf = bwdtc::Cfg<kBwdN>;
   const int64_t tiles = std::max<int64_t>(1, (T + bwdtc::kBM - 1) / bwdtc::kBM);
@@ -552,9 +567,27 @@ BwdTcPlan bwd_tc_plan(int64_t T, int D, int sms) {
     const int S_K = D / Dc;
     const int64_t S_T = std::min<int64_t>(std::max(1, sms / S_K), tiles);
     const int64_t waves = ((int64_t)S_K * S_T + sms - 1) / sms;
-    const double cost = (double)waves * (double)((tiles + S_T - 1) / S_T) * Dc;
+    BwdTcPlan cand{Dc, S_K, (int)S_T};
+    double cost = (double)waves * (double)((tiles + S_T - 1) / S_T) * Dc;
+    const int64_t spare = (int64_t)sms - (int64_t)S_K * S_T;
+    const int64_t R = tiles % S_T;
+    if (waves == 1 && spare > 0 && R > 0) {
+      int Ex = 0;
+      for (int e = 1; e <= spare && e <= S_K; ++e)
+        if (S_K % e == 0) Ex = e;
+      const int64_t J = tiles / S_T;
+      const int64_t extra_units = R * (S_K / Ex);
+      const double bal = (double)std::max(J, extra_units) * Dc;
+      if (bal < cost - 1e-9) {
+        cand.J = (int)J;
+        cand.E = Ex;
+        cand.ES = S_K / Ex;
+        cand.R = (int)R;
+        cost = bal;
+      }
+    }
     if (best.Dc == 0 || cost <= best_cost + 1e-9) {
-      best = BwdTcPlan{Dc, S_K, (int)S_T};
+      best = cand;
       best_cost = cost;
     }
   }
@@ -594,7 +627,7 @@ BwdTcLayout bwd_tc_layout(int64_t T, int D, int sms) {
   L.rec = off;
   off = align_up(off + sizeof(float) * (size_t)T * Cf::RECW, kWsAlign);
   L.gpart = off;
-  off = align_up(off + sizeof(float) * (size_t)L.plan.S_T * Cf::N_OUT * nD, kWsAlign);
+  off = align_up(off + sizeof(float) * (size_t)L.plan.gpart_slots() * Cf::N_OUT * nD, kWsAlign);
   L.abpart = off;
   off = align_up(off + sizeof(float) * (size_t)L.rows_grid * kRowsWarps * Cf::CW, kWsAlign);
   L.total = off;
@@ -662,15 +695,19 @@ int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s, int sms) {
   p.Dc = L.plan.Dc;
   p.S_K = L.plan.S_K;
   p.S_T = L.plan.S_T;
+  p.J = L.plan.J;
+  p.E = L.plan.E;
+  p.ES = L.plan.ES;
+  p.R = L.plan.R;
   p.num_tiles = num_tiles;
 
   if ((st = set_smem_limit_once(bwdtc::bwd_kernel<n>, Cf::SMEM))) return st;
-  bwdtc::bwd_kernel<n><<<L.plan.S_K * L.plan.S_T, bwdtc::kThreads, Cf::SMEM, s>>>(m_x2d, m_dh, m_dx, m_rec, p);
+  bwdtc::bwd_kernel<n><<<L.plan.ctas(), bwdtc::kThreads, Cf::SMEM, s>>>(m_x2d, m_dh, m_dx, m_rec, p);
   if ((st = after_launch())) return st;
 
   generic::finalize_param_kernel<Cf::N_OUT>
       <<<(nD + generic::kFinCols - 1) / generic::kFinCols + 3 + Cf::N_OUT, generic::kThreads, 0, s>>>(
-          gpart, L.plan.S_T, a->phi, a->gamma, a->dphi, a->dgamma, nD, abpart, (int64_t)L.rows_grid * kRowsWarps,
+          gpart, L.plan.gpart_slots(), a->phi, a->gamma, a->dphi, a->dgamma, nD, abpart, (int64_t)L.rows_grid * kRowsWarps,
           a->dalpha, a->dbias);
   return after_launch();
 }
@@ -1097,7 +1134,7 @@ const char* mhc_status_string(int status) {
 
 const char* mhc_last_cuda_error(void) { return t_last_cuda_error.c_str(); }
 
-int mhc_abi_version(void) { return 10300; }
+int mhc_abi_version(void) { return 10400; }
 
 uint64_t mhc_launch_count(void) { return g_launch_count.load(std::memory_order_relaxed); }
 
@@ -1386,6 +1423,19 @@ int mhc_bwd_recompute_workspace_size(int64_t tokens, int32_t n, int32_t D, size_
   int sms = 0;
   if ((st = current_sm_count(&sms))) return st;
   *bytes = bwd_recompute_layout(tokens, n, D, sms).total;
+  return MHC_OK;
+}
+
+int mhc_query_bwd_grid(int64_t tokens, int32_t n, int32_t D, int32_t sms, int32_t* grid) {
+  if (!grid) return MHC_ERR_NULL_POINTER;
+  int st = check_shape(tokens, n, D);
+  if (st) return st;
+  if (sms < 0 || sms > 4096) return MHC_ERR_BAD_SHAPE;
+  if (sms == 0 && (st = current_sm_count(&sms))) return st;
+  if (!bwd_tc_shape(tokens, n, D)) return MHC_ERR_BAD_SHAPE;
+  const BwdTcPlan p = bwd_tc_plan(tokens, D, sms);
+  const int32_t v[6] = {p.Dc, p.S_K, p.S_T, p.J, p.E, p.R};
+  for (int i = 0; i < 6; ++i) grid[i] = v[i];
   return MHC_OK;
 }
 

@@ -81,7 +81,7 @@ int main(void) {
 
 
 def test_status_strings_and_version(lib):
-    assert lib.mhc_abi_version() == 10300
+    assert lib.mhc_abi_version() == 10400
     assert lib.mhc_status_string(0) == b"ok"
     for code in range(1, 11):
         assert lib.mhc_status_string(code) != b"unknown mhc status"

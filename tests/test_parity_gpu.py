@@ -107,6 +107,17 @@ def test_every_stream_count_on_the_tensor_core_forward_vs_oracle(B, S, n, D):
     _live_case(B, S, n, D, seed=17)
 
 
+@pytest.mark.parametrize("B,S,D", [(1, 1350, 4096), (1, 1664, 2048), (1, 5888, 1024)])
+def test_backward_with_leftover_tile_ctas_vs_oracle(B, S, D):
+    """Token counts whose 128-token tiles do not split evenly over the token
+    groups of the n = 4 tensor-core backward: the leftover tiles run on extra
+    CTAs (whole d-slices each, their own slot of the G partials); forward and
+    backward against the oracle over all tokens (1350: a ragged last tile)."""
+    q = _lib.query_plan(1, B * S, 4, D)
+    assert q["path"] == "tensor-core" and q["leftover_ctas"] > 0, q
+    _live_case(B, S, 4, D, seed=19)
+
+
 @pytest.mark.parametrize("B,S,n,D", [(1, 4096, 4, 2560), (2, 2048, 8, 1280)])
 def test_reference_forward_test_shapes_vs_oracle(B, S, n, D):
     """The largest shapes of the reference's forward tests

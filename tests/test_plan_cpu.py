@@ -50,6 +50,63 @@ def test_plans_scale_with_tokens_and_sms(T):
         assert b["d_slices"] * b["token_groups"] <= max(sms, b["d_slices"])
 
 
+def _bwd_grid(T, D, sms=SMS):
+    g = (ctypes.c_int32 * 6)()
+    assert _lib.load().mhc_query_bwd_grid(T, 4, D, sms, g) == 0
+    return tuple(g)
+
+
+def _bwd_units(T, D, sms=SMS):
+    """The (tile, d-slice) units of every CTA of the n = 4 tensor-core
+    backward, with the G-partial slot each CTA writes, as the kernel walks them."""
+    Dc, S_K, S_T, J, E, R = _bwd_grid(T, D, sms)
+    tiles = max(1, -(-T // 128))
+    ctas = []
+    for b in range(S_K * S_T + E):
+        if b >= S_K * S_T:
+            e = b - S_K * S_T
+            units = [(R - 1 - u % R, e * (S_K // E) + u // R) for u in range(S_K // E * R)]
+            slot = S_T
+        else:
+            s, g = b % S_K, b // S_K
+            count = J if E else ((tiles - 1 - g) // S_T + 1 if g < tiles else 0)
+            units = [(tiles - 1 - (g + u * S_T), s) for u in range(count)]
+            slot = g
+        ctas.append((slot, units))
+    return (Dc, S_K, S_T, J, E, R), tiles, ctas
+
+
+@pytest.mark.parametrize("T", [1, 128, 1350, 1408, 4096, 5888, 16384, 32768, 100000])
+@pytest.mark.parametrize("D", [1024, 4096, 7168])
+@pytest.mark.parametrize("sms", [74, 144, 148])
+def test_bwd_grid_covers_every_unit_once_and_balances(T, D, sms):
+    """Every (tile, d-slice) unit is done by exactly one CTA, every (slot,
+    d-slice) G partial has exactly one writer, the grid fits one wave, and no
+    CTA does more units than round robin over the token groups would give."""
+    (Dc, S_K, S_T, J, E, R), tiles, ctas = _bwd_units(T, D, sms)
+    assert D == S_K * Dc and len(ctas) <= max(sms, S_K)
+    seen, writers = {}, {}
+    for b, (slot, units) in enumerate(ctas):
+        for t, s in units:
+            assert 0 <= t < tiles and 0 <= s < S_K
+            assert (t, s) not in seen, (t, s)
+            seen[(t, s)] = b
+            writers.setdefault((slot, s), set()).add(b)
+    assert len(seen) == tiles * S_K
+    assert all(len(w) == 1 for w in writers.values())
+    busiest = max(len(u) for _, u in ctas)
+    assert busiest <= -(-tiles // S_T) * -(-(S_K * S_T) // sms)
+    if E:
+        assert busiest < -(-tiles // S_T)     # the leftover CTAs are only taken when they help
+
+
+def test_bwd_grid_at_the_llm_shape_fills_the_sms():
+    (Dc, S_K, S_T, J, E, R), tiles, ctas = _bwd_units(16384, 4096)
+    assert len(ctas) == SMS and E > 0 and R > 0
+    assert max(len(u) for _, u in ctas) == -(-tiles * S_K // SMS)   # 14 = ceil(2048 / 148): no CTA above the ideal
+    assert plan(1, 16384, 4, 4096)["ctas"] == SMS
+
+
 def test_bwd_workspace_grows_with_tokens():
     lib = _lib.load()
     sizes = []
