@@ -530,6 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 1; k < n; ++k)
             if (i == k) hpi = hp_cur[k];
+          const float2 hp2 = make_float2(hpi, hpi), nc2 = make_float2(-c_cur, -c_cur);
           // this group's staging buffer is free once its previous store has read it
           if (issuer) bulk_wait_read0();
           named_sync(2 + eh, kThreadsE / 2);
@@ -557,11 +558,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 bf16x8_to_f32(xv[hc], xf);
                 bf16x8_to_f32(dhv[c], gf);
                 uint32_t o[4];
+                // dx = (dvecX + h_pre dh_in) - c x, two elements per packed FMA
 #pragma unroll
                 for (int e = 0; e < 8; e += 2) {
-                  const float d0 = v[hc * 8 + e] + ((-c_cur) * xf[e] + hpi * gf[e]);
-                  const float d1 = v[hc * 8 + e + 1] + ((-c_cur) * xf[e + 1] + hpi * gf[e + 1]);
-                  o[e / 2] = pack_bf16x2(d0, d1);
+                  float2 d = __ffma2_rn(hp2, make_float2(gf[e], gf[e + 1]),
+                                        make_float2(v[hc * 8 + e], v[hc * 8 + e + 1]));
+                  d = __ffma2_rn(nc2, make_float2(xf[e], xf[e + 1]), d);
+                  o[e / 2] = pack_bf16x2(d.x, d.y);
                 }
                 sts128(st_row + (uint32_t)((c ^ (row & 7)) << 4), make_uint4(o[0], o[1], o[2], o[3]));
               }

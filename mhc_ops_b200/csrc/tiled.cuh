@@ -679,9 +679,10 @@ __global__ void __launch_bounds__(kGThreads, 1)
           for (int e = 0; e < 8; e += 2) {
             const float a0 = (hc < 2 ? v0[(hc * 8 + e) & 15] : v1[(hc * 8 + e) & 15]);
             const float a1 = (hc < 2 ? v0[(hc * 8 + e + 1) & 15] : v1[(hc * 8 + e + 1) & 15]);
-            const float d0 = a0 + ((-c_t) * xf[e] + hpi * gf[e]);
-            const float d1 = a1 + ((-c_t) * xf[e + 1] + hpi * gf[e + 1]);
-            o[e / 2] = pack_bf16x2(d0, d1);
+            // dx = (dvecX + h_pre dh_in) - c x, two elements per packed FMA
+            float2 d = __ffma2_rn(make_float2(hpi, hpi), make_float2(gf[e], gf[e + 1]), make_float2(a0, a1));
+            d = __ffma2_rn(make_float2(-c_t, -c_t), make_float2(xf[e], xf[e + 1]), d);
+            o[e / 2] = pack_bf16x2(d.x, d.y);
           }
           bwdtc::sts128(o_row + sw, make_uint4(o[0], o[1], o[2], o[3]));
         }
@@ -935,9 +936,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
             for (int e = 0; e < 8; e += 2) {
               const float a0 = (hc < 2 ? v0[(hc * 8 + e) & 15] : v1[(hc * 8 + e) & 15]);
               const float a1 = (hc < 2 ? v0[(hc * 8 + e + 1) & 15] : v1[(hc * 8 + e + 1) & 15]);
-              const float d0 = a0 + ((-c_t) * xf[e] + hpi * gf[e]);
-              const float d1 = a1 + ((-c_t) * xf[e + 1] + hpi * gf[e + 1]);
-              o[e / 2] = pack_bf16x2(d0, d1);
+              // dx = (dvecX + h_pre dh_in) - c x, two elements per packed FMA
+              float2 d = __ffma2_rn(make_float2(hpi, hpi), make_float2(gf[e], gf[e + 1]), make_float2(a0, a1));
+              d = __ffma2_rn(make_float2(-c_t, -c_t), make_float2(xf[e], xf[e + 1]), d);
+              o[e / 2] = pack_bf16x2(d.x, d.y);
             }
             bwdtc::sts128(x_row + sw, make_uint4(o[0], o[1], o[2], o[3]));
           }
