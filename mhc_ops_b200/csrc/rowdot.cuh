@@ -206,8 +206,10 @@ __device__ __forceinline__ void bwd_row_token(const BwdRowArgs& a, int64_t t, in
     acc.al1 += dal1;
     acc.al2 += dal2;
   }
-  for (int w = N_OUT + 1 + lane; w < R::W; w += 32)
-    MHC_ST(rt + w, (w - N_OUT - 1 < n) ? MHC_LDG(a.h_pre + t * n + (w - N_OUT - 1)) : 0.f);
+  // record tail: h_pre[lane] is this lane's gin[0] (loaded before the row
+  // stream), so the record needs no second load of it
+  static_assert(R::W - N_OUT - 1 <= 32, "record tail wider than a warp");
+  if (N_OUT + 1 + lane < R::W) MHC_ST(rt + N_OUT + 1 + lane, lane < n ? gin[0] : 0.f);
 }
 
 // B1 over all tokens: token t is owned by global warp t % W, so every sum
