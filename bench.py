@@ -486,13 +486,14 @@ def post_op_timing(x, y, dev, n, D, T, reps=10):
 
 
 def kernel_sources_sha16() -> str:
-    """Hash of the device code (mhc_ops_b200/csrc/*.cuh): the DRAM traffic of
-    a committed ncu capture is reported only while the kernels it measured are
-    the ones being timed."""
+    """Hash of the device code and launch plans (mhc_ops_b200/csrc/*.cuh and
+    mhc_ops.cu): the DRAM traffic of a committed ncu capture is reported only
+    while the kernels it measured are the ones being timed."""
     import glob
     import hashlib
     h = hashlib.sha256()
-    for f in sorted(glob.glob(os.path.join(ROOT, "mhc_ops_b200", "csrc", "*.cuh"))):
+    for f in sorted(glob.glob(os.path.join(ROOT, "mhc_ops_b200", "csrc", "*.cuh")) +
+                    [os.path.join(ROOT, "mhc_ops_b200", "csrc", "mhc_ops.cu")]):
         h.update(os.path.basename(f).encode())
         with open(f, "rb") as fh:
             h.update(fh.read())
