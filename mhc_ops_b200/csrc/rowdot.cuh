@@ -344,7 +344,7 @@ __device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<
 #pragma unroll
     for (int i = 0; i < n; ++i) hp[i] *= sc;
     const uint8_t* xr8 = a.x8 + t * nD;
-    constexpr int U8 = n <= 4 ? 2 : 1;   // 512-element chunks in flight per lane (16 bytes per stream)
+    constexpr int U8 = 2;   // 512-element chunks in flight per lane (16 bytes per stream)
     for (int c0 = 0; c0 < D; c0 += 512 * U8) {
       uint4 xv[U8][n];
 #pragma unroll
@@ -357,35 +357,37 @@ __device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<
       for (int u = 0; u < U8; ++u) {
         const int d = c0 + u * 512 + lane * 16;
         if (d < D) {
-          float acc[16];
-#pragma unroll
-          for (int i = 0; i < n; ++i) {
-            const uint32_t w[4] = {xv[u][i].x, xv[u][i].y, xv[u][i].z, xv[u][i].w};
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const uint32_t pair = w[q / 2] >> (16 * (q & 1));
-              const __half2_raw h2 = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(pair & 0xFFFFu), __NV_E4M3);
-              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
-              if (i == 0) {
-                acc[2 * q] = hp[0] * f.x;
-                acc[2 * q + 1] = hp[0] * f.y;
-              } else {
-                acc[2 * q] = fmaf(hp[i], f.x, acc[2 * q]);
-                acc[2 * q + 1] = fmaf(hp[i], f.y, acc[2 * q + 1]);
-              }
-            }
-          }
-          uint4 o[2];
+          // two halves of 8 elements (words 2hh, 2hh+1 of each stream's 16
+          // bytes), so only 8 sums are live at a time
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
-            o[hh].x = pack_bf16x2(acc[8 * hh], acc[8 * hh + 1]);
-            o[hh].y = pack_bf16x2(acc[8 * hh + 2], acc[8 * hh + 3]);
-            o[hh].z = pack_bf16x2(acc[8 * hh + 4], acc[8 * hh + 5]);
-            o[hh].w = pack_bf16x2(acc[8 * hh + 6], acc[8 * hh + 7]);
-            MHC_ST(reinterpret_cast<uint4*>(hr + d + 8 * hh), o[hh]);
+            float acc[8];
+#pragma unroll
+            for (int i = 0; i < n; ++i) {
+              const uint32_t w[2] = {hh ? xv[u][i].z : xv[u][i].x, hh ? xv[u][i].w : xv[u][i].y};
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const uint32_t pair = w[q / 2] >> (16 * (q & 1));
+                const __half2_raw h2 = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(pair & 0xFFFFu), __NV_E4M3);
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+                if (i == 0) {
+                  acc[2 * q] = hp[0] * f.x;
+                  acc[2 * q + 1] = hp[0] * f.y;
+                } else {
+                  acc[2 * q] = fmaf(hp[i], f.x, acc[2 * q]);
+                  acc[2 * q + 1] = fmaf(hp[i], f.y, acc[2 * q + 1]);
+                }
+              }
+            }
+            uint4 o;
+            o.x = pack_bf16x2(acc[0], acc[1]);
+            o.y = pack_bf16x2(acc[2], acc[3]);
+            o.z = pack_bf16x2(acc[4], acc[5]);
+            o.w = pack_bf16x2(acc[6], acc[7]);
+            MHC_ST(reinterpret_cast<uint4*>(hr + d + 8 * hh), o);
             if (a.h_in_rstd) {
               float r[8];
-              bf16x8(o[hh], r);
+              bf16x8(o, r);
 #pragma unroll
               for (int e = 0; e < 8; ++e) sq = fmaf(r[e], r[e], sq);
             }
