@@ -192,6 +192,29 @@ __device__ __forceinline__ void wait_rows_done(volatile int* rows_done, int need
   }
 }
 
+// Adds the accumulator columns of outputs [J0, J0 + JN) into part[0 .. JN):
+// column t*N_OUT + j holds term t of output j; the terms of an output are
+// summed smallest first, then added to its running partial (the same order
+// as the one-group fold below, so both give the same bits).
+template <int N_OUT, int NT, int J0, int JN>
+__device__ __forceinline__ void fold_outputs(uint32_t taddr, float (&part)[JN]) {
+  static_assert(J0 % 16 == 0 && JN % 16 == 0, "whole 16-column loads");
+#pragma unroll
+  for (int c16 = 0; c16 < JN / 16; ++c16) {
+    float w[NT][16];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) tmem_ld16(taddr + t * N_OUT + J0 + c16 * 16, w[t]);
+    tmem_wait_ld();
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      float v = w[NT - 1][e];
+#pragma unroll
+      for (int tt = NT - 2; tt >= 0; --tt) v += w[tt][e];
+      part[c16 * 16 + e] += v;
+    }
+  }
+}
+
 template <int n, bool kFused, int kNT = default_terms(n), bool kFp8 = false>
 __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
     proj_kernel(const __grid_constant__ CUtensorMap map_x2d, const __grid_constant__ CUtensorMap map_phi,
@@ -200,6 +223,14 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
   using B = Bars<n, kNT, kFp8>;
   constexpr int N_OUT = Cf::N_OUT;
   constexpr int S = Cf::S;
+  // n = 8 (80 outputs), bf16 x: the fold is split over two warp groups so
+  // that no thread holds all 80 partials (which spilled): WG_F outputs
+  // [0, 48), WG_S outputs [48, 80) and the sum of x^2, each storing its part
+  // of the row.  Not for fp8 x, whose WG_S also widens every stage.
+  constexpr bool kSplit = (N_OUT == 80) && !kFp8;
+  constexpr int JF = kSplit ? 48 : N_OUT;   // outputs WG_F folds
+  static_assert(!(kSplit && kFused), "the fused form signals a unit from WG_F alone");
+  static_assert(!kSplit || (Cf::RW == 88 && JF % 4 == 0), "partial-row halves on 16-byte boundaries");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -221,7 +252,7 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
     }
     for (int i = 0; i < Cf::NBUF; ++i) {
       mbar_init(bar(B::acc_full + i), 1);
-      mbar_init(bar(B::acc_empty + i), 4);
+      mbar_init(bar(B::acc_empty + i), kSplit ? 8 : 4);   // the folding warps
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(B::sq_full + i), 4);
@@ -311,6 +342,28 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
     uint32_t g = 0, uc = 0;
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++uc) {
       const int tile = u / p.S_K, ks = u - (u / p.S_K) * p.S_K;
+      if constexpr (kSplit) {
+        float part[JF];
+#pragma unroll
+        for (int jj = 0; jj < JF; ++jj) part[jj] = 0.f;
+        for (int kb = 0; kb < KB; kb += kKG, ++g) {
+          const int ab = g % Cf::NBUF;
+          mbar_wait(bar(B::acc_full + ab), (g / Cf::NBUF) & 1, wc);
+          tc_fence_after();
+          fold_outputs<N_OUT, Cf::NT, 0, JF>(tmem_base + ((uint32_t)(32 * q) << 16) + ab * Cf::ACC_COLS, part);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(B::acc_empty + ab));
+        }
+        const int64_t t = (int64_t)tile * kBM + row;
+        if (t < p.T && !*abort_flag) {
+          float4* dst = reinterpret_cast<float4*>(p.part + t * p.part_stride + (int64_t)ks * Cf::RW);
+#pragma unroll
+          for (int c = 0; c < JF / 4; ++c)
+            MHC_ST(dst + c, make_float4(part[4 * c], part[4 * c + 1], part[4 * c + 2], part[4 * c + 3]));
+        }
+        continue;
+      }
       float part[N_OUT];
 #pragma unroll
       for (int jj = 0; jj < N_OUT; ++jj) part[jj] = 0.f;
@@ -375,9 +428,13 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
   } else if (warp < kThreads / 32) {
     // ------------------------------------------------ WG_S: sum of squares, store partial sum x^2
     const int row = 32 * (warp & 3) + lane;   // token row of the tile = smem row
-    uint32_t it = 0, uc = 0;
+    uint32_t it = 0, uc = 0, g = 0;
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++uc) {
       float sq = 0.f;
+      constexpr int JS = kSplit ? N_OUT - JF : 16;   // outputs WG_S folds (n = 8)
+      float part[JS];
+#pragma unroll
+      for (int jj = 0; jj < JS; ++jj) part[jj] = 0.f;
       float scale = 1.f;   // fp8: 2^e of this row's token (rows past the batch are zero anyway)
       if constexpr (kFp8) {
         const int64_t t = (int64_t)(u / p.S_K) * kBM + row;
@@ -438,6 +495,34 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
           c8[c] = a + b;
         }
         sq += ((c8[0] + c8[1]) + (c8[2] + c8[3])) + ((c8[4] + c8[5]) + (c8[6] + c8[7]));
+        if constexpr (kSplit) {
+          if ((kb % kKG) == kKG - 1 || kb == KB - 1) {   // the accumulator of this K-block group is complete
+            const int ab = g % Cf::NBUF;
+            mbar_wait(bar(B::acc_full + ab), (g / Cf::NBUF) & 1, wc);
+            tc_fence_after();
+            fold_outputs<N_OUT, Cf::NT, JF, JS>(tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + ab * Cf::ACC_COLS,
+                                                 part);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B::acc_empty + ab));
+            ++g;
+          }
+        }
+      }
+      if constexpr (kSplit) {
+        // outputs [48, 80), sum x^2 and the zero padding of the partial row
+        const int64_t t = (int64_t)(u / p.S_K) * kBM + row;
+        const int ks = u - (u / p.S_K) * p.S_K;
+        if (t < p.T && !*abort_flag) {
+          float rowv[Cf::RW - JF];
+#pragma unroll
+          for (int jj = 0; jj < Cf::RW - JF; ++jj) rowv[jj] = jj < JS ? part[jj < JS ? jj : 0] : (jj == JS ? sq : 0.f);
+          float4* dst = reinterpret_cast<float4*>(p.part + t * p.part_stride + (int64_t)ks * Cf::RW + JF);
+#pragma unroll
+          for (int c = 0; c < (Cf::RW - JF) / 4; ++c)
+            MHC_ST(dst + c, make_float4(rowv[4 * c], rowv[4 * c + 1], rowv[4 * c + 2], rowv[4 * c + 3]));
+        }
+        continue;
       }
       // hand the unit's sum x^2 to WG_F, which stores the partial row
       const int sb = (int)(uc & 1);
