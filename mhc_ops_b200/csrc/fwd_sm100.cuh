@@ -31,7 +31,8 @@
 //     K steps drifts (about 2^-23 per step, one-signed), across 8 it does not
 //     -- and stores the unit's partial row (h_mix and WG_S's sum x^2, whole
 //     32-byte sectors);
-//   * WG_S (4 warps, one thread per token row) sums x^2 of its row from the
+//   * WG_S (4 warps, one thread per token row; 2 warps with two rows a
+//     thread in the fused bf16 form) sums x^2 of its rows from the
 //     smem stages (tree per stage) and hands it to WG_F through shared memory.
 // phi is split into NT bf16 terms (hi, mid[, lo]) stacked as UMMA N rows, so
 // x (exact in bf16) times phi is exact to ~2^-(8*NT) before fp32 accumulation.
@@ -58,7 +59,17 @@ constexpr int kBM = 128;          // tokens per tile = UMMA M = TMEM lanes
 constexpr int kBK = 64;           // bf16 elements per 128-byte row
 constexpr int kThreads = 10 * 32; // W0, W1, WG_F(4), WG_S(4)
 constexpr int kRowWarps = 8;      // WG_R of the fused forward
-constexpr int kThreadsFused = kThreads + kRowWarps * 32;
+// WG_S warps: 4 (a token row per thread), or 2 in the fused bf16 forward (two
+// rows per thread), which leaves a 512-thread CTA and so up to 128 registers
+// a thread, enough for the row warps to keep 6 chunks per lane in flight.
+constexpr int s_warps(bool fused, bool fp8) { return fused && !fp8 ? 2 : 4; }
+constexpr int threads_of(bool fused, bool fp8) { return (6 + s_warps(fused, fp8) + (fused ? kRowWarps : 0)) * 32; }
+// 256-element chunks in flight per lane in the fused form's row warps (0:
+// the row kernel's default).  Measured at the LLM shape with 128 registers a
+// thread: 2, 3, 4, 5, 6 chunks gave a forward of 0.230, 0.223, 0.221, 0.229,
+// 0.253 ms -- more loads in flight than 4 per lane slow the projection's
+// stream more than they speed the row warps.
+constexpr int fused_row_chunks(int n, bool fp8) { return !fp8 && n <= 4 ? 4 : 0; }
 constexpr int kUnitSignals = 4;   // WG_F warps: arrivals on a tile's counter per unit
 // Fused form: W0 starts this CTA's unit j only once WG_R has finished unit
 // j - kRowLag.  Without a bound the projection can run away from the row
@@ -216,13 +227,16 @@ __device__ __forceinline__ void fold_outputs(uint32_t taddr, float (&part)[JN]) 
 }
 
 template <int n, bool kFused, int kNT = default_terms(n), bool kFp8 = false>
-__global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
+__global__ void __launch_bounds__(threads_of(kFused, kFp8), 1)
     proj_kernel(const __grid_constant__ CUtensorMap map_x2d, const __grid_constant__ CUtensorMap map_phi,
                 const Params p) {
   using Cf = Cfg<n, kNT, kFp8>;
   using B = Bars<n, kNT, kFp8>;
   constexpr int N_OUT = Cf::N_OUT;
   constexpr int S = Cf::S;
+  constexpr int SW = s_warps(kFused, kFp8);   // WG_S warps
+  constexpr int RPT = 4 / SW;                 // token rows per WG_S thread
+  constexpr int kRow0 = 6 + SW;               // first WG_R warp
   // n = 8 (80 outputs), bf16 x: the fold is split over two warp groups so
   // that no thread holds all 80 partials (which spilled): WG_F outputs
   // [0, 48), WG_S outputs [48, 80) and the sum of x^2, each storing its part
@@ -230,6 +244,7 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
   constexpr bool kSplit = (N_OUT == 80) && !kFp8;
   constexpr int JF = kSplit ? 48 : N_OUT;   // outputs WG_F folds
   static_assert(!(kSplit && kFused), "the fused form signals a unit from WG_F alone");
+  static_assert(!kSplit || SW == 4, "the split fold reads TMEM with all four WG_S lane quadrants");
   static_assert(!kSplit || (Cf::RW == 88 && JF % 4 == 0), "partial-row halves on 16-byte boundaries");
 
   extern __shared__ uint8_t smem_raw[];
@@ -247,15 +262,15 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(bar(B::full + i), 1);
-      mbar_init(bar(B::empty + i), 1 + 4);   // MMA commit + the 4 WG_S warps
-      mbar_init(bar(B::conv + i), 4);        // fp8: the 4 WG_S warps wrote the bf16 tile
+      mbar_init(bar(B::empty + i), 1 + SW);   // MMA commit + the WG_S warps
+      mbar_init(bar(B::conv + i), SW);        // fp8: the WG_S warps wrote the bf16 tile
     }
     for (int i = 0; i < Cf::NBUF; ++i) {
       mbar_init(bar(B::acc_full + i), 1);
       mbar_init(bar(B::acc_empty + i), kSplit ? 8 : 4);   // the folding warps
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(bar(B::sq_full + i), 4);
+      mbar_init(bar(B::sq_full + i), SW);
       mbar_init(bar(B::sq_empty + i), 4);
     }
     *abort_flag = 0;
@@ -362,8 +377,7 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
           for (int c = 0; c < JF / 4; ++c)
             MHC_ST(dst + c, make_float4(part[4 * c], part[4 * c + 1], part[4 * c + 2], part[4 * c + 3]));
         }
-        continue;
-      }
+      } else {
       float part[N_OUT];
 #pragma unroll
       for (int jj = 0; jj < N_OUT; ++jj) part[jj] = 0.f;
@@ -424,8 +438,51 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
           MHC_ST(dst + c, make_float4(rowv[4 * c], rowv[4 * c + 1], rowv[4 * c + 2], rowv[4 * c + 3]));
       }
       if constexpr (kFused) signal_unit(p.tile_done + tile, lane);
+      }
     }
-  } else if (warp < kThreads / 32) {
+  } else if (warp < 6 + SW && RPT == 2) {
+    // ------------------------------------------------ WG_S (fused bf16 form, 2 warps): sum of squares
+    // Thread (w, lane) sums x^2 of token rows 32 w + lane and 32 (w + 2) + lane
+    // of each stage, in the same order as the one-row-per-thread form below.
+    const int w = warp - 6;
+    uint32_t it = 0, uc = 0;
+    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++uc) {
+      float sq[2] = {0.f, 0.f};
+      for (int kb = 0; kb < KB; ++kb, ++it) {
+        const int s = it % S;
+        mbar_wait(bar(B::full + s), (it / S) & 1, wc);
+        uint4 xv[2][8];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int row = 32 * (w + 2 * r) + lane;
+          const uint32_t base = smem_u32(ring + s * Cf::STAGE_BYTES) + row * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) xv[r][c] = lds128(base + (((c + row) & 7) << 4));
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B::empty + s));
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          float c8[8];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            float f[8];
+            bf16x8_to_f32(xv[r][c], f);
+            const float a = fmaf(f[0], f[0], f[1] * f[1]) + fmaf(f[2], f[2], f[3] * f[3]);
+            const float b = fmaf(f[4], f[4], f[5] * f[5]) + fmaf(f[6], f[6], f[7] * f[7]);
+            c8[c] = a + b;
+          }
+          sq[r] += ((c8[0] + c8[1]) + (c8[2] + c8[3])) + ((c8[4] + c8[5]) + (c8[6] + c8[7]));
+        }
+      }
+      const int sb = (int)(uc & 1);
+      mbar_wait(bar(B::sq_empty + sb), ((uc >> 1) & 1) ^ 1, wc);
+      sq_buf[sb * kBM + 32 * w + lane] = sq[0];
+      sq_buf[sb * kBM + 32 * (w + 2) + lane] = sq[1];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B::sq_full + sb));
+    }
+  } else if (warp < 6 + SW) {
     // ------------------------------------------------ WG_S: sum of squares, store partial sum x^2
     const int row = 32 * (warp & 3) + lane;   // token row of the tile = smem row
     uint32_t it = 0, uc = 0, g = 0;
@@ -539,7 +596,7 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
       // until all S_K units of its tile have stored their partials, then
       // reads x a second time -- from L2, about one round of units after
       // W0 brought it in.
-      const int rw = warp - kThreads / 32;
+      const int rw = warp - kRow0;
       rowdot::FwdRow<n> k;
       k.load(p.rows, lane);
       const int per_unit = (kBM + p.S_K - 1) / p.S_K;
@@ -565,7 +622,7 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
             (void)ld_acquire(p.tile_done + tile);   // every lane acquires the partials' stores
             ready = true;
           }
-          rowdot::fwd_row_token<n, kFp8>(p.rows, k, t, lane);
+          rowdot::fwd_row_token<n, kFp8, fused_row_chunks(n, kFp8)>(p.rows, k, t, lane);
         }
         if (lane == 0) rows_done[rw] = lu + 1;
       }

@@ -308,7 +308,7 @@ bool fwd_fused_supported() {
             cudaFuncSetAttribute(fwdtc::proj_kernel<n, true, NT, FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  fwdtc::Cfg<n, NT, FP8>::SMEM) == cudaSuccess &&
             cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fwdtc::proj_kernel<n, true, NT, FP8>,
-                                                          fwdtc::kThreadsFused,
+                                                          fwdtc::threads_of(true, FP8),
                                                           fwdtc::Cfg<n, NT, FP8>::SMEM) == cudaSuccess &&
             blocks >= 1;
   (void)cudaGetLastError();
@@ -377,7 +377,7 @@ struct FwdTc {
     attr[0].val.cooperative = 1;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(P.grid);
-    cfg.blockDim = dim3(fwdtc::kThreadsFused);
+    cfg.blockDim = dim3(fwdtc::threads_of(true, FP8));
     cfg.dynamicSmemBytes = Cf::SMEM;
     cfg.stream = s;
     cfg.attrs = attr;

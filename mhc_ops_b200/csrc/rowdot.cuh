@@ -326,7 +326,8 @@ __device__ __forceinline__ float fwd_row_gates(const FwdRowArgs& a, const FwdRow
 }
 
 // kFp8: x comes as e4m3 bytes (a.x8, scaled by 2^a.x_exp[t]) instead of bf16.
-template <int n, bool kFp8 = false>
+// kU: 256-element chunks of x in flight per lane (0: the default for n).
+template <int n, bool kFp8 = false, int kU = 0>
 __device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<n>& k, int64_t t, int lane) {
   const int D = a.D;
   const int64_t nD = (int64_t)n * D;
@@ -402,7 +403,7 @@ __device__ __forceinline__ void fwd_row_token(const FwdRowArgs& a, const FwdRow<
   } else {
   // (3) h_in = sum_i h_pre[i] x[i, :], streamed (U 256-element chunks in flight per lane)
   const uint16_t* xr = a.x + t * nD;
-  constexpr int U = n <= 4 ? 4 : 2;
+  constexpr int U = kU > 0 ? kU : (n <= 4 ? 4 : 2);
   for (int c0 = 0; c0 < D; c0 += 256 * U) {
     uint4 xv[U][n];
 #pragma unroll
