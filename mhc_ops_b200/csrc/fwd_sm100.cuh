@@ -76,7 +76,7 @@ constexpr int kUnitSignals = 4;   // WG_F warps: arrivals on a tile's counter pe
 // warps, whose second read of x then misses L2 and slows them further.  The
 // rows of a unit need only units of the same or the next round (a tile's
 // S_K units are consecutive), so any kRowLag >= 2 cannot deadlock.
-constexpr int kRowLag = 5;
+constexpr int kRowLag = 4;
 constexpr int kKG = 2;            // K-blocks accumulated per TMEM accumulator
 constexpr int kSmemLimit = 232448;
 
