@@ -87,3 +87,19 @@ def test_fp8_x_forward_refuses_shapes_off_the_tensor_cores():
     x8, e = quantize_fp8_pow2(d.x)
     with pytest.raises(_lib.MhcError):
         mhc_forward_pre_fp8(x8, e, d.phi, d.alpha, d.bias)
+
+
+@pytest.mark.parametrize("B,S,n,D,budget", [(4, 1024, 4, 4096, 140),   # fused forward on 140 of the SMs
+                                            (4, 1024, 4, 4096, 37),    # a quarter of them
+                                            (1, 300, 8, 1024, 100)])   # projection + row kernel
+def test_sm_budget_gives_the_same_bits(B, S, n, D, budget):
+    """sm_budget (the data-parallel bench leaves that many SMs to the NCCL
+    all-reduce) only shrinks the grids: every output equals, bit for bit, the
+    forward on every SM."""
+    inp = make_inputs(B, S, n, D, seed=43)
+    d = inp.to(DEV)
+    a = mhc_forward_pre(d.x, d.phi, d.alpha, d.bias, outflag=True)
+    b = mhc_forward_pre(d.x, d.phi, d.alpha, d.bias, outflag=True, sm_budget=budget)
+    torch.cuda.synchronize()
+    for i, (u, v) in enumerate(zip(a, b)):
+        assert torch.equal(u, v), f"output {i}: sm_budget={budget} differs from the full grid"
