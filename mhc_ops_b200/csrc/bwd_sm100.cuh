@@ -202,16 +202,6 @@ __device__ __forceinline__ uint32_t interleave_off(int row, int kk, int sbo) {
 __device__ __forceinline__ int prod_a_term(int pr) { return pr == 0 ? 1 : pr == 1 ? 2 : pr == 3 ? 1 : 0; }
 __device__ __forceinline__ int prod_b_term(int pr) { return pr == 0 ? 1 : pr == 2 ? 2 : pr == 4 ? 1 : 0; }
 
-// t-th bf16 term of v (0 = hi, 1 = mid, 2 = lo): each rounds what is left.
-__device__ __forceinline__ uint16_t split_term(float v, int term) {
-  uint16_t out = 0;
-  for (int tt = 0; tt <= term; ++tt) {
-    out = f32_to_bf16_bits(v);
-    v -= bf16_bits_to_f32(out);
-  }
-  return out;
-}
-
 // One token's DHM row from its record: segment e holds bf16 term e of
 // dh_mix[0..N_OUT), zero padded to SEGW (K-major interleaved image).  Half EH
 // writes the 16-byte chunks kc = EH, EH+2, ... of the row; the partner warp
@@ -627,53 +617,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
-  }
-}
-
-// phi [N_OUT, nD] f32, gamma [nD] (NULL = ones) -> per 64-k block the K-major
-// interleaved image W1 reads as the B operand of dvecX: row kk, column
-// e*SEGW + j holds bf16 term e (hi, mid, lo) of phi[j][k] * gamma[k],
-// k = block*64 + kk; padding columns are zero.
-// One CTA per 64-k block: the block's phi columns are staged in smem, then
-// each thread writes whole 16-byte chunks, consecutive threads consecutive chunks.
-template <int n>
-__global__ void __launch_bounds__(256) phit_kernel(const float* __restrict__ phi, const float* __restrict__ gamma,
-                                                   uint16_t* __restrict__ img, int nD) {
-  using Cf = Cfg<n>;
-  constexpr int CPR = Cf::KA / 8;                  // 16-byte chunks per image row
-  __shared__ float cols[Cf::N_OUT][kBK + 1];
-  const int blk = blockIdx.x;
-  // all of this thread's loads first (one round trip), then the smem stores
-  constexpr int PER = (Cf::N_OUT * kBK + 255) / 256;
-  float v[PER];
-#pragma unroll
-  for (int it = 0; it < PER; ++it) {
-    const int idx = it * 256 + (int)threadIdx.x;
-    const int j = idx / kBK, kk = idx - j * kBK;
-    const int64_t k = (int64_t)blk * kBK + kk;
-    v[it] = idx < Cf::N_OUT * kBK ? MHC_LDG(phi + (int64_t)j * nD + k) * (gamma ? MHC_LDG(gamma + k) : 1.0f) : 0.f;
-  }
-#pragma unroll
-  for (int it = 0; it < PER; ++it) {
-    const int idx = it * 256 + (int)threadIdx.x;
-    if (idx < Cf::N_OUT * kBK) cols[idx / kBK][idx % kBK] = v[it];
-  }
-  __syncthreads();
-  uint8_t* out = reinterpret_cast<uint8_t*>(img) + (size_t)blk * Cf::PH_BYTES;
-  for (int t = threadIdx.x; t < Cf::PH_BYTES / 16; t += 256) {
-    // byte offset 16*t = (kk/8)*RG_BYTES + cc*128 + (kk%8)*16
-    const int grp = t / (8 * CPR), rem = t - grp * 8 * CPR;
-    const int cc = rem >> 3, kk = grp * 8 + (rem & 7);
-    const int e = (cc * 8) / Cf::SEGW, j0 = cc * 8 - e * Cf::SEGW;
-    uint32_t w[4];
-#pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      const int ja = j0 + 2 * h, jb = ja + 1;
-      const uint32_t lo = ja < Cf::N_OUT ? split_term(cols[ja][kk], e) : 0;
-      const uint32_t hi = jb < Cf::N_OUT ? split_term(cols[jb][kk], e) : 0;
-      w[h] = lo | (hi << 16);
-    }
-    MHC_ST(reinterpret_cast<uint4*>(out + (size_t)t * 16), make_uint4(w[0], w[1], w[2], w[3]));
   }
 }
 

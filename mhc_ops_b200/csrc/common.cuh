@@ -53,6 +53,16 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(f));
 }
 
+// t-th bf16 term of v (0 = hi, 1 = mid, 2 = lo): each rounds what is left.
+__device__ __forceinline__ uint16_t split_term(float v, int term) {
+  uint16_t out = 0;
+  for (int tt = 0; tt <= term; ++tt) {
+    out = f32_to_bf16_bits(v);
+    v -= bf16_bits_to_f32(out);
+  }
+  return out;
+}
+
 // Two floats -> packed bf16x2 bits (lo in the low half), round-to-nearest-even,
 // one conversion instruction for both.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

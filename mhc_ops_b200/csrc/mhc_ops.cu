@@ -608,6 +608,22 @@ rowdot::BwdRowArgs bwd_row_args(const mhc_bwd_args* a, float* rec) {
   r.rec = rec;
   r.D = a->D;
   r.hc_eps = a->hc_eps;
+  r.img_phi = nullptr;
+  r.img_gamma = nullptr;
+  r.img = nullptr;
+  r.img_blocks = 0;
+  return r;
+}
+
+// The row kernel's arguments with the split phi * gamma images to build into
+// img (one warp per 64-k block, before its tokens): the layout of
+// bwdtc::Cfg<4> / tiled::DxCfg<n> (3 term segments of round_up(N, 16) columns).
+rowdot::BwdRowArgs bwd_row_args_with_image(const mhc_bwd_args* a, float* rec, uint8_t* img) {
+  rowdot::BwdRowArgs r = bwd_row_args(a, rec);
+  r.img_phi = a->phi;
+  r.img_gamma = a->gamma;
+  r.img = img;
+  r.img_blocks = a->n * a->D / 64;
   return r;
 }
 
@@ -658,10 +674,10 @@ int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s, int sms) {
   const int num_tiles = (int)((T + bwdtc::kBM - 1) / bwdtc::kBM);
   int st;
 
-  bwdtc::phit_kernel<n><<<nD / bwdtc::kBK, 256, 0, s>>>(a->phi, a->gamma, reinterpret_cast<uint16_t*>(ws + L.phit),
-                                                        nD);
-  if ((st = after_launch())) return st;
-  rowdot::bwd_rows_kernel<n><<<L.rows_grid, rowdot::kThreads, 0, s>>>(bwd_row_args(a, rec), abpart, T);
+  static_assert(Cf::KA == 3 * ((Cf::N_OUT + 15) / 16 * 16) && Cf::PH_BYTES == 8 * (Cf::KA / 8) * 128,
+                "phi images as rowdot::split_image_block lays them out");
+  rowdot::bwd_rows_kernel<n><<<L.rows_grid, rowdot::kThreads, 0, s>>>(
+      bwd_row_args_with_image(a, rec, reinterpret_cast<uint8_t*>(ws + L.phit)), abpart, T);
   if ((st = after_launch())) return st;
 
   CUtensorMap m_x2d, m_dh, m_dx, m_rec;
@@ -713,7 +729,7 @@ int bwd_tc_run(const mhc_bwd_args* a, cudaStream_t s, int sms) {
 }
 
 // ----------------------------------------------------------------- tiled backward (n != 4)
-// rowdot::bwd_rows_kernel (records), dx (tiled::phimg_kernel + dx_tc_kernel
+// rowdot::bwd_rows_kernel (records and the split phi images), dx (dx_tc_kernel
 // on the tensor cores, or transpose_kernel + dx_kernel on the CUDA cores),
 // tiled::gimg_kernel + g_tc_kernel (tcgen05), then the shared finalize kernel.  Shapes: every n the tensor-core backward does
 // not take, D a multiple of 8, 16-byte aligned x / dh_in / dx / phi / gamma,
@@ -841,15 +857,18 @@ struct BwdTiled {
     float* abpart = reinterpret_cast<float*>(ws + L.abpart);
     float* gpart = reinterpret_cast<float*>(ws + L.gpart);
     int st;
-    rowdot::bwd_rows_kernel<n><<<L.rows_grid, rowdot::kThreads, 0, s>>>(bwd_row_args(a, rec), abpart, T);
+    // dx on the tensor cores reads split phi * gamma images, which the row
+    // kernel's warps build before their tokens
+    static_assert(tiled::DxCfg<n>::KA == 3 * ((N + 15) / 16 * 16) &&
+                      tiled::DxCfg<n>::PH_BYTES == 8 * (tiled::DxCfg<n>::KA / 8) * 128,
+                  "phi images as rowdot::split_image_block lays them out");
+    uint8_t* img = L.dx_tc ? reinterpret_cast<uint8_t*>(ws + L.phimg) : nullptr;
+    rowdot::bwd_rows_kernel<n><<<L.rows_grid, rowdot::kThreads, 0, s>>>(
+        img ? bwd_row_args_with_image(a, rec, img) : bwd_row_args(a, rec), abpart, T);
     if ((st = after_launch())) return st;
     if (L.dx_tc) {
-      // dx on the tensor cores: split phi * gamma images, then one CTA per
-      // (token tile, range of 64-k blocks)
+      // dx on the tensor cores: one CTA per (token tile, range of 64-k blocks)
       using Dc = tiled::DxCfg<n>;
-      uint8_t* img = reinterpret_cast<uint8_t*>(ws + L.phimg);
-      tiled::phimg_kernel<n><<<nD / 64, 256, 0, s>>>(a->phi, a->gamma, img, nD);
-      if ((st = after_launch())) return st;
       CUtensorMap m_x, m_dh;
       {
         const uint64_t dims[2] = {(uint64_t)nD, (uint64_t)T};

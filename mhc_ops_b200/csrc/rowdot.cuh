@@ -82,7 +82,53 @@ struct BwdRowArgs {
   float* rec;
   int D;
   float hc_eps;
+  // optional: the split phi * gamma images the next kernel reads (NULL: none)
+  const float* img_phi;
+  const float* img_gamma;   // NULL = ones
+  uint8_t* img;
+  int img_blocks;           // 64-k blocks, n*D/64
 };
+
+// The split image of phi * gamma for the 64-k block blk, built by one warp:
+// row kk (k = 64 blk + kk), column e*SEGW + j = bf16 term e (hi, mid, lo) of
+// phi[j][k] * gamma[k] (zeros for j >= N_OUT), K-major interleaved in 8 x
+// 16-byte core matrices -- the 16 bytes of (kk, column chunk cc) at
+// (kk / 8) * RG + cc * 128 + (kk % 8) * 16, RG = (3 SEGW / 8) * 128 -- as the
+// n = 4 tensor-core backward (its phi images) and the tiled dx kernels read
+// it.  Lane l builds rows l and l + 32 from its own loads (coalesced across
+// the lanes).  Needs n*D % 64 == 0.
+template <int n>
+__device__ __forceinline__ void split_image_block(const BwdRowArgs& a, int blk, int lane) {
+  constexpr int N_OUT = n * n + 2 * n;
+  constexpr int SEGW = (N_OUT + 15) / 16 * 16;
+  constexpr int CPR = 3 * SEGW / 8;   // 16-byte chunks per image row
+  constexpr int RG = CPR * 128;
+  const int64_t nD = (int64_t)n * a.D;
+  uint8_t* out = a.img + (size_t)blk * 8 * RG;
+#pragma unroll 1
+  for (int half = 0; half < 2; ++half) {
+    const int kk = lane + 32 * half;
+    const int64_t k = (int64_t)blk * 64 + kk;
+    const float gm = a.img_gamma ? MHC_LDG(a.img_gamma + k) : 1.0f;
+    float v[N_OUT];
+#pragma unroll
+    for (int j = 0; j < N_OUT; ++j) v[j] = MHC_LDG(a.img_phi + (int64_t)j * nD + k) * gm;
+    uint8_t* row = out + (kk >> 3) * RG + (kk & 7) * 16;
+#pragma unroll
+    for (int cc = 0; cc < CPR; ++cc) {
+      const int e = (cc * 8) / SEGW, j0 = cc * 8 - e * SEGW;
+      uint32_t w[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const int ja = j0 + 2 * h, jb = ja + 1;
+        const uint32_t lo = ja < N_OUT ? split_term(v[ja < N_OUT ? ja : 0], e) : 0;
+        const uint32_t hi = jb < N_OUT ? split_term(v[jb < N_OUT ? jb : 0], e) : 0;
+        w[h] = lo | (hi << 16);
+      }
+      MHC_ST(reinterpret_cast<uint4*>(row + cc * 128), make_uint4(w[0], w[1], w[2], w[3]));
+    }
+  }
+}
 
 // B1 for one token t, one warp (src/backward/golden.py:51-62, 74, 77-86, 89):
 //   dh_pre[i] = sum_d dh_in[d] x[i,d]; dh_pre2, dh_post2; dh_mix = tmp * inv_rms;
@@ -221,6 +267,10 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_rows_kernel(const BwdRowArgs 
   const int lane = threadIdx.x & 31;
   const int64_t gw = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
   const int64_t W = (int64_t)gridDim.x * kWarps;
+  // The split phi * gamma images first, one 64-k block per warp, from the
+  // last warp down: the last warps own a token fewer when T % W != 0.
+  if (a.img != nullptr)
+    for (int64_t b = W - 1 - gw; b < a.img_blocks; b += W) split_image_block<n>(a, (int)b, lane);
   RowAcc<n> acc;
   for (int64_t t = gw; t < T; t += W) bwd_row_token<n>(a, t, lane, acc);
   acc.store(abpart + gw * Rec<n>::CW, lane);

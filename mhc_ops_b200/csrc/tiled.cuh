@@ -8,7 +8,8 @@
 //     h_pre[n]} (golden.py:49-62, 74, 89), and the dalpha/dbias partials;
 //   * dx[t,k] = (sum_j dh_mix[t,j] phi[j,k]) gamma[k] - c[t] x[t,k]
 //     + h_pre[t,i] dh_in[t,d]  (k = i*D + d; golden.py:65, 89-94):
-//     - D % 64 == 0: phimg_kernel (split phi * gamma images per 64-k block),
+//     - D % 64 == 0: split phi * gamma images per 64-k block (built by the
+//       row kernel's warps, rowdot::split_image_block),
 //       then dx_tc_pair_kernel (even n: pairs of streams over one d-range,
 //       N = 128 MMAs) or dx_tc_kernel (odd n: one 64-k block at a time),
 //       both with the tile's dh_mix terms in tensor memory (below);
@@ -279,8 +280,8 @@ __global__ void __launch_bounds__(128) gimg_kernel(const float* __restrict__ rec
     uint32_t w[4];
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
-      const uint32_t lo = bwdtc::split_term(r[j0 + 2 * h], e);
-      const uint32_t hi = bwdtc::split_term(r[j0 + 2 * h + 1], e);
+      const uint32_t lo = split_term(r[j0 + 2 * h], e);
+      const uint32_t hi = split_term(r[j0 + 2 * h + 1], e);
       w[h] = lo | (hi << 16);
     }
     MHC_ST(reinterpret_cast<uint4*>(dst + bwdtc::interleave_off(row, kc * 8, Cf::RG)), make_uint4(w[0], w[1], w[2], w[3]));
@@ -433,7 +434,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
 //     core without shared-memory traffic;
 //   * W0 streams per 64-k block the x and dh_in boxes (TMA, 128-B swizzle)
 //     and the block's split phi * gamma image (bulk copy from the image
-//     phimg_kernel leaves in the workspace) into an ST-deep ring;
+//     row kernel leaves in the workspace) into an ST-deep ring;
 //   * W1 issues 6 x SEGW/16 tcgen05.mma (M = 128 tokens, N = 64 k, K = 16,
 //     A from tensor memory) per block into one of two TMEM accumulators;
 //   * WG_E reads the accumulator (TMEM lane = token row), adds -c x + h_pre
@@ -461,40 +462,6 @@ struct DxCfg {
   static_assert(DHM_COL + KA / 2 <= TMEM_COLS, "TMEM");
   static_assert(SMEM <= 232448, "shared memory");
 };
-
-// Split images of phi * gamma: block kb (64 k) -> img + kb * PH_BYTES, row kk
-// (= k - 64 kb), column e * SEGW + j = bf16 term e of phi[j][k] * gamma[k]
-// (zeros for j >= N_OUT), K-major interleaved.  One CTA per block.
-template <int n>
-__global__ void __launch_bounds__(256) phimg_kernel(const float* __restrict__ phi, const float* __restrict__ gamma,
-                                                    uint8_t* __restrict__ img, int nD) {
-  using Cf = DxCfg<n>;
-  constexpr int CPR = Cf::KA / 8;
-  __shared__ float cols[Cf::N_OUT][65];
-  const int blk = blockIdx.x;
-  for (int idx = threadIdx.x; idx < Cf::N_OUT * 64; idx += 256) {
-    const int j = idx / 64, kk = idx - j * 64;
-    const int64_t k = (int64_t)blk * 64 + kk;
-    cols[j][kk] = k < nD ? MHC_LDG(phi + (int64_t)j * nD + k) * (gamma ? MHC_LDG(gamma + k) : 1.0f) : 0.f;
-  }
-  __syncthreads();
-  uint8_t* out = img + (size_t)blk * Cf::PH_BYTES;
-  for (int t = threadIdx.x; t < Cf::PH_BYTES / 16; t += 256) {
-    // byte offset 16*t = (kk/8)*RG + cc*128 + (kk%8)*16
-    const int grp = t / (8 * CPR), rem = t - grp * 8 * CPR;
-    const int cc = rem >> 3, kk = grp * 8 + (rem & 7);
-    const int e = (cc * 8) / Cf::SEGW, j0 = cc * 8 - e * Cf::SEGW;
-    uint32_t w[4];
-#pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      const int ja = j0 + 2 * h, jb = ja + 1;
-      const uint32_t lo = ja < Cf::N_OUT ? bwdtc::split_term(cols[ja < Cf::N_OUT ? ja : 0][kk], e) : 0;
-      const uint32_t hi = jb < Cf::N_OUT ? bwdtc::split_term(cols[jb < Cf::N_OUT ? jb : 0][kk], e) : 0;
-      w[h] = lo | (hi << 16);
-    }
-    MHC_ST(reinterpret_cast<uint4*>(out + (size_t)t * 16), make_uint4(w[0], w[1], w[2], w[3]));
-  }
-}
 
 template <int n>
 __global__ void __launch_bounds__(kGThreads, 1)
@@ -629,8 +596,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
           uint32_t w[8];
 #pragma unroll
           for (int h = 0; h < 8; ++h) {
-            const uint32_t lo = bwdtc::split_term(r[16 * c + 2 * h], e);
-            const uint32_t hi = bwdtc::split_term(r[16 * c + 2 * h + 1], e);
+            const uint32_t lo = split_term(r[16 * c + 2 * h], e);
+            const uint32_t hi = split_term(r[16 * c + 2 * h + 1], e);
             w[h] = lo | (hi << 16);
           }
           tmem_st8(tmem_base + lane_off + Cf::DHM_COL + e * (Cf::SEGW / 2) + 8 * c, w);
@@ -889,8 +856,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
           uint32_t w[8];
 #pragma unroll
           for (int h = 0; h < 8; ++h) {
-            const uint32_t lo = bwdtc::split_term(r[16 * c + 2 * h], e);
-            const uint32_t hi = bwdtc::split_term(r[16 * c + 2 * h + 1], e);
+            const uint32_t lo = split_term(r[16 * c + 2 * h], e);
+            const uint32_t hi = split_term(r[16 * c + 2 * h + 1], e);
             w[h] = lo | (hi << 16);
           }
           tmem_st8(tmem_base + lane_off + Cf::DHM_COL + e * (Cf::SEGW / 2) + 8 * c, w);
