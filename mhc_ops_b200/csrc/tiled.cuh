@@ -689,6 +689,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
 // groups of four warps, group h on block h of the pair) writes dx over the x
 // boxes it has read (each thread its own row), and one thread TMA-stores them
 // and releases the stage once the stores have read it.
+// Two rings: XST slots of {x pair, dh_in} (read by the epilogue, dx written
+// over the x boxes and stored from there) and PST slots of the pair's two
+// split phi images (read by the MMA only, so released at its commit).
 template <int n>
 struct DxPairCfg {
   static constexpr int N_OUT = n * n + 2 * n;
@@ -697,21 +700,25 @@ struct DxPairCfg {
   static constexpr int RG = (KA / 8) * 128;
   static constexpr int PH_BYTES = 8 * RG;                // one 64-k block's image
   static constexpr int BOX_BYTES = 128 * 128;
-  static constexpr int STAGE_BYTES = 3 * BOX_BYTES + 2 * PH_BYTES;   // x0, x1, dh_in, image0 | image1
-  static constexpr int ST_FIT = (232448 - 1024 - 256) / STAGE_BYTES;
-  static constexpr int ST = ST_FIT < 4 ? ST_FIT : 4;
+  static constexpr int XD_BYTES = 3 * BOX_BYTES;         // x0, x1, dh_in
+  static constexpr int PH2_BYTES = 2 * PH_BYTES;         // image0 | image1
+  static constexpr int kBudget = 232448 - 1024 - 256;
+  // as many x / dh_in slots as fit beside two image slots (at most 4), else one image slot
+  static constexpr int PST = (kBudget - 2 * PH2_BYTES) / XD_BYTES >= 2 ? 2 : 1;
+  static constexpr int XST_FIT = (kBudget - PST * PH2_BYTES) / XD_BYTES;
+  static constexpr int XST = XST_FIT < 4 ? XST_FIT : 4;
   static constexpr int DHM_COL = 256;                    // TMEM: accumulators 0..255, DHM from here
   static constexpr int TMEM_COLS = 512;
   static constexpr int RW = Dims<n>::RW;
-  static constexpr int SMEM = 1024 + ST * STAGE_BYTES + 256;
+  static constexpr int SMEM = 1024 + XST * XD_BYTES + PST * PH2_BYTES + 256;
   static_assert(n % 2 == 0, "pairs of streams");
-  static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 128-B swizzle atoms aligned");
-  static_assert(ST >= 2, "ring depth");
+  static_assert(XD_BYTES % 1024 == 0 && PH2_BYTES % 1024 == 0, "slots keep the 128-B swizzle atoms aligned");
+  static_assert(XST >= 2 && PST >= 1, "ring depth");
   static_assert(DHM_COL + KA / 2 <= TMEM_COLS, "TMEM");
   static_assert(SMEM <= 232448, "shared memory");
 };
 
-constexpr int kPThreads = 10 * 32;   // W0, W1, WG_E(8)
+constexpr int kPThreads = 11 * 32;   // W0 (x, dh_in), W1 (MMA), WG_E(8), W10 (phi images)
 
 // grid = (tiles, slices); CTA (tile, y) takes the pairs [y * kp_per, ...) of
 // the nD / 128 pairs; pair p = blocks q = 2p, 2p + 1 of the stream-fastest
@@ -724,12 +731,13 @@ __global__ void __launch_bounds__(kPThreads, 1)
   using namespace sm100;
   using Cf = DxPairCfg<n>;
   constexpr int N_OUT = Cf::N_OUT;
-  constexpr int ST = Cf::ST;
-  constexpr int FULL = 0, EMPTY = ST, ACC_FULL = 2 * ST, ACC_EMPTY = 2 * ST + 2, DHM_FULL = 2 * ST + 4,
-                NBARS = 2 * ST + 5;
+  constexpr int XST = Cf::XST, PST = Cf::PST;
+  constexpr int FULL = 0, EMPTY = XST, PFULL = 2 * XST, PEMPTY = PFULL + PST, ACC_FULL = PEMPTY + PST,
+                ACC_EMPTY = ACC_FULL + 2, DHM_FULL = ACC_EMPTY + 2, NBARS = DHM_FULL + 1;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(stages + ST * Cf::STAGE_BYTES);
+  uint8_t* images = stages + XST * Cf::XD_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(images + PST * Cf::PH2_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -743,9 +751,13 @@ __global__ void __launch_bounds__(kPThreads, 1)
   auto kb_of = [&](int q) { return (q % n) * DB + q / n; };
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < ST; ++i) {
+    for (int i = 0; i < XST; ++i) {
       mbar_init(bar(FULL + i), 1);
-      mbar_init(bar(EMPTY + i), 2);   // MMA commit + the store issuer once its stores have read the stage
+      mbar_init(bar(EMPTY + i), 1);   // the store issuer once its stores have read the slot
+    }
+    for (int i = 0; i < PST; ++i) {
+      mbar_init(bar(PFULL + i), 1);
+      mbar_init(bar(PEMPTY + i), 1);  // the MMA commit
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(ACC_FULL + i), 1);
@@ -771,23 +783,35 @@ __global__ void __launch_bounds__(kPThreads, 1)
   const WaitCtx wc{abort_flag, status};
 
   if (warp == 0) {
-    // ---------------------------------------------------------- W0: x pair, dh_in, phi image pair
+    // ---------------------------------------------------------- W0: x pair, dh_in
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
       for (int b = 0; b < npairs; ++b) {
-        const int s = b % ST;
+        const int s = b % XST;
         const int q = 2 * (p0 + b);
         const int kb0 = kb_of(q), kb1 = kb_of(q + 1);
-        mbar_wait(bar(EMPTY + s), ((b / ST) & 1) ^ 1, wc);
+        mbar_wait(bar(EMPTY + s), ((b / XST) & 1) ^ 1, wc);
         if (*abort_flag) continue;
-        const uint32_t st = smem_u32(stages + s * Cf::STAGE_BYTES);
-        mbar_arrive_expect_tx(bar(FULL + s), Cf::STAGE_BYTES);
+        const uint32_t st = smem_u32(stages + s * Cf::XD_BYTES);
+        mbar_arrive_expect_tx(bar(FULL + s), Cf::XD_BYTES);
         tma_load_2d(st, &map_x, bar(FULL + s), kb0 * 64, tile * 128, pol);
         tma_load_2d(st + Cf::BOX_BYTES, &map_x, bar(FULL + s), kb1 * 64, tile * 128, pol);
         tma_load_2d(st + 2 * Cf::BOX_BYTES, &map_dh, bar(FULL + s), (kb0 * 64) % D, tile * 128, pol);
-        bulk_g2s(st + 3 * Cf::BOX_BYTES, img + (size_t)kb0 * Cf::PH_BYTES, Cf::PH_BYTES, bar(FULL + s));
-        bulk_g2s(st + 3 * Cf::BOX_BYTES + Cf::PH_BYTES, img + (size_t)kb1 * Cf::PH_BYTES, Cf::PH_BYTES,
-                 bar(FULL + s));
+      }
+    }
+  } else if (warp == 10) {
+    // ---------------------------------------------------------- W10: phi image pair
+    if (lane == 0) {
+      for (int b = 0; b < npairs; ++b) {
+        const int s = b % PST;
+        const int q = 2 * (p0 + b);
+        const int kb0 = kb_of(q), kb1 = kb_of(q + 1);
+        mbar_wait(bar(PEMPTY + s), ((b / PST) & 1) ^ 1, wc);
+        if (*abort_flag) continue;
+        const uint32_t im = smem_u32(images + s * Cf::PH2_BYTES);
+        mbar_arrive_expect_tx(bar(PFULL + s), Cf::PH2_BYTES);
+        bulk_g2s(im, img + (size_t)kb0 * Cf::PH_BYTES, Cf::PH_BYTES, bar(PFULL + s));
+        bulk_g2s(im + Cf::PH_BYTES, img + (size_t)kb1 * Cf::PH_BYTES, Cf::PH_BYTES, bar(PFULL + s));
       }
     }
   } else if (warp == 1) {
@@ -798,14 +822,13 @@ __global__ void __launch_bounds__(kPThreads, 1)
       tc_fence_after();
       const uint32_t a_t = tmem_base + Cf::DHM_COL;
       for (int b = 0; b < npairs; ++b) {
-        const int s = b % ST, ab = b & 1;
-        mbar_wait(bar(FULL + s), (b / ST) & 1, wc);
+        const int s = b % PST, ab = b & 1;
+        mbar_wait(bar(PFULL + s), (b / PST) & 1, wc);
         mbar_wait(bar(ACC_EMPTY + ab), ((b >> 1) & 1) ^ 1, wc);
         tc_fence_after();
         if (*abort_flag) continue;
         // the two images stack into one 128-row K-major interleaved operand
-        const uint64_t b_dv = bwdtc::desc_kmajor_interleave(
-            smem_u32(stages + s * Cf::STAGE_BYTES + 3 * Cf::BOX_BYTES), 128, Cf::RG);
+        const uint64_t b_dv = bwdtc::desc_kmajor_interleave(smem_u32(images + s * Cf::PH2_BYTES), 128, Cf::RG);
         const uint32_t d = tmem_base + ab * 128;
 #pragma unroll
         for (int pr = 0; pr < 6; ++pr) {
@@ -816,7 +839,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
             umma_bf16_ta(d, a_t + ca, b_dv + (cb >> 4), idesc, pr != 0 || ks != 0);
           }
         }
-        umma_commit(bar(EMPTY + s));
+        umma_commit(bar(PEMPTY + s));
         umma_commit(bar(ACC_FULL + ab));
       }
     }
@@ -869,12 +892,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
     const uint64_t pol_out = l2_policy_evict_first();
     for (int b = 0; b < npairs; ++b) {
-      const int s = b % ST, ab = b & 1;
+      const int s = b % XST, ab = b & 1;
       const int q = 2 * (p0 + b);
       mbar_wait(bar(ACC_FULL + ab), (b >> 1) & 1, wc);
-      mbar_wait(bar(FULL + s), (b / ST) & 1, wc);   // the stage's boxes (already complete)
+      mbar_wait(bar(FULL + s), (b / XST) & 1, wc);   // the slot's x and dh_in boxes
       tc_fence_after();
-      const uint32_t st = smem_u32(stages + s * Cf::STAGE_BYTES);
+      const uint32_t st = smem_u32(stages + s * Cf::XD_BYTES);
       const uint32_t g_row = st + 2 * Cf::BOX_BYTES + row * 128;
       {
         const int h = grp;
